@@ -1,0 +1,510 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized-FFN path (one JSON line on rank 0).
+
+Default workload: a 48-layer stack of qwen3next-shaped
+MoE feed-forward layers (hidden 2048, 512 experts, top-10, intermediate 512,
+shared expert, gate/up Q4_K, down Q6_K), decode batch 32, each layer
+x <- x + MoE(rms_norm(x)) as in the qwen3next block (llambda.lisp
+L5738-5746).  Weights are synthetic (seeded generator, 50 GB at N=1), made on
+the device.  With --gpus N the 512 experts of every layer are split over N
+ranks (expert parallel, 512/N each), every rank holds the replicated
+activations, and the per-layer partial outputs meet in one NCCL all-reduce.
+
+Reported:
+  value         tokens/s of the whole job, device-resident, CUDA events,
+                max over ranks
+  e2e           the same through the C ABI with host buffers: one
+                llambda_cuda_moe_session_run per layer per step, host copies
+                inside the timed region
+  roofline      the MoE layer (router + experts + combine) as the unit:
+                algorithmic bytes (router + shared + distinct experts) per
+                layer / measured layer time, against the measured HBM peak
+  kernels       dense dequant-GEMV roofline (configs 1 and 2) timed alone
+  cpu_baseline  the CPU oracle (a C restatement of the reference path, AVX2,
+                all host threads) on a bounded sample, rank 0 only
+
+--impl reference times the reference's CPU path (the oracle port; the Lisp
+reference cannot run here: no SBCL, Windows-only) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+NOMINAL_HBM_GBS = 8000.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--layers", type=int, default=48)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-kernels", action="store_true")
+    p.add_argument("--workload", default="stack",
+                   choices=["stack", "config1", "config2", "config3", "config4"])
+    return p.parse_args()
+
+
+def hbm_peak():
+    try:
+        with open(PEAKS_PATH) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- distributed
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=300))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------- workload
+
+def build_stack(cfg, layers, rank, world, seed, max_tokens, torch):
+    """Device-resident synthetic layers; returns (sessions, owned bytes)."""
+    import llambda_b200 as LB
+    from llambda_b200 import configs as CF
+    E = cfg.experts
+    eb, ee = rank * E // world, (rank + 1) * E // world
+    sessions, keep = [], []
+    norm_w = torch.ones(cfg.hidden, dtype=torch.float32)  # post_attention_norm, unit weights
+    for layer in range(layers):
+        s = CF.layer_seed(seed, layer)
+        tensors = {}
+        for name, t, ne0, ne1, ne2, stream, scale in CF.moe_tensor_specs(cfg):
+            unit = 4 if t == LB.TYPE_F32 else (144 if t == LB.TYPE_Q4_K else 210)
+            per = CF.tensor_units(t, ne0, ne1, 1)
+            if ne2 > 1:
+                first, count = per * eb, per * (ee - eb)   # only this rank's experts
+            else:
+                first, count = 0, per
+            buf = torch.empty(count * unit + 256, dtype=torch.uint8, device="cuda")
+            LB.synth_fill_device(t, s, stream, first, count, scale, buf)
+            keep.append(buf)
+            if name in ("exp_probs_b.bias", "ffn_gate_inp_shexp"):
+                tensors[name] = buf
+            else:
+                # the session indexes experts globally: point at expert 0
+                tensors[name] = (t, ne0, ne1, ne2, _ShiftedPtr(buf, -(per * unit * eb) if ne2 > 1 else 0))
+        sess = LB.MoeSession.create(
+            cfg.arch, cfg.hidden, cfg.top_k, tensors, weight_scale=cfg.weight_scale,
+            weights_norm=cfg.weights_norm, on_device=True, expert_range=(eb, ee),
+            shared_here=(rank == 0), max_tokens=max_tokens,
+            input_norm=norm_w.cuda(), norm_epsilon=1e-6, add_residual=(rank == 0))
+        sessions.append(sess)
+    torch.cuda.synchronize()
+    return sessions, keep
+
+
+class _ShiftedPtr:
+    """A device pointer offset from a torch buffer (expert shards index from
+    the global expert 0)."""
+
+    def __init__(self, buf, offset):
+        self.buf, self.offset = buf, offset
+
+    def data_ptr(self):
+        return self.buf.data_ptr() + self.offset
+
+
+def distinct_experts(sel: np.ndarray, E: int) -> int:
+    return int(np.unique(sel[sel >= 0]).size)
+
+
+# ----------------------------------------------------------------- CPU side
+
+def cpu_layer_sample(cfg, seed, tokens):
+    """One host layer (oracle generator) and a timed CPU forward of `tokens`."""
+    from oracle import oracle as O
+    from tests.helpers import host_layer, oracle_layer
+    tensors = host_layer(cfg, seed)
+    L = oracle_layer(cfg, tensors, input_norm=np.ones(cfg.hidden, np.float32), eps=1e-6,
+                     residual=True)
+    x = O.synth_f32(seed, 1, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
+    return O, L, x, tensors
+
+
+def time_cpu_stack(cfg, layers, batch, seed, steps, warmup):
+    """Seconds per layer for `batch` tokens through one layer on all host cores."""
+    O, L, x, keep = cpu_layer_sample(cfg, seed, batch)
+    O.set_workers(os.cpu_count() or 1)
+    for _ in range(warmup):
+        O.moe_forward(L, x, batch, cfg.top_k)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        O.moe_forward(L, x, batch, cfg.top_k)
+        ts.append(time.perf_counter() - t0)
+    per_layer = statistics.median(ts)
+    tok_s = batch / (per_layer * layers)
+    return tok_s, per_layer
+
+
+# ----------------------------------------------------------------- kernels alone
+
+def time_dense_gemv(torch, LB, cfg, tokens, reps=20):
+    """Dense GEMV (configs 1/2) timed alone; rotates weight copies past L2."""
+    from llambda_b200 import configs as CF
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    wb = cfg.weight_bytes
+    copies = max(1, math.ceil(3 * l2 / wb))
+    unit = 144 if cfg.type == LB.TYPE_Q4_K else 210
+    bufs, sessions = [], []
+    for c in range(copies):
+        b = torch.empty(wb + 256, dtype=torch.uint8, device="cuda")
+        LB.synth_fill_device(cfg.type, c, CF.S_DENSE, 0, wb // unit, cfg.dscale, b)
+        bufs.append(b)
+        sessions.append(LB.ProjectionSession.from_device(cfg.type, cfg.cols, cfg.rows, b))
+    x = torch.randn(tokens, cfg.cols, device="cuda")
+    y = torch.empty(tokens, cfg.rows, device="cuda")
+    stream = torch.cuda.current_stream()
+    for i in range(3):
+        sessions[i % copies].run_device(x, y, tokens, stream)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    for i in range(reps):
+        sessions[i % copies].run_device(x, y, tokens, stream)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / reps
+    nbytes = cfg.algorithmic_bytes(tokens)
+    for s in sessions:
+        s.close()
+    del bufs
+    torch.cuda.empty_cache()
+    return {"workload": cfg.name, "tokens": tokens, "us_per_launch": ms * 1e3,
+            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms * 1e-3) / 1e9,
+            "weight_copies_rotated": copies}
+
+
+# ----------------------------------------------------------------- main arms
+
+def run_reference(args):
+    """--impl reference: the reference CPU path (oracle port) on host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from llambda_b200 import configs as CF
+    cfg = CF.CONFIG3
+    sample_tokens = args.batch
+    cores = os.cpu_count() or 1
+    O, L, x, keep = cpu_layer_sample(cfg, args.seed, sample_tokens)
+    O.set_workers(cores)
+    for _ in range(max(1, args.warmup)):
+        O.moe_forward(L, x, sample_tokens, cfg.top_k)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.moe_forward(L, x, sample_tokens, cfg.top_k)
+        ts.append(time.perf_counter() - t0)
+    per_layer = sum(ts) / len(ts)
+    value = sample_tokens / (per_layer * args.layers)
+    sample = (f"{sample_tokens} decode tokens through 1 of the {args.layers} qwen3next layers per "
+              f"step, time x {args.layers} layers (CPU oracle: C restatement of llambda.lisp "
+              f"L4338-4658/L5321-5426, AVX2+FMA, {cores} OpenMP threads)")
+    line = {"impl": "reference", "metric": "MoE FFN decode tokens/s", "value": value,
+            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per_layer * args.layers * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config5_qwen3next_moe_stack_{args.layers}L_decode_b{args.batch}",
+                       "batch": args.batch, "layers": args.layers},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "SBCL path unavailable on this box; the timed reference is the oracle port"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import llambda_b200 as LB
+    from llambda_b200 import configs as CF
+    rank, world, local = dist_setup(args.gpus)
+    if LB.probe() != 1:
+        raise SystemExit("CUDA backend unavailable: " + LB._native.last_error())
+    cfg = CF.CONFIG3
+    B, NL = args.batch, args.layers
+    t_setup = time.time()
+    sessions, keep = build_stack(cfg, NL, rank, world, args.seed, max(B, 1), torch)
+    setup_s = time.time() - t_setup
+    x0 = torch.empty(B, cfg.hidden, device="cuda")
+    LB.synth_fill_device(LB.TYPE_F32, args.seed, CF.S_ACT, 0, B * cfg.hidden, 1.0, x0)
+    bufs = [torch.empty(B, cfg.hidden, device="cuda") for _ in range(2)]
+    stream = torch.cuda.current_stream()
+    if world > 1:
+        import torch.distributed as dist
+
+    def step(record=None):
+        cur = x0
+        for li, s in enumerate(sessions):
+            out = bufs[li % 2]
+            if record is not None:
+                record[li][0].record(stream)
+            s.run_device(cur, out, B, stream=stream)
+            if world > 1:
+                dist.all_reduce(out)
+            if record is not None:
+                record[li][1].record(stream)
+            cur = out
+        return cur
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    for s in sessions:
+        if s.status() != 0:
+            raise SystemExit("device status reported a non-positive router weight sum")
+    layer_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(NL)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(args.steps):
+        step(layer_ev if k == args.steps - 1 else None)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms, world)
+    value = B / (ms * 1e-3)
+    layer_ms = [a.elapsed_time(b) for a, b in layer_ev]
+
+    # routing of the timed steps (identical every step: same x0) -> algorithmic bytes
+    sel = torch.empty(B, cfg.top_k, dtype=torch.int32, device="cuda")
+    cur = x0
+    distinct = []
+    for li, s in enumerate(sessions):
+        out = bufs[li % 2]
+        s.run_device(cur, out, B, sel_dev=sel, stream=stream)
+        if world > 1:
+            dist.all_reduce(out)
+        distinct.append(distinct_experts(sel.cpu().numpy(), cfg.experts))
+        cur = out
+    torch.cuda.synchronize()
+    eb, ee = rank * cfg.experts // world, (rank + 1) * cfg.experts // world
+    own_distinct = []
+    cur = x0
+    for li, s in enumerate(sessions):
+        out = bufs[li % 2]
+        s.run_device(cur, out, B, sel_dev=sel, stream=stream)
+        if world > 1:
+            dist.all_reduce(out)
+        ss = sel.cpu().numpy()
+        own_distinct.append(int(np.unique(ss[(ss >= eb) & (ss < ee)]).size))
+        cur = out
+    layer_bytes = [cfg.router_bytes() + (cfg.shared_bytes() if rank == 0 else 0)
+                   + u * cfg.expert_bytes() + 2 * 4 * B * cfg.hidden for u in own_distinct]
+    peak, peak_kind = hbm_peak()
+    achieved = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "moe_layer (rms_norm+router+route+up+down+combine)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                "algorithmic_bytes_per_layer": int(sum(layer_bytes) / NL),
+                "layer_us_mean": round(statistics.mean(layer_ms) * 1e3, 2),
+                "traffic": None}
+
+    # e2e through the C ABI with host buffers (one call per layer per step)
+    e2e = None
+    if not args.no_e2e:
+        x_host = x0.cpu().numpy().copy()
+        if world > 1:
+            import torch.distributed as dist
+            gloo = dist.new_group(backend="gloo")
+
+        def e2e_step():
+            cur_h = x_host
+            for s in sessions:
+                out_h = s.run(cur_h)
+                if world > 1:
+                    t = torch.from_numpy(out_h)
+                    dist.all_reduce(t, group=gloo)
+                    out_h = t.numpy()
+                cur_h = out_h
+            return cur_h
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        dt = (time.perf_counter() - t0) / args.steps
+        dt = max_over_ranks(dt, world)
+        e2e = {"value": B / dt, "unit": "tokens/s",
+               "h2d_bytes_per_step": NL * B * cfg.hidden * 4,
+               "d2h_bytes_per_step": NL * B * cfg.hidden * 4,
+               "path": "llambda_cuda_moe_session_run per layer (host float buffers)"}
+
+    kernels = None
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_kernels:
+            for s in sessions:
+                pass
+            kernels = {}
+            try:
+                kernels["config1_b1"] = time_dense_gemv(torch, LB, CF.CONFIG1, 1)
+                kernels["config2_b1"] = time_dense_gemv(torch, LB, CF.CONFIG2, 1)
+                kernels["config2_b8"] = time_dense_gemv(torch, LB, CF.CONFIG2, 8)
+                for v in kernels.values():
+                    v["frac"] = round(v["achieved_gbs"] / peak, 4)
+            except Exception as e:  # memory pressure at N=1 with the stack resident
+                kernels["error"] = str(e)
+        if not args.no_cpu_baseline:
+            cores = os.cpu_count() or 1
+            tok_s, per_layer = time_cpu_stack(cfg, NL, B, args.seed, steps=3, warmup=1)
+            cpu = {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                   "sample": f"{B} tokens through 1 qwen3next layer per sample "
+                             f"({per_layer * 1e3:.1f} ms), scaled to {NL} layers"}
+
+    launches_per_layer = 6
+    line = {"metric": "MoE FFN decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config5_qwen3next_moe_stack_{NL}L_decode_b{B}",
+                       "batch": B, "layers": NL, "experts": cfg.experts, "top_k": cfg.top_k,
+                       "hidden": cfg.hidden, "parallelism": f"ep{world}",
+                       "l2": "weights streamed per step exceed L2 (no flush needed)",
+                       "setup_s": round(setup_s, 1)},
+            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": launches_per_layer * NL * args.steps,
+            "distinct_experts_per_layer_mean": round(statistics.mean(distinct), 1)}
+    if kernels is not None:
+        line["kernels"] = kernels
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for s in sessions:
+        s.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,770 @@
+// C ABI of the llambda B200 backend (declarations and contract in
+// include/llambda_cuda.h).  Host-side session management: uploads raw GGUF
+// tensors once, keeps one CUDA stream and pinned bounce buffers per session,
+// serialises calls per session, and reports failures through a status int
+// plus a thread-local message, as llambda's ONNX bridge does
+// (native/llambda_npu.cpp:24, 43-49).
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/llambda_cuda.h"
+#include "kernels.h"
+
+extern "C" void lb_sha256_hex(const void* data, size_t n, char out[65]);
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Failure : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+void set_error(const std::string& m) { g_last_error = m; }
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear a sticky launch error where possible
+    throw Failure(std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                  cudaGetErrorString(e) + ")");
+  }
+}
+
+size_t row_bytes(int type, uint64_t ne0) {
+  switch (type) {
+    case LLAMBDA_CUDA_TYPE_F32: return ne0 * 4;
+    case LLAMBDA_CUDA_TYPE_Q4_K: return ne0 % 256 ? 0 : ne0 / 256 * 144;
+    case LLAMBDA_CUDA_TYPE_Q6_K: return ne0 % 256 ? 0 : ne0 / 256 * 210;
+    default: return 0;
+  }
+}
+
+const char* type_name(int type) {
+  switch (type) {
+    case LLAMBDA_CUDA_TYPE_F32: return "F32";
+    case LLAMBDA_CUDA_TYPE_Q4_K: return "Q4_K";
+    case LLAMBDA_CUDA_TYPE_Q6_K: return "Q6_K";
+    default: return "unsupported";
+  }
+}
+
+void require_rows(int type, uint64_t ne0, const char* what) {
+  if (type != LLAMBDA_CUDA_TYPE_F32 && type != LLAMBDA_CUDA_TYPE_Q4_K &&
+      type != LLAMBDA_CUDA_TYPE_Q6_K)
+    throw Failure(std::string(what) + ": unsupported GGML type tag " + std::to_string(type));
+  if (!row_bytes(type, ne0))
+    throw Failure(std::string(what) + ": " + type_name(type) + " rows need a multiple of 256 "
+                  "columns, got " + std::to_string(ne0));
+}
+
+int current_device() {
+  int d = 0;
+  cuda_check(cudaGetDevice(&d), "cudaGetDevice");
+  return d;
+}
+
+void require_b200(int dev) {
+  cudaDeviceProp p;
+  cuda_check(cudaGetDeviceProperties(&p, dev), "cudaGetDeviceProperties");
+  if (p.major != 10 || p.minor != 0)
+    throw Failure(std::string("device ") + p.name + " is sm_" + std::to_string(p.major) +
+                  std::to_string(p.minor) + "; this library is built for sm_100a (B200)");
+}
+
+// Device allocation with 256 bytes of slack: the Q6_K loaders read up to
+// 4 bytes past a 16-byte chunk inside a block, never past the tensor, but the
+// slack keeps every read of a tensor's last block inside the allocation.
+void* dev_alloc(size_t bytes) {
+  void* p = nullptr;
+  cuda_check(cudaMalloc(&p, bytes + 256), "cudaMalloc");
+  return p;
+}
+
+void validate_scales(int type, const void* dev, size_t bytes, cudaStream_t s, const char* what) {
+  if (type != LLAMBDA_CUDA_TYPE_Q4_K && type != LLAMBDA_CUDA_TYPE_Q6_K) return;
+  const size_t blocks = bytes / (type == LLAMBDA_CUDA_TYPE_Q4_K ? 144 : 210);
+  unsigned* bad = nullptr;
+  cuda_check(cudaMalloc(&bad, sizeof(unsigned)), "cudaMalloc");
+  unsigned host = 0;
+  cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess) e = lb::check_fp16_scales(type, dev, blocks, bad, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&host, bad, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(bad);
+  cuda_check(e, "fp16 scale check");
+  if (host)
+    throw Failure(std::string(what) + ": " + std::to_string(host) +
+                  " block(s) have an Inf/NaN fp16 scale (unsupported fp16 special value)");
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Pinned host bounce buffer, grown on demand.
+struct Pinned {
+  void* p = nullptr;
+  size_t n = 0;
+  void* get(size_t bytes) {
+    if (bytes > n) {
+      if (p) cudaFreeHost(p);
+      p = nullptr;
+      n = 0;
+      cuda_check(cudaMallocHost(&p, bytes), "cudaMallocHost");
+      n = bytes;
+    }
+    return p;
+  }
+  ~Pinned() {
+    if (p) cudaFreeHost(p);
+  }
+};
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  void* get(size_t bytes) {
+    if (bytes > n) {
+      if (p) cudaFree(p);
+      p = nullptr;
+      n = 0;
+      cuda_check(cudaMalloc(&p, bytes), "cudaMalloc");
+      n = bytes;
+    }
+    return p;
+  }
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    g_last_error.clear();
+    return f();
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return -1;
+  } catch (...) {
+    set_error("unknown error");
+    return -1;
+  }
+}
+
+}  // namespace
+
+struct llambda_cuda_session {
+  int type = 0;
+  uint64_t ne0 = 0, ne1 = 0, ne2 = 1;
+  size_t rb = 0;
+  int device = 0;
+  void* weights = nullptr;
+  bool owned = false;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  Pinned hin, hout;
+  DevBuf din, dout;
+  ~llambda_cuda_session() {
+    if (stream) cudaStreamDestroy(stream);
+    if (owned && weights) cudaFree(weights);
+  }
+};
+
+struct llambda_cuda_moe_session {
+  lb::MoeDevice m{};
+  lb::MoeWork w{};
+  int device = 0;
+  int max_tokens = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  std::vector<void*> owned;
+  void* work = nullptr;
+  Pinned hx, hout, hsel, hw;
+  DevBuf dx, dout, dsel, dw;
+  ~llambda_cuda_moe_session() {
+    if (stream) cudaStreamDestroy(stream);
+    for (void* p : owned) cudaFree(p);
+    if (work) cudaFree(work);
+  }
+};
+
+extern "C" {
+
+int llambda_cuda_probe(void) {
+  try {
+    g_last_error.clear();
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver || n == 0) {
+      cudaGetLastError();
+      set_error(std::string("No usable CUDA device: ") + cudaGetErrorString(e));
+      return 0;
+    }
+    cuda_check(e, "cudaGetDeviceCount");
+    try {
+      require_b200(current_device());
+    } catch (const Failure& f) {
+      set_error(f.what());
+      return 0;
+    }
+    return 1;
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return -1;
+  }
+}
+
+const char* llambda_cuda_bridge_version(void) { return "cuda-sm100a-1"; }
+
+const char* llambda_cuda_runtime_version(void) {
+  try {
+    g_last_error.clear();
+    thread_local std::string v;
+    int rt = 0, drv = 0;
+    cuda_check(cudaRuntimeGetVersion(&rt), "cudaRuntimeGetVersion");
+    cuda_check(cudaDriverGetVersion(&drv), "cudaDriverGetVersion");
+    char buf[256];
+    std::snprintf(buf, sizeof(buf), "CUDA runtime %d.%d, driver %d.%d", rt / 1000, (rt % 1000) / 10,
+                  drv / 1000, (drv % 1000) / 10);
+    v = buf;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) == cudaSuccess && n > 0) {
+      cudaDeviceProp p;
+      if (cudaGetDeviceProperties(&p, current_device()) == cudaSuccess)
+        v += std::string(", ") + p.name + " sm_" + std::to_string(p.major) + std::to_string(p.minor);
+    } else {
+      cudaGetLastError();
+    }
+    return v.c_str();
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return nullptr;
+  }
+}
+
+const char* llambda_cuda_last_error(void) { return g_last_error.c_str(); }
+
+int llambda_cuda_sha256(const void* data, size_t data_size, char* output, size_t output_size) {
+  if ((!data && data_size != 0) || !output || output_size < 65) {
+    set_error("SHA-256 requires input data and a 65-byte output buffer.");
+    return -1;
+  }
+  g_last_error.clear();
+  lb_sha256_hex(data, data_size, output);
+  return 0;
+}
+
+static int session_make(int type, uint64_t ne0, uint64_t ne1, uint64_t ne2, const void* data,
+                        size_t data_size, bool on_device, llambda_cuda_session** result) {
+  if (!result) {
+    set_error("A result pointer is required.");
+    return -1;
+  }
+  *result = nullptr;
+  return guarded([&] {
+    if (!data) throw Failure("Tensor data is required.");
+    if (ne0 == 0 || ne1 == 0) throw Failure("Tensor dimensions must be positive.");
+    if (ne2 == 0) ne2 = 1;
+    require_rows(type, ne0, "projection tensor");
+    const size_t rb = row_bytes(type, ne0);
+    const size_t bytes = rb * ne1 * ne2;
+    if (!on_device && data_size != bytes)
+      throw Failure("Tensor data size " + std::to_string(data_size) + " does not match " +
+                    std::to_string(bytes) + " bytes of " + type_name(type) + " data.");
+    if (ne1 > 0x7fffffffull || ne0 > 0x7fffffffull) throw Failure("Tensor too large.");
+    auto s = new llambda_cuda_session();
+    try {
+      s->type = type;
+      s->ne0 = ne0;
+      s->ne1 = ne1;
+      s->ne2 = ne2;
+      s->rb = rb;
+      s->device = current_device();
+      require_b200(s->device);
+      cuda_check(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+      if (on_device) {
+        s->weights = const_cast<void*>(data);
+        s->owned = false;
+      } else {
+        s->weights = dev_alloc(bytes);
+        s->owned = true;
+        cuda_check(cudaMemcpyAsync(s->weights, data, bytes, cudaMemcpyHostToDevice, s->stream),
+                   "upload tensor");
+      }
+      validate_scales(type, s->weights, bytes, s->stream, "projection tensor");
+    } catch (...) {
+      delete s;
+      throw;
+    }
+    *result = s;
+    return 0;
+  });
+}
+
+int llambda_cuda_session_create_from_tensor(int type, uint64_t ne0, uint64_t ne1, uint64_t ne2,
+                                            const void* data, size_t data_size,
+                                            llambda_cuda_session** result) {
+  return session_make(type, ne0, ne1, ne2, data, data_size, false, result);
+}
+
+int llambda_cuda_session_create_device(int type, uint64_t ne0, uint64_t ne1, uint64_t ne2,
+                                       const void* device_data, llambda_cuda_session** result) {
+  return session_make(type, ne0, ne1, ne2, device_data, 0, true, result);
+}
+
+int llambda_cuda_session_create(const char* model_path, llambda_cuda_session** result) {
+  if (!model_path || !result) {
+    set_error("Model path and result pointer are required.");
+    return -1;
+  }
+  *result = nullptr;
+  std::vector<unsigned char> data;
+  uint32_t type = 0;
+  uint64_t ne0 = 0, ne1 = 0, ne2 = 0;
+  int rc = guarded([&] {
+    FILE* f = std::fopen(model_path, "rb");
+    if (!f) throw Failure(std::string("Cannot open projection file ") + model_path);
+    struct Closer {
+      FILE* f;
+      ~Closer() { std::fclose(f); }
+    } closer{f};
+    unsigned char hdr[56];
+    if (std::fread(hdr, 1, sizeof(hdr), f) != sizeof(hdr) || std::memcmp(hdr, "LLBCUDA1", 8) != 0)
+      throw Failure(std::string("Not a llambda CUDA projection file: ") + model_path);
+    auto u32 = [&](int o) {
+      uint32_t v;
+      std::memcpy(&v, hdr + o, 4);
+      return v;
+    };
+    auto u64 = [&](int o) {
+      uint64_t v;
+      std::memcpy(&v, hdr + o, 8);
+      return v;
+    };
+    if (u32(8) != 1) throw Failure("Unsupported projection file version.");
+    type = u32(12);
+    ne0 = u64(16);
+    ne1 = u64(24);
+    ne2 = u64(32);
+    const uint64_t nbytes = u64(40), offset = u64(48);
+    require_rows((int)type, ne0, "projection file");
+    if (nbytes != row_bytes((int)type, ne0) * ne1 * (ne2 ? ne2 : 1))
+      throw Failure("Projection file data size does not match its dimensions.");
+    if (offset < sizeof(hdr) || std::fseek(f, (long)offset, SEEK_SET) != 0)
+      throw Failure("Projection file data offset is invalid.");
+    data.resize(nbytes);
+    if (std::fread(data.data(), 1, nbytes, f) != nbytes)
+      throw Failure("Projection file is truncated.");
+    return 0;
+  });
+  if (rc) return rc;
+  return session_make((int)type, ne0, ne1, ne2, data.data(), data.size(), false, result);
+}
+
+void llambda_cuda_session_destroy(llambda_cuda_session* session) {
+  if (!session) return;
+  try {
+    DeviceGuard g(session->device);
+    if (session->stream) cudaStreamSynchronize(session->stream);
+    delete session;
+  } catch (...) {
+    delete session;
+  }
+}
+
+size_t llambda_cuda_session_input_element_count(const llambda_cuda_session* s) {
+  return s ? s->ne0 : 0;
+}
+
+size_t llambda_cuda_session_output_element_count(const llambda_cuda_session* s) {
+  return s ? s->ne1 : 0;
+}
+
+static int session_run_rows(llambda_cuda_session* s, int expert, const float* input, size_t tokens,
+                            float* output) {
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    if (expert < 0 || (uint64_t)expert >= s->ne2)
+      throw Failure("Expert index " + std::to_string(expert) + " is out of range for a tensor with " +
+                    std::to_string(s->ne2) + " experts.");
+    const size_t in_bytes = tokens * s->ne0 * 4, out_bytes = tokens * s->ne1 * 4;
+    float* hin = static_cast<float*>(s->hin.get(in_bytes));
+    float* hout = static_cast<float*>(s->hout.get(out_bytes));
+    float* din = static_cast<float*>(s->din.get(in_bytes));
+    float* dout = static_cast<float*>(s->dout.get(out_bytes));
+    std::memcpy(hin, input, in_bytes);
+    cuda_check(cudaMemcpyAsync(din, hin, in_bytes, cudaMemcpyHostToDevice, s->stream), "input copy");
+    const uint8_t* W = static_cast<const uint8_t*>(s->weights) + (size_t)expert * s->ne1 * s->rb;
+    cuda_check(lb::launch_gemv(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, din, (long)s->ne0,
+                               (int)s->ne0, (int)tokens, dout, (long)s->ne1, s->stream),
+               "GEMV launch");
+    cuda_check(cudaMemcpyAsync(hout, dout, out_bytes, cudaMemcpyDeviceToHost, s->stream), "output copy");
+    cuda_check(cudaStreamSynchronize(s->stream), "GEMV");
+    std::memcpy(output, hout, out_bytes);
+    return 0;
+  });
+}
+
+int llambda_cuda_session_run(llambda_cuda_session* session, const float* input,
+                             size_t input_element_count, float* output,
+                             size_t output_element_count) {
+  if (!session || !input || !output) {
+    set_error("Session, input, and output are required.");
+    return -1;
+  }
+  if (input_element_count != session->ne0 || output_element_count != session->ne1) {
+    set_error("Input or output element count does not match the projection tensor.");
+    return -1;
+  }
+  return session_run_rows(session, 0, input, 1, output);
+}
+
+int llambda_cuda_session_run_batch(llambda_cuda_session* session, const float* input,
+                                   size_t tokens, float* output) {
+  if (!session || !input || !output || tokens == 0) {
+    set_error("Session, input, output and a positive token count are required.");
+    return -1;
+  }
+  return session_run_rows(session, 0, input, tokens, output);
+}
+
+int llambda_cuda_session_run_expert(llambda_cuda_session* session, int expert, const float* input,
+                                    size_t input_element_count, float* output,
+                                    size_t output_element_count) {
+  if (!session || !input || !output) {
+    set_error("Session, input, and output are required.");
+    return -1;
+  }
+  if (input_element_count != session->ne0 || output_element_count != session->ne1) {
+    set_error("Input or output element count does not match the expert tensor.");
+    return -1;
+  }
+  return session_run_rows(session, expert, input, 1, output);
+}
+
+int llambda_cuda_session_run_device(llambda_cuda_session* s, const float* device_input,
+                                    size_t tokens, float* device_output, void* cuda_stream) {
+  if (!s || !device_input || !device_output || tokens == 0) {
+    set_error("Session, device input/output and a positive token count are required.");
+    return -1;
+  }
+  return guarded([&] {
+    DeviceGuard g(s->device);
+    cuda_check(lb::launch_gemv(s->type, s->weights, s->rb, (int)s->ne1, (int)s->ne0, device_input,
+                               (long)s->ne0, (int)s->ne0, (int)tokens, device_output, (long)s->ne1,
+                               static_cast<cudaStream_t>(cuda_stream)),
+               "GEMV launch");
+    return 0;
+  });
+}
+
+// ------------------------------------------------------------------ MoE
+
+static void check_tensor(const llambda_cuda_tensor& t, const char* what, bool required) {
+  if (!t.data) {
+    if (required) throw Failure(std::string("MoE tensor ") + what + " is required.");
+    return;
+  }
+  require_rows(t.type, t.ne0, what);
+  if (t.type == LLAMBDA_CUDA_TYPE_F32 && std::strcmp(what, "ffn_gate_inp") != 0)
+    throw Failure(std::string("MoE tensor ") + what + " must be Q4_K or Q6_K.");
+}
+
+int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
+                                    llambda_cuda_moe_session** result) {
+  if (!result) {
+    set_error("A result pointer is required.");
+    return -1;
+  }
+  *result = nullptr;
+  if (!d) {
+    set_error("A MoE descriptor is required.");
+    return -1;
+  }
+  return guarded([&] {
+    if (d->arch != LLAMBDA_CUDA_ARCH_QWEN3NEXT && d->arch != LLAMBDA_CUDA_ARCH_NEMOTRON_H_MOE)
+      throw Failure("Unknown MoE architecture " + std::to_string(d->arch));
+    const bool qwen = d->arch == LLAMBDA_CUDA_ARCH_QWEN3NEXT;
+    const uint64_t H = d->hidden;
+    if (!H || H > (1u << 20)) throw Failure("MoE hidden size must be positive.");
+    if (!d->router.data || d->router.type != LLAMBDA_CUDA_TYPE_F32)
+      throw Failure("MoE router ffn_gate_inp must be an F32 tensor.");
+    if (d->router.ne0 != H) throw Failure("Router row width does not match the hidden size.");
+    const uint64_t E = d->router.ne1;
+    if (E == 0 || E > 1024) throw Failure("MoE expert count must be in 1..1024.");
+    check_tensor(d->up_exps, "ffn_up_exps", true);
+    check_tensor(d->down_exps, "ffn_down_exps", true);
+    check_tensor(d->gate_exps, "ffn_gate_exps", qwen);
+    const bool shared = d->up_shexp.data != nullptr;
+    if (shared) {
+      check_tensor(d->up_shexp, "ffn_up_shexp", true);
+      check_tensor(d->down_shexp, "ffn_down_shexp", true);
+      check_tensor(d->gate_shexp, "ffn_gate_shexp", qwen);
+      if (qwen && !d->shared_gate_inp) throw Failure("ffn_gate_inp_shexp is required.");
+    }
+    const uint64_t I = d->up_exps.ne1;
+    auto dims = [&](const llambda_cuda_tensor& t, uint64_t min_ne0, uint64_t ne1, uint64_t ne2,
+                    const char* what) {
+      if (t.ne0 < min_ne0 || t.ne1 != ne1 || (ne2 && (t.ne2 ? t.ne2 : 1) != ne2))
+        throw Failure(std::string("MoE tensor ") + what + " has unexpected dimensions.");
+    };
+    dims(d->up_exps, H, I, E, "ffn_up_exps");
+    if (qwen) {
+      dims(d->gate_exps, H, I, E, "ffn_gate_exps");
+      if (d->gate_exps.ne0 != d->up_exps.ne0 || d->gate_exps.type != d->up_exps.type)
+        throw Failure("ffn_gate_exps and ffn_up_exps must share type and width.");
+    }
+    dims(d->down_exps, I, H, E, "ffn_down_exps");
+    uint64_t Ish = 0;
+    if (shared) {
+      Ish = d->up_shexp.ne1;
+      dims(d->up_shexp, H, Ish, 0, "ffn_up_shexp");
+      dims(d->down_shexp, Ish, H, 0, "ffn_down_shexp");
+      if (qwen) {
+        dims(d->gate_shexp, H, Ish, 0, "ffn_gate_shexp");
+        if (d->gate_shexp.type != d->up_shexp.type || d->gate_shexp.ne0 != d->up_shexp.ne0)
+          throw Failure("ffn_gate_shexp and ffn_up_shexp must share type and width.");
+      }
+      if (d->up_shexp.type != d->up_exps.type || d->down_shexp.type != d->down_exps.type)
+        throw Failure("Shared and routed expert tensors must share their types.");
+    }
+    const int top_k = (int)std::min<uint64_t>((uint64_t)std::max(d->top_k, 1), E);
+    if (d->top_k < 1 || top_k > 32) throw Failure("top_k must be in 1..32.");
+    int eb = d->expert_begin, ee = d->expert_end;
+    if (eb == 0 && ee == 0) ee = (int)E;
+    if (eb < 0 || ee > (int)E || eb >= ee) throw Failure("Invalid owned expert range.");
+    if (d->max_tokens < 1 || (int64_t)d->max_tokens * top_k > 4096)
+      throw Failure("max_tokens must be positive and max_tokens * top_k at most 4096.");
+
+    auto s = new llambda_cuda_moe_session();
+    try {
+      s->device = current_device();
+      require_b200(s->device);
+      cuda_check(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+      const cudaMemcpyKind kind =
+          d->data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+      auto upload = [&](const void* src, size_t bytes) -> void* {
+        void* p = dev_alloc(bytes);
+        s->owned.push_back(p);
+        cuda_check(cudaMemcpyAsync(p, src, bytes, kind, s->stream), "upload");
+        return p;
+      };
+      // Expert tensors: only the owned experts [eb, ee) are kept on this device.
+      auto experts = [&](const llambda_cuda_tensor& t, const char* what) -> const uint8_t* {
+        if (!t.data) return nullptr;
+        const size_t per = row_bytes(t.type, t.ne0) * t.ne1;
+        const size_t bytes = per * (size_t)(ee - eb);
+        const uint8_t* src = static_cast<const uint8_t*>(t.data) + per * (size_t)eb;
+        const uint8_t* p;
+        if (d->data_on_device) {
+          p = src;  // borrowed
+        } else {
+          p = static_cast<const uint8_t*>(upload(src, bytes));
+        }
+        validate_scales(t.type, p, bytes, s->stream, what);
+        return p - per * (size_t)eb;  // indexable by global expert id in [eb, ee)
+      };
+      auto plain = [&](const llambda_cuda_tensor& t, const char* what) -> const uint8_t* {
+        if (!t.data) return nullptr;
+        const size_t bytes = row_bytes(t.type, t.ne0) * t.ne1;
+        const uint8_t* p = d->data_on_device ? static_cast<const uint8_t*>(t.data)
+                                             : static_cast<const uint8_t*>(upload(t.data, bytes));
+        validate_scales(t.type, p, bytes, s->stream, what);
+        return p;
+      };
+      lb::MoeDevice& m = s->m;
+      m.arch = d->arch;
+      m.hidden = (int)H;
+      m.experts = (int)E;
+      m.top_k = top_k;
+      m.weights_norm = d->weights_norm ? 1 : 0;
+      m.weight_scale = d->weight_scale;
+      m.inter = (int)I;
+      m.inter_sh = (int)Ish;
+      m.k_in = (int)d->up_exps.ne0;
+      m.k_down = (int)d->down_exps.ne0;
+      m.k_in_sh = shared ? (int)d->up_shexp.ne0 : 0;
+      m.k_down_sh = shared ? (int)d->down_shexp.ne0 : 0;
+      m.gate_type = qwen ? d->gate_exps.type : d->up_exps.type;
+      m.up_type = d->up_exps.type;
+      m.down_type = d->down_exps.type;
+      m.gate_sh_type = qwen && shared ? d->gate_shexp.type : m.gate_type;
+      m.up_sh_type = shared ? d->up_shexp.type : m.up_type;
+      m.down_sh_type = shared ? d->down_shexp.type : m.down_type;
+      // Router, with the qwen3next shared-expert gate vector appended as row E.
+      {
+        const size_t rbytes = (size_t)E * H * 4;
+        float* r = static_cast<float*>(dev_alloc(rbytes + H * 4));
+        s->owned.push_back(r);
+        cuda_check(cudaMemcpyAsync(r, d->router.data, rbytes, kind, s->stream), "upload router");
+        if (qwen && shared)
+          cuda_check(cudaMemcpyAsync(r + E * H, d->shared_gate_inp, H * 4, kind, s->stream),
+                     "upload shared gate");
+        else
+          cuda_check(cudaMemsetAsync(r + E * H, 0, H * 4, s->stream), "memset");
+        m.router = r;
+      }
+      if (d->router_bias) {
+        if (qwen) throw Failure("A router bias is only defined for nemotron_h_moe.");
+        m.router_bias = static_cast<const float*>(upload(d->router_bias, E * 4));
+      }
+      m.gate_exps = qwen ? experts(d->gate_exps, "ffn_gate_exps") : nullptr;
+      m.up_exps = experts(d->up_exps, "ffn_up_exps");
+      m.down_exps = experts(d->down_exps, "ffn_down_exps");
+      m.gate_rb = qwen ? row_bytes(d->gate_exps.type, d->gate_exps.ne0) : 0;
+      m.up_rb = row_bytes(d->up_exps.type, d->up_exps.ne0);
+      m.down_rb = row_bytes(d->down_exps.type, d->down_exps.ne0);
+      m.shared_here = shared && d->shared_here ? 1 : 0;
+      if (m.shared_here) {
+        m.gate_sh = qwen ? plain(d->gate_shexp, "ffn_gate_shexp") : nullptr;
+        m.up_sh = plain(d->up_shexp, "ffn_up_shexp");
+        m.down_sh = plain(d->down_shexp, "ffn_down_shexp");
+        m.gate_sh_rb = qwen ? row_bytes(d->gate_shexp.type, d->gate_shexp.ne0) : 0;
+        m.up_sh_rb = row_bytes(d->up_shexp.type, d->up_shexp.ne0);
+        m.down_sh_rb = row_bytes(d->down_shexp.type, d->down_shexp.ne0);
+      } else {
+        m.inter_sh = 0;
+      }
+      m.expert_begin = eb;
+      m.expert_end = ee;
+      if (d->input_norm) m.input_norm = static_cast<const float*>(upload(d->input_norm, H * 4));
+      m.norm_epsilon = d->norm_epsilon;
+      m.add_residual = d->add_residual ? 1 : 0;
+      s->max_tokens = d->max_tokens;
+      const size_t wb = lb::moe_work_bytes(m, d->max_tokens);
+      cuda_check(cudaMalloc(&s->work, wb), "cudaMalloc workspace");
+      cuda_check(cudaMemsetAsync(s->work, 0, wb, s->stream), "memset workspace");
+      lb::moe_work_carve(m, d->max_tokens, s->work, &s->w);
+      cuda_check(cudaStreamSynchronize(s->stream), "MoE session upload");
+    } catch (...) {
+      delete s;
+      throw;
+    }
+    *result = s;
+    return 0;
+  });
+}
+
+void llambda_cuda_moe_session_destroy(llambda_cuda_moe_session* session) {
+  if (!session) return;
+  try {
+    DeviceGuard g(session->device);
+    if (session->stream) cudaStreamSynchronize(session->stream);
+    delete session;
+  } catch (...) {
+    delete session;
+  }
+}
+
+size_t llambda_cuda_moe_session_hidden(const llambda_cuda_moe_session* s) {
+  return s ? (size_t)s->m.hidden : 0;
+}
+
+int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, size_t tokens,
+                                 float* out, int32_t* selected, float* weights) {
+  if (!s || !x || !out || tokens == 0) {
+    set_error("Session, input, output and a positive token count are required.");
+    return -1;
+  }
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    if ((int64_t)tokens > s->max_tokens)
+      throw Failure("Token count " + std::to_string(tokens) + " exceeds the session's max_tokens " +
+                    std::to_string(s->max_tokens) + ".");
+    const int T = (int)tokens, k = s->m.top_k;
+    const size_t xb = tokens * s->m.hidden * 4, sb = tokens * k * 4;
+    float* hx = static_cast<float*>(s->hx.get(xb));
+    float* hout = static_cast<float*>(s->hout.get(xb));
+    float* dx = static_cast<float*>(s->dx.get(xb));
+    float* dout = static_cast<float*>(s->dout.get(xb));
+    std::memcpy(hx, x, xb);
+    int status = 0;
+    cuda_check(cudaMemsetAsync(s->w.status, 0, 4, s->stream), "memset");
+    cuda_check(cudaMemcpyAsync(dx, hx, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
+    cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, s->stream), "MoE launch");
+    cuda_check(cudaMemcpyAsync(hout, dout, xb, cudaMemcpyDeviceToHost, s->stream), "output copy");
+    int32_t* hsel = selected ? static_cast<int32_t*>(s->hsel.get(sb)) : nullptr;
+    float* hw = weights ? static_cast<float*>(s->hw.get(sb)) : nullptr;
+    if (hsel)
+      cuda_check(cudaMemcpyAsync(hsel, s->w.sel, sb, cudaMemcpyDeviceToHost, s->stream), "copy");
+    if (hw) cuda_check(cudaMemcpyAsync(hw, s->w.wts, sb, cudaMemcpyDeviceToHost, s->stream), "copy");
+    cuda_check(cudaMemcpyAsync(&status, s->w.status, 4, cudaMemcpyDeviceToHost, s->stream), "copy");
+    cuda_check(cudaStreamSynchronize(s->stream), "MoE layer");
+    if (status)
+      throw Failure("MoE router produced non-positive top-k weight sum.");
+    std::memcpy(out, hout, xb);
+    if (hsel) std::memcpy(selected, hsel, sb);
+    if (hw) std::memcpy(weights, hw, sb);
+    return 0;
+  });
+}
+
+int llambda_cuda_moe_session_run_device(llambda_cuda_moe_session* s, const float* device_x,
+                                        size_t tokens, float* device_out,
+                                        int32_t* device_selected, float* device_weights,
+                                        void* cuda_stream) {
+  if (!s || !device_x || !device_out || tokens == 0) {
+    set_error("Session, device input/output and a positive token count are required.");
+    return -1;
+  }
+  return guarded([&] {
+    DeviceGuard g(s->device);
+    if ((int64_t)tokens > s->max_tokens) throw Failure("Token count exceeds max_tokens.");
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    cuda_check(lb::launch_moe(s->m, s->w, device_x, (int)tokens, device_out, st), "MoE launch");
+    const size_t sb = tokens * s->m.top_k * 4;
+    if (device_selected)
+      cuda_check(cudaMemcpyAsync(device_selected, s->w.sel, sb, cudaMemcpyDeviceToDevice, st), "copy");
+    if (device_weights)
+      cuda_check(cudaMemcpyAsync(device_weights, s->w.wts, sb, cudaMemcpyDeviceToDevice, st), "copy");
+    return 0;
+  });
+}
+
+int llambda_cuda_moe_session_status(llambda_cuda_moe_session* s) {
+  if (!s) {
+    set_error("A session is required.");
+    return -1;
+  }
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    int status = 0;
+    cuda_check(cudaMemcpy(&status, s->w.status, 4, cudaMemcpyDeviceToHost), "status copy");
+    cuda_check(cudaMemset(s->w.status, 0, 4), "status clear");
+    return status;
+  });
+}
+
+int llambda_cuda_synth_fill_device(int type, uint64_t seed, uint64_t stream_id, uint64_t first,
+                                   size_t count, float scale, void* device_out, void* cuda_stream) {
+  if (!device_out) {
+    set_error("An output buffer is required.");
+    return -1;
+  }
+  return guarded([&] {
+    cuda_check(lb::synth_fill(type, seed, stream_id, first, count, scale, device_out,
+                              static_cast<cudaStream_t>(cuda_stream)),
+               "synthetic fill");
+    return 0;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,144 @@
+"""GPU parity of the MoE feed-forward layer (qwen3next-moe-into, L5321-5426;
+nemotron-h-moe-ffn-into, L5827-5949) against the CPU oracle on identical
+seeded tensors, through the C ABI."""
+import dataclasses
+
+import numpy as np
+import pytest
+
+import llambda_b200 as LB
+from llambda_b200 import configs as CF
+from oracle import oracle as O
+from tests.helpers import MAX_REL, gpu_tensors, host_layer, max_rel, oracle_layer
+
+pytestmark = pytest.mark.gpu
+
+SMALL_QWEN = dataclasses.replace(CF.CONFIG3, name="small_qwen", hidden=512, experts=24, top_k=5,
+                                 inter=256, inter_sh=512)
+SMALL_NEMO = dataclasses.replace(CF.CONFIG4, name="small_nemo", hidden=400, experts=16, top_k=3,
+                                 inter=200, inter_sh=300)
+
+
+def _session(cfg, tensors, max_tokens, **kw):
+    return LB.MoeSession.create(cfg.arch, cfg.hidden, cfg.top_k, gpu_tensors(tensors),
+                                weight_scale=cfg.weight_scale, weights_norm=cfg.weights_norm,
+                                max_tokens=max_tokens, **kw)
+
+
+def _check_selection(cfg, tensors, x, sel_gpu, sel_ref):
+    """Selected experts must be identical wherever the k-th/(k+1)-th score
+    margin exceeds 1e-6."""
+    t, ne0, ne1, _, router = tensors["ffn_gate_inp"]
+    bias = tensors["exp_probs_b.bias"][4] if "exp_probs_b.bias" in tensors else None
+    checked = 0
+    for i, xi in enumerate(x):
+        logits = O.gemv(O.TYPE_F32, router, ne0, ne1, xi)
+        if bias is not None:
+            logits = logits + bias
+        srt = np.sort(logits)[::-1]
+        k = cfg.top_k
+        if k < srt.size and srt[k - 1] - srt[k] <= 1e-6:
+            continue
+        assert set(sel_gpu[i].tolist()) == set(sel_ref[i].tolist())
+        gaps = -np.diff(srt[:k])
+        if np.all(gaps > 1e-6):
+            assert sel_gpu[i].tolist() == sel_ref[i].tolist()
+        checked += 1
+    assert checked >= max(1, len(x) // 2)
+
+
+@pytest.mark.parametrize("cfg", [SMALL_QWEN, SMALL_NEMO], ids=lambda c: c.name)
+@pytest.mark.parametrize("tokens", [1, 3, 9, 33])
+def test_small_layer_matches_oracle(cfg, tokens):
+    tensors = host_layer(cfg, seed=5)
+    x = O.synth_f32(5, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
+    ref, sel_ref, w_ref = O.moe_forward(oracle_layer(cfg, tensors), x, tokens, cfg.top_k)
+    s = _session(cfg, tensors, max_tokens=64)
+    out, sel, w = s.run(x, with_routing=True)
+    _check_selection(cfg, tensors, x, sel, sel_ref)
+    same = np.all(sel == sel_ref, axis=1)
+    assert same.mean() > 0.5
+    assert max_rel(out[same], ref[same]) < MAX_REL
+    assert max_rel(out[same], ref[same]) < 1e-5
+    assert max_rel(w[same], w_ref[same]) < 1e-6
+
+
+@pytest.mark.parametrize("norm", [False, True])
+@pytest.mark.parametrize("scale", [1.0, 2.5])
+def test_nemotron_weight_policy(norm, scale):
+    cfg = dataclasses.replace(SMALL_NEMO, weights_norm=norm, weight_scale=scale)
+    tensors = host_layer(cfg, seed=8)
+    x = O.synth_f32(8, CF.S_ACT, 0, 4 * cfg.hidden, 1.0).reshape(4, cfg.hidden)
+    ref, sel_ref, w_ref = O.moe_forward(oracle_layer(cfg, tensors), x, 4, cfg.top_k)
+    out, sel, w = _session(cfg, tensors, 8).run(x, with_routing=True)
+    same = np.all(sel == sel_ref, axis=1)
+    assert same.all()
+    assert max_rel(w, w_ref) < 1e-6
+    assert max_rel(out, ref) < 1e-5
+
+
+def test_norm_and_residual():
+    cfg = SMALL_QWEN
+    tensors = host_layer(cfg, seed=3)
+    nw = O.synth_f32(3, 30, 0, cfg.hidden, 1.0)
+    x = O.synth_f32(3, CF.S_ACT, 0, 5 * cfg.hidden, 3.0).reshape(5, cfg.hidden)
+    ref, sel_ref, _ = O.moe_forward(oracle_layer(cfg, tensors, input_norm=nw, eps=1e-6,
+                                                 residual=True), x, 5, cfg.top_k)
+    out, sel, _ = _session(cfg, tensors, 8, input_norm=nw, norm_epsilon=1e-6,
+                           add_residual=True).run(x, with_routing=True)
+    same = np.all(sel == sel_ref, axis=1)
+    assert same.mean() > 0.5
+    assert max_rel(out[same], ref[same]) < 1e-5
+
+
+def test_expert_parallel_split_sums_to_full():
+    """Expert-parallel shards (owned expert ranges, shared expert on one
+    shard) add up to the whole layer."""
+    cfg = SMALL_QWEN
+    tensors = host_layer(cfg, seed=4)
+    x = O.synth_f32(4, CF.S_ACT, 0, 7 * cfg.hidden, 1.0).reshape(7, cfg.hidden)
+    full = _session(cfg, tensors, 8).run(x)
+    parts = [_session(cfg, tensors, 8, expert_range=(a, b), shared_here=(a == 0)).run(x)
+             for a, b in ((0, 10), (10, 17), (17, cfg.experts))]
+    assert max_rel(sum(parts), full) < 1e-5
+
+
+def test_non_positive_weight_sum_is_an_error():
+    # nemotron with norm on and a weight scale; all-zero router with a bias of
+    # -inf-like values makes every sigmoid 0 -> the reference errors (L5903-5905)
+    cfg = dataclasses.replace(SMALL_NEMO, weights_norm=True)
+    tensors = host_layer(cfg, seed=2)
+    t = list(tensors["exp_probs_b.bias"])
+    t[4] = np.full(cfg.experts, -1e30, np.float32)
+    tensors["exp_probs_b.bias"] = tuple(t)
+    x = O.synth_f32(2, CF.S_ACT, 0, cfg.hidden, 1.0)
+    with pytest.raises(O.OracleError):
+        O.moe_forward(oracle_layer(cfg, tensors), x, 1, cfg.top_k)
+    with pytest.raises(LB.LlambdaCudaError, match="non-positive"):
+        _session(cfg, tensors, 2).run(x)
+
+
+@pytest.mark.parametrize("tokens", [1, 16])
+def test_config3_full_layer(tokens):
+    cfg = CF.CONFIG3
+    tensors = host_layer(cfg, seed=0)
+    x = O.synth_f32(0, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
+    ref, sel_ref, w_ref = O.moe_forward(oracle_layer(cfg, tensors), x, tokens, cfg.top_k)
+    out, sel, w = _session(cfg, tensors, 64).run(x, with_routing=True)
+    _check_selection(cfg, tensors, x, sel, sel_ref)
+    same = np.all(sel == sel_ref, axis=1)
+    assert max_rel(out[same], ref[same]) < MAX_REL
+    assert max_rel(out[same], ref[same]) < 1e-5
+
+
+@pytest.mark.parametrize("tokens", [1, 64])
+def test_config4_full_layer(tokens):
+    cfg = CF.CONFIG4
+    tensors = host_layer(cfg, seed=0)
+    x = O.synth_f32(0, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
+    ref, sel_ref, w_ref = O.moe_forward(oracle_layer(cfg, tensors), x, tokens, cfg.top_k)
+    out, sel, w = _session(cfg, tensors, 64).run(x, with_routing=True)
+    _check_selection(cfg, tensors, x, sel, sel_ref)
+    same = np.all(sel == sel_ref, axis=1)
+    assert max_rel(out[same], ref[same]) < MAX_REL
+    assert max_rel(out[same], ref[same]) < 1e-5
