@@ -212,6 +212,40 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_run_device(llambda_cuda_moe_sessio
  * a CUDA error. */
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_status(llambda_cuda_moe_session* session);
 
+/* One MoE layer without any device allocation.  This entry point has no
+ * counterpart in the reference.
+ *
+ * It is for callers that cannot call cudaMalloc: a host whose device memory
+ * is already claimed by its own pooling allocator (so a cudaMalloc would
+ * fail or fragment the pool), or a latency-critical decode loop that must not
+ * pay for cudaMalloc/cudaFree and the device-wide synchronisation they can
+ * cause.  Such callers keep every tensor in device memory themselves and pass
+ * it here: `desc` must have data_on_device = 1 (weights, router, bias, norm
+ * and the qwen3next shared-gate vector all in device memory, expert tensors
+ * starting at expert 0), `device_x` and `device_out` are [tokens][hidden]
+ * device arrays, and nothing is uploaded or copied into owned buffers.
+ *
+ * Working memory comes from one static device array of
+ * LLAMBDA_CUDA_STATIC_SCRATCH_BYTES (16 MiB) that every GPU loading this
+ * library holds until the process exits.  A call whose working set (it grows
+ * with tokens, top_k, the expert intermediate size and hidden) does not fit
+ * fails with a message naming the limit.  All calls share the array and it
+ * keeps the previous call's contents: the call clears what must start at
+ * zero, but two calls that overlap on the GPU (different streams, threads or
+ * devices sharing a context) race on it, so serialise them.
+ *
+ * The first call on each device looks up the array's device address with
+ * that device current; make that first call before any stream capture.  The
+ * call enqueues on `cuda_stream`, then waits for it, and returns -1 (message
+ * in last_error) when a token's top-k weight sum is not positive, like
+ * llambda_cuda_moe_session_run.  Inf/NaN fp16 scales are not checked here
+ * (sessions check them at creation). */
+#define LLAMBDA_CUDA_STATIC_SCRATCH_BYTES (16u << 20)
+LLAMBDA_CUDA_API int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
+                                                             const float* device_x,
+                                                             size_t tokens, float* device_out,
+                                                             void* cuda_stream);
+
 /* ------------------------------------------------------------------------
  * Synthetic GGUF data for benchmarks and tests (seeded, counter-based; the
  * same generator runs on the host in the test oracle, byte for byte).

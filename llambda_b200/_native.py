@@ -81,6 +81,7 @@ SIGNATURES = {
     "llambda_cuda_moe_session_run": (C.c_int, [_vp, _fp, _sz, _fp, _i32p, _fp]),
     "llambda_cuda_moe_session_run_device": (C.c_int, [_vp, _vp, _sz, _vp, _vp, _vp, _vp]),
     "llambda_cuda_moe_session_status": (C.c_int, [_vp]),
+    "llambda_cuda_moe_forward_static_scratch": (C.c_int, [C.POINTER(MoeDesc), _vp, _sz, _vp, _vp]),
     "llambda_cuda_synth_fill_device": (C.c_int, [C.c_int, _u64, _u64, _u64, _sz, C.c_float, _vp,
                                                  _vp]),
 }

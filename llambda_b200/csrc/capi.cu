@@ -753,6 +753,177 @@ int llambda_cuda_moe_session_status(llambda_cuda_moe_session* s) {
   });
 }
 
+}  // extern "C"
+
+// ------------------------------------------------- MoE layer, no allocation
+//
+// For callers that cannot allocate device memory (their allocator owns the
+// device, or their decode loop must not pay for cudaMalloc and its implicit
+// synchronisation): the layer's working memory is this one static array, and
+// every tensor is the caller's device memory.  The array exists on every GPU
+// that loads the library, for the life of the process.
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_moe_static_scratch[LLAMBDA_CUDA_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxScratchDevices] = {};
+
+// Device address of the static array on the current device, looked up once
+// per device with that device current.  The name g_moe_static_scratch in
+// host code is only a host-side handle; kernels must get this address.
+void* static_scratch_address(int dev) {
+  if (dev < 0 || dev >= kMaxScratchDevices) throw Failure("device index out of range");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    cuda_check(cudaGetSymbolAddress(&p, g_moe_static_scratch), "cudaGetSymbolAddress");
+    if (!p) throw Failure("cudaGetSymbolAddress returned a null scratch address");
+    g_scratch_addr[dev] = p;
+  }
+  return g_scratch_addr[dev];
+}
+
+// The layer description of a device-resident desc, without uploads.
+lb::MoeDevice static_layer(const llambda_cuda_moe_desc* d) {
+  if (!d->data_on_device) throw Failure("The static-scratch MoE call needs data_on_device = 1.");
+  if (d->arch != LLAMBDA_CUDA_ARCH_QWEN3NEXT && d->arch != LLAMBDA_CUDA_ARCH_NEMOTRON_H_MOE)
+    throw Failure("Unknown MoE architecture " + std::to_string(d->arch));
+  const bool qwen = d->arch == LLAMBDA_CUDA_ARCH_QWEN3NEXT;
+  const uint64_t H = d->hidden;
+  if (!H || H > (1u << 20)) throw Failure("MoE hidden size must be positive.");
+  if (!d->router.data || d->router.type != LLAMBDA_CUDA_TYPE_F32 || d->router.ne0 != H)
+    throw Failure("MoE router ffn_gate_inp must be an F32 tensor of row width hidden.");
+  const uint64_t E = d->router.ne1;
+  if (E == 0 || E > 1024) throw Failure("MoE expert count must be in 1..1024.");
+  check_tensor(d->up_exps, "ffn_up_exps", true);
+  check_tensor(d->down_exps, "ffn_down_exps", true);
+  check_tensor(d->gate_exps, "ffn_gate_exps", qwen);
+  const bool shared = d->up_shexp.data != nullptr;
+  if (shared) {
+    check_tensor(d->up_shexp, "ffn_up_shexp", true);
+    check_tensor(d->down_shexp, "ffn_down_shexp", true);
+    check_tensor(d->gate_shexp, "ffn_gate_shexp", qwen);
+    if (qwen && !d->shared_gate_inp) throw Failure("ffn_gate_inp_shexp is required.");
+  }
+  const uint64_t I = d->up_exps.ne1, Ish = shared ? d->up_shexp.ne1 : 0;
+  auto dims = [&](const llambda_cuda_tensor& t, uint64_t min_ne0, uint64_t ne1, uint64_t ne2,
+                  const char* what) {
+    if (t.ne0 < min_ne0 || t.ne1 != ne1 || (ne2 && (t.ne2 ? t.ne2 : 1) != ne2))
+      throw Failure(std::string("MoE tensor ") + what + " has unexpected dimensions.");
+  };
+  dims(d->up_exps, H, I, E, "ffn_up_exps");
+  dims(d->down_exps, I, H, E, "ffn_down_exps");
+  if (qwen) {
+    dims(d->gate_exps, H, I, E, "ffn_gate_exps");
+    if (d->gate_exps.ne0 != d->up_exps.ne0 || d->gate_exps.type != d->up_exps.type)
+      throw Failure("ffn_gate_exps and ffn_up_exps must share type and width.");
+  }
+  if (shared) {
+    dims(d->up_shexp, H, Ish, 0, "ffn_up_shexp");
+    dims(d->down_shexp, Ish, H, 0, "ffn_down_shexp");
+    if (qwen) {
+      dims(d->gate_shexp, H, Ish, 0, "ffn_gate_shexp");
+      if (d->gate_shexp.type != d->up_shexp.type || d->gate_shexp.ne0 != d->up_shexp.ne0)
+        throw Failure("ffn_gate_shexp and ffn_up_shexp must share type and width.");
+    }
+    if (d->up_shexp.type != d->up_exps.type || d->down_shexp.type != d->down_exps.type)
+      throw Failure("Shared and routed expert tensors must share their types.");
+  }
+  if (d->router_bias && qwen) throw Failure("A router bias is only defined for nemotron_h_moe.");
+  const int top_k = (int)std::min<uint64_t>((uint64_t)std::max(d->top_k, 1), E);
+  if (d->top_k < 1 || top_k > 32) throw Failure("top_k must be in 1..32.");
+  int eb = d->expert_begin, ee = d->expert_end;
+  if (eb == 0 && ee == 0) ee = (int)E;
+  if (eb < 0 || ee > (int)E || eb >= ee) throw Failure("Invalid owned expert range.");
+  lb::MoeDevice m{};
+  m.arch = d->arch;
+  m.hidden = (int)H;
+  m.experts = (int)E;
+  m.top_k = top_k;
+  m.weights_norm = d->weights_norm ? 1 : 0;
+  m.weight_scale = d->weight_scale;
+  m.inter = (int)I;
+  m.k_in = (int)d->up_exps.ne0;
+  m.k_down = (int)d->down_exps.ne0;
+  m.gate_type = qwen ? d->gate_exps.type : d->up_exps.type;
+  m.up_type = d->up_exps.type;
+  m.down_type = d->down_exps.type;
+  m.router = static_cast<const float*>(d->router.data);
+  m.router_extra_row = qwen && shared ? d->shared_gate_inp : nullptr;
+  m.router_bias = d->router_bias;
+  m.gate_exps = qwen ? static_cast<const uint8_t*>(d->gate_exps.data) : nullptr;
+  m.up_exps = static_cast<const uint8_t*>(d->up_exps.data);
+  m.down_exps = static_cast<const uint8_t*>(d->down_exps.data);
+  m.gate_rb = qwen ? row_bytes(d->gate_exps.type, d->gate_exps.ne0) : 0;
+  m.up_rb = row_bytes(d->up_exps.type, d->up_exps.ne0);
+  m.down_rb = row_bytes(d->down_exps.type, d->down_exps.ne0);
+  m.shared_here = shared && d->shared_here ? 1 : 0;
+  if (m.shared_here) {
+    m.inter_sh = (int)Ish;
+    m.k_in_sh = (int)d->up_shexp.ne0;
+    m.k_down_sh = (int)d->down_shexp.ne0;
+    m.gate_sh_type = qwen ? d->gate_shexp.type : m.gate_type;
+    m.up_sh_type = d->up_shexp.type;
+    m.down_sh_type = d->down_shexp.type;
+    m.gate_sh = qwen ? static_cast<const uint8_t*>(d->gate_shexp.data) : nullptr;
+    m.up_sh = static_cast<const uint8_t*>(d->up_shexp.data);
+    m.down_sh = static_cast<const uint8_t*>(d->down_shexp.data);
+    m.gate_sh_rb = qwen ? row_bytes(d->gate_shexp.type, d->gate_shexp.ne0) : 0;
+    m.up_sh_rb = row_bytes(d->up_shexp.type, d->up_shexp.ne0);
+    m.down_sh_rb = row_bytes(d->down_shexp.type, d->down_shexp.ne0);
+  } else {
+    m.gate_sh_type = m.gate_type;
+    m.up_sh_type = m.up_type;
+    m.down_sh_type = m.down_type;
+  }
+  m.expert_begin = eb;
+  m.expert_end = ee;
+  m.input_norm = d->input_norm;
+  m.norm_epsilon = d->norm_epsilon;
+  m.add_residual = d->add_residual ? 1 : 0;
+  return m;
+}
+
+}  // namespace
+
+extern "C" {
+
+int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
+                                            const float* device_x, size_t tokens,
+                                            float* device_out, void* cuda_stream) {
+  if (!desc || !device_x || !device_out || tokens == 0) {
+    set_error("A descriptor, device input/output and a positive token count are required.");
+    return -1;
+  }
+  return guarded([&] {
+    const lb::MoeDevice m = static_layer(desc);
+    if ((int64_t)tokens * m.top_k > 4096)
+      throw Failure("tokens * top_k must be at most 4096.");
+    const int T = (int)tokens;
+    const size_t need = lb::moe_work_bytes(m, T);
+    if (need > LLAMBDA_CUDA_STATIC_SCRATCH_BYTES)
+      throw Failure("This layer call needs " + std::to_string(need) +
+                    " bytes of working memory; the static scratch holds " +
+                    std::to_string((size_t)LLAMBDA_CUDA_STATIC_SCRATCH_BYTES) +
+                    " bytes (use fewer tokens per call or a MoE session).");
+    void* base = static_scratch_address(current_device());
+    lb::MoeWork w{};
+    lb::moe_work_carve(m, T, base, &w);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    int status = 0;
+    cuda_check(cudaMemsetAsync(w.status, 0, sizeof(int), st), "clear status");
+    cuda_check(lb::launch_moe(m, w, device_x, T, device_out, st), "MoE launch");
+    cuda_check(cudaMemcpyAsync(&status, w.status, sizeof(int), cudaMemcpyDeviceToHost, st),
+               "status copy");
+    cuda_check(cudaStreamSynchronize(st), "MoE layer");
+    if (status) throw Failure("MoE router produced non-positive top-k weight sum.");
+    return 0;
+  });
+}
+
 int llambda_cuda_synth_fill_device(int type, uint64_t seed, uint64_t stream_id, uint64_t first,
                                    size_t count, float scale, void* device_out, void* cuda_stream) {
   if (!device_out) {

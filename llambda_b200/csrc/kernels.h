@@ -55,6 +55,9 @@ struct MoeDevice {
   const float* input_norm;                  // rms-norm weight applied to x first, or null
   float norm_epsilon;
   int add_residual;                         // out = x + moe(norm(x))
+  // Shared-expert gate row kept apart from `router` (router then has E rows);
+  // null when the row is appended to `router` as row E.
+  const float* router_extra_row;
 };
 
 // Scratch for one layer call with up to max_tokens tokens.

@@ -437,13 +437,18 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   if (T > w.max_tokens || m.experts > kMaxExperts || m.top_k > 32 || T * m.top_k > 4 * 1024)
     return cudaErrorInvalidValue;
   const int E = m.experts;
-  const int router_rows = E + (m.arch == 0 ? 1 : 0);
+  const int router_rows = E + (m.arch == 0 && !m.router_extra_row ? 1 : 0);
   const float* x_in = x;
   cudaError_t e;
   if (m.input_norm) {
     rms_norm_kernel<<<T, 256, 0, s>>>(x, m.input_norm, m.norm_epsilon, m.hidden, w.xnorm);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     x = w.xnorm;
+  }
+  if (m.arch == 0 && m.router_extra_row) {  // shared-expert gate logit into column E
+    e = launch_gemv(LB_TYPE_F32, m.router_extra_row, (size_t)m.hidden * 4, 1, m.hidden, x,
+                    m.hidden, m.hidden, T, w.logits + E, E + 1, s);
+    if (e != cudaSuccess) return e;
   }
   e = launch_gemv(LB_TYPE_F32, m.router, (size_t)m.hidden * 4, router_rows, m.hidden,
                               x, m.hidden, m.hidden, T, w.logits, E + 1, s);
