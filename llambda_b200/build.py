@@ -18,7 +18,7 @@ LIB = os.path.join(HERE, "libllambda_cuda.so")
 
 CU_SOURCES = ["gemv.cu", "moe.cu", "capi.cu"]
 C_SOURCES = ["sha256.c"]
-HEADERS = ["common.cuh", "rowdot.cuh", "kernels.h", "synth.h"]
+HEADERS = ["common.cuh", "engine.cuh", "kernels.h", "synth.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",

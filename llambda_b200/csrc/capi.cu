@@ -178,12 +178,41 @@ struct llambda_cuda_session {
   cudaStream_t stream = nullptr;
   std::mutex mu;
   Pinned hin, hout;
-  DevBuf din, dout;
+  DevBuf din, dout, dxp;
+  int* status = nullptr;  // device status word of the GEMV kernels
   ~llambda_cuda_session() {
     if (stream) cudaStreamDestroy(stream);
     if (owned && weights) cudaFree(weights);
+    if (status) cudaFree(status);
   }
 };
+
+namespace {
+
+// The GEMV of `tokens` device vectors through the session's scratch.
+void session_launch(llambda_cuda_session* s, const uint8_t* W, const float* din, size_t tokens,
+                    float* dout, cudaStream_t st) {
+  if (s->type == LLAMBDA_CUDA_TYPE_F32) {
+    cuda_check(lb::launch_gemv_f32(W, (int)s->ne1, (int)s->ne0, din, (long)s->ne0, (int)tokens,
+                                   dout, (long)s->ne1, st),
+               "GEMV launch");
+    return;
+  }
+  float* xp = static_cast<float*>(s->dxp.get(lb::xprep_floats((int)s->ne0, (int)tokens) * 4));
+  cuda_check(lb::launch_prep(s->type, din, (long)s->ne0, (int)s->ne0, (int)s->ne0, (int)tokens,
+                             nullptr, xp, st),
+             "activation prep");
+  cuda_check(lb::launch_gemv_prepped(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, xp,
+                                     (int)tokens, dout, (long)s->ne1, s->status, st),
+             "GEMV launch");
+}
+
+void require_aligned16(const void* p, const char* what) {
+  if (reinterpret_cast<uintptr_t>(p) & 15)
+    throw Failure(std::string(what) + ": device pointers must be 16-byte aligned.");
+}
+
+}  // namespace
 
 struct llambda_cuda_moe_session {
   lb::MoeDevice m{};
@@ -297,7 +326,10 @@ static int session_make(int type, uint64_t ne0, uint64_t ne1, uint64_t ne2, cons
       s->device = current_device();
       require_b200(s->device);
       cuda_check(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+      cuda_check(cudaMalloc(&s->status, sizeof(int)), "cudaMalloc");
+      cuda_check(cudaMemsetAsync(s->status, 0, sizeof(int), s->stream), "memset");
       if (on_device) {
+        require_aligned16(data, "projection tensor");
         s->weights = const_cast<void*>(data);
         s->owned = false;
       } else {
@@ -411,11 +443,17 @@ static int session_run_rows(llambda_cuda_session* s, int expert, const float* in
     std::memcpy(hin, input, in_bytes);
     cuda_check(cudaMemcpyAsync(din, hin, in_bytes, cudaMemcpyHostToDevice, s->stream), "input copy");
     const uint8_t* W = static_cast<const uint8_t*>(s->weights) + (size_t)expert * s->ne1 * s->rb;
-    cuda_check(lb::launch_gemv(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, din, (long)s->ne0,
-                               (int)s->ne0, (int)tokens, dout, (long)s->ne1, s->stream),
-               "GEMV launch");
+    session_launch(s, W, din, tokens, dout, s->stream);
+    int status = 0;
     cuda_check(cudaMemcpyAsync(hout, dout, out_bytes, cudaMemcpyDeviceToHost, s->stream), "output copy");
+    cuda_check(cudaMemcpyAsync(&status, s->status, sizeof(int), cudaMemcpyDeviceToHost, s->stream),
+               "status copy");
     cuda_check(cudaStreamSynchronize(s->stream), "GEMV");
+    if (status) {
+      cudaMemsetAsync(s->status, 0, sizeof(int), s->stream);
+      throw Failure("A GEMV shared-memory stage wait timed out (device status " +
+                    std::to_string(status) + ").");
+    }
     std::memcpy(output, hout, out_bytes);
     return 0;
   });
@@ -466,10 +504,9 @@ int llambda_cuda_session_run_device(llambda_cuda_session* s, const float* device
   }
   return guarded([&] {
     DeviceGuard g(s->device);
-    cuda_check(lb::launch_gemv(s->type, s->weights, s->rb, (int)s->ne1, (int)s->ne0, device_input,
-                               (long)s->ne0, (int)s->ne0, (int)tokens, device_output, (long)s->ne1,
-                               static_cast<cudaStream_t>(cuda_stream)),
-               "GEMV launch");
+    std::lock_guard<std::mutex> lock(s->mu);
+    session_launch(s, static_cast<const uint8_t*>(s->weights), device_input, tokens,
+                   device_output, static_cast<cudaStream_t>(cuda_stream));
     return 0;
   });
 }
@@ -573,6 +610,7 @@ int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
         const uint8_t* src = static_cast<const uint8_t*>(t.data) + per * (size_t)eb;
         const uint8_t* p;
         if (d->data_on_device) {
+          require_aligned16(t.data, what);
           p = src;  // borrowed
         } else {
           p = static_cast<const uint8_t*>(upload(src, bytes));
@@ -583,6 +621,7 @@ int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
       auto plain = [&](const llambda_cuda_tensor& t, const char* what) -> const uint8_t* {
         if (!t.data) return nullptr;
         const size_t bytes = row_bytes(t.type, t.ne0) * t.ne1;
+        if (d->data_on_device) require_aligned16(t.data, what);
         const uint8_t* p = d->data_on_device ? static_cast<const uint8_t*>(t.data)
                                              : static_cast<const uint8_t*>(upload(t.data, bytes));
         validate_scales(t.type, p, bytes, s->stream, what);
@@ -851,6 +890,9 @@ lb::MoeDevice static_layer(const llambda_cuda_moe_desc* d) {
   m.gate_type = qwen ? d->gate_exps.type : d->up_exps.type;
   m.up_type = d->up_exps.type;
   m.down_type = d->down_exps.type;
+  for (const llambda_cuda_tensor* t : {&d->gate_exps, &d->up_exps, &d->down_exps, &d->gate_shexp,
+                                       &d->up_shexp, &d->down_shexp})
+    if (t->data) require_aligned16(t->data, "MoE tensor");
   m.router = static_cast<const float*>(d->router.data);
   m.router_extra_row = qwen && shared ? d->shared_gate_inp : nullptr;
   m.router_bias = d->router_bias;

@@ -1,121 +1,208 @@
-// Dense dequant-fused GEMV for raw GGUF Q4_K / Q6_K / F32 tensors, the fp16
-// scale validator and the synthetic-data fill kernels.
+// Dense dequant-fused GEMV for raw GGUF Q4_K / Q6_K tensors (warp TMA
+// pipeline, engine.cuh), the F32 GEMV of the MoE router, the activation
+// preparation kernel, the fp16 scale validator and the synthetic-data fill.
 //
 // Replaces %gguf-model-matrix-vector-multiply-into (llambda.lisp L4542-4658),
 // which splits rows over lparallel workers and runs an 8-lane AVX2 loop per
-// row.  Here every warp owns rows and its lanes own 64-weight tasks of a row;
-// weights stream once from HBM in 16-byte loads and never touch shared memory,
-// activations are staged once per CTA in a bank-conflict-free task-minor
-// layout and reused by every row the CTA computes.
+// row.
 #include <algorithm>
+#include <map>
+#include <mutex>
 
+#include "engine.cuh"
 #include "kernels.h"
-#include "rowdot.cuh"
 #include "synth.h"
 
 namespace lb {
 
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+int kernel_occupancy(const void* kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, size_t>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(kernel, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+      cudaSuccess)
+    return -1;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem) != cudaSuccess)
+    return -1;
+  cache[key] = occ;
+  return occ;
+}
+
+UnitPlan plan_units(size_t rb, int tasks, int ranges) {
+  UnitPlan p{};
+  p.lpr = lanes_for(tasks);
+  p.rl = 4;
+  while (p.rl > 1 && (size_t)p.rl * (32 / p.lpr) * rb * ranges > 7 * 1024) p.rl /= 2;
+  const size_t ru = (size_t)p.rl * (32 / p.lpr);
+  p.stage_bytes = (int)(((size_t)ranges * (ru * rb + 32) + 127) & ~size_t(127));
+  p.stages = std::max(2, std::min(4, (16 * 1024) / p.stage_bytes));
+  p.warps = 4;
+  return p;
+}
+
 namespace {
 
-constexpr int kThreads = 256;
+// ------------------------------------------------------------ preparation
 
-template <int TYPE, int NT>
-__global__ void __launch_bounds__(kThreads) gemv_quant_kernel(const uint8_t* __restrict__ W,
-                                                               size_t rb, int rows, int K,
-                                                               const float* __restrict__ x,
-                                                               long ldx, int n_valid, int tokens,
-                                                               float* __restrict__ y, long ldy) {
-  extern __shared__ float4 smem4[];
+// One block per (256-value super-block, token): 64 threads, one float4 each.
+template <int TYPE>
+__global__ void __launch_bounds__(64) prep_kernel(const float* __restrict__ x, long ldx,
+                                                  int n_valid, int K, const int* __restrict__ gather,
+                                                  float* __restrict__ xp) {
+  const int sb = blockIdx.x, tok = blockIdx.y;
   const int tasks = K >> 6;
-  constexpr int G = group_size<TYPE>();
-  float4* xs = smem4;
-  float* sx = reinterpret_cast<float*>(smem4 + NT * 16 * tasks);
-  const XView xv{xs, sx, tasks, K / G};
-  const int lpr = lanes_per_row(tasks);
-  const int rpw = 32 / lpr;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
-  const int lt = lane % lpr;
-  for (int t0 = 0; t0 < tokens; t0 += NT) {
-    const int nt = min(NT, tokens - t0);
-    if (t0) __syncthreads();
-    stage_x<TYPE>(xs, sx, x + (long)t0 * ldx, ldx, nullptr, nt, K, n_valid);
-    __syncthreads();
-    for (int r0 = (blockIdx.x * nwarps + warp) * rpw; r0 < rows; r0 += gridDim.x * nwarps * rpw) {
-      const int row = r0 + lane / lpr;
-      const bool ok = row < rows;
-      float acc[NT];
-      row_dot<TYPE, NT>(W + (size_t)(ok ? row : 0) * rb, ok, xv, nt, lt, lpr, acc);
-      if (lt == 0 && ok) {
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-          if (t < nt) y[(long)(t0 + t) * ldy + row] = acc[t];
-      }
-    }
+  const long row = gather ? gather[tok] : tok;
+  const float* s = x + row * ldx;
+  const int e = sb * 256 + threadIdx.x * 4;
+  float4 v;
+  if (e + 3 < n_valid && (reinterpret_cast<uintptr_t>(s + e) & 15u) == 0) {
+    v = *reinterpret_cast<const float4*>(s + e);
+  } else {
+    v.x = e < n_valid ? s[e] : 0.f;
+    v.y = e + 1 < n_valid ? s[e + 1] : 0.f;
+    v.z = e + 2 < n_valid ? s[e + 2] : 0.f;
+    v.w = e + 3 < n_valid ? s[e + 3] : 0.f;
+  }
+  float* out = xp + (long)tok * xp_stride(K);
+  *reinterpret_cast<float4*>(out + xp_index<TYPE>(e, tasks)) = v;
+  if (TYPE == LB_TYPE_Q4_K) {
+    // sum over each 32-value sub-block: 8 consecutive threads
+    float part = (v.x + v.y) + (v.z + v.w);
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    part += __shfl_xor_sync(0xffffffffu, part, 4);
+    if ((threadIdx.x & 7) == 0) out[K + (e >> 5)] = part;
   }
 }
 
-// F32 rows (the MoE router, ffn_gate_inp): one warp per row, float4 loads.
-template <int NT>
-__global__ void __launch_bounds__(kThreads) gemv_f32_kernel(const float* __restrict__ W, int rows,
-                                                             int K, const float* __restrict__ x,
-                                                             long ldx, int tokens,
-                                                             float* __restrict__ y, long ldy) {
-  extern __shared__ float4 smem4[];
-  float* xs = reinterpret_cast<float*>(smem4);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
-  const int K4 = K >> 2;
-  for (int t0 = 0; t0 < tokens; t0 += NT) {
-    const int nt = min(NT, tokens - t0);
-    if (t0) __syncthreads();
-    for (int i = threadIdx.x; i < nt * K; i += blockDim.x) {
-      const int t = i / K, k = i - t * K;
-      xs[t * K + k] = x[(long)(t0 + t) * ldx + k];
+// ------------------------------------------------------------ dense GEMV
+
+// Each warp owns a contiguous run of units (RU rows each), streams them
+// through its TMA ring and computes every token against each staged unit.
+template <int TYPE, int LPR, int RL>
+__global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ W, size_t rb,
+                                                   int rows, int tasks,
+                                                   const float* __restrict__ xp, int tokens,
+                                                   float* __restrict__ y, long ldy, int stages,
+                                                   int stage_bytes, int* status) {
+  constexpr int RPP = 32 / LPR, RU = RL * RPP;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)nwarps * stages * stage_bytes);
+  const WarpRing ring{smem + (size_t)warp * stages * stage_bytes, bars + warp * stages,
+                      stage_bytes, stages};
+  ring_init(ring, lane);
+  const long xld = xp_stride(tasks * 64);
+  const int units = (rows + RU - 1) / RU;
+  const int gw = blockIdx.x * nwarps + warp, total = gridDim.x * nwarps;
+  const int chunk = (units + total - 1) / total;
+  const int u0 = gw * chunk;
+  const int n_my = max(0, min(units, u0 + chunk) - u0);
+  auto issue = [&](int idx) {
+    const int row0 = (u0 + idx) * RU;
+    ring_issue(ring, idx % stages, W + (size_t)row0 * rb, (size_t)min(RU, rows - row0) * rb,
+               nullptr, 0);
+  };
+  int issued = 0;
+  if (lane == 0)
+    for (; issued < stages - 1 && issued < n_my; ++issued) issue(issued);
+  issued = __shfl_sync(0xffffffffu, issued, 0);
+  XCache xc;
+  xc.key = -1;
+  const int grp = lane / LPR, lt = lane % LPR;
+  int i = 0;
+  bool ok = true;
+  for (; i < n_my; ++i) {
+    if (issued < n_my && issued <= i + stages - 1) {
+      if (lane == 0) issue(issued);
+      ++issued;
     }
-    __syncthreads();
-    for (int row = blockIdx.x * nwarps + warp; row < rows; row += gridDim.x * nwarps) {
-      const float* wr = W + (size_t)row * K;
-      float acc[NT];
+    ok = __all_sync(0xffffffffu, mbar_wait(&ring.bars[i % stages], (i / stages) & 1, status));
+    if (!ok) break;
+    const int row0 = (u0 + i) * RU, nrows = min(RU, rows - row0);
+    const uint8_t* gsrc = W + (size_t)row0 * rb;
+    const uint8_t* rowsp =
+        ring.smem + (size_t)(i % stages) * stage_bytes + (reinterpret_cast<uintptr_t>(gsrc) & 15);
+    for (int t = 0; t < tokens; ++t) {
+      float a[RL], unused[RL];
+      unit_rows<TYPE, LPR, RL, false>(rowsp, (int)rb, nullptr, 0, nrows, tasks, xp + t * xld, t,
+                                      xc, lane, a, unused);
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-      if ((reinterpret_cast<uintptr_t>(wr) & 15) == 0) {
-        const float4* w4 = reinterpret_cast<const float4*>(wr);
-        for (int k4 = lane; k4 < K4; k4 += 32) {
-          const float4 w = __ldg(w4 + k4);
+      for (int q = 0; q < RL; ++q) {
+        const int r = grp + q * RPP;
+        if (lt == q && r < nrows) y[(long)t * ldy + row0 + r] = a[q];
+      }
+    }
+    __syncwarp();
+  }
+  if (!ok)  // drain copies still in flight before the warp exits
+    for (int k = i + 1; k < issued; ++k) mbar_wait(&ring.bars[k % stages], (k / stages) & 1, nullptr);
+}
+
+// F32 rows (the MoE router, ffn_gate_inp): one warp per (row, group of up to
+// 8 tokens); activations are read straight from global memory (they stay in
+// L1/L2), so there is no staging and every SM takes part.
+__global__ void __launch_bounds__(128) gemv_f32_kernel(const float* __restrict__ W, int rows,
+                                                       int K, const float* __restrict__ x,
+                                                       long ldx, int tokens,
+                                                       float* __restrict__ y, long ldy) {
+  const int lane = threadIdx.x & 31;
+  const int groups = (tokens + 7) / 8;
+  const long items = (long)rows * groups;
+  const bool vec = (K & 3) == 0 && (ldx & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  for (long it = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += (long)gridDim.x * (blockDim.x >> 5)) {
+    const int row = (int)(it / groups), t0 = (int)(it - (long)row * groups) * 8;
+    const int nt = min(8, tokens - t0);
+    const float* wr = W + (size_t)row * K;
+    float acc[8];
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            if (t < nt) {
-              const float4 v = reinterpret_cast<const float4*>(xs + t * K)[k4];
-              acc[t] = fmaf(w.x, v.x, acc[t]);
-              acc[t] = fmaf(w.y, v.y, acc[t]);
-              acc[t] = fmaf(w.z, v.z, acc[t]);
-              acc[t] = fmaf(w.w, v.w, acc[t]);
-            }
+    for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+    if (vec) {
+      const float4* w4 = reinterpret_cast<const float4*>(wr);
+      for (int k4 = lane; k4 < (K >> 2); k4 += 32) {
+        const float4 wv = __ldg(w4 + k4);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          if (t < nt) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(x + (long)(t0 + t) * ldx) + k4);
+            acc[t] = fmaf(wv.x, v.x, acc[t]);
+            acc[t] = fmaf(wv.y, v.y, acc[t]);
+            acc[t] = fmaf(wv.z, v.z, acc[t]);
+            acc[t] = fmaf(wv.w, v.w, acc[t]);
           }
         }
-        for (int k = K4 * 4 + lane; k < K; k += 32) {
-          const float w = __ldg(wr + k);
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-            if (t < nt) acc[t] = fmaf(w, xs[t * K + k], acc[t]);
-        }
-      } else {
-        for (int k = lane; k < K; k += 32) {
-          const float w = __ldg(wr + k);
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-            if (t < nt) acc[t] = fmaf(w, xs[t * K + k], acc[t]);
-        }
       }
+    } else {
+      for (int k = lane; k < K; k += 32) {
+        const float wv = __ldg(wr + k);
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = warp_sum(acc[t]);
-      if (lane == 0) {
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-          if (t < nt) y[(long)(t0 + t) * ldy + row] = acc[t];
+        for (int t = 0; t < 8; ++t)
+          if (t < nt) acc[t] = fmaf(wv, __ldg(x + (long)(t0 + t) * ldx + k), acc[t]);
       }
     }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) acc[t] = warp_sum(acc[t]);
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+      if (lane == t && t < nt) y[(long)(t0 + t) * ldy + row] = acc[t];
   }
 }
 
@@ -169,94 +256,70 @@ __global__ void synth_f32_kernel(uint64_t seed, uint64_t sid, uint64_t first, si
     out[i] = lb_f32_value(seed, sid, first + i, s);
 }
 
-int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
-
-template <int TYPE, int NT>
-cudaError_t launch_quant(const void* W, size_t rb, int rows, int K, const float* x, long ldx,
-                         int n_valid, int tokens, float* y, long ldy, cudaStream_t stream) {
-  const size_t smem = stage_bytes<TYPE>(NT, K);
-  auto kern = gemv_quant_kernel<TYPE, NT>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  const int tasks = K / 64;
-  const int rpw = 32 / lanes_per_row(tasks);
-  const long warps_needed = (rows + rpw - 1) / rpw;
-  const int per_sm = std::max(1, (int)std::min<size_t>(8, (200 * 1024) / std::max<size_t>(smem, 1)));
-  const long blocks = std::min<long>((warps_needed + 7) / 8, (long)sm_count() * per_sm);
-  kern<<<(int)std::max<long>(blocks, 1), kThreads, smem, stream>>>(
-      static_cast<const uint8_t*>(W), rb, rows, K, x, ldx, n_valid, tokens, y, ldy);
+template <int TYPE, int LPR, int RL>
+cudaError_t launch_dense(const UnitPlan& p, const void* W, size_t rb, int rows, int K,
+                         const float* xp, int tokens, float* y, long ldy, int* status,
+                         cudaStream_t stream) {
+  auto kern = gemv_kernel<TYPE, LPR, RL>;
+  const size_t smem = (size_t)p.warps * p.stages * (p.stage_bytes + 8);
+  const int occ = prepared_occupancy(kern, p.warps * 32, smem);
+  if (occ < 0) return cudaErrorUnknown;
+  const int ru = RL * (32 / LPR);
+  const long units = (rows + ru - 1) / ru;
+  const long blocks = std::min<long>((units + p.warps - 1) / p.warps,
+                                     (long)sm_count() * std::max(occ, 1));
+  kern<<<(int)std::max<long>(blocks, 1), p.warps * 32, smem, stream>>>(
+      static_cast<const uint8_t*>(W), rb, rows, K / 64, xp, tokens, y, ldy, p.stages,
+      p.stage_bytes, status);
   return cudaGetLastError();
-}
-
-template <int NT>
-cudaError_t launch_f32(const void* W, int rows, int K, const float* x, long ldx, int tokens,
-                       float* y, long ldy, cudaStream_t stream) {
-  const size_t smem = (size_t)NT * K * 4;
-  auto kern = gemv_f32_kernel<NT>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  const long blocks = std::min<long>((rows + 7) / 8, (long)sm_count() * 8);
-  kern<<<(int)std::max<long>(blocks, 1), kThreads, smem, stream>>>(
-      static_cast<const float*>(W), rows, K, x, ldx, tokens, y, ldy);
-  return cudaGetLastError();
-}
-
-// Largest token tile (1, 2, 4 or 8) whose staging fits comfortably in shared memory.
-int token_tile(int tokens, size_t bytes_per_token) {
-  int nt = 1;
-  while (nt < 8 && nt < tokens && (size_t)(nt * 2) * bytes_per_token <= 160 * 1024) nt *= 2;
-  return nt;
 }
 
 }  // namespace
 
-cudaError_t launch_gemv(int type, const void* W, size_t rb, int rows, int K, const float* x,
-                        long ldx, int n_valid, int tokens, float* y, long ldy,
-                        cudaStream_t stream) {
+// ------------------------------------------------------------ host API
+
+size_t xprep_floats(int K, int tokens) { return (size_t)xp_stride(K) * tokens; }
+
+cudaError_t launch_prep(int type, const float* x, long ldx, int n_valid, int K, int tokens,
+                        const int* gather, float* xp, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  if (K % 256) return cudaErrorInvalidValue;
+  dim3 grid(K / 256, tokens);
+  if (type == LB_TYPE_Q4_K)
+    prep_kernel<LB_TYPE_Q4_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
+  else if (type == LB_TYPE_Q6_K)
+    prep_kernel<LB_TYPE_Q6_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_prepped(int type, const void* W, size_t rb, int rows, int K,
+                                const float* xp, int tokens, float* y, long ldy, int* status,
+                                cudaStream_t stream) {
   if (rows <= 0 || tokens <= 0) return cudaSuccess;
-  if (type == LB_TYPE_F32) {
-    const int nt = token_tile(tokens, (size_t)K * 4);
-    switch (nt) {
-      case 1: return launch_f32<1>(W, rows, K, x, ldx, tokens, y, ldy, stream);
-      case 2: return launch_f32<2>(W, rows, K, x, ldx, tokens, y, ldy, stream);
-      case 4: return launch_f32<4>(W, rows, K, x, ldx, tokens, y, ldy, stream);
-      default: return launch_f32<8>(W, rows, K, x, ldx, tokens, y, ldy, stream);
-    }
-  }
-  if (type == LB_TYPE_Q4_K) {
-    const int nt = token_tile(tokens, stage_bytes<LB_TYPE_Q4_K>(1, K));
-    switch (nt) {
-      case 1: return launch_quant<LB_TYPE_Q4_K, 1>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-      case 2: return launch_quant<LB_TYPE_Q4_K, 2>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-      case 4: return launch_quant<LB_TYPE_Q4_K, 4>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-      default: return launch_quant<LB_TYPE_Q4_K, 8>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-    }
-  }
-  if (type == LB_TYPE_Q6_K) {
-    const int nt = token_tile(tokens, stage_bytes<LB_TYPE_Q6_K>(1, K));
-    switch (nt) {
-      case 1: return launch_quant<LB_TYPE_Q6_K, 1>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-      case 2: return launch_quant<LB_TYPE_Q6_K, 2>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-      case 4: return launch_quant<LB_TYPE_Q6_K, 4>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-      default: return launch_quant<LB_TYPE_Q6_K, 8>(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
-    }
-  }
+  const UnitPlan p = plan_units(rb, K / 64, 1);
+#define LB_DENSE(T, L, RR)                                                                   \
+  if (type == T && p.lpr == L && p.rl == RR)                                                 \
+    return launch_dense<T, L, RR>(p, W, rb, rows, K, xp, tokens, y, ldy, status, stream);
+#define LB_DENSE_T(T)                                                                        \
+  LB_DENSE(T, 8, 1) LB_DENSE(T, 8, 2) LB_DENSE(T, 8, 4) LB_DENSE(T, 16, 1) LB_DENSE(T, 16, 2)  \
+  LB_DENSE(T, 16, 4) LB_DENSE(T, 32, 1) LB_DENSE(T, 32, 2) LB_DENSE(T, 32, 4)
+  LB_DENSE_T(LB_TYPE_Q4_K)
+  LB_DENSE_T(LB_TYPE_Q6_K)
+#undef LB_DENSE_T
+#undef LB_DENSE
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long ldx, int tokens,
+                            float* y, long ldy, cudaStream_t stream) {
+  if (rows <= 0 || tokens <= 0) return cudaSuccess;
+  const long items = (long)rows * ((tokens + 7) / 8);
+  const long blocks = std::min<long>((items + 3) / 4, (long)sm_count() * 16);
+  gemv_f32_kernel<<<(int)std::max<long>(blocks, 1), 128, 0, stream>>>(
+      static_cast<const float*>(W), rows, K, x, ldx, tokens, y, ldy);
+  return cudaGetLastError();
 }
 
 cudaError_t check_fp16_scales(int type, const void* W, size_t blocks, unsigned* bad,

@@ -7,12 +7,36 @@
 
 namespace lb {
 
-// Dense GEMV / small-batch GEMM over a raw GGUF tensor:
-//   y[t][r] = sum_k W[r][k] * x[t][k]   for r < rows, t < tokens
-// x rows hold n_valid values (zero-padded to K); y rows have stride ldy.
-cudaError_t launch_gemv(int type, const void* W, size_t row_bytes, int rows, int K,
-                        const float* x, long ldx, int n_valid, int tokens, float* y, long ldy,
-                        cudaStream_t stream);
+// ------------------------------------------------------------ dense GEMV
+//
+// Quantized GEMV runs in two launches: the activations are first prepared
+// (permuted to the weight type's task layout, sub-block sums for Q4_K) into
+// a scratch buffer of xprep_floats(K, tokens) floats, then the TMA-staged
+// GEMV reads them.  y[t][r] = sum_k W[r][k] * x[t][k], x zero-padded from
+// n_valid to K.
+
+// Work decomposition of one pass over a matrix: units of rl * (32/lpr) rows
+// (lpr lanes per row), staged through `stages` shared-memory stages per warp.
+struct UnitPlan {
+  int lpr;          // lanes per row: 8, 16 or 32
+  int rl;           // rows per lane
+  int stage_bytes;  // bytes of one shared-memory stage
+  int stages;       // stages per warp
+  int warps;        // warps per CTA
+};
+
+// `ranges` matrices (gate and up) share one stage.
+UnitPlan plan_units(size_t row_bytes, int tasks, int ranges);
+int sm_count();
+size_t xprep_floats(int K, int tokens);
+cudaError_t launch_prep(int type, const float* x, long ldx, int n_valid, int K, int tokens,
+                        const int* gather, float* xp, cudaStream_t stream);
+cudaError_t launch_gemv_prepped(int type, const void* W, size_t row_bytes, int rows, int K,
+                                const float* xp, int tokens, float* y, long ldy, int* status,
+                                cudaStream_t stream);
+// F32 rows (router): x natural layout, no preparation.
+cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long ldx, int tokens,
+                            float* y, long ldy, cudaStream_t stream);
 
 // Checks every fp16 scale (d, dmin) of a Q4_K / Q6_K tensor for Inf/NaN,
 // which llambda rejects (fp16-to-single-float, llambda.lisp L727-728).
@@ -23,6 +47,8 @@ cudaError_t check_fp16_scales(int type, const void* W, size_t blocks, unsigned* 
 // Synthetic GGUF data straight into device memory (synth.h generator).
 cudaError_t synth_fill(int type, uint64_t seed, uint64_t stream_id, uint64_t first,
                        size_t count, float scale, void* out, cudaStream_t stream);
+
+// ------------------------------------------------------------ MoE layer
 
 // One MoE feed-forward layer on device-resident tensors.
 struct MoeDevice {
@@ -69,19 +95,22 @@ struct MoeWork {
   float* shw;         // [T] shared-expert weight
   int* counts;        // [E]
   int* offsets;       // [E+1]
-  int* entries;       // [T*k] token*k + rank, grouped by expert
+  int* entries;       // [2*T*k]: per-entry position, then entry ids grouped by expert
   int* active;        // [E+1] active experts, then count at [E]
-  int* status;        // [1] device status word (0 ok; 1 non-positive weight sum)
-  float* hbuf;        // [T*k + T][inter_max] expert intermediates
-  float* partial;     // [T][k+1][H]
-  float* xnorm;       // [T][H] normalised input (when input_norm is set)
+  int* status;        // [1] device status word (bit 0: non-positive weight sum,
+                      //  bit 1: a TMA stage wait timed out)
+  float* xn;          // [T][H] normalised input (when input_norm is set)
+  float* xp_up;       // [T] prepared gate/up inputs (stride xp_stride(k_in))
+  float* xp_down;     // [T*k + T] prepared down inputs: routed entry ids, then
+                      // shared token rows (stride xp_stride(max(k_down, k_down_sh)))
+  float* partial;     // [T][k+1][H] unscaled down outputs per (token, rank)
   size_t bytes;
 };
 
 size_t moe_work_bytes(const MoeDevice& m, int max_tokens);
 void moe_work_carve(const MoeDevice& m, int max_tokens, void* base, MoeWork* w);
 
-// out[t][h] for t < tokens; sel/wts optional device outputs [T][k].
+// out[t][h] for t < tokens.
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int tokens,
                        float* out, cudaStream_t stream);
 
