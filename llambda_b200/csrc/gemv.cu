@@ -11,6 +11,7 @@
 
 #include "engine.cuh"
 #include "kernels.h"
+#include "mma.cuh"
 #include "synth.h"
 
 namespace lb {
@@ -78,15 +79,11 @@ __global__ void __launch_bounds__(64) prep_kernel(const float* __restrict__ x, l
     v.z = e + 2 < n_valid ? s[e + 2] : 0.f;
     v.w = e + 3 < n_valid ? s[e + 3] : 0.f;
   }
-  float* out = xp + (long)tok * xp_stride(K);
-  *reinterpret_cast<float4*>(out + xp_index<TYPE>(e, tasks)) = v;
-  if (TYPE == LB_TYPE_Q4_K) {
-    // sum over each 32-value sub-block: 8 consecutive threads
-    float part = (v.x + v.y) + (v.z + v.w);
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    part += __shfl_xor_sync(0xffffffffu, part, 4);
-    if ((threadIdx.x & 7) == 0) out[K + (e >> 5)] = part;
+  if (TYPE == LB_TYPE_Q4_K) {  // tensor-core layout (mma.cuh)
+    mx_store4(reinterpret_cast<uint8_t*>(xp) + (size_t)tok * mx_bytes(K), K, e, v);
+  } else {
+    float* out = xp + (long)tok * xp_stride(K);
+    *reinterpret_cast<float4*>(out + xp_index<TYPE>(e, tasks)) = v;
   }
 }
 
@@ -152,6 +149,73 @@ __global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ W
   }
   if (!ok)  // drain copies still in flight before the warp exits
     for (int k = i + 1; k < issued; ++k) mbar_wait(&ring.bars[k % stages], (k / stages) & 1, nullptr);
+}
+
+// Q4_K rows on the tensor cores (mma.cuh): each CTA owns a contiguous run of
+// 16-row tiles, stages them through its bulk-copy ring, and computes the
+// tokens in groups of NT against each staged tile.
+template <int NT, int NW>
+__global__ void __launch_bounds__(NW * 32, 1)
+    gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, size_t rb, int rows, int nsb,
+                        const uint8_t* __restrict__ mx, int tokens, float* __restrict__ y,
+                        long ldy, TilePlan plan, int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)plan.stages * plan.stage_bytes);
+  float* red = reinterpret_cast<float*>(full + 8);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < plan.stages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const size_t mxb = mx_bytes(nsb * 256);
+  const int tiles = (rows + kTileRows - 1) / kTileRows;
+  const int u0 = (int)((long)blockIdx.x * tiles / gridDim.x);
+  const int n_my = (int)((long)(blockIdx.x + 1) * tiles / gridDim.x) - u0;
+  auto issue = [&](int idx) {
+    const int row0 = (u0 + idx) * kTileRows, s = idx % plan.stages;
+    tile_issue(smem + (size_t)s * plan.stage_bytes, &full[s], plan.pitch,
+               min(kTileRows, rows - row0), rb, W + (size_t)row0 * rb, nullptr, lane);
+  };
+  int issued = 0;  // meaningful in warp 0 (the producer)
+  if (warp == 0)
+    for (; issued < plan.stages && issued < n_my; ++issued) issue(issued);
+  int i = 0, buf = 0;
+  bool stop = false;
+  for (; i < n_my; ++i) {
+    const int s = i % plan.stages;
+    const bool ok = mbar_wait(&full[s], (i / plan.stages) & 1, status);
+    const int row0 = (u0 + i) * kTileRows, nr = min(kTileRows, rows - row0);
+    const uint8_t* st = smem + (size_t)s * plan.stage_bytes;
+    int t0 = 0;
+    do {
+      const int nt = min(NT, tokens - t0);
+      const uint8_t* mxp[NT];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mxp[n] = mx + (size_t)min(t0 + n, tokens - 1) * mxb;
+      float2 acc[1][2][NT];
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int n = 0; n < NT; ++n) acc[0][r][n] = make_float2(0.f, 0.f);
+      if (ok) tile_items<NT, 1, NW>(st, plan.pitch, nsb, warp, lane, mxp, nt, acc);
+      float* rbuf = red + buf * (tile_red_floats<NT, 1, NW>() / 2);
+      tile_partials_store<NT, 1>(rbuf, warp, lane, acc);
+      stop = __syncthreads_or(!ok);  // also: every warp is done with this stage
+      if (stop) break;
+      const int r = threadIdx.x & 15, n = threadIdx.x >> 4;
+      if (n < nt && r < nr) y[(long)(t0 + n) * ldy + row0 + r] = tile_row_sum<NT, 1, NW>(rbuf, 0, r, n);
+      buf ^= 1;
+      t0 += NT;
+    } while (t0 < tokens);
+    if (stop) break;
+    if (warp == 0 && issued < n_my) {
+      issue(issued);
+      ++issued;
+    }
+  }
+  if (stop && threadIdx.x == 0)  // drain copies still in flight before the CTA exits
+    for (int q = i; q < issued; ++q) mbar_wait(&full[q % plan.stages], (q / plan.stages) & 1, nullptr);
 }
 
 // F32 rows (the MoE router, ffn_gate_inp): one warp per (row, group of up to
@@ -274,11 +338,30 @@ cudaError_t launch_dense(const UnitPlan& p, const void* W, size_t rb, int rows, 
   return cudaGetLastError();
 }
 
+template <int NT, int NW>
+cudaError_t launch_q4k_mma(const void* W, size_t rb, int rows, int K, const float* xp,
+                           int tokens, float* y, long ldy, int* status, cudaStream_t stream) {
+  auto kern = gemv_q4k_mma_kernel<NT, NW>;
+  const size_t extra = 64 + (size_t)tile_red_floats<NT, 1, NW>() * 4;
+  const TilePlan plan = tile_plan(rb, 1, kTileSmemBudget - extra);
+  if (plan.stages < 2) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)plan.stages * plan.stage_bytes + extra;
+  if (prepared_occupancy(kern, NW * 32, smem) < 1) return cudaErrorUnknown;
+  const int tiles = (rows + kTileRows - 1) / kTileRows;
+  const int grid = std::min(tiles, sm_count());
+  kern<<<grid, NW * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, K / 256,
+                                                reinterpret_cast<const uint8_t*>(xp), tokens, y,
+                                                ldy, plan, status);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 // ------------------------------------------------------------ host API
 
-size_t xprep_floats(int K, int tokens) { return (size_t)xp_stride(K) * tokens; }
+size_t xprep_floats(int K, int tokens) {
+  return std::max((size_t)xp_stride(K), mx_bytes(K) / 4) * tokens;
+}
 
 cudaError_t launch_prep(int type, const float* x, long ldx, int n_valid, int K, int tokens,
                         const int* gather, float* xp, cudaStream_t stream) {
@@ -305,7 +388,11 @@ cudaError_t launch_gemv_prepped(int type, const void* W, size_t rb, int rows, in
 #define LB_DENSE_T(T)                                                                        \
   LB_DENSE(T, 8, 1) LB_DENSE(T, 8, 2) LB_DENSE(T, 8, 4) LB_DENSE(T, 16, 1) LB_DENSE(T, 16, 2)  \
   LB_DENSE(T, 16, 4) LB_DENSE(T, 32, 1) LB_DENSE(T, 32, 2) LB_DENSE(T, 32, 4)
-  LB_DENSE_T(LB_TYPE_Q4_K)
+  if (type == LB_TYPE_Q4_K) {
+    if (tokens == 1) return launch_q4k_mma<1, 16>(W, rb, rows, K, xp, tokens, y, ldy, status, stream);
+    if (tokens == 2) return launch_q4k_mma<2, 16>(W, rb, rows, K, xp, tokens, y, ldy, status, stream);
+    return launch_q4k_mma<4, 8>(W, rb, rows, K, xp, tokens, y, ldy, status, stream);
+  }
   LB_DENSE_T(LB_TYPE_Q6_K)
 #undef LB_DENSE_T
 #undef LB_DENSE

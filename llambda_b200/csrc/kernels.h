@@ -97,6 +97,8 @@ struct MoeWork {
   int* offsets;       // [E+1]
   int* entries;       // [2*T*k]: per-entry position, then entry ids grouped by expert
   int* active;        // [E+1] active experts, then count at [E]
+  int* pass_off;      // [E+1] per active expert: token passes (of the up pass's
+                      //  tokens per pass) before it; total at [active count]
   int* status;        // [1] device status word (bit 0: non-positive weight sum,
                       //  bit 1: a TMA stage wait timed out)
   float* xn;          // [T][H] normalised input (when input_norm is set)

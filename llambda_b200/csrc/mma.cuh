@@ -1,0 +1,333 @@
+// Tensor-core dequant-GEMV for Q4_K rows (the gate/up projections of the MoE
+// experts and dense Q4_K matrices).
+//
+// Exactness.  A 4-bit quant q becomes the f16 subnormal q * 2^-24 (low
+// nibble) or 16q * 2^-24 (high nibble) by one AND of the packed qs word, so
+// the tensor core multiplies exact integers.  The activations of each
+// 32-value sub-block are scaled by a power of two so that the largest lies in
+// [1024, 2048) and split into an f16 high part and an f16 low part (x' = hi +
+// lo to 2^-23 of the sub-block's largest value).  Both parts are columns of
+// the same mma, so every product is exact and the sums are fp32 sums.  The
+// K-quant arithmetic around them is the reference's: per sub-block
+// (d*sc) * sum(q*x) - (dmin*m) * sum(x) (dot-product-with-q4-k-m-tensor-data,
+// llambda.lisp L4338-4382).
+//
+// Fragment mapping ("slots").  mma.sync.m16n8k16 (A 16x16 f16 row-major, B
+// 16x8 f16 column-major, D fp32) is used with thread (g, t) of each quad
+// (g = lane/4, t = lane%4) holding A at k in {2t, 2t+1, 2t+8, 2t+9}; all four
+// positions belong to sub-block slot t.  Output column n = 2*slot + part
+// (part 0: high, 1: low), and B[k][n] is zero unless k's slot is n's slot.
+// After a k-step thread (g, t) therefore holds, for rows g and g+8, the sums
+// over its own sub-block in both parts (its D columns 2t, 2t+1), and applies
+// that sub-block's scale and min itself: each scale is decoded once per row.
+//
+// A Q4_K super-block is 16 k-steps: for j = 0..7, word j of the 32 qs bytes
+// of pair t (bytes 32t + 4j .. 32t + 4j + 3, values 4j..4j+3 of sub-blocks 2t
+// in the low nibbles and 2t+1 in the high nibbles) gives the low-set step
+// (AND 0x000F000F: values 4j, 4j+2 at k = 2t, 2t+1; the same of the word
+// shifted right by 8: values 4j+1, 4j+3 at k = 2t+8, 2t+9) and the high-set
+// step (AND 0x00F000F0).
+//
+// Pipeline.  A CTA of W warps owns a contiguous run of 16-row tiles.  Each
+// tile's rows (of one or two matrices: gate and up) are copied by per-row 1-D
+// bulk copies, one lane per row, into a stage whose row pitch is 16 bytes
+// past a multiple of 128 (so the 8 row groups of a fragment load fall in
+// different shared-memory banks); stages complete on an mbarrier and are
+// waited on with a bounded spin.  The warps split the tile's (matrix,
+// super-block) items, partial sums meet in shared memory, and one CTA barrier
+// per token group also tells the producer that the stage may be refilled.
+#pragma once
+
+#include "engine.cuh"
+
+namespace lb {
+
+constexpr int kTileRows = 16;
+// Dynamic shared memory of a tile kernel (stages, barriers, partial sums);
+// kernel_occupancy() opts every kernel in to 200 KiB.
+constexpr size_t kTileSmemBudget = 200 * 1024;
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------ activations
+//
+// Prepared activations of one token for the Q4_K mma path ("mx"),
+// mx_bytes(K) bytes (16-byte aligned):
+//   frag[sb][set][col][j] : uint2 (b0, b1), the B fragment of k-step j of
+//       super-block sb's set (0: even sub-blocks, low nibbles; 1: odd, high
+//       nibbles) for the thread of column col = 2*slot + part: halves
+//       (x[4j], x[4j+2]) and (x[4j+1], x[4j+3]) of sub-block 2*slot + set,
+//       scaled, part 0 = high, part 1 = low;
+//   meta[sb][slot] : float4 (back_even, sum_even, back_odd, sum_odd): back
+//       turns a D sum of the set back into sum(q*x) (the inverse power of two
+//       times 2^24 for the low nibbles, 2^20 for the high nibbles), sum is
+//       the plain fp32 sum of the sub-block's x.
+__host__ __device__ __forceinline__ size_t mx_bytes(int K) { return (size_t)(K / 256) * 1088; }
+
+__device__ __forceinline__ float pow2f(int e) {  // 2^e, e in [-126, 127]
+  return __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
+// Stores the four values e..e+3 (e % 4 == 0) of one token into its mx
+// buffer.  The 8 consecutive lanes (lane % 8 == 0 first) that hold one
+// 32-value sub-block must call this together.
+__device__ __forceinline__ void mx_store4(uint8_t* mx, int K, int e, float4 v) {
+  float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  float sum = (v.x + v.y) + (v.z + v.w);
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  // amax = m * 2^ex with m in [0.5, 1); ex is clamped so every scale is a
+  // normal binary32 number (sub-blocks whose largest |x| lies outside
+  // [2^-101, 2^100) lose precision gradually instead).
+  int ex = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 126;
+  ex = min(max(ex, -100), 100);
+  const float f = pow2f(11 - ex);
+  const float xs[4] = {v.x * f, v.y * f, v.z * f, v.w * f};
+  __half hi[4], lo[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    hi[q] = __float2half_rn(xs[q]);
+    lo[q] = __float2half_rn(xs[q] - __half2float(hi[q]));
+  }
+  const int sb = e >> 8, s = (e >> 5) & 7, j = (e & 31) >> 2;
+  const int set = s & 1, slot = s >> 1;
+  uint2* frag = reinterpret_cast<uint2*>(mx);
+  const long u = (((long)sb * 2 + set) * 8 + 2 * slot) * 8 + j;
+  frag[u] = make_uint2(pack_half2(hi[0], hi[2]), pack_half2(hi[1], hi[3]));
+  frag[u + 8] = make_uint2(pack_half2(lo[0], lo[2]), pack_half2(lo[1], lo[3]));
+  if ((e & 31) == 0) {
+    float* meta = reinterpret_cast<float*>(mx + (size_t)(K / 256) * 1024) + (sb * 4 + slot) * 4;
+    meta[set * 2 + 0] = pow2f(ex + (set ? 9 : 13));  // 2^(ex-11) * 2^24 or 2^20
+    meta[set * 2 + 1] = sum;
+  }
+}
+
+// ------------------------------------------------------------ tile math
+
+// d*sc and dmin*m of sub-blocks 2t and 2t+1 of the Q4_K super-block whose
+// first 16 bytes are hh (get-scale-min-k4-at, llambda.lisp L4316-4336, for
+// both sub-blocks at once and without branches: bytes 2t, 2t+1 of the scale
+// words are one 16-bit field).  delta = d*sc, offset = dmin*m, each rounded
+// once (L4363-4366).
+__device__ __forceinline__ void q4k_pair_scales(const uint4& hh, int t, float2& dsc,
+                                                float2& dmn) {
+  const float d = half_bits_to_float(hh.x), dmin = half_bits_to_float(hh.x >> 16);
+  const int sh = (t & 1) * 16;
+  const uint32_t h0 = hh.y >> sh, h1 = hh.z >> sh, h2 = hh.w >> sh;
+  const uint32_t sc_a = h0 & 0x3F3Fu, mn_a = h1 & 0x3F3Fu;  // sub-blocks 0..3
+  const uint32_t sc_b = (h2 & 0x0F0Fu) | ((h0 >> 2) & 0x3030u);  // sub-blocks 4..7
+  const uint32_t mn_b = ((h2 >> 4) & 0x0F0Fu) | ((h1 >> 2) & 0x3030u);
+  const uint32_t sc = t < 2 ? sc_a : sc_b, mn = t < 2 ? mn_a : mn_b;
+  // 6-bit integers to float exactly: 2^23 + v, minus 2^23
+  const float2 bias = make_float2(-8388608.0f, -8388608.0f);
+  const float2 scf = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(sc, 0x4B000000u, 0x7440u)),
+                                            __uint_as_float(__byte_perm(sc, 0x4B000000u, 0x7441u))),
+                                bias);
+  const float2 mnf = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(mn, 0x4B000000u, 0x7440u)),
+                                            __uint_as_float(__byte_perm(mn, 0x4B000000u, 0x7441u))),
+                                bias);
+  dsc = __fmul2_rn(make_float2(d, d), scf);
+  dmn = __fmul2_rn(make_float2(dmin, dmin), mnf);
+}
+
+// Adds to y[r][n] (r = 0: row g, r = 1: row g + 8 of a 16-row block; .x the
+// even sub-block of the lane's slot, .y the odd one) this lane's share of the
+// dot products of super-block sb of the block's rows with tokens n < nt.
+// rg / rg8: the super-block of rows g and g+8 in shared memory (16-byte
+// aligned; the 8 row groups must fall in different bank groups, e.g. rows
+// 144 bytes apart or a pitch of 16 mod 128).
+template <int NT>
+__device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8, int sb,
+                                           const uint8_t* const (&mx)[NT], int nt, int nsb,
+                                           int lane, float2 (&y)[2][NT]) {
+  const int g = lane >> 2, t = lane & 3;
+  const bool bthread = t == (g >> 1);  // the lane whose B column g can be non-zero
+  {
+    const uint4 wg0 = *reinterpret_cast<const uint4*>(rg + 16 + 32 * t);
+    const uint4 w80 = *reinterpret_cast<const uint4*>(rg8 + 16 + 32 * t);
+    const uint4 wg1 = *reinterpret_cast<const uint4*>(rg + 32 + 32 * t);
+    const uint4 w81 = *reinterpret_cast<const uint4*>(rg8 + 32 + 32 * t);
+    const uint32_t Wg[8] = {wg0.x, wg0.y, wg0.z, wg0.w, wg1.x, wg1.y, wg1.z, wg1.w};
+    const uint32_t W8[8] = {w80.x, w80.y, w80.z, w80.w, w81.x, w81.y, w81.z, w81.w};
+    float de[NT][4], dodd[NT][4];  // D of the even and odd set
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) de[n][q] = dodd[n][q] = 0.f;
+    const uint4* fr[NT];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+      fr[n] = reinterpret_cast<const uint4*>(mx[n]) + (((long)sb * 2) * 8 + g) * 4;
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      uint4 be[NT], bo[NT];  // B of k-steps j, j+1 (even set, odd set)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        be[n] = bo[n] = make_uint4(0, 0, 0, 0);
+        if (bthread && n < nt) {
+          be[n] = __ldg(fr[n] + j / 2);
+          bo[n] = __ldg(fr[n] + 32 + j / 2);
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const uint32_t wg = Wg[j + jj], w8 = W8[j + jj];
+        const uint32_t gs = wg >> 8, g8s = w8 >> 8;
+        const uint32_t al0 = wg & 0x000F000Fu, al1 = w8 & 0x000F000Fu;
+        const uint32_t al2 = gs & 0x000F000Fu, al3 = g8s & 0x000F000Fu;
+        const uint32_t ah0 = wg & 0x00F000F0u, ah1 = w8 & 0x00F000F0u;
+        const uint32_t ah2 = gs & 0x00F000F0u, ah3 = g8s & 0x00F000F0u;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          if (n < nt) {
+            const uint32_t e0 = jj ? be[n].z : be[n].x, e1 = jj ? be[n].w : be[n].y;
+            const uint32_t o0 = jj ? bo[n].z : bo[n].x, o1 = jj ? bo[n].w : bo[n].y;
+            mma_f16(de[n], al0, al1, al2, al3, e0, e1);
+            mma_f16(dodd[n], ah0, ah1, ah2, ah3, o0, o1);
+          }
+        }
+      }
+    }
+    float2 dsc[2], dmn[2];
+    q4k_pair_scales(*reinterpret_cast<const uint4*>(rg), t, dsc[0], dmn[0]);
+    q4k_pair_scales(*reinterpret_cast<const uint4*>(rg8), t, dsc[1], dmn[1]);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      if (n < nt) {
+        const float4 mt =
+            __ldg(reinterpret_cast<const float4*>(mx[n] + (size_t)nsb * 1024) + sb * 4 + t);
+        const float2 back = make_float2(mt.x, mt.z), sums = make_float2(-mt.y, -mt.w);
+        // D: [0] row g high, [1] row g low, [2] row g+8 high, [3] row g+8 low
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          float2 s = __fadd2_rn(make_float2(de[n][2 * r], dodd[n][2 * r]),
+                                make_float2(de[n][2 * r + 1], dodd[n][2 * r + 1]));
+          s = __fmul2_rn(s, back);  // sum(q*x) of the even and odd sub-block
+          float2 a = __ffma2_rn(dsc[r], s, y[r][n]);
+          y[r][n] = __ffma2_rn(dmn[r], sums, a);
+        }
+      }
+    }
+  }
+}
+
+// q4k_sb_mma over super-blocks [sb0, sb1) of a 16-row tile whose row 0 is
+// `tile`, rows `pitch` bytes apart (pitch % 128 == 16).
+template <int NT>
+__device__ __forceinline__ void q4k_tile_mma(const uint8_t* tile, int pitch, int sb0, int sb1,
+                                             const uint8_t* const (&mx)[NT], int nt, int nsb,
+                                             int lane, float2 (&y)[2][NT]) {
+  const int g = lane >> 2;
+  for (int sb = sb0; sb < sb1; ++sb) {
+    const uint8_t* rg = tile + g * pitch + sb * LB_Q4K;
+    q4k_sb_mma<NT>(rg, rg + 8 * pitch, sb, mx, nt, nsb, lane, y);
+  }
+}
+
+// This warp's share of a staged tile: the (matrix, super-block) items
+// [warp*I/W, (warp+1)*I/W) of I = MATS * nsb.
+template <int NT, int MATS, int W>
+__device__ __forceinline__ void tile_items(const uint8_t* stage, int pitch, int nsb, int warp,
+                                           int lane, const uint8_t* const (&mx)[NT], int nt,
+                                           float2 (&y)[MATS][2][NT]) {
+  const int items = MATS * nsb;
+  const int i0 = warp * items / W, i1 = (warp + 1) * items / W;
+#pragma unroll
+  for (int mat = 0; mat < MATS; ++mat) {
+    const int sb0 = max(i0 - mat * nsb, 0), sb1 = min(i1 - mat * nsb, nsb);
+    if (sb0 < sb1)
+      q4k_tile_mma<NT>(stage + (size_t)mat * kTileRows * pitch, pitch, sb0, sb1, mx, nt, nsb,
+                       lane, y[mat]);
+  }
+}
+
+// Sums y over each quad and stores the row sums into red[warp][mat][row][n].
+template <int NT, int MATS>
+__device__ __forceinline__ void tile_partials_store(float* red, int warp, int lane,
+                                                    const float2 (&y)[MATS][2][NT]) {
+  float v[MATS][2][NT];
+#pragma unroll
+  for (int mat = 0; mat < MATS; ++mat)
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        float s = y[mat][r][n].x + y[mat][r][n].y;
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        v[mat][r][n] = s;
+      }
+  if ((lane & 3) == 0) {
+    const int g = lane >> 2;
+#pragma unroll
+    for (int mat = 0; mat < MATS; ++mat)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+          red[((warp * MATS + mat) * kTileRows + g + 8 * r) * NT + n] = v[mat][r][n];
+  }
+}
+
+// Row sum (row r, token n, matrix mat) of a tile from the warps' partials.
+template <int NT, int MATS, int W>
+__device__ __forceinline__ float tile_row_sum(const float* red, int mat, int r, int n) {
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < W; ++w) s += red[((w * MATS + mat) * kTileRows + r) * NT + n];
+  return s;
+}
+
+template <int NT, int MATS, int W>
+__host__ __device__ __forceinline__ int tile_red_floats() {
+  return 2 * W * MATS * kTileRows * NT;  // double-buffered
+}
+
+// ------------------------------------------------------------ tile staging
+
+// Shared-memory plan of a tile pipeline.
+struct TilePlan {
+  int pitch;        // padded row pitch in shared memory
+  int stage_bytes;  // MATS * 16 * pitch, rounded to 128
+  int stages;
+};
+
+__host__ __device__ __forceinline__ TilePlan tile_plan(size_t row_bytes, int mats, size_t budget) {
+  TilePlan p;
+  p.pitch = (int)(((row_bytes + 127) & ~size_t(127)) + 16);  // pitch % 128 == 16
+  p.stage_bytes = (int)(((size_t)mats * kTileRows * p.pitch + 127) & ~size_t(127));
+  p.stages = (int)(budget / p.stage_bytes);
+  if (p.stages > 5) p.stages = 5;
+  return p;
+}
+
+// Issues the copies of one tile into stage `st` (all lanes of one warp):
+// rows [0, nr) of matrix 0 from src0 and, when src1 is set, of matrix 1 from
+// src1, each row `rb` bytes (rb % 16 == 0, sources 16-byte aligned).
+__device__ __forceinline__ void tile_issue(uint8_t* st, uint64_t* bar, int pitch, int nr,
+                                           size_t rb, const uint8_t* src0, const uint8_t* src1,
+                                           int lane) {
+  const int mats = src1 ? 2 : 1;
+  if (lane == 0) mbar_expect_tx(bar, (uint32_t)(mats * nr * rb));
+  __syncwarp();
+  const int mat = lane >> 4, r = lane & 15;
+  if (mat < mats && r < nr)
+    tma_load_1d(st + (size_t)(mat * kTileRows + r) * pitch, (mat ? src1 : src0) + (size_t)r * rb,
+                (uint32_t)rb, bar);
+}
+
+}  // namespace lb

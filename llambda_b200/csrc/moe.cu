@@ -19,16 +19,29 @@
 // In 4 and 5 every warp takes a contiguous run of units, so the expert's
 // routing metadata and the token's activations stay in registers across the
 // expert's units.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "engine.cuh"
 #include "kernels.h"
+#include "mma.cuh"
 
 namespace lb {
 
 namespace {
 
 constexpr int kMaxExperts = 1024;
+constexpr int kSlabMaxStages = 10;
+
+// Floats per token of the prepared gate/up input: room for either layout
+// (Q4_K: the tensor-core layout of mma.cuh; Q6_K: the warp engine's).
+__host__ __device__ __forceinline__ long up_ld_floats(int K) {
+  const long a = xp_stride(K), b = (long)(mx_bytes(K) / 4);
+  return a > b ? a : b;
+}
 
 // exp of a single-float as SBCL evaluates it (in double, rounded to single),
 // then silu / sigmoid divide in double (llambda.lisp L926-930).
@@ -126,7 +139,8 @@ __global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T)
 }
 
 // Groups the (token, rank) entries by owned expert, stably.
-__global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int T) {
+// pass_nt: tokens per pass of the up kernel; pass_off counts passes.
+__global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int T, int pass_nt) {
   __shared__ int s_count[kMaxExperts];
   __shared__ int s_offset[kMaxExperts + 1];
   const int E = m.experts, k = m.top_k;
@@ -154,26 +168,38 @@ __global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int 
       __syncwarp();
       if (id < n) w.entries[id] = own ? (base + rank) : -1;  // position, fixed below
     }
-    // exclusive scan over experts, active list in increasing expert id
-    int run = 0, nact = 0;
+    // exclusive scans over experts (entries and token passes), active list in
+    // increasing expert id
+    int run = 0, nact = 0, prun = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
       const int e = e0 + lane;
       const int cnt = e < E ? s_count[e] : 0;
-      int incl = cnt;
+      const int pc = (cnt + pass_nt - 1) / pass_nt;
+      int incl = cnt, pincl = pc;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
+        const int pv = __shfl_up_sync(0xffffffffu, pincl, o);
+        if (lane >= o) {
+          incl += v;
+          pincl += pv;
+        }
       }
       if (e < E) s_offset[e] = run + incl - cnt;
       const unsigned nz = __ballot_sync(0xffffffffu, cnt > 0);
-      if (cnt > 0) w.active[nact + __popc(nz & lt_mask)] = e;
+      if (cnt > 0) {
+        const int a = nact + __popc(nz & lt_mask);
+        w.active[a] = e;
+        w.pass_off[a] = prun + pincl - pc;
+      }
       nact += __popc(nz);
       run += __shfl_sync(0xffffffffu, incl, 31);
+      prun += __shfl_sync(0xffffffffu, pincl, 31);
     }
     if (lane == 0) {
       s_offset[E] = run;
       w.active[E] = nact;
+      w.pass_off[nact] = prun;
     }
   }
   __syncthreads();
@@ -216,7 +242,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, m.norm_epsilon)));
   }
   float* xn = w.xn + (long)blockIdx.x * H;
-  float* xp = w.xp_up + (long)blockIdx.x * xp_stride(K);
+  float* xp = w.xp_up + (long)blockIdx.x * up_ld_floats(K);
   for (int base = 0; base < K; base += 4 * blockDim.x) {
     const int e = base + 4 * threadIdx.x;
     float v[4];
@@ -234,14 +260,11 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
       v[q] = val;
     }
     if (e < K) {  // K is a multiple of 256, so whole warps agree here
-      *reinterpret_cast<float4*>(xp + xp_index<UT>(e, tasks)) = make_float4(v[0], v[1], v[2], v[3]);
-      if (UT == LB_TYPE_Q4_K) {
-        float part = (v[0] + v[1]) + (v[2] + v[3]);
-        part += __shfl_xor_sync(0xffffffffu, part, 1);
-        part += __shfl_xor_sync(0xffffffffu, part, 2);
-        part += __shfl_xor_sync(0xffffffffu, part, 4);
-        if ((threadIdx.x & 7) == 0) xp[K + (e >> 5)] = part;
-      }
+      if (UT == LB_TYPE_Q4_K)  // tensor-core layout (mma.cuh)
+        mx_store4(reinterpret_cast<uint8_t*>(xp), K, e, make_float4(v[0], v[1], v[2], v[3]));
+      else
+        *reinterpret_cast<float4*>(xp + xp_index<UT>(e, tasks)) =
+            make_float4(v[0], v[1], v[2], v[3]);
     }
   }
 }
@@ -287,7 +310,7 @@ __global__ void __launch_bounds__(128) moe_up_kernel(MoeDevice m, MoeWork w, int
   const int tasks = K >> 6;
   const int kd = shared_pass ? m.k_down_sh : m.k_down;
   const int tasks_d = kd >> 6;
-  const long ld_up = xp_stride(m.k_in);
+  const long ld_up = up_ld_floats(m.k_in);
   const long ld_dn = xp_stride(max(m.k_down, m.k_down_sh));
   const size_t grb = shared_pass ? m.gate_sh_rb : m.gate_rb;
   const size_t urb = shared_pass ? m.up_sh_rb : m.up_rb;
@@ -375,6 +398,253 @@ __global__ void __launch_bounds__(128) moe_up_kernel(MoeDevice m, MoeWork w, int
   }
   if (!ok)
     for (int q = i + 1; q < issued; ++q) mbar_wait(&ring.bars[q % stages], (q / stages) & 1, nullptr);
+}
+
+// ---------------------------------------------------------------- up (slabs)
+// Q4_K gate/up rows on the tensor cores, K-sliced: a unit is a slab of RU
+// rows of each matrix (gate and up: RU = 16 * CW / 2; up only: 16 * CW) of
+// one routed expert, or of the shared expert for a chunk of tokens.  Consumer
+// warp w owns row block w (16 rows of one matrix) across the whole K, so its
+// sums stay in registers; a pipeline stage is one super-block column slice of
+// the slab: CW boxes of 16 rows x 144 bytes, loaded by 2-D tensor copies
+// (rows 144 bytes apart in shared memory: the 8 row groups of a fragment load
+// fall in different bank groups).  Warp CW is the producer: it waits until
+// all consumer warps released a stage (empty barrier) before refilling it.
+// With gate and up, the up warps hand their row sums to the gate warps once
+// per slab through a double-buffered exchange guarded by two more barriers.
+// Every wait is bounded; a timeout raises a CTA-wide abort flag.
+struct SlabSync {
+  uint64_t full[kSlabMaxStages];
+  uint64_t empty[kSlabMaxStages];
+  uint64_t xfull[2];
+  uint64_t xempty[2];
+  int abort;
+  int pad[3];
+};
+
+template <int NT, bool PAIR, int DT, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
+    moe_up_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, long map_row_base,
+                       const __grid_constant__ CUtensorMap tm_gate,
+                       const __grid_constant__ CUtensorMap tm_up,
+                       const __grid_constant__ CUtensorMap tm_gate_sh,
+                       const __grid_constant__ CUtensorMap tm_up_sh) {
+  constexpr int MATS = PAIR ? 2 : 1;
+  constexpr int RBM = CW / MATS;       // row blocks per matrix
+  constexpr int RU = RBM * kTileRows;  // rows per matrix per slab
+  constexpr int BOX = kTileRows * LB_Q4K;
+  constexpr int STAGE = CW * BOX;
+  extern __shared__ __align__(128) uint8_t smem[];
+  SlabSync* sync = reinterpret_cast<SlabSync*>(smem + (size_t)stages * STAGE);
+  float* xch = reinterpret_cast<float*>(sync + 1);  // [2][RU][NT] up-row sums
+  volatile int* abort = &sync->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&sync->full[s], 1);
+      mbar_init(&sync->empty[s], CW);
+    }
+    for (int p = 0; p < 2; ++p) {
+      mbar_init(&sync->xfull[p], RBM);
+      mbar_init(&sync->xempty[p], RBM);
+    }
+    sync->abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int k = m.top_k;
+  const int per_r = (m.inter + RU - 1) / RU;
+  const int per_s = (m.inter_sh + RU - 1) / RU;
+  const int passes_s = (T + NT - 1) / NT;
+  const int nact = w.active[m.experts];
+  // work items: (slab, pass of up to NT tokens), all of one cost; routed ones
+  // expert-major (passes of expert a: pass_off[a] ..), then slab, then pass
+  const int n_routed = w.pass_off[nact] * per_r;
+  const int n_shared = (m.shared_here && m.inter_sh) ? per_s * passes_s : 0;
+  const int units = n_routed + n_shared;
+  const int u0 = (int)((long)blockIdx.x * units / gridDim.x);
+  const int n_my = (int)((long)(blockIdx.x + 1) * units / gridDim.x) - u0;
+  const int nsb = m.k_in >> 8;
+
+  struct Unit {
+    int row0, rows_e, t_begin, t_end;
+    long map_row;  // row of the slab's first row in its tensor map
+    bool shared;
+  };
+  ExpertView view;
+  int a_hint = 0;  // active index of the previous item (items are visited in order)
+  auto unit_at = [&](int u) {
+    Unit x;
+    if (u < n_routed) {
+      int a = a_hint;  // first a with pass_off[a + 1] * per_r > u, searched from the hint
+      if (w.pass_off[a] * per_r > u) a = 0;
+      int hi = nact;
+      while (hi - a > 1) {
+        const int mid = (a + hi) >> 1;
+        if (w.pass_off[mid] * per_r <= u) a = mid; else hi = mid;
+      }
+      a_hint = a;
+      view_expert(m, w, T, a, view);
+      const int np = w.pass_off[a + 1] - w.pass_off[a];
+      const int local = u - w.pass_off[a] * per_r, slab = local / np, p = local - slab * np;
+      x.shared = false;
+      x.rows_e = m.inter;
+      x.row0 = slab * RU;
+      x.t_begin = p * NT;
+      x.t_end = min(view.ntok, x.t_begin + NT);
+      x.map_row = (long)view.e * m.inter - map_row_base + x.row0;
+    } else {
+      const int q = u - n_routed, slab = q / passes_s, p = q - slab * passes_s;
+      x.shared = true;
+      x.rows_e = m.inter_sh;
+      x.row0 = slab * RU;
+      x.t_begin = p * NT;
+      x.t_end = min(T, x.t_begin + NT);
+      x.map_row = x.row0;
+    }
+    return x;
+  };
+
+  if (warp == CW) {  // ---------------- producer
+    if (lane == 0) {
+      int q = 0;
+      bool ok = true;
+      for (int i = 0; i < n_my && ok; ++i) {
+        const Unit x = unit_at(u0 + i);
+        for (int t0 = x.t_begin; t0 < x.t_end && ok; t0 += NT) {
+          for (int sb = 0; sb < nsb; ++sb, ++q) {
+            const int s = q % stages;
+            if (q >= stages &&
+                !mbar_wait_or_abort(&sync->empty[s], ((q / stages) - 1) & 1, w.status, abort)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&sync->full[s], STAGE);
+            uint8_t* st = smem + (size_t)s * STAGE;
+#pragma unroll
+            for (int b = 0; b < CW; ++b) {
+              const bool gate = PAIR && b < RBM;
+              const CUtensorMap* tm = x.shared ? (gate ? &tm_gate_sh : &tm_up_sh)
+                                               : (gate ? &tm_gate : &tm_up);
+              tma_load_2d(st + b * BOX, tm, sb * LB_Q4K, (int)(x.map_row + (b % RBM) * kTileRows),
+                          &sync->full[s]);
+            }
+          }
+        }
+      }
+      // every copy issued must land before the CTA may exit
+      for (int r = max(0, q - stages); r < q; ++r)
+        mbar_wait(&sync->full[r % stages], (r / stages) & 1, nullptr);
+    }
+    return;
+  }
+
+  // ---------------- consumers
+  const int mat = warp / RBM, rb = warp % RBM;
+  const int g = lane >> 2, t = lane & 3;
+  const long ld_up = up_ld_floats(m.k_in);
+  const long ld_dn = xp_stride(max(m.k_down, m.k_down_sh));
+  int q = 0, pass = 0;
+  bool ok = true;
+  for (int i = 0; i < n_my && ok; ++i) {
+    const Unit x = unit_at(u0 + i);
+    const int kd = x.shared ? m.k_down_sh : m.k_down, tasks_d = kd >> 6;
+    for (int t0 = x.t_begin; t0 < x.t_end && ok; t0 += NT, ++pass) {
+      const int nt = min(NT, x.t_end - t0);
+      int ids[NT];
+      const uint8_t* mxp[NT];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int tt = min(t0 + n, x.t_end - 1);
+        ids[n] = x.shared ? T * k + tt : view.list[tt];
+        const int tok = x.shared ? tt : ids[n] / k;
+        mxp[n] = reinterpret_cast<const uint8_t*>(w.xp_up + tok * ld_up);
+      }
+      float2 acc[2][NT];
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int n = 0; n < NT; ++n) acc[r][n] = make_float2(0.f, 0.f);
+      for (int sb = 0; sb < nsb; ++sb, ++q) {
+        const int s = q % stages;
+        if (!mbar_wait_or_abort(&sync->full[s], (q / stages) & 1, w.status, abort)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* blk = smem + (size_t)s * STAGE + warp * BOX;
+        q4k_sb_mma<NT>(blk + g * LB_Q4K, blk + (g + 8) * LB_Q4K, sb, mxp, nt, nsb, lane, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sync->empty[s]);
+      }
+      if (!ok) break;
+      // row sums of rows g and g+8 of this block on lane t == 0 of each quad
+      float v[2][NT];
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          float s = acc[r][n].x + acc[r][n].y;
+          s += __shfl_xor_sync(0xffffffffu, s, 1);
+          s += __shfl_xor_sync(0xffffffffu, s, 2);
+          v[r][n] = s;
+        }
+      const int par = pass & 1, use = pass >> 1;
+      float* xb = xch + (size_t)par * RU * NT;
+      auto store_h = [&](float up_or_h, int r, int n, bool gated, float gate) {
+        const int row = x.row0 + rb * kTileRows + g + 8 * r;
+        if (row < x.rows_e && n < nt) {
+          const float hv = gated ? __fmul_rn(silu_ref(gate), up_or_h) : relu_sq_ref(up_or_h);
+          int id = ids[0];
+#pragma unroll
+          for (int n2 = 1; n2 < NT; ++n2)
+            if (n2 == n) id = ids[n2];
+          w.xp_down[(long)id * ld_dn + xp_index<DT>(row, tasks_d)] = hv;
+        }
+      };
+      if (PAIR && mat == 1) {  // up warps: hand the sums to the gate warps
+        if (use > 0 && !mbar_wait_or_abort(&sync->xempty[par], (use - 1) & 1, w.status, abort)) {
+          ok = false;
+          break;
+        }
+        if (t == 0)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int n = 0; n < NT; ++n) xb[(rb * kTileRows + g + 8 * r) * NT + n] = v[r][n];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sync->xfull[par]);
+      } else if (PAIR) {  // gate warps: silu(gate) * up
+        if (!mbar_wait_or_abort(&sync->xfull[par], use & 1, w.status, abort)) {
+          ok = false;
+          break;
+        }
+        if (t == 0)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+              store_h(xb[(rb * kTileRows + g + 8 * r) * NT + n], r, n, true, v[r][n]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sync->xempty[par]);
+      } else if (t == 0) {  // up only: relu(up)^2
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int n = 0; n < NT; ++n) store_h(v[r][n], r, n, false, 0.f);
+      }
+      if (warp == 0 && x.row0 + RU >= x.rows_e) {  // last slab: zero the padding up to kd
+        const int pad = kd - x.rows_e;
+        for (int qq = lane; qq < nt * pad; qq += 32) {
+          const int nn = qq / pad, pe = x.rows_e + (qq - nn * pad);
+          int id = ids[0];
+#pragma unroll
+          for (int n2 = 1; n2 < NT; ++n2)
+            if (n2 == nn) id = ids[n2];
+          w.xp_down[(long)id * ld_dn + xp_index<DT>(pe, tasks_d)] = 0.f;
+        }
+      }
+    }
+  }
 }
 
 // Q4_K down inputs need sub-block sums; Q6_K inputs do not.
@@ -555,10 +825,114 @@ cudaError_t launch_down(const MoeDevice& m, const MoeWork& w, int T, int shared_
   return cudaErrorInvalidValue;
 }
 
+// 2-D tensor map over `rows` Q4_K rows of `rb` bytes at `base`; one box is
+// one super-block (144 bytes) of 16 rows.
+bool q4k_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t rb) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!encode || rows == 0) return false;
+  const cuuint64_t dims[2] = {rb, rows};
+  const cuuint64_t strides[1] = {rb};
+  const cuuint32_t box[2] = {LB_Q4K, kTileRows};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct SlabMaps {
+  CUtensorMap gate, up, gate_sh, up_sh;
+  long row_base;  // global row (expert_begin * inter) of the routed maps' row 0
+};
+
+template <int NT, bool PAIR, int DT, int CW>
+cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
+                              cudaStream_t s) {
+  auto kern = moe_up_slab_kernel<NT, PAIR, DT, CW>;
+  constexpr int RU = CW / (PAIR ? 2 : 1) * kTileRows;
+  const size_t stage = (size_t)CW * kTileRows * LB_Q4K;
+  const size_t extra = sizeof(SlabSync) + (size_t)2 * RU * NT * 4;
+  const int stages = (int)std::min<size_t>(kSlabMaxStages, (kTileSmemBudget - extra) / stage);
+  if (stages < 2) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)stages * stage + extra;
+  if (prepared_occupancy(kern, (CW + 1) * 32, smem) < 1) return cudaErrorUnknown;
+  kern<<<sm_count(), (CW + 1) * 32, smem, s>>>(m, w, T, stages, mp.row_base, mp.gate,
+                                                mp.up, mp.gate_sh, mp.up_sh);
+  return cudaGetLastError();
+}
+
+// Tokens per pass (NT) of the tensor-core gate/up launch, from the expected
+// tokens per active expert; the route kernel counts passes with the same NT.
+int up_pass_tokens(const MoeDevice& m, int T) {
+  if (m.up_type != LB_TYPE_Q4_K || T == 1) return 1;
+  const long entries = (long)T * m.top_k;
+  const long owned = std::max(1, m.expert_end - m.expert_begin);
+  const double per_expert = (double)entries / (double)std::min(entries, owned);
+  return per_expert < 2.5 ? 2 : 4;
+}
+
+// Routed and shared gate/up in one tensor-core launch.
+template <int DT>
+cudaError_t launch_up_mma(const MoeDevice& m, const MoeWork& w, int T, cudaStream_t s) {
+  const bool pair = m.arch == 0;
+  SlabMaps mp;
+  mp.row_base = (long)m.expert_begin * m.inter;
+  const uint64_t owned_rows = (uint64_t)std::max(0, m.expert_end - m.expert_begin) * m.inter;
+  const bool shared = m.shared_here && m.inter_sh;
+  if (shared) {
+    if (!q4k_rows_map(&mp.up_sh, m.up_sh, m.inter_sh, m.up_sh_rb)) return cudaErrorInvalidValue;
+    mp.gate_sh = mp.up_sh;
+    if (pair && !q4k_rows_map(&mp.gate_sh, m.gate_sh, m.inter_sh, m.gate_sh_rb))
+      return cudaErrorInvalidValue;
+  }
+  if (owned_rows) {
+    const uint8_t* up0 = m.up_exps + (size_t)mp.row_base * m.up_rb;
+    if (!q4k_rows_map(&mp.up, up0, owned_rows, m.up_rb)) return cudaErrorInvalidValue;
+    mp.gate = mp.up;
+    if (pair && !q4k_rows_map(&mp.gate, m.gate_exps + (size_t)mp.row_base * m.gate_rb,
+                              owned_rows, m.gate_rb))
+      return cudaErrorInvalidValue;
+  } else if (shared) {  // no routed rows here: the routed maps are never used
+    mp.up = mp.up_sh;
+    mp.gate = mp.gate_sh;
+  } else {
+    return cudaSuccess;
+  }
+  if (!shared) {
+    mp.up_sh = mp.up;
+    mp.gate_sh = mp.gate;
+  }
+  switch (up_pass_tokens(m, T)) {
+    case 1:
+      return pair ? launch_up_slab_nt<1, true, DT, 8>(m, w, T, mp, s)
+                  : launch_up_slab_nt<1, false, DT, 8>(m, w, T, mp, s);
+    case 2:
+      return pair ? launch_up_slab_nt<2, true, DT, 8>(m, w, T, mp, s)
+                  : launch_up_slab_nt<2, false, DT, 8>(m, w, T, mp, s);
+    default:
+      return pair ? launch_up_slab_nt<4, true, DT, 8>(m, w, T, mp, s)
+                  : launch_up_slab_nt<4, false, DT, 8>(m, w, T, mp, s);
+  }
+}
+
 template <int UT, int DT>
 cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T, cudaStream_t s) {
-  cudaError_t e = launch_up<UT, DT>(m, w, T, 0, s);
-  if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_up<UT, DT>(m, w, T, 1, s);
+  cudaError_t e;
+  if constexpr (UT == LB_TYPE_Q4_K) {
+    e = launch_up_mma<DT>(m, w, T, s);
+  } else {
+    e = launch_up<UT, DT>(m, w, T, 0, s);
+    if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_up<UT, DT>(m, w, T, 1, s);
+  }
   if (e != cudaSuccess) return e;
   if (DT == LB_TYPE_Q4_K) {
     moe_down_sums_kernel<<<std::min(T * m.top_k + T, sm_count() * 4), 128, 0, s>>>(m, w, T);
@@ -594,9 +968,10 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
   w->offsets = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
   w->entries = reinterpret_cast<int*>(take((size_t)T * k * 2 * 4));
   w->active = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
+  w->pass_off = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
   w->status = reinterpret_cast<int*>(take(4));
   w->xn = reinterpret_cast<float*>(take(m.input_norm ? (size_t)T * m.hidden * 4 : 4));
-  w->xp_up = reinterpret_cast<float*>(take((size_t)T * xp_stride(m.k_in) * 4));
+  w->xp_up = reinterpret_cast<float*>(take((size_t)T * up_ld_floats(m.k_in) * 4));
   w->xp_down = reinterpret_cast<float*>(
       take((size_t)(T * k + T) * xp_stride(std::max(m.k_down, m.k_down_sh)) * 4));
   w->partial = reinterpret_cast<float*>(take((size_t)T * (k + 1) * m.hidden * 4));
@@ -626,7 +1001,7 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   if (e != cudaSuccess) return e;
   topk_kernel<<<T, 32, 0, s>>>(m, w, T);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  route_kernel<<<1, 256, 0, s>>>(m, w, T);
+  route_kernel<<<1, 256, 0, s>>>(m, w, T, up_pass_tokens(m, T));
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
   if (!gate_ok) return cudaErrorInvalidValue;
