@@ -87,6 +87,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// Prefetches [src, src + bytes) into L2 (src and bytes multiples of 16).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  if (bytes)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }

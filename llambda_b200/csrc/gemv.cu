@@ -193,11 +193,11 @@ __global__ void __launch_bounds__(NW * 32, 1)
       const uint8_t* mxp[NT];
 #pragma unroll
       for (int n = 0; n < NT; ++n) mxp[n] = mx + (size_t)min(t0 + n, tokens - 1) * mxb;
-      float2 acc[1][2][NT];
+      float2 acc[1][NT][2];
 #pragma unroll
       for (int r = 0; r < 2; ++r)
 #pragma unroll
-        for (int n = 0; n < NT; ++n) acc[0][r][n] = make_float2(0.f, 0.f);
+        for (int n = 0; n < NT; ++n) acc[0][n][r] = make_float2(0.f, 0.f);
       if (ok) tile_items<NT, 1, NW>(st, plan.pitch, nsb, warp, lane, mxp, nt, acc);
       float* rbuf = red + buf * (tile_red_floats<NT, 1, NW>() / 2);
       tile_partials_store<NT, 1>(rbuf, warp, lane, acc);
@@ -218,7 +218,94 @@ __global__ void __launch_bounds__(NW * 32, 1)
     for (int q = i; q < issued; ++q) mbar_wait(&full[q % plan.stages], (q / plan.stages) & 1, nullptr);
 }
 
-// F32 rows (the MoE router, ffn_gate_inp): one warp per (row, group of up to
+// F32 rows (the MoE router, ffn_gate_inp), tiled: a CTA of 4 warps takes 16
+// rows (4 per warp) and up to kF32Tok tokens, whose activations it first
+// copies into shared memory, so that each weight float4 read from global
+// memory serves 8 tokens and each activation read serves 4 rows.  Lane l
+// sums columns 4l.., 4(l+32).. of its 32 (row, token) products, and the 32
+// sums meet in a 31-shuffle butterfly that leaves lane l with product l.
+constexpr int kF32Rows = 4, kF32Tok = 8;
+__global__ void __launch_bounds__(128) gemv_f32_tile_kernel(const float* __restrict__ W, int rows,
+                                                            int K, const float* __restrict__ x,
+                                                            long ldx, int tokens,
+                                                            float* __restrict__ y, long ldy) {
+  extern __shared__ float4 xs4[];  // [kF32Tok][K/4]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ __align__(8) uint64_t bar;
+  const int t0 = blockIdx.y * kF32Tok, nt = min(kF32Tok, tokens - t0);
+  const int K4 = K >> 2;
+  const int crow0 = blockIdx.x * 4 * kF32Rows, crows = min(4 * kF32Rows, rows - crow0);
+  float4* ws4 = xs4 + kF32Tok * K4;  // [16][K/4] this CTA's weight rows
+  // one bulk copy of the token rows and one of the weight rows, so the loads
+  // cost one round trip instead of one per loop iteration
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    const uint32_t xb = (uint32_t)K * 4u;
+    mbar_expect_tx(&bar, xb * (uint32_t)(nt + crows));
+    if (ldx == K) {
+      tma_load_1d(xs4, x + (long)t0 * ldx, xb * nt, &bar);
+    } else {
+      for (int n = 0; n < nt; ++n) tma_load_1d(xs4 + n * K4, x + (long)(t0 + n) * ldx, xb, &bar);
+    }
+    tma_load_1d(ws4, W + (size_t)crow0 * K, xb * crows, &bar);
+  }
+  for (int i = nt * K4 + threadIdx.x; i < kF32Tok * K4; i += blockDim.x)
+    xs4[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // tokens past the end
+  __syncthreads();
+  mbar_wait(&bar, 0, nullptr);
+  const int row0 = (blockIdx.x * 4 + warp) * kF32Rows;
+  if (row0 >= rows) return;
+  float2 acc[kF32Rows][kF32Tok / 2];  // (token 2p, token 2p+1)
+#pragma unroll
+  for (int r = 0; r < kF32Rows; ++r)
+#pragma unroll
+    for (int p = 0; p < kF32Tok / 2; ++p) acc[r][p] = make_float2(0.f, 0.f);
+  const float4* wr[kF32Rows];
+#pragma unroll
+  for (int r = 0; r < kF32Rows; ++r)
+    wr[r] = ws4 + (size_t)min(warp * kF32Rows + r, crows - 1) * K4;
+  for (int c = lane; c < K4; c += 32) {
+    float4 wv[kF32Rows];
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r) wv[r] = wr[r][c];
+#pragma unroll
+    for (int p = 0; p < kF32Tok / 2; ++p) {
+      const float4 xa = xs4[(2 * p) * K4 + c], xb = xs4[(2 * p + 1) * K4 + c];
+#pragma unroll
+      for (int r = 0; r < kF32Rows; ++r) {
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].x, wv[r].x), make_float2(xa.x, xb.x), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].y, wv[r].y), make_float2(xa.y, xb.y), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].z, wv[r].z), make_float2(xa.z, xb.z), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].w, wv[r].w), make_float2(xa.w, xb.w), acc[r][p]);
+      }
+    }
+  }
+  // butterfly: value v[i], i = r * 8 + n, ends on lane i
+  float v[32];
+#pragma unroll
+  for (int r = 0; r < kF32Rows; ++r)
+#pragma unroll
+    for (int p = 0; p < kF32Tok / 2; ++p) {
+      v[r * 8 + 2 * p] = acc[r][p].x;
+      v[r * 8 + 2 * p + 1] = acc[r][p].y;
+    }
+#pragma unroll
+  for (int h = 16; h >= 1; h >>= 1) {
+    const bool upper = (lane & h) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = upper ? v[i] : v[i + h];
+      const float keep = upper ? v[i + h] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  const int r = lane >> 3, n = lane & 7;
+  if (row0 + r < rows && n < nt) y[(long)(t0 + n) * ldy + row0 + r] = v[0];
+}
+
+// F32 rows without the tile's shared memory (very wide rows or unaligned
+// data): one warp per (row, group of up to
 // 8 tokens); activations are read straight from global memory (they stay in
 // L1/L2), so there is no staging and every SM takes part.
 __global__ void __launch_bounds__(128) gemv_f32_kernel(const float* __restrict__ W, int rows,
@@ -402,6 +489,15 @@ cudaError_t launch_gemv_prepped(int type, const void* W, size_t rb, int rows, in
 cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long ldx, int tokens,
                             float* y, long ldy, cudaStream_t stream) {
   if (rows <= 0 || tokens <= 0) return cudaSuccess;
+  const size_t smem = (size_t)(kF32Tok + 4 * kF32Rows) * K * sizeof(float);
+  const bool vec = (K & 3) == 0 && (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  if (vec && smem <= 192 * 1024 && prepared_occupancy(gemv_f32_tile_kernel, 128, smem) >= 1) {
+    dim3 grid((rows + kF32Rows * 4 - 1) / (kF32Rows * 4), (tokens + kF32Tok - 1) / kF32Tok);
+    gemv_f32_tile_kernel<<<grid, 128, smem, stream>>>(static_cast<const float*>(W), rows, K, x,
+                                                      ldx, tokens, y, ldy);
+    return cudaGetLastError();
+  }
   const long items = (long)rows * ((tokens + 7) / 8);
   const long blocks = std::min<long>((items + 3) / 4, (long)sm_count() * 16);
   gemv_f32_kernel<<<(int)std::max<long>(blocks, 1), 128, 0, stream>>>(

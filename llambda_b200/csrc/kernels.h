@@ -99,6 +99,7 @@ struct MoeWork {
   int* active;        // [E+1] active experts, then count at [E]
   int* pass_off;      // [E+1] per active expert: token passes (of the up pass's
                       //  tokens per pass) before it; total at [active count]
+  int* pass_off_dn;   // [E+1] the same for the down pass (4 entries per pass)
   int* status;        // [1] device status word (bit 0: non-positive weight sum,
                       //  bit 1: a TMA stage wait timed out)
   float* xn;          // [T][H] normalised input (when input_norm is set)

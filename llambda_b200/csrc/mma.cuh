@@ -144,16 +144,35 @@ __device__ __forceinline__ void q4k_pair_scales(const uint4& hh, int t, float2& 
   dmn = __fmul2_rn(make_float2(dmin, dmin), mnf);
 }
 
-// Adds to y[r][n] (r = 0: row g, r = 1: row g + 8 of a 16-row block; .x the
+// One token's activations for one Q4_K super-block: its 1024 fragment bytes
+// (frag[set][col][j]) and its 64 meta bytes (meta[slot]), in global memory or
+// staged in shared memory.
+struct BSlice {
+  const uint8_t* frag;
+  const uint8_t* meta;
+};
+
+__device__ __forceinline__ BSlice mx_slice(const uint8_t* mx, int sb, int nsb) {
+  return BSlice{mx + (size_t)sb * 1024, mx + (size_t)nsb * 1024 + (size_t)sb * 64};
+}
+
+template <bool SMEM>
+__device__ __forceinline__ uint4 ld_b16(const void* p) {
+  if (SMEM) return *reinterpret_cast<const uint4*>(p);
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Adds to y[n][r] (r = 0: row g, r = 1: row g + 8 of a 16-row block; .x the
 // even sub-block of the lane's slot, .y the odd one) this lane's share of the
-// dot products of super-block sb of the block's rows with tokens n < nt.
-// rg / rg8: the super-block of rows g and g+8 in shared memory (16-byte
-// aligned; the 8 row groups must fall in different bank groups, e.g. rows
-// 144 bytes apart or a pitch of 16 mod 128).
-template <int NT>
-__device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8, int sb,
-                                           const uint8_t* const (&mx)[NT], int nt, int nsb,
-                                           int lane, float2 (&y)[2][NT]) {
+// dot products of one super-block of the block's rows with the NT tokens of
+// bs (SMEM: the slices are in shared memory).  rg / rg8: the super-block of
+// rows g and g+8 in shared memory (16-byte aligned; the 8 row groups must
+// fall in different bank groups, e.g. rows 144 bytes apart or a pitch of 16
+// mod 128).
+template <int NT, bool SMEM>
+__device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8,
+                                           const BSlice (&bs)[NT], int lane,
+                                           float2 (&y)[NT][2]) {
   const int g = lane >> 2, t = lane & 3;
   const bool bthread = t == (g >> 1);  // the lane whose B column g can be non-zero
   {
@@ -168,19 +187,16 @@ __device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int q = 0; q < 4; ++q) de[n][q] = dodd[n][q] = 0.f;
-    const uint4* fr[NT];
-#pragma unroll
-    for (int n = 0; n < NT; ++n)
-      fr[n] = reinterpret_cast<const uint4*>(mx[n]) + (((long)sb * 2) * 8 + g) * 4;
 #pragma unroll
     for (int j = 0; j < 8; j += 2) {
       uint4 be[NT], bo[NT];  // B of k-steps j, j+1 (even set, odd set)
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         be[n] = bo[n] = make_uint4(0, 0, 0, 0);
-        if (bthread && n < nt) {
-          be[n] = __ldg(fr[n] + j / 2);
-          bo[n] = __ldg(fr[n] + 32 + j / 2);
+        if (bthread) {
+          const uint4* fr = reinterpret_cast<const uint4*>(bs[n].frag) + g * 4;
+          be[n] = ld_b16<SMEM>(fr + j / 2);
+          bo[n] = ld_b16<SMEM>(fr + 32 + j / 2);
         }
       }
 #pragma unroll
@@ -193,12 +209,10 @@ __device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8
         const uint32_t ah2 = gs & 0x00F000F0u, ah3 = g8s & 0x00F000F0u;
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
-          if (n < nt) {
-            const uint32_t e0 = jj ? be[n].z : be[n].x, e1 = jj ? be[n].w : be[n].y;
-            const uint32_t o0 = jj ? bo[n].z : bo[n].x, o1 = jj ? bo[n].w : bo[n].y;
-            mma_f16(de[n], al0, al1, al2, al3, e0, e1);
-            mma_f16(dodd[n], ah0, ah1, ah2, ah3, o0, o1);
-          }
+          const uint32_t e0 = jj ? be[n].z : be[n].x, e1 = jj ? be[n].w : be[n].y;
+          const uint32_t o0 = jj ? bo[n].z : bo[n].x, o1 = jj ? bo[n].w : bo[n].y;
+          mma_f16(de[n], al0, al1, al2, al3, e0, e1);
+          mma_f16(dodd[n], ah0, ah1, ah2, ah3, o0, o1);
         }
       }
     }
@@ -207,34 +221,53 @@ __device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8
     q4k_pair_scales(*reinterpret_cast<const uint4*>(rg8), t, dsc[1], dmn[1]);
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
-      if (n < nt) {
-        const float4 mt =
-            __ldg(reinterpret_cast<const float4*>(mx[n] + (size_t)nsb * 1024) + sb * 4 + t);
-        const float2 back = make_float2(mt.x, mt.z), sums = make_float2(-mt.y, -mt.w);
-        // D: [0] row g high, [1] row g low, [2] row g+8 high, [3] row g+8 low
+      const uint4 mw = ld_b16<SMEM>(bs[n].meta + 16 * t);
+      const float4 mt = make_float4(__uint_as_float(mw.x), __uint_as_float(mw.y),
+                                    __uint_as_float(mw.z), __uint_as_float(mw.w));
+      const float2 back = make_float2(mt.x, mt.z), sums = make_float2(-mt.y, -mt.w);
+      // D: [0] row g high, [1] row g low, [2] row g+8 high, [3] row g+8 low
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          float2 s = __fadd2_rn(make_float2(de[n][2 * r], dodd[n][2 * r]),
-                                make_float2(de[n][2 * r + 1], dodd[n][2 * r + 1]));
-          s = __fmul2_rn(s, back);  // sum(q*x) of the even and odd sub-block
-          float2 a = __ffma2_rn(dsc[r], s, y[r][n]);
-          y[r][n] = __ffma2_rn(dmn[r], sums, a);
-        }
+      for (int r = 0; r < 2; ++r) {
+        float2 s = __fadd2_rn(make_float2(de[n][2 * r], dodd[n][2 * r]),
+                              make_float2(de[n][2 * r + 1], dodd[n][2 * r + 1]));
+        s = __fmul2_rn(s, back);  // sum(q*x) of the even and odd sub-block
+        float2 a = __ffma2_rn(dsc[r], s, y[n][r]);
+        y[n][r] = __ffma2_rn(dmn[r], sums, a);
       }
     }
   }
 }
 
+// q4k_sb_mma for nt (1..NT) tokens: the first nt entries of bs and y.
+template <int NT, bool SMEM>
+__device__ __forceinline__ void q4k_sb_mma_n(int nt, const uint8_t* rg, const uint8_t* rg8,
+                                             const BSlice (&bs)[NT], int lane,
+                                             float2 (&y)[NT][2]) {
+  if constexpr (NT == 1) {
+    q4k_sb_mma<1, SMEM>(rg, rg8, bs, lane, y);
+  } else {
+    if (nt >= NT)
+      q4k_sb_mma<NT, SMEM>(rg, rg8, bs, lane, y);
+    else
+      q4k_sb_mma_n<NT - 1, SMEM>(nt, rg, rg8, reinterpret_cast<const BSlice(&)[NT - 1]>(bs),
+                                 lane, reinterpret_cast<float2(&)[NT - 1][2]>(y));
+  }
+}
+
 // q4k_sb_mma over super-blocks [sb0, sb1) of a 16-row tile whose row 0 is
-// `tile`, rows `pitch` bytes apart (pitch % 128 == 16).
+// `tile`, rows `pitch` bytes apart (pitch % 128 == 16), with nt tokens whose
+// prepared activations (global memory) start at mx[n].
 template <int NT>
 __device__ __forceinline__ void q4k_tile_mma(const uint8_t* tile, int pitch, int sb0, int sb1,
                                              const uint8_t* const (&mx)[NT], int nt, int nsb,
-                                             int lane, float2 (&y)[2][NT]) {
+                                             int lane, float2 (&y)[NT][2]) {
   const int g = lane >> 2;
   for (int sb = sb0; sb < sb1; ++sb) {
     const uint8_t* rg = tile + g * pitch + sb * LB_Q4K;
-    q4k_sb_mma<NT>(rg, rg + 8 * pitch, sb, mx, nt, nsb, lane, y);
+    BSlice bs[NT];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) bs[n] = mx_slice(mx[n], sb, nsb);
+    q4k_sb_mma_n<NT, false>(nt, rg, rg + 8 * pitch, bs, lane, y);
   }
 }
 
@@ -243,7 +276,7 @@ __device__ __forceinline__ void q4k_tile_mma(const uint8_t* tile, int pitch, int
 template <int NT, int MATS, int W>
 __device__ __forceinline__ void tile_items(const uint8_t* stage, int pitch, int nsb, int warp,
                                            int lane, const uint8_t* const (&mx)[NT], int nt,
-                                           float2 (&y)[MATS][2][NT]) {
+                                           float2 (&y)[MATS][NT][2]) {
   const int items = MATS * nsb;
   const int i0 = warp * items / W, i1 = (warp + 1) * items / W;
 #pragma unroll
@@ -258,7 +291,7 @@ __device__ __forceinline__ void tile_items(const uint8_t* stage, int pitch, int 
 // Sums y over each quad and stores the row sums into red[warp][mat][row][n].
 template <int NT, int MATS>
 __device__ __forceinline__ void tile_partials_store(float* red, int warp, int lane,
-                                                    const float2 (&y)[MATS][2][NT]) {
+                                                    const float2 (&y)[MATS][NT][2]) {
   float v[MATS][2][NT];
 #pragma unroll
   for (int mat = 0; mat < MATS; ++mat)
@@ -266,7 +299,7 @@ __device__ __forceinline__ void tile_partials_store(float* red, int warp, int la
     for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
-        float s = y[mat][r][n].x + y[mat][r][n].y;
+        float s = y[mat][n][r].x + y[mat][n][r].y;
         s += __shfl_xor_sync(0xffffffffu, s, 1);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         v[mat][r][n] = s;
@@ -295,6 +328,164 @@ __device__ __forceinline__ float tile_row_sum(const float* red, int mat, int r, 
 template <int NT, int MATS, int W>
 __host__ __device__ __forceinline__ int tile_red_floats() {
   return 2 * W * MATS * kTileRows * NT;  // double-buffered
+}
+
+// ------------------------------------------------------------ Q6_K rows
+//
+// A Q6_K sub-block is 16 values, so one m16n8k16 k-step is one sub-block of
+// all 16 rows of a block, and no slot mapping is needed: the B columns are
+// 4 tokens x (high, low) parts (column n = 2*token + part), and lane (g, t)
+// ends the k-step holding the whole sub-block's sums of token t for rows g
+// and g+8 (D columns 2t, 2t+1).  The quant q (0..63) enters as the exact f16
+// subnormal q * 2^-24; the reference's -32 offset is applied with the
+// sub-block sum of x: sum((q-32)*x) = sum(q*x) - 32*sum(x), scaled by
+// delta = d*sc (dot-product-with-q6-k-tensor-data, llambda.lisp L4458-4506).
+//
+// Lane t supplies k = 2t, 2t+1, 2t+8, 2t+9 = values 4t, 4t+2, 4t+1, 4t+3 of
+// the sub-block, i.e. bytes 0, 2, 1, 3 of word t of its 16-byte runs.  The 16
+// k-steps of a super-block run in the order q = (2c + h) * 4 + gg over chunk
+// c, half h and group gg, sub-block s = 8c + 2gg + h (expand-q6-k-group,
+// L4203-4310): value i of sub-block s has its low 4 bits in ql byte
+// 64c + 32(gg%2) + 16h + i (low nibble for gg < 2, high nibble otherwise)
+// and its high 2 bits in qh byte 128 + 32c + 16h + i, bits 2gg and 2gg+1.
+
+// Prepared down-projection input of one entry (token, rank) for Q6_K rows
+// ("m6"), m6_bytes(K) bytes (16-byte aligned), per super-block (1152 bytes):
+//   frag[part][t][q] : uint2, halves (x[4t], x[4t+2]) and (x[4t+1], x[4t+3])
+//       of k-step q's sub-block, scaled, part 0 = high, 1 = low (1024 bytes);
+//   meta[q] : float2 (back, -32 * sum(x)) of k-step q's sub-block (128 bytes).
+__host__ __device__ __forceinline__ size_t m6_bytes(int K) { return (size_t)(K / 256) * 1152; }
+
+__host__ __device__ __forceinline__ int q6_step_of(int s) {
+  return ((s >> 3) * 2 + (s & 1)) * 4 + ((s & 7) >> 1);
+}
+
+// Stores sub-block s_glob of one entry into its m6 buffer: lane (g, 0) holds
+// value g in va and value g + 8 in vb; the other lanes pass zeros.  Whole
+// warp.
+__device__ __forceinline__ void m6_store_subblock(uint8_t* m6, int s_glob, float va, float vb,
+                                                  int lane) {
+  float amax = fmaxf(fabsf(va), fabsf(vb)), sum = va + vb;
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  int ex = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 126;  // as in mx_store4
+  ex = min(max(ex, -100), 100);
+  const float f = pow2f(11 - ex);
+  uint8_t* base = m6 + (size_t)(s_glob >> 4) * 1152;
+  const int q = q6_step_of(s_glob & 15);
+  if ((lane & 3) == 0) {
+    const int g = lane >> 2;
+    __half* h = reinterpret_cast<__half*>(base);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = g + 8 * r;
+      const float xs = (r ? vb : va) * f;
+      const __half hi = __float2half_rn(xs);
+      const __half lo = __float2half_rn(xs - __half2float(hi));
+      const int t4 = i >> 2, pos = i & 3, hp = (pos & 1) * 2 + (pos >> 1);
+      h[((0 * 4 + t4) * 16 + q) * 4 + hp] = hi;
+      h[((1 * 4 + t4) * 16 + q) * 4 + hp] = lo;
+    }
+    if (g == 0)
+      reinterpret_cast<float2*>(base + 1024)[q] = make_float2(pow2f(ex + 13), -32.0f * sum);
+  }
+}
+
+// Zeroes sub-block s_glob of an m6 buffer (padding past the matrix's rows).
+// 16 lanes; lane l < 16 writes 8 bytes of the fragments, lane 0 the meta.
+__device__ __forceinline__ void m6_zero_subblock(uint8_t* m6, int s_glob, int l) {
+  uint8_t* base = m6 + (size_t)(s_glob >> 4) * 1152;
+  const int q = q6_step_of(s_glob & 15);
+  if (l < 8) reinterpret_cast<uint2*>(base)[l * 16 + q] = make_uint2(0, 0);  // (part, t) = l
+  if (l == 0) reinterpret_cast<float2*>(base + 1024)[q] = make_float2(0.f, 0.f);
+}
+
+// int8 byte b of w as a float, exactly (2^23 + 128 + v, minus 2^23 + 128).
+__device__ __forceinline__ float s8_to_float(uint32_t w_xor80, int b) {
+  return __uint_as_float(__byte_perm(w_xor80, 0x4B000000u, 0x7440u | b)) - 8388736.0f;
+}
+
+// Adds token t's (this lane's, t < nt) dot products over super-block sb of a
+// 16-row Q6_K block to y (.x row g, .y row g+8).  rg / rg8: the super-block
+// of rows g and g+8 in shared memory (2-byte aligned); m6[n]: the m6 buffers
+// of the group's tokens (n < nt valid; SMEM: staged in shared memory).
+template <bool SMEM>
+__device__ __forceinline__ void q6k_sb_mma(const uint8_t* rg, const uint8_t* rg8, int sb,
+                                           const uint8_t* const (&m6)[4], int nt, int lane,
+                                           float2& y) {
+  const int g = lane >> 2, t = lane & 3;
+  const int bn = g >> 1, part = g & 1;
+  const bool bval = bn < nt;
+  const uint4* bsrc =
+      reinterpret_cast<const uint4*>(m6[bn] + (size_t)sb * 1152) + (part * 4 + t) * 8;
+  const float4* msrc = reinterpret_cast<const float4*>(m6[t] + (size_t)sb * 1152 + 1024);
+  const float d = half_bits_to_float(lds_u16(rg + 208));
+  const float d8 = half_bits_to_float(lds_u16(rg8 + 208));
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    // 8 scale bytes of chunk c (sub-blocks 8c..8c+7), sign bit flipped
+    const uint32_t sg0 = lds_w32_align2(rg + 192 + 8 * c) ^ 0x80808080u;
+    const uint32_t sg1 = lds_w32_align2(rg + 196 + 8 * c) ^ 0x80808080u;
+    const uint32_t s80 = lds_w32_align2(rg8 + 192 + 8 * c) ^ 0x80808080u;
+    const uint32_t s81 = lds_w32_align2(rg8 + 196 + 8 * c) ^ 0x80808080u;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int o = 64 * c + 16 * h + 4 * t;
+      uint32_t qg[4], q8[4];
+      {
+        const uint32_t A = lds_w32_align2(rg + o), B = lds_w32_align2(rg + o + 32);
+        const uint32_t H = lds_w32_align2(rg + 128 + 32 * c + 16 * h + 4 * t);
+        qg[0] = (A & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
+        qg[1] = (B & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
+        qg[2] = ((A >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
+        qg[3] = ((B >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
+      }
+      {
+        const uint32_t A = lds_w32_align2(rg8 + o), B = lds_w32_align2(rg8 + o + 32);
+        const uint32_t H = lds_w32_align2(rg8 + 128 + 32 * c + 16 * h + 4 * t);
+        q8[0] = (A & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
+        q8[1] = (B & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
+        q8[2] = ((A >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
+        q8[3] = ((B >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
+      }
+      const int q0 = (2 * c + h) * 4;  // first k-step of this (c, h)
+      uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
+      if (bval) {
+        b01 = ld_b16<SMEM>(bsrc + q0 / 2);
+        b23 = ld_b16<SMEM>(bsrc + q0 / 2 + 1);
+      }
+      float4 m01 = make_float4(0.f, 0.f, 0.f, 0.f), m23 = m01;
+      if (t < nt) {
+        const uint4 u01 = ld_b16<SMEM>(msrc + q0 / 2), u23 = ld_b16<SMEM>(msrc + q0 / 2 + 1);
+        m01 = make_float4(__uint_as_float(u01.x), __uint_as_float(u01.y), __uint_as_float(u01.z),
+                          __uint_as_float(u01.w));
+        m23 = make_float4(__uint_as_float(u23.x), __uint_as_float(u23.y), __uint_as_float(u23.z),
+                          __uint_as_float(u23.w));
+      }
+#pragma unroll
+      for (int gg = 0; gg < 4; ++gg) {
+        float dv[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t b0 = gg == 0 ? b01.x : gg == 1 ? b01.z : gg == 2 ? b23.x : b23.z;
+        const uint32_t b1 = gg == 0 ? b01.y : gg == 1 ? b01.w : gg == 2 ? b23.y : b23.w;
+        mma_f16(dv, __byte_perm(qg[gg], 0, 0x4240), __byte_perm(q8[gg], 0, 0x4240),
+                __byte_perm(qg[gg], 0, 0x4341), __byte_perm(q8[gg], 0, 0x4341), b0, b1);
+        const float back = gg == 0 ? m01.x : gg == 1 ? m01.z : gg == 2 ? m23.x : m23.z;
+        const float off = gg == 0 ? m01.y : gg == 1 ? m01.w : gg == 2 ? m23.y : m23.w;
+        // sub-block s = 8c + 2gg + h: scale byte 2gg + h of the chunk's 8
+        const int sbyte = 2 * gg + h;
+        const uint32_t wg = sbyte < 4 ? sg0 : sg1, w8 = sbyte < 4 ? s80 : s81;
+        const float2 dsc = __fmul2_rn(make_float2(d, d8),
+                                      make_float2(s8_to_float(wg, sbyte & 3),
+                                                  s8_to_float(w8, sbyte & 3)));
+        float2 s2 = __fadd2_rn(make_float2(dv[0], dv[2]), make_float2(dv[1], dv[3]));
+        s2 = __ffma2_rn(s2, make_float2(back, back), make_float2(off, off));
+        y = __ffma2_rn(dsc, s2, y);
+      }
+    }
+  }
 }
 
 // ------------------------------------------------------------ tile staging

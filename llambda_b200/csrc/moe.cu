@@ -36,10 +36,24 @@ namespace {
 constexpr int kMaxExperts = 1024;
 constexpr int kSlabMaxStages = 10;
 
+// Bytes of one gate/up slab stage: CW boxes of 16 Q4_K rows x one super-block
+// and NT tokens' activation slices (1024 fragment + 64 meta bytes each).
+__host__ __device__ constexpr int up_stage_bytes(int cw, int nt) {
+  return (cw * 16 * 144 + nt * 1088 + 127) & ~127;
+}
+
 // Floats per token of the prepared gate/up input: room for either layout
 // (Q4_K: the tensor-core layout of mma.cuh; Q6_K: the warp engine's).
 __host__ __device__ __forceinline__ long up_ld_floats(int K) {
   const long a = xp_stride(K), b = (long)(mx_bytes(K) / 4);
+  return a > b ? a : b;
+}
+
+// Floats per entry of the prepared down input: room for the warp engine's
+// layout and for the Q6_K tensor-core layout (m6, mma.cuh).
+__host__ __device__ __forceinline__ long down_ld_floats(const MoeDevice& m) {
+  const int K = m.k_down > m.k_down_sh ? m.k_down : m.k_down_sh;
+  const long a = xp_stride(K), b = (long)(m6_bytes(K) / 4);
   return a > b ? a : b;
 }
 
@@ -63,61 +77,139 @@ __device__ __forceinline__ float relu_sq_ref(float v) {
 // each rank is a warp arg-max (ties to the lower index, as the strict > of
 // select-top-k-logits-into keeps the earlier logit) after which only the
 // winning lane rescans its candidates.
+// Sortable key of a score: a larger float has a larger key.  0 marks what the
+// reference's strict > against most-negative-single-float never selects
+// (NaN, -inf, -most-positive); -0.0 and +0.0 compare equal there, so they
+// share a key.
+__device__ __forceinline__ uint32_t topk_key(float v) {
+  if (!(v > -3.40282347e38f)) return 0u;
+  const uint32_t u = __float_as_uint(v == 0.f ? 0.f : v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// The k best scores of one token, in the order the reference's repeated
+// strict-> scan finds them (descending score, ties to the lower index).  The
+// k-th largest key is found by an 8-bit radix select (four passes of a
+// shared-memory histogram over the keys that match the bytes found so far);
+// every key above it is taken and the ties at it in index order, and the k
+// winners are ranked by (score, index).  PER: candidates per lane (E <= 32*PER).
+template <int PER>
 __global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T) {
+  __shared__ float s_val[32];
+  __shared__ uint32_t s_key[32];
+  __shared__ int s_idx[32];
+  __shared__ int s_hist[256];
   const int t = blockIdx.x, lane = threadIdx.x;
   const int E = m.experts, k = m.top_k;
   const float* L = w.logits + (long)t * (E + 1);
-  const int per = (E + 31) / 32;
-  float lv[32];
-  uint32_t taken = 0;  // bit q: candidate q of this lane is used or absent
+  const unsigned lt_mask = (1u << lane) - 1u;
+  float lv[PER];
+  uint32_t key[PER];
 #pragma unroll
-  for (int q = 0; q < 32; ++q) {
+  for (int q = 0; q < PER; ++q) {
     const int i = lane + 32 * q;
     float v = 0.f;
-    if (q < per && i < E) {
+    uint32_t kq = 0u;
+    if (i < E) {
       v = L[i];
       if (m.router_bias) v = v + m.router_bias[i];
-    } else {
-      taken |= 1u << q;
+      kq = topk_key(v);
     }
     lv[q] = v;
+    key[q] = kq;
   }
-  auto local_best = [&](float& bv, int& bi) {
-    bv = -3.40282347e38f;  // most-negative-single-float: never selected
-    bi = -1;
+  uint32_t th = 0u;  // the k-th largest key (0: fewer than k selectable scores)
+  int krem = k;      // its rank among the keys equal to it
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const uint32_t hi = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
-      if (!((taken >> q) & 1u) && lv[q] > bv) {  // strict: lower index wins ties
-        bv = lv[q];
-        bi = lane + 32 * q;
+    for (int j = 0; j < 8; ++j) s_hist[lane * 8 + j] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < PER; ++q)
+      if (key[q] != 0u && (key[q] & hi) == th) atomicAdd(&s_hist[(key[q] >> shift) & 255], 1);
+    __syncwarp();
+    // lane l holds bins 255-8l .. 248-8l, highest first
+    int c[8], tot = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = s_hist[255 - 8 * lane - j];
+      tot += c[j];
+    }
+    int incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const bool here = incl - tot < krem && incl >= krem;
+    int bin = 0, above = 0;
+    if (here) {
+      int run = incl - tot;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (run + c[j] >= krem) {
+          bin = 255 - 8 * lane - j;
+          above = run;
+          break;
+        }
+        run += c[j];
       }
-  };
-  float bv;
-  int bi;
-  local_best(bv, bi);
-  int my_i = -1;  // lane j keeps rank j's expert and logit
+    }
+    const unsigned hm = __ballot_sync(0xffffffffu, here);
+    __syncwarp();
+    if (hm == 0u) {  // fewer than k selectable scores
+      th = 0u;
+      krem = 0;
+      break;
+    }
+    const int src = __ffs(hm) - 1;
+    th |= (uint32_t)__shfl_sync(0xffffffffu, bin, src) << shift;
+    krem -= __shfl_sync(0xffffffffu, above, src);
+  }
+  const int need = krem;  // ties at th to take, lowest index first
+  int nsel = 0, tie_base = 0;
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const bool eq = th != 0u && key[q] == th;
+    const unsigned eqm = __ballot_sync(0xffffffffu, eq);
+    const bool take = key[q] > th || (eq && tie_base + __popc(eqm & lt_mask) < need);
+    tie_base += __popc(eqm);
+    const unsigned tm = __ballot_sync(0xffffffffu, take);
+    if (take && nsel + __popc(tm & lt_mask) < 32) {
+      const int pos = nsel + __popc(tm & lt_mask);
+      s_val[pos] = lv[q];
+      s_key[pos] = key[q];
+      s_idx[pos] = lane + 32 * q;
+    }
+    nsel += __popc(tm);
+  }
+  nsel = min(nsel, k);
+  __syncwarp();
   float my_v = 0.f;
-  for (int j = 0; j < k; ++j) {
-    float gv = bv;
-    int gi = bi;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, gv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
-      if (oi >= 0 && (gi < 0 || ov > gv || (ov == gv && oi < gi))) {
-        gv = ov;
-        gi = oi;
-      }
-    }
-    if (lane == j) {
-      my_i = gi;
-      my_v = gv;
-    }
-    if (gi >= 0 && (gi & 31) == lane) {
-      taken |= 1u << (gi >> 5);
-      local_best(bv, bi);
-    }
+  int my_i = -1;
+  uint32_t my_k = 0u;
+  if (lane < nsel) {
+    my_v = s_val[lane];
+    my_k = s_key[lane];
+    my_i = s_idx[lane];
   }
+  int rank = 0;
+  for (int j = 0; j < nsel; ++j) {
+    const uint32_t kj = s_key[j];
+    const int ij = s_idx[j];
+    rank += (kj > my_k || (kj == my_k && ij < my_i)) ? 1 : 0;
+  }
+  __syncwarp();
+  if (lane < nsel) {
+    s_val[rank] = my_v;
+    s_idx[rank] = my_i;
+  }
+  __syncwarp();
+  // lane j keeps rank j's expert and score (-1: fewer than k selectable)
+  my_v = lane < nsel ? s_val[lane] : 0.f;
+  my_i = lane < nsel ? s_idx[lane] : -1;
   // sigmoid per rank in parallel; the sum runs in rank order, as in L5367-5372
   float wv = lane < k ? sigmoid_ref(my_v) : 0.f;
   float wsum = 0.f;
@@ -151,9 +243,20 @@ __global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int 
   const int n = T * k;
   if (warp == 0) {
     const unsigned lt_mask = (1u << lane) - 1u;
+    int ev[8];  // selections of the next 8 chunks, loaded ahead of the serial part
     for (int c = 0; c < n; c += 32) {
+      const int u = (c >> 5) & 7;
+      if (u == 0)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int idj = c + 32 * j + lane;
+          ev[j] = idj < n ? w.sel[idj] : -1;
+        }
       const int id = c + lane;
-      int e = id < n ? w.sel[id] : -1;
+      int e = ev[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j)
+        if (j == u) e = ev[j];
       const bool own = e >= m.expert_begin && e < m.expert_end;
       const unsigned act = __ballot_sync(0xffffffffu, own);
       int rank = 0;
@@ -168,38 +271,70 @@ __global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int 
       __syncwarp();
       if (id < n) w.entries[id] = own ? (base + rank) : -1;  // position, fixed below
     }
-    // exclusive scans over experts (entries and token passes), active list in
-    // increasing expert id
-    int run = 0, nact = 0, prun = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) {
+  }
+  __syncthreads();
+  // Exclusive scans over experts (entries, up passes, down passes) and the
+  // active list in increasing expert id: warp wp takes experts
+  // [wp*per_w, (wp+1)*per_w); pass 1 sums each warp's range, pass 2 scans it
+  // from the sum of the ranges before it.
+  {
+    __shared__ int s_tot[8][4];
+    const int nw = blockDim.x >> 5;
+    const int per_w = ((E + nw - 1) / nw + 31) & ~31;
+    const int e_lo = warp * per_w, e_hi = min(E, e_lo + per_w);
+    const unsigned lt_mask = (1u << lane) - 1u;
+    int tot[4] = {0, 0, 0, 0};  // entries, active experts, up passes, down passes
+    for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
       const int e = e0 + lane;
-      const int cnt = e < E ? s_count[e] : 0;
-      const int pc = (cnt + pass_nt - 1) / pass_nt;
-      int incl = cnt, pincl = pc;
+      const int cnt = e < e_hi ? s_count[e] : 0;
+      tot[0] += (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
+      tot[1] += __popc(__ballot_sync(0xffffffffu, cnt > 0));
+      tot[2] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_nt - 1) / pass_nt));
+      tot[3] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + 3) / 4));
+    }
+    if (lane < 4) s_tot[warp][lane] = tot[lane];
+    __syncthreads();
+    int run = 0, nact = 0, prun = 0, drun = 0;
+    for (int q = 0; q < warp; ++q) {
+      run += s_tot[q][0];
+      nact += s_tot[q][1];
+      prun += s_tot[q][2];
+      drun += s_tot[q][3];
+    }
+    for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
+      const int e = e0 + lane;
+      const int cnt = e < e_hi ? s_count[e] : 0;
+      const int pc = (cnt + pass_nt - 1) / pass_nt, dc = (cnt + 3) / 4;
+      int incl = cnt, pincl = pc, dincl = dc;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         const int pv = __shfl_up_sync(0xffffffffu, pincl, o);
+        const int dv = __shfl_up_sync(0xffffffffu, dincl, o);
         if (lane >= o) {
           incl += v;
           pincl += pv;
+          dincl += dv;
         }
       }
-      if (e < E) s_offset[e] = run + incl - cnt;
+      if (e < e_hi) s_offset[e] = run + incl - cnt;
       const unsigned nz = __ballot_sync(0xffffffffu, cnt > 0);
       if (cnt > 0) {
         const int a = nact + __popc(nz & lt_mask);
         w.active[a] = e;
         w.pass_off[a] = prun + pincl - pc;
+        w.pass_off_dn[a] = drun + dincl - dc;
       }
       nact += __popc(nz);
       run += __shfl_sync(0xffffffffu, incl, 31);
       prun += __shfl_sync(0xffffffffu, pincl, 31);
+      drun += __shfl_sync(0xffffffffu, dincl, 31);
     }
-    if (lane == 0) {
+    if (warp == nw - 1 && lane == 0) {
       s_offset[E] = run;
       w.active[E] = nact;
       w.pass_off[nact] = prun;
+      w.pass_off_dn[nact] = drun;
     }
   }
   __syncthreads();
@@ -225,13 +360,50 @@ __global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int 
 template <int UT>
 __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
                                                        const float* __restrict__ x) {
+  constexpr int kCached = 8;  // chunks of 1024 values kept in registers (K <= 8192)
   __shared__ float s_part[8];
   const int H = m.hidden, K = m.k_in, tasks = K >> 6;
   const float* xt = x + (long)blockIdx.x * H;
+  const int nchunk = (K + 1023) >> 10;
+  if (threadIdx.x == 0) {  // the router GEMV that follows finds its weights in L2
+    const int rows = m.experts + (m.arch == 0 && !m.router_extra_row ? 1 : 0);
+    const size_t bytes = (size_t)rows * H * sizeof(float);
+    const size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
+    const size_t lo = (size_t)blockIdx.x * per;
+    if (lo < bytes && (reinterpret_cast<uintptr_t>(m.router) & 15) == 0)
+      prefetch_l2(reinterpret_cast<const uint8_t*>(m.router) + lo,
+                  (uint32_t)(std::min(per, bytes - lo) & ~size_t(15)));
+  }
+  const bool vec = (H & 3) == 0 && (reinterpret_cast<uintptr_t>(xt) & 15) == 0;
+  auto load4 = [&](int e) {  // x[e..e+3], zero past H
+    if (vec && e + 3 < H) return __ldg(reinterpret_cast<const float4*>(xt + e));
+    float4 r;
+    r.x = e < H ? xt[e] : 0.f;
+    r.y = e + 1 < H ? xt[e + 1] : 0.f;
+    r.z = e + 2 < H ? xt[e + 2] : 0.f;
+    r.w = e + 3 < H ? xt[e + 3] : 0.f;
+    return r;
+  };
+  // one read of x: every chunk's four values are loaded before the reduction
+  float4 v[kCached];
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < kCached; ++c) {
+    v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < nchunk) {
+      v[c] = load4(c * 1024 + 4 * threadIdx.x);
+      acc = fmaf(v[c].x, v[c].x, acc);
+      acc = fmaf(v[c].y, v[c].y, acc);
+      acc = fmaf(v[c].z, v[c].z, acc);
+      acc = fmaf(v[c].w, v[c].w, acc);
+    }
+  }
+  for (int c = kCached; c < nchunk; ++c) {
+    const float4 u = load4(c * 1024 + 4 * threadIdx.x);
+    acc = fmaf(u.x, u.x, fmaf(u.y, u.y, fmaf(u.z, u.z, fmaf(u.w, u.w, acc))));
+  }
   float scale = 1.f;
-  if (m.input_norm) {
-    float acc = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) acc = fmaf(xt[i], xt[i], acc);
+  if (m.input_norm) {  // rms-norm-into, llambda.lisp L859-879
     acc = warp_sum(acc);
     if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
     __syncthreads();
@@ -243,29 +415,31 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
   }
   float* xn = w.xn + (long)blockIdx.x * H;
   float* xp = w.xp_up + (long)blockIdx.x * up_ld_floats(K);
-  for (int base = 0; base < K; base += 4 * blockDim.x) {
-    const int e = base + 4 * threadIdx.x;
-    float v[4];
+  auto emit = [&](int e, float4 u) {
+    float val[4] = {u.x, u.y, u.z, u.w};
+    if (m.input_norm) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int i = e + q;
-      float val = 0.f;
-      if (i < H) {
-        val = xt[i];
-        if (m.input_norm) {
-          val = __fmul_rn(__fmul_rn(val, m.input_norm[i]), scale);
-          xn[i] = val;
+      for (int q = 0; q < 4; ++q)
+        if (e + q < H) {
+          val[q] = __fmul_rn(__fmul_rn(val[q], m.input_norm[e + q]), scale);
+          xn[e + q] = val[q];
         }
-      }
-      v[q] = val;
     }
-    if (e < K) {  // K is a multiple of 256, so whole warps agree here
-      if (UT == LB_TYPE_Q4_K)  // tensor-core layout (mma.cuh)
-        mx_store4(reinterpret_cast<uint8_t*>(xp), K, e, make_float4(v[0], v[1], v[2], v[3]));
-      else
-        *reinterpret_cast<float4*>(xp + xp_index<UT>(e, tasks)) =
-            make_float4(v[0], v[1], v[2], v[3]);
-    }
+    const float4 o = make_float4(val[0], val[1], val[2], val[3]);
+    if (UT == LB_TYPE_Q4_K)  // tensor-core layout (mma.cuh)
+      mx_store4(reinterpret_cast<uint8_t*>(xp), K, e, o);
+    else
+      *reinterpret_cast<float4*>(xp + xp_index<UT>(e, tasks)) = o;
+  };
+  // K is a multiple of 256 and blockDim 256, so whole warps agree on e < K
+#pragma unroll
+  for (int c = 0; c < kCached; ++c) {
+    const int e = c * 1024 + 4 * threadIdx.x;
+    if (c < nchunk && e < K) emit(e, v[c]);
+  }
+  for (int c = kCached; c < nchunk; ++c) {
+    const int e = c * 1024 + 4 * threadIdx.x;
+    if (e < K) emit(e, load4(e));
   }
 }
 
@@ -311,7 +485,7 @@ __global__ void __launch_bounds__(128) moe_up_kernel(MoeDevice m, MoeWork w, int
   const int kd = shared_pass ? m.k_down_sh : m.k_down;
   const int tasks_d = kd >> 6;
   const long ld_up = up_ld_floats(m.k_in);
-  const long ld_dn = xp_stride(max(m.k_down, m.k_down_sh));
+  const long ld_dn = down_ld_floats(m);
   const size_t grb = shared_pass ? m.gate_sh_rb : m.gate_rb;
   const size_t urb = shared_pass ? m.up_sh_rb : m.up_rb;
   const int gw = blockIdx.x * nwarps + warp, total = gridDim.x * nwarps;
@@ -422,7 +596,7 @@ struct SlabSync {
   int pad[3];
 };
 
-template <int NT, bool PAIR, int DT, int CW>
+template <int NT, bool PAIR, int DT, bool M6, int CW>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_up_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, long map_row_base,
                        const __grid_constant__ CUtensorMap tm_gate,
@@ -433,7 +607,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   constexpr int RBM = CW / MATS;       // row blocks per matrix
   constexpr int RU = RBM * kTileRows;  // rows per matrix per slab
   constexpr int BOX = kTileRows * LB_Q4K;
-  constexpr int STAGE = CW * BOX;
+  constexpr int STAGE_W = CW * BOX;  // weights; then NT activation slices of 1088 bytes
+  constexpr int STAGE = up_stage_bytes(CW, NT);
   extern __shared__ __align__(128) uint8_t smem[];
   SlabSync* sync = reinterpret_cast<SlabSync*>(smem + (size_t)stages * STAGE);
   float* xch = reinterpret_cast<float*>(sync + 1);  // [2][RU][NT] up-row sums
@@ -505,6 +680,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     return x;
   };
 
+  const long ld_up = up_ld_floats(m.k_in);
   if (warp == CW) {  // ---------------- producer
     if (lane == 0) {
       int q = 0;
@@ -519,7 +695,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
               ok = false;
               break;
             }
-            mbar_expect_tx(&sync->full[s], STAGE);
+            const int nt = min(NT, x.t_end - t0);
+            mbar_expect_tx(&sync->full[s], STAGE_W + nt * 1088);
             uint8_t* st = smem + (size_t)s * STAGE;
 #pragma unroll
             for (int b = 0; b < CW; ++b) {
@@ -527,6 +704,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
               const CUtensorMap* tm = x.shared ? (gate ? &tm_gate_sh : &tm_up_sh)
                                                : (gate ? &tm_gate : &tm_up);
               tma_load_2d(st + b * BOX, tm, sb * LB_Q4K, (int)(x.map_row + (b % RBM) * kTileRows),
+                          &sync->full[s]);
+            }
+            // the pass's tokens' activation slices for this super-block
+            for (int n = 0; n < nt; ++n) {
+              const int tok = x.shared ? t0 + n : view.list[t0 + n] / k;
+              const uint8_t* mx = reinterpret_cast<const uint8_t*>(w.xp_up + tok * ld_up);
+              tma_load_1d(st + STAGE_W + n * 1088, mx + (size_t)sb * 1024, 1024, &sync->full[s]);
+              tma_load_1d(st + STAGE_W + n * 1088 + 1024, mx + (size_t)nsb * 1024 + sb * 64, 64,
                           &sync->full[s]);
             }
           }
@@ -542,8 +727,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   // ---------------- consumers
   const int mat = warp / RBM, rb = warp % RBM;
   const int g = lane >> 2, t = lane & 3;
-  const long ld_up = up_ld_floats(m.k_in);
-  const long ld_dn = xp_stride(max(m.k_down, m.k_down_sh));
+  const long ld_dn = down_ld_floats(m);
   int q = 0, pass = 0;
   bool ok = true;
   for (int i = 0; i < n_my && ok; ++i) {
@@ -552,27 +736,29 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     for (int t0 = x.t_begin; t0 < x.t_end && ok; t0 += NT, ++pass) {
       const int nt = min(NT, x.t_end - t0);
       int ids[NT];
-      const uint8_t* mxp[NT];
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         const int tt = min(t0 + n, x.t_end - 1);
         ids[n] = x.shared ? T * k + tt : view.list[tt];
-        const int tok = x.shared ? tt : ids[n] / k;
-        mxp[n] = reinterpret_cast<const uint8_t*>(w.xp_up + tok * ld_up);
       }
-      float2 acc[2][NT];
+      float2 acc[NT][2];
 #pragma unroll
-      for (int r = 0; r < 2; ++r)
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int n = 0; n < NT; ++n) acc[r][n] = make_float2(0.f, 0.f);
+        for (int r = 0; r < 2; ++r) acc[n][r] = make_float2(0.f, 0.f);
       for (int sb = 0; sb < nsb; ++sb, ++q) {
         const int s = q % stages;
         if (!mbar_wait_or_abort(&sync->full[s], (q / stages) & 1, w.status, abort)) {
           ok = false;
           break;
         }
-        const uint8_t* blk = smem + (size_t)s * STAGE + warp * BOX;
-        q4k_sb_mma<NT>(blk + g * LB_Q4K, blk + (g + 8) * LB_Q4K, sb, mxp, nt, nsb, lane, acc);
+        const uint8_t* st = smem + (size_t)s * STAGE;
+        const uint8_t* blk = st + warp * BOX;
+        BSlice bs[NT];
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+          bs[n] = BSlice{st + STAGE_W + n * 1088, st + STAGE_W + n * 1088 + 1024};
+        q4k_sb_mma_n<NT, true>(nt, blk + g * LB_Q4K, blk + (g + 8) * LB_Q4K, bs, lane, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sync->empty[s]);
       }
@@ -583,24 +769,24 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       for (int r = 0; r < 2; ++r)
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
-          float s = acc[r][n].x + acc[r][n].y;
+          float s = acc[n][r].x + acc[n][r].y;
           s += __shfl_xor_sync(0xffffffffu, s, 1);
           s += __shfl_xor_sync(0xffffffffu, s, 2);
           v[r][n] = s;
         }
       const int par = pass & 1, use = pass >> 1;
       float* xb = xch + (size_t)par * RU * NT;
-      auto store_h = [&](float up_or_h, int r, int n, bool gated, float gate) {
-        const int row = x.row0 + rb * kTileRows + g + 8 * r;
-        if (row < x.rows_e && n < nt) {
-          const float hv = gated ? __fmul_rn(silu_ref(gate), up_or_h) : relu_sq_ref(up_or_h);
-          int id = ids[0];
+      auto id_of = [&](int nn) {  // ids[nn] without indexing registers dynamically
+        int id = ids[0];
 #pragma unroll
-          for (int n2 = 1; n2 < NT; ++n2)
-            if (n2 == n) id = ids[n2];
-          w.xp_down[(long)id * ld_dn + xp_index<DT>(row, tasks_d)] = hv;
-        }
+        for (int n2 = 1; n2 < NT; ++n2)
+          if (n2 == nn) id = ids[n2];
+        return id;
       };
+      // h = silu(gate) * up or relu(up)^2 of rows g, g+8 (zero past rows_e),
+      // on lane t == 0 of each quad; zero elsewhere
+      float hv[2][NT];
+      bool writer = !PAIR;
       if (PAIR && mat == 1) {  // up warps: hand the sums to the gate warps
         if (use > 0 && !mbar_wait_or_abort(&sync->xempty[par], (use - 1) & 1, w.status, abort)) {
           ok = false;
@@ -618,31 +804,240 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
           ok = false;
           break;
         }
-        if (t == 0)
-#pragma unroll
-          for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-              store_h(xb[(rb * kTileRows + g + 8 * r) * NT + n], r, n, true, v[r][n]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sync->xempty[par]);
-      } else if (t == 0) {  // up only: relu(up)^2
 #pragma unroll
         for (int r = 0; r < 2; ++r)
 #pragma unroll
-          for (int n = 0; n < NT; ++n) store_h(v[r][n], r, n, false, 0.f);
+          for (int n = 0; n < NT; ++n) {
+            const int row = x.row0 + rb * kTileRows + g + 8 * r;
+            hv[r][n] = (t == 0 && row < x.rows_e && n < nt)
+                           ? __fmul_rn(silu_ref(v[r][n]), xb[(rb * kTileRows + g + 8 * r) * NT + n])
+                           : 0.f;
+          }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sync->xempty[par]);
+        writer = true;
       }
-      if (warp == 0 && x.row0 + RU >= x.rows_e) {  // last slab: zero the padding up to kd
-        const int pad = kd - x.rows_e;
-        for (int qq = lane; qq < nt * pad; qq += 32) {
-          const int nn = qq / pad, pe = x.rows_e + (qq - nn * pad);
-          int id = ids[0];
+      if (!PAIR) {  // up only: relu(up)^2
 #pragma unroll
-          for (int n2 = 1; n2 < NT; ++n2)
-            if (n2 == nn) id = ids[n2];
-          w.xp_down[(long)id * ld_dn + xp_index<DT>(pe, tasks_d)] = 0.f;
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            const int row = x.row0 + rb * kTileRows + g + 8 * r;
+            hv[r][n] = (t == 0 && row < x.rows_e && n < nt) ? relu_sq_ref(v[r][n]) : 0.f;
+          }
+      }
+      if (writer) {
+        if (M6) {  // the block's 16 rows are one Q6_K sub-block of the down input
+          const int s_glob = (x.row0 + rb * kTileRows) >> 4;
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+            if (n < nt)
+              m6_store_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(n) * ld_dn),
+                                s_glob, hv[0][n], hv[1][n], lane);
+        } else if (t == 0) {
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const int row = x.row0 + rb * kTileRows + g + 8 * r;
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+              if (row < x.rows_e && n < nt)
+                w.xp_down[(long)id_of(n) * ld_dn + xp_index<DT>(row, tasks_d)] = hv[r][n];
+          }
         }
       }
+      if (warp == 0 && x.row0 + RU >= x.rows_e) {  // last slab: zero the padding up to kd
+        if (M6) {  // sub-blocks past the slab (the slab's own are written above)
+          const int s_from = (x.row0 + RU) >> 4, s_to = kd >> 4;
+          for (int qq = lane >> 4; qq < nt * (s_to - s_from); qq += 2) {
+            const int nn = qq / (s_to - s_from), sg = s_from + (qq - nn * (s_to - s_from));
+            m6_zero_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(nn) * ld_dn), sg,
+                             lane & 15);
+          }
+        } else {
+          const int pad = kd - x.rows_e;
+          for (int qq = lane; qq < nt * pad; qq += 32) {
+            const int nn = qq / pad, pe = x.rows_e + (qq - nn * pad);
+            w.xp_down[(long)id_of(nn) * ld_dn + xp_index<DT>(pe, tasks_d)] = 0.f;
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- down (slabs)
+// Q6_K down rows on the tensor cores (mma.cuh, Q6_K rows): a work item is a
+// slab of RU = 16 * CW / KSPLIT rows of one routed expert's down matrix (or
+// the shared expert's) for one pass of up to 4 entries.  A stage holds the
+// slab's 16-row blocks whole (16 rows x row bytes is a multiple of 16 bytes,
+// so each block is one aligned 1-D bulk copy); consumer warp w takes block
+// w / KSPLIT and super-blocks part w % KSPLIT of K.  With KSPLIT > 1 the
+// other parts' sums reach the part-0 warp through shared memory, guarded by
+// a per-stage barrier.  Lane (g, t) ends with rows g, g+8 of its block for
+// the pass's entry t and writes them to `partial`.
+struct DownSync {
+  uint64_t full[kSlabMaxStages];
+  uint64_t empty[kSlabMaxStages];
+  uint64_t red[kSlabMaxStages];
+  int abort;
+  int pad[3];
+};
+
+// SB: the pass's entries' prepared inputs are staged with the weights (at
+// stage_w, m6_bytes(K) each) instead of being read through L1.
+template <int KSPLIT, int CW, bool SB>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
+    moe_down_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, int stage_bytes,
+                         int stage_w, int shared_pass) {
+  constexpr int NB = CW / KSPLIT;  // 16-row blocks per slab
+  constexpr int RU = NB * kTileRows;
+  constexpr int NT = 4;
+  extern __shared__ __align__(128) uint8_t smem[];
+  DownSync* sync = reinterpret_cast<DownSync*>(smem + (size_t)stages * stage_bytes);
+  float2* red = reinterpret_cast<float2*>(sync + 1);  // [stages][CW][32]
+  volatile int* abort = &sync->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&sync->full[s], 1);
+      mbar_init(&sync->empty[s], CW);
+      mbar_init(&sync->red[s], CW - NB);
+    }
+    sync->abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int k = m.top_k, H = m.hidden;
+  const int per = (H + RU - 1) / RU;
+  const int passes_s = (T + NT - 1) / NT;
+  const int nact = w.active[m.experts];
+  const int n_routed = shared_pass ? 0 : w.pass_off_dn[nact] * per;
+  const int n_shared = (shared_pass && m.shared_here && m.inter_sh) ? per * passes_s : 0;
+  const int units = n_routed + n_shared;
+  const int u0 = (int)((long)blockIdx.x * units / gridDim.x);
+  const int n_my = (int)((long)(blockIdx.x + 1) * units / gridDim.x) - u0;
+  const int K = shared_pass ? m.k_down_sh : m.k_down;
+  const int nsb = K >> 8;
+  const size_t rb = shared_pass ? m.down_sh_rb : m.down_rb;
+  const long ld_dn = down_ld_floats(m);
+
+  struct Unit {
+    int row0, t_begin, t_end;
+    const uint8_t* src;  // row row0 of the slab in global memory
+  };
+  ExpertView view;
+  int a_hint = 0;
+  auto unit_at = [&](int u) {
+    Unit x;
+    if (!shared_pass) {
+      int a = a_hint;
+      if (w.pass_off_dn[a] * per > u) a = 0;
+      int hi = nact;
+      while (hi - a > 1) {
+        const int mid = (a + hi) >> 1;
+        if (w.pass_off_dn[mid] * per <= u) a = mid; else hi = mid;
+      }
+      a_hint = a;
+      view_expert(m, w, T, a, view);
+      const int np = w.pass_off_dn[a + 1] - w.pass_off_dn[a];
+      const int local = u - w.pass_off_dn[a] * per, slab = local / np, p = local - slab * np;
+      x.row0 = slab * RU;
+      x.t_begin = p * NT;
+      x.t_end = min(view.ntok, x.t_begin + NT);
+      x.src = m.down_exps + ((size_t)view.e * H + x.row0) * rb;
+    } else {
+      const int slab = u / passes_s, p = u - slab * passes_s;
+      x.row0 = slab * RU;
+      x.t_begin = p * NT;
+      x.t_end = min(T, x.t_begin + NT);
+      x.src = m.down_sh + (size_t)x.row0 * rb;
+    }
+    return x;
+  };
+
+  if (warp == CW) {  // ---------------- producer
+    if (lane == 0) {
+      int q = 0;
+      for (int i = 0; i < n_my; ++i, ++q) {
+        const Unit x = unit_at(u0 + i);
+        const int s = q % stages;
+        if (q >= stages &&
+            !mbar_wait_or_abort(&sync->empty[s], ((q / stages) - 1) & 1, w.status, abort))
+          break;
+        const int nblk = min(NB, (H - x.row0) / kTileRows);  // H % 16 == 0
+        const int nt = x.t_end - x.t_begin;
+        const uint32_t m6b = (uint32_t)m6_bytes(K);
+        mbar_expect_tx(&sync->full[s], (uint32_t)(nblk * kTileRows * rb) + (SB ? nt * m6b : 0u));
+        uint8_t* st = smem + (size_t)s * stage_bytes;
+        for (int b = 0; b < nblk; ++b)
+          tma_load_1d(st + (size_t)b * kTileRows * rb, x.src + (size_t)b * kTileRows * rb,
+                      (uint32_t)(kTileRows * rb), &sync->full[s]);
+        if (SB)
+          for (int n = 0; n < nt; ++n) {
+            const int id = shared_pass ? T * k + x.t_begin + n : view.list[x.t_begin + n];
+            tma_load_1d(st + stage_w + n * m6b, w.xp_down + id * ld_dn, m6b, &sync->full[s]);
+          }
+      }
+      for (int r = max(0, q - stages); r < q; ++r)
+        mbar_wait(&sync->full[r % stages], (r / stages) & 1, nullptr);
+    }
+    return;
+  }
+
+  // ---------------- consumers
+  const int b = warp / KSPLIT, kp = warp % KSPLIT;
+  const int sb0 = kp * nsb / KSPLIT, sb1 = (kp + 1) * nsb / KSPLIT;
+  const int g = lane >> 2, t = lane & 3;
+  for (int i = 0, q = 0; i < n_my; ++i, ++q) {
+    const Unit x = unit_at(u0 + i);
+    const int s = q % stages;
+    if (!mbar_wait_or_abort(&sync->full[s], (q / stages) & 1, w.status, abort)) break;
+    const int nt = x.t_end - x.t_begin;
+    const int row_blk = x.row0 + b * kTileRows;
+    int ids[NT];
+    const uint8_t* m6[NT];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int tt = x.t_begin + min(n, nt - 1);
+      ids[n] = shared_pass ? T * k + tt : view.list[tt];
+      m6[n] = SB ? smem + (size_t)s * stage_bytes + stage_w + min(n, nt - 1) * m6_bytes(K)
+                 : reinterpret_cast<const uint8_t*>(w.xp_down + ids[n] * ld_dn);
+    }
+    float2 y = make_float2(0.f, 0.f);
+    if (row_blk < H) {
+      const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
+      for (int sb = sb0; sb < sb1; ++sb)
+        q6k_sb_mma<SB>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, m6, nt,
+                       lane, y);
+    }
+    if (KSPLIT > 1) {
+      float2* rs = red + ((size_t)s * CW) * 32;
+      if (kp != 0) {
+        rs[warp * 32 + lane] = y;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sync->red[s]);
+      } else {
+        if (!mbar_wait_or_abort(&sync->red[s], (q / stages) & 1, w.status, abort)) break;
+#pragma unroll
+        for (int p = 1; p < KSPLIT; ++p) {
+          const float2 o = rs[(warp + p) * 32 + lane];
+          y.x += o.x;
+          y.y += o.y;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sync->empty[s]);
+    if (kp == 0 && row_blk < H && t < nt) {
+      int id = ids[0];
+#pragma unroll
+      for (int n2 = 1; n2 < NT; ++n2)
+        if (n2 == t) id = ids[n2];
+      const int tok = shared_pass ? x.t_begin + t : id / k;
+      const int slot = shared_pass ? k : id - tok * k;
+      float* out = w.partial + ((long)tok * (k + 1) + slot) * H + row_blk;
+      out[g] = y.x;
+      out[g + 8] = y.y;
     }
   }
 }
@@ -650,7 +1045,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
 // Q4_K down inputs need sub-block sums; Q6_K inputs do not.
 __global__ void moe_down_sums_kernel(MoeDevice m, MoeWork w, int T) {
   const int k = m.top_k;
-  const long ld_dn = xp_stride(max(m.k_down, m.k_down_sh));
+  const long ld_dn = down_ld_floats(m);
   const int n_entries = T * k + T;
   for (int id = blockIdx.x; id < n_entries; id += gridDim.x) {
     const bool shared = id >= T * k;
@@ -692,7 +1087,7 @@ __global__ void __launch_bounds__(128) moe_down_kernel(MoeDevice m, MoeWork w, i
                         : w.active[m.experts] * per;
   const int K = shared_pass ? m.k_down_sh : m.k_down;
   const int tasks = K >> 6;
-  const long ld_dn = xp_stride(max(m.k_down, m.k_down_sh));
+  const long ld_dn = down_ld_floats(m);
   const size_t rb = shared_pass ? m.down_sh_rb : m.down_rb;
   const int gw = blockIdx.x * nwarps + warp, total = gridDim.x * nwarps;
   const int chunk = (units + total - 1) / total;
@@ -758,24 +1153,51 @@ __global__ void __launch_bounds__(128) moe_down_kernel(MoeDevice m, MoeWork w, i
 }
 
 // ---------------------------------------------------------------- combine
+// VEC: four hidden values per thread (H % 4 == 0, x / out 16-byte aligned).
+template <bool VEC>
 __global__ void combine_kernel(MoeDevice m, MoeWork w, int T, const float* x, float* out) {
-  const int H = m.hidden, k = m.top_k;
-  const long n = (long)T * H;
+  constexpr int V = VEC ? 4 : 1;
+  const int H = m.hidden, k = m.top_k, HV = H / V;
+  const long n = (long)T * HV;
+  const bool shared = m.shared_here && m.inter_sh;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const int t = (int)(i / H), h = (int)(i - (long)t * H);
+    const int t = (int)(i / HV), h = (int)(i - (long)t * HV) * V;
     const float* p = w.partial + (long)t * (k + 1) * H + h;
-    float acc = 0.f;
+    float acc[V];
+#pragma unroll
+    for (int c = 0; c < V; ++c) acc[c] = 0.f;
+#pragma unroll 4
     for (int j = 0; j < k; ++j) {
       const int e = w.sel[t * k + j];
-      if (e >= m.expert_begin && e < m.expert_end)
-        acc = __fadd_rn(acc, __fmul_rn(w.wts[t * k + j], p[(long)j * H]));
+      const float wt = w.wts[t * k + j];
+      float pv[V];  // loaded unconditionally (a valid address), so all loads go out at once
+      if (VEC) {
+        const float4 q = *reinterpret_cast<const float4*>(p + (long)j * H);
+        pv[0] = q.x;
+        pv[V > 1 ? 1 : 0] = q.y;
+        pv[V > 2 ? 2 : 0] = q.z;
+        pv[V > 3 ? 3 : 0] = q.w;
+      } else {
+        pv[0] = p[(long)j * H];
+      }
+      // experts of other devices add +0.0, which leaves a sum that starts at
+      // +0.0 unchanged (it can never be -0.0)
+      const bool own = e >= m.expert_begin && e < m.expert_end;
+#pragma unroll
+      for (int c = 0; c < V; ++c) acc[c] = __fadd_rn(acc[c], own ? __fmul_rn(wt, pv[c]) : 0.f);
     }
-    if (m.shared_here && m.inter_sh) {
-      const float s = p[(long)k * H];
-      acc = (m.arch == 0) ? __fadd_rn(acc, __fmul_rn(w.shw[t], s)) : __fadd_rn(acc, s);
+    if (shared) {
+      const float sw = m.arch == 0 ? w.shw[t] : 1.0f;
+#pragma unroll
+      for (int c = 0; c < V; ++c) {
+        const float sv = p[(long)k * H + c];
+        acc[c] = m.arch == 0 ? __fadd_rn(acc[c], __fmul_rn(sw, sv)) : __fadd_rn(acc[c], sv);
+      }
     }
     // vector-add-into x x ffn-output (L5746) when the layer carries the residual
-    out[i] = m.add_residual ? __fadd_rn(x[i], acc) : acc;
+    const long o = (long)t * H + h;
+#pragma unroll
+    for (int c = 0; c < V; ++c) out[o + c] = m.add_residual ? __fadd_rn(x[o + c], acc[c]) : acc[c];
   }
 }
 
@@ -854,12 +1276,12 @@ struct SlabMaps {
   long row_base;  // global row (expert_begin * inter) of the routed maps' row 0
 };
 
-template <int NT, bool PAIR, int DT, int CW>
-cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
+template <int NT, bool PAIR, int DT, bool M6, int CW>
+cudaError_t launch_up_slab_cw(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
                               cudaStream_t s) {
-  auto kern = moe_up_slab_kernel<NT, PAIR, DT, CW>;
+  auto kern = moe_up_slab_kernel<NT, PAIR, DT, M6, CW>;
   constexpr int RU = CW / (PAIR ? 2 : 1) * kTileRows;
-  const size_t stage = (size_t)CW * kTileRows * LB_Q4K;
+  const size_t stage = up_stage_bytes(CW, NT);
   const size_t extra = sizeof(SlabSync) + (size_t)2 * RU * NT * 4;
   const int stages = (int)std::min<size_t>(kSlabMaxStages, (kTileSmemBudget - extra) / stage);
   if (stages < 2) return cudaErrorInvalidValue;
@@ -868,6 +1290,80 @@ cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const
   kern<<<sm_count(), (CW + 1) * 32, smem, s>>>(m, w, T, stages, mp.row_base, mp.gate,
                                                 mp.up, mp.gate_sh, mp.up_sh);
   return cudaGetLastError();
+}
+
+// Shape of the Q6_K down slabs for rows of rb bytes: the most 16-row blocks
+// (8, 4, 2 or 1) whose stage fits 56 KiB, K split over 16 / blocks warps.
+struct DownPlan {
+  int nb, stages, stage_bytes, stage_w;
+  bool staged;  // entries' inputs staged with the weights
+};
+constexpr int kDownWarps = 16;
+
+bool down_plan(size_t rb, int K, DownPlan* p) {
+  const size_t block = (size_t)kTileRows * rb;
+  int nb = 8;
+  while (nb > 1 && nb * block > 56 * 1024) nb >>= 1;
+  p->nb = nb;
+  p->stage_w = (int)((nb * block + 127) & ~size_t(127));
+  p->staged = 4 * m6_bytes(K) <= 24 * 1024;
+  p->stage_bytes = p->stage_w + (p->staged ? (int)(4 * m6_bytes(K)) : 0);
+  const size_t per_stage = (size_t)p->stage_bytes + (size_t)kDownWarps * 32 * sizeof(float2);
+  p->stages = (int)std::min<size_t>(kSlabMaxStages, (kTileSmemBudget - sizeof(DownSync)) / per_stage);
+  return p->stages >= 2;
+}
+
+// The down input is written in the m6 layout and the down pass runs on the
+// Q6_K tensor-core slabs when the gate/up pass is the tensor-core one, the
+// down rows are Q6_K, the hidden size is a multiple of 16 and the slabs fit.
+bool down_uses_m6(const MoeDevice& m) {
+  DownPlan p;
+  if (m.up_type != LB_TYPE_Q4_K || m.down_type != LB_TYPE_Q6_K || m.hidden % kTileRows) return false;
+  if (!down_plan(m.down_rb, m.k_down, &p)) return false;
+  return !(m.shared_here && m.inter_sh) || down_plan(m.down_sh_rb, m.k_down_sh, &p);
+}
+
+template <int KSPLIT, bool SB>
+cudaError_t launch_down_slab_k(const MoeDevice& m, const MoeWork& w, int T, int shared_pass,
+                               const DownPlan& p, cudaStream_t s) {
+  auto kern = moe_down_slab_kernel<KSPLIT, kDownWarps, SB>;
+  const size_t smem = (size_t)p.stages * p.stage_bytes + sizeof(DownSync) +
+                      (size_t)p.stages * kDownWarps * 32 * sizeof(float2);
+  if (prepared_occupancy(kern, (kDownWarps + 1) * 32, smem) < 1) return cudaErrorUnknown;
+  kern<<<sm_count(), (kDownWarps + 1) * 32, smem, s>>>(m, w, T, p.stages, p.stage_bytes,
+                                                        p.stage_w, shared_pass);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_down_slab(const MoeDevice& m, const MoeWork& w, int T, int shared_pass,
+                             cudaStream_t s) {
+  DownPlan p;
+  if (!down_plan(shared_pass ? m.down_sh_rb : m.down_rb, shared_pass ? m.k_down_sh : m.k_down,
+                 &p))
+    return cudaErrorInvalidValue;
+#define LB_DOWN_SLAB(KS)                                                                \
+  return p.staged ? launch_down_slab_k<KS, true>(m, w, T, shared_pass, p, s)              \
+                  : launch_down_slab_k<KS, false>(m, w, T, shared_pass, p, s);
+  switch (kDownWarps / p.nb) {
+    case 2: LB_DOWN_SLAB(2)
+    case 4: LB_DOWN_SLAB(4)
+    case 8: LB_DOWN_SLAB(8)
+    default: LB_DOWN_SLAB(16)
+  }
+#undef LB_DOWN_SLAB
+}
+
+template <int NT, int DT>
+cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
+                              cudaStream_t s) {
+  // 16 consumer warps where their registers fit (120 each), else 8
+  constexpr int CW = NT <= 2 ? 16 : 8;
+  const bool pair = m.arch == 0;
+  if (DT == LB_TYPE_Q6_K && down_uses_m6(m))
+    return pair ? launch_up_slab_cw<NT, true, DT, true, CW>(m, w, T, mp, s)
+                : launch_up_slab_cw<NT, false, DT, true, CW>(m, w, T, mp, s);
+  return pair ? launch_up_slab_cw<NT, true, DT, false, CW>(m, w, T, mp, s)
+              : launch_up_slab_cw<NT, false, DT, false, CW>(m, w, T, mp, s);
 }
 
 // Tokens per pass (NT) of the tensor-core gate/up launch, from the expected
@@ -913,14 +1409,11 @@ cudaError_t launch_up_mma(const MoeDevice& m, const MoeWork& w, int T, cudaStrea
   }
   switch (up_pass_tokens(m, T)) {
     case 1:
-      return pair ? launch_up_slab_nt<1, true, DT, 8>(m, w, T, mp, s)
-                  : launch_up_slab_nt<1, false, DT, 8>(m, w, T, mp, s);
+      return launch_up_slab_nt<1, DT>(m, w, T, mp, s);
     case 2:
-      return pair ? launch_up_slab_nt<2, true, DT, 8>(m, w, T, mp, s)
-                  : launch_up_slab_nt<2, false, DT, 8>(m, w, T, mp, s);
+      return launch_up_slab_nt<2, DT>(m, w, T, mp, s);
     default:
-      return pair ? launch_up_slab_nt<4, true, DT, 8>(m, w, T, mp, s)
-                  : launch_up_slab_nt<4, false, DT, 8>(m, w, T, mp, s);
+      return launch_up_slab_nt<4, DT>(m, w, T, mp, s);
   }
 }
 
@@ -937,6 +1430,11 @@ cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T, cu
   if (DT == LB_TYPE_Q4_K) {
     moe_down_sums_kernel<<<std::min(T * m.top_k + T, sm_count() * 4), 128, 0, s>>>(m, w, T);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (DT == LB_TYPE_Q6_K && down_uses_m6(m)) {
+    e = launch_down_slab(m, w, T, 0, s);
+    if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_down_slab(m, w, T, 1, s);
+    return e;
   }
   e = launch_down<DT>(m, w, T, 0, s);
   if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_down<DT>(m, w, T, 1, s);
@@ -969,11 +1467,12 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
   w->entries = reinterpret_cast<int*>(take((size_t)T * k * 2 * 4));
   w->active = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
   w->pass_off = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
+  w->pass_off_dn = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
   w->status = reinterpret_cast<int*>(take(4));
   w->xn = reinterpret_cast<float*>(take(m.input_norm ? (size_t)T * m.hidden * 4 : 4));
   w->xp_up = reinterpret_cast<float*>(take((size_t)T * up_ld_floats(m.k_in) * 4));
   w->xp_down = reinterpret_cast<float*>(
-      take((size_t)(T * k + T) * xp_stride(std::max(m.k_down, m.k_down_sh)) * 4));
+      take((size_t)(T * k + T) * down_ld_floats(m) * 4));
   w->partial = reinterpret_cast<float*>(take((size_t)T * (k + 1) * m.hidden * 4));
   w->bytes = off;
 }
@@ -999,7 +1498,15 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   }
   e = launch_gemv_f32(m.router, router_rows, m.hidden, xr, m.hidden, T, w.logits, E + 1, s);
   if (e != cudaSuccess) return e;
-  topk_kernel<<<T, 32, 0, s>>>(m, w, T);
+  {
+    const int per = (E + 31) / 32;
+    if (per <= 1) topk_kernel<1><<<T, 32, 0, s>>>(m, w, T);
+    else if (per <= 2) topk_kernel<2><<<T, 32, 0, s>>>(m, w, T);
+    else if (per <= 4) topk_kernel<4><<<T, 32, 0, s>>>(m, w, T);
+    else if (per <= 8) topk_kernel<8><<<T, 32, 0, s>>>(m, w, T);
+    else if (per <= 16) topk_kernel<16><<<T, 32, 0, s>>>(m, w, T);
+    else topk_kernel<32><<<T, 32, 0, s>>>(m, w, T);
+  }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   route_kernel<<<1, 256, 0, s>>>(m, w, T, up_pass_tokens(m, T));
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1016,9 +1523,14 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   else
     return cudaErrorInvalidValue;
   if (e != cudaSuccess) return e;
-  const long n = (long)T * m.hidden;
+  const bool vec = (m.hidden & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const long n = (long)T * m.hidden / (vec ? 4 : 1);
   const int grid = (int)std::min<long>((n + 255) / 256, (long)sm_count() * 8);
-  combine_kernel<<<std::max(grid, 1), 256, 0, s>>>(m, w, T, x, out);
+  if (vec)
+    combine_kernel<true><<<std::max(grid, 1), 256, 0, s>>>(m, w, T, x, out);
+  else
+    combine_kernel<false><<<std::max(grid, 1), 256, 0, s>>>(m, w, T, x, out);
   return cudaGetLastError();
 }
 

@@ -63,6 +63,44 @@ def test_small_layer_matches_oracle(cfg, tokens):
     assert max_rel(w[same], w_ref[same]) < 1e-6
 
 
+@pytest.mark.parametrize("cfg", [SMALL_QWEN, SMALL_NEMO], ids=lambda c: c.name)
+def test_topk_ties_take_lower_index(cfg):
+    """Equal scores rank by lower expert index, as the reference's repeated
+    strict-> scan (select-top-k-logits-into, L5265-5292) finds them: experts
+    2j and 2j+1 get identical router rows, and a block of experts gets zero
+    rows (scores +0.0 / -0.0, which compare equal)."""
+    cfg = dataclasses.replace(cfg, experts=32, top_k=6)
+    tensors = host_layer(cfg, seed=11)
+    t, ne0, ne1, ne2, router = tensors["ffn_gate_inp"]
+    r = router.reshape(ne1, ne0).copy()
+    r[1::2] = r[0::2]
+    r[20:26] = 0.0
+    tensors["ffn_gate_inp"] = (t, ne0, ne1, ne2, np.ascontiguousarray(r.reshape(-1)))
+    if "exp_probs_b.bias" in tensors:  # keep the pairs tied after the bias
+        tb, b0, b1, b2, bias = tensors["exp_probs_b.bias"]
+        b = bias.copy()
+        b[1::2] = b[0::2]
+        b[20:26] = 0.0
+        tensors["exp_probs_b.bias"] = (tb, b0, b1, b2, b)
+    tokens = 12
+    x = O.synth_f32(11, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
+    ref, sel_ref, w_ref = O.moe_forward(oracle_layer(cfg, tensors), x, tokens, cfg.top_k)
+    _, sel, w = _session(cfg, tensors, max_tokens=16).run(x, with_routing=True)
+    bias = tensors["exp_probs_b.bias"][4] if "exp_probs_b.bias" in tensors else 0.0
+    checked = 0
+    for i in range(tokens):
+        scores = O.gemv(O.TYPE_F32, tensors["ffn_gate_inp"][4], ne0, ne1, x[i]) + bias
+        uniq = np.unique(scores)[::-1][: cfg.top_k + 2]
+        if uniq.size > 1 and np.min(-np.diff(uniq)) <= 1e-5:
+            continue  # distinct scores too close for an exact order
+        assert sel[i].tolist() == sel_ref[i].tolist()
+        for j in range(cfg.top_k - 1):  # tied neighbours in index order
+            if scores[sel[i][j]] == scores[sel[i][j + 1]]:
+                assert sel[i][j] < sel[i][j + 1]
+        checked += 1
+    assert checked >= tokens // 2
+
+
 @pytest.mark.parametrize("norm", [False, True])
 @pytest.mark.parametrize("scale", [1.0, 2.5])
 def test_nemotron_weight_policy(norm, scale):
