@@ -46,6 +46,9 @@ sys.path.insert(0, ROOT)
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 NOMINAL_HBM_GBS = 8000.0
+# ncu DRAM traffic of one config-5 b32 layer on one GPU: gate/up 286.8 MB +
+# routed down 209.6 MB + router, shared down and small kernels ~5.6 MB
+LAYER_TRAFFIC_BYTES_N1 = 502_000_000
 
 
 def parse():
@@ -60,6 +63,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-kernels", action="store_true")
+    p.add_argument("--no-graph", action="store_true",
+                   help="launch every layer from Python instead of replaying one CUDA graph")
     p.add_argument("--workload", default="stack",
                    choices=["stack", "config1", "config2", "config3", "config4"])
     return p.parse_args()
@@ -347,22 +352,32 @@ def run_ours(args):
         import torch.distributed as dist
 
     def step(record=None):
+        st = torch.cuda.current_stream()  # the capture stream while a graph records
         cur = x0
         for li, s in enumerate(sessions):
             out = bufs[li % 2]
             if record is not None:
-                record[li][0].record(stream)
-            s.run_device(cur, out, B, stream=stream)
+                record[li][0].record(st)
+            s.run_device(cur, out, B, stream=st)
             if world > 1:
                 dist.all_reduce(out)
             if record is not None:
-                record[li][1].record(stream)
+                record[li][1].record(st)
             cur = out
         return cur
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # one CUDA graph replays the whole stack step (single GPU; with N > 1 the
+    # NCCL all-reduce stays outside graphs)
+    graph = None
+    if world == 1 and not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
     for s in sessions:
         if s.status() != 0:
             raise SystemExit("device status reported a non-positive router weight sum")
@@ -374,7 +389,10 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for k in range(args.steps):
-        step(layer_ev if k == args.steps - 1 else None)
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
@@ -382,6 +400,8 @@ def run_ours(args):
     ms = e0.elapsed_time(e1) / args.steps
     ms = max_over_ranks(ms, world)
     value = B / (ms * 1e-3)
+    step(layer_ev)  # per-layer times (launched eagerly) for the roofline
+    torch.cuda.synchronize()
     layer_ms = [a.elapsed_time(b) for a, b in layer_ev]
 
     # routing of the timed steps (identical every step: same x0) -> algorithmic bytes
@@ -417,7 +437,10 @@ def run_ours(args):
                 "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
                 "algorithmic_bytes_per_layer": int(sum(layer_bytes) / NL),
                 "layer_us_mean": round(statistics.mean(layer_ms) * 1e3, 2),
-                "traffic": None}
+                # DRAM read+write bytes of one layer at N=1, from one ncu capture of
+                # the layer's kernels (profiles/moe_slab_kernels_config5_b32.md)
+                "traffic": LAYER_TRAFFIC_BYTES_N1 if world == 1 else None,
+                "traffic_unit": "bytes per layer (ncu dram__bytes_read+write)"}
 
     # e2e through the C ABI with host buffers (one call per layer per step)
     e2e = None
@@ -473,7 +496,9 @@ def run_ours(args):
                    "sample": f"{B} tokens through 1 qwen3next layer per sample "
                              f"({per_layer * 1e3:.1f} ms), scaled to {NL} layers"}
 
-    launches_per_layer = 6
+    # prep, router GEMV, top-k, route, gate/up, routed down, shared down (the
+    # shared expert's rank only), combine
+    launches_per_layer = 8 if rank == 0 else 7
     line = {"metric": "MoE FFN decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",

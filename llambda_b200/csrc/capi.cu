@@ -199,7 +199,8 @@ void session_launch(llambda_cuda_session* s, const uint8_t* W, const float* din,
     return;
   }
   float* xp = static_cast<float*>(s->dxp.get(lb::xprep_floats((int)s->ne0, (int)tokens) * 4));
-  cuda_check(lb::launch_prep(s->type, din, (long)s->ne0, (int)s->ne0, (int)s->ne0, (int)tokens,
+  cuda_check(lb::launch_prep(s->type, (int)s->ne1, din, (long)s->ne0, (int)s->ne0, (int)s->ne0,
+                             (int)tokens,
                              nullptr, xp, st),
              "activation prep");
   cuda_check(lb::launch_gemv_prepped(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, xp,
@@ -217,6 +218,7 @@ void require_aligned16(const void* p, const char* what) {
 struct llambda_cuda_moe_session {
   lb::MoeDevice m{};
   lb::MoeWork w{};
+  lb::SlabMaps maps{};  // tensor maps of the gate/up matrices, built once
   int device = 0;
   int max_tokens = 0;
   cudaStream_t stream = nullptr;
@@ -690,6 +692,7 @@ int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
       cuda_check(cudaMalloc(&s->work, wb), "cudaMalloc workspace");
       cuda_check(cudaMemsetAsync(s->work, 0, wb, s->stream), "memset workspace");
       lb::moe_work_carve(m, d->max_tokens, s->work, &s->w);
+      cuda_check(lb::moe_maps_build(m, &s->maps), "tensor maps");
       cuda_check(cudaStreamSynchronize(s->stream), "MoE session upload");
     } catch (...) {
       delete s;
@@ -737,7 +740,7 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
     int status = 0;
     cuda_check(cudaMemsetAsync(s->w.status, 0, 4, s->stream), "memset");
     cuda_check(cudaMemcpyAsync(dx, hx, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
-    cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, s->stream), "MoE launch");
+    cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, &s->maps, s->stream), "MoE launch");
     cuda_check(cudaMemcpyAsync(hout, dout, xb, cudaMemcpyDeviceToHost, s->stream), "output copy");
     int32_t* hsel = selected ? static_cast<int32_t*>(s->hsel.get(sb)) : nullptr;
     float* hw = weights ? static_cast<float*>(s->hw.get(sb)) : nullptr;
@@ -767,7 +770,8 @@ int llambda_cuda_moe_session_run_device(llambda_cuda_moe_session* s, const float
     DeviceGuard g(s->device);
     if ((int64_t)tokens > s->max_tokens) throw Failure("Token count exceeds max_tokens.");
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    cuda_check(lb::launch_moe(s->m, s->w, device_x, (int)tokens, device_out, st), "MoE launch");
+    cuda_check(lb::launch_moe(s->m, s->w, device_x, (int)tokens, device_out, &s->maps, st),
+               "MoE launch");
     const size_t sb = tokens * s->m.top_k * 4;
     if (device_selected)
       cuda_check(cudaMemcpyAsync(device_selected, s->w.sel, sb, cudaMemcpyDeviceToDevice, st), "copy");
@@ -957,7 +961,7 @@ int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     int status = 0;
     cuda_check(cudaMemsetAsync(w.status, 0, sizeof(int), st), "clear status");
-    cuda_check(lb::launch_moe(m, w, device_x, T, device_out, st), "MoE launch");
+    cuda_check(lb::launch_moe(m, w, device_x, T, device_out, nullptr, st), "MoE launch");
     cuda_check(cudaMemcpyAsync(&status, w.status, sizeof(int), cudaMemcpyDeviceToHost, st),
                "status copy");
     cuda_check(cudaStreamSynchronize(st), "MoE layer");

@@ -117,6 +117,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return false;
 }
 
+// Position in a ring of `stages` stages: the stage index and the parity of
+// its current use, advanced without a division.
+struct RingPos {
+  int s = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int stages) {
+    if (++s == stages) {
+      s = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 // Bounded wait that also gives up as soon as another warp of the CTA has
 // raised *abort (after its own wait timed out).
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int* status,

@@ -87,7 +87,132 @@ __global__ void __launch_bounds__(64) prep_kernel(const float* __restrict__ x, l
   }
 }
 
+// The Q6_K tensor-core layout (mma.cuh, "m6") of token rows: one block per
+// (super-block, token), two warps storing 8 of its 16 sub-blocks each.
+__global__ void __launch_bounds__(64) m6_prep_kernel(const float* __restrict__ x, long ldx,
+                                                     int n_valid, int K,
+                                                     const int* __restrict__ gather,
+                                                     uint8_t* __restrict__ m6) {
+  const int sb = blockIdx.x, tok = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long row = gather ? gather[tok] : tok;
+  const float* s = x + row * ldx;
+  uint8_t* dst = m6 + (size_t)tok * m6_bytes(K);
+  const int g = lane >> 2;
+  for (int j = 0; j < 8; ++j) {
+    const int sub = warp * 8 + j;
+    const int e0 = sb * 256 + sub * 16;
+    float va = 0.f, vb = 0.f;
+    if ((lane & 3) == 0) {
+      va = e0 + g < n_valid ? s[e0 + g] : 0.f;
+      vb = e0 + g + 8 < n_valid ? s[e0 + g + 8] : 0.f;
+    }
+    m6_store_subblock(dst, sb * 16 + sub, va, vb, lane);
+  }
+}
+
 // ------------------------------------------------------------ dense GEMV
+
+// Q6_K rows on the tensor cores (mma.cuh): a unit is a 16-row block with its
+// whole K (16 rows x row bytes, one aligned bulk copy), staged by warp CW
+// through full/empty mbarriers; consumer warp w takes super-blocks
+// [w*nsb/CW, (w+1)*nsb/CW) of every block, and warp 0 adds the other warps'
+// sums (in warp order) and writes the rows.  NG groups of 4 tokens share the
+// decoded weights; the tokens' prepared inputs (m6) are read through L1.
+struct DenseSync {
+  uint64_t full[8], empty[8], red[8];
+  int abort;
+  int pad[3];
+};
+
+template <int NG, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
+    gemv_q6k_slab_kernel(const uint8_t* __restrict__ W, size_t rb, int rows, int nsb,
+                         const uint8_t* __restrict__ m6, int tokens, float* __restrict__ y,
+                         long ldy, int stages, int stage_bytes, int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  DenseSync* sync = reinterpret_cast<DenseSync*>(smem + (size_t)stages * stage_bytes);
+  float2* red = reinterpret_cast<float2*>(sync + 1);  // [stages][CW][32][NG]
+  volatile int* abort = &sync->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&sync->full[s], 1);
+      mbar_init(&sync->empty[s], CW);
+      mbar_init(&sync->red[s], CW - 1);
+    }
+    sync->abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int units = rows / kTileRows;  // rows % 16 == 0
+  const int u0 = (int)((long)blockIdx.x * units / gridDim.x);
+  const int n_my = (int)((long)(blockIdx.x + 1) * units / gridDim.x) - u0;
+  const uint32_t block_bytes = (uint32_t)(kTileRows * rb);
+  if (warp == CW) {  // ---------------- producer
+    if (lane == 0) {
+      RingPos rp;
+      int q = 0;
+      for (int i = 0; i < n_my; ++i, ++q, rp.next(stages)) {
+        if (q >= stages && !mbar_wait_or_abort(&sync->empty[rp.s], rp.phase ^ 1u, status, abort))
+          break;
+        mbar_expect_tx(&sync->full[rp.s], block_bytes);
+        tma_load_1d(smem + (size_t)rp.s * stage_bytes, W + (size_t)(u0 + i) * block_bytes,
+                    block_bytes, &sync->full[rp.s]);
+      }
+      for (int r = max(0, q - stages); r < q; ++r)
+        mbar_wait(&sync->full[r % stages], (r / stages) & 1, nullptr);
+    }
+    return;
+  }
+  const int sb0 = warp * nsb / CW, sb1 = (warp + 1) * nsb / CW;
+  const int g = lane >> 2, t = lane & 3;
+  const size_t m6b = m6_bytes(nsb * 256);
+  const uint8_t* m6p[4 * NG];
+#pragma unroll
+  for (int n = 0; n < 4 * NG; ++n) m6p[n] = m6 + (size_t)min(n, tokens - 1) * m6b;
+  RingPos rp;
+  for (int i = 0; i < n_my; ++i, rp.next(stages)) {
+    const int s = rp.s;
+    if (!mbar_wait_or_abort(&sync->full[s], rp.phase, status, abort)) break;
+    const uint8_t* blk = smem + (size_t)s * stage_bytes;
+    float2 acc[NG];
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) acc[grp] = make_float2(0.f, 0.f);
+    for (int sb = sb0; sb < sb1; ++sb)
+      q6k_sb_mma<false, NG>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, m6p,
+                            tokens, lane, acc);
+    float2* rs = red + (size_t)s * CW * 32 * NG;
+    if (warp != 0) {
+#pragma unroll
+      for (int grp = 0; grp < NG; ++grp) rs[(warp * 32 + lane) * NG + grp] = acc[grp];
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sync->red[s]);
+        mbar_arrive(&sync->empty[s]);
+      }
+    } else {
+      if (!mbar_wait_or_abort(&sync->red[s], rp.phase, status, abort)) break;
+      for (int w2 = 1; w2 < CW; ++w2)
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+          const float2 o = rs[(w2 * 32 + lane) * NG + grp];
+          acc[grp].x += o.x;
+          acc[grp].y += o.y;
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sync->empty[s]);
+      const int row = (u0 + i) * kTileRows + g;
+#pragma unroll
+      for (int grp = 0; grp < NG; ++grp) {
+        const int n = 4 * grp + t;
+        if (n < tokens) {
+          y[(long)n * ldy + row] = acc[grp].x;
+          y[(long)n * ldy + row + 8] = acc[grp].y;
+        }
+      }
+    }
+  }
+}
 
 // Each warp owns a contiguous run of units (RU rows each), streams them
 // through its TMA ring and computes every token against each staged unit.
@@ -442,21 +567,54 @@ cudaError_t launch_q4k_mma(const void* W, size_t rb, int rows, int K, const floa
   return cudaGetLastError();
 }
 
+template <int NG>
+cudaError_t launch_q6k_slab(const void* W, size_t rb, int rows, int K, const uint8_t* m6,
+                            int tokens, float* y, long ldy, int* status, cudaStream_t stream) {
+  const int nsb = K / 256;
+  const int stage_bytes = (int)((kTileRows * rb + 127) & ~size_t(127));
+  const bool wide = nsb >= 16;
+  const int cw = wide ? 16 : 8;
+  const size_t per_stage = (size_t)stage_bytes + (size_t)cw * 32 * NG * sizeof(float2);
+  const int stages = (int)std::min<size_t>(8, (kTileSmemBudget - sizeof(DenseSync)) / per_stage);
+  if (stages < 2) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)stages * per_stage + sizeof(DenseSync);
+  const int units = rows / kTileRows;
+  const int grid = std::max(1, std::min(units, sm_count()));
+  if (wide) {
+    auto kern = gemv_q6k_slab_kernel<NG, 16>;
+    if (prepared_occupancy(kern, 17 * 32, smem) < 1) return cudaErrorUnknown;
+    kern<<<grid, 17 * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, nsb, m6,
+                                          tokens, y, ldy, stages, stage_bytes, status);
+  } else {
+    auto kern = gemv_q6k_slab_kernel<NG, 8>;
+    if (prepared_occupancy(kern, 9 * 32, smem) < 1) return cudaErrorUnknown;
+    kern<<<grid, 9 * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, nsb, m6,
+                                         tokens, y, ldy, stages, stage_bytes, status);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 // ------------------------------------------------------------ host API
 
 size_t xprep_floats(int K, int tokens) {
-  return std::max((size_t)xp_stride(K), mx_bytes(K) / 4) * tokens;
+  return std::max({(size_t)xp_stride(K), mx_bytes(K) / 4, m6_bytes(K) / 4}) * tokens;
 }
 
-cudaError_t launch_prep(int type, const float* x, long ldx, int n_valid, int K, int tokens,
-                        const int* gather, float* xp, cudaStream_t stream) {
+// Q6_K matrices of whole 16-row blocks run on the tensor cores.
+static bool q6k_dense_mma(int rows) { return rows % kTileRows == 0; }
+
+cudaError_t launch_prep(int type, int rows, const float* x, long ldx, int n_valid, int K,
+                        int tokens, const int* gather, float* xp, cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
   if (K % 256) return cudaErrorInvalidValue;
   dim3 grid(K / 256, tokens);
   if (type == LB_TYPE_Q4_K)
     prep_kernel<LB_TYPE_Q4_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
+  else if (type == LB_TYPE_Q6_K && q6k_dense_mma(rows))
+    m6_prep_kernel<<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather,
+                                            reinterpret_cast<uint8_t*>(xp));
   else if (type == LB_TYPE_Q6_K)
     prep_kernel<LB_TYPE_Q6_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
   else
@@ -475,6 +633,19 @@ cudaError_t launch_gemv_prepped(int type, const void* W, size_t rb, int rows, in
 #define LB_DENSE_T(T)                                                                        \
   LB_DENSE(T, 8, 1) LB_DENSE(T, 8, 2) LB_DENSE(T, 8, 4) LB_DENSE(T, 16, 1) LB_DENSE(T, 16, 2)  \
   LB_DENSE(T, 16, 4) LB_DENSE(T, 32, 1) LB_DENSE(T, 32, 2) LB_DENSE(T, 32, 4)
+  if (type == LB_TYPE_Q6_K && q6k_dense_mma(rows)) {
+    const uint8_t* m6 = reinterpret_cast<const uint8_t*>(xp);
+    for (int t0 = 0; t0 < tokens; t0 += 8) {  // 8 tokens per pass over the weights
+      const int nt = std::min(8, tokens - t0);
+      const cudaError_t e =
+          nt <= 4 ? launch_q6k_slab<1>(W, rb, rows, K, m6 + (size_t)t0 * m6_bytes(K), nt,
+                                       y + (long)t0 * ldy, ldy, status, stream)
+                  : launch_q6k_slab<2>(W, rb, rows, K, m6 + (size_t)t0 * m6_bytes(K), nt,
+                                       y + (long)t0 * ldy, ldy, status, stream);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
   if (type == LB_TYPE_Q4_K) {
     if (tokens == 1) return launch_q4k_mma<1, 16>(W, rb, rows, K, xp, tokens, y, ldy, status, stream);
     if (tokens == 2) return launch_q4k_mma<2, 16>(W, rb, rows, K, xp, tokens, y, ldy, status, stream);

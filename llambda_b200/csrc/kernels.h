@@ -1,6 +1,7 @@
 // Host-side launch interface of the CUDA kernels (internal to the library).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -29,8 +30,9 @@ struct UnitPlan {
 UnitPlan plan_units(size_t row_bytes, int tasks, int ranges);
 int sm_count();
 size_t xprep_floats(int K, int tokens);
-cudaError_t launch_prep(int type, const float* x, long ldx, int n_valid, int K, int tokens,
-                        const int* gather, float* xp, cudaStream_t stream);
+// rows: the matrix the prepared input is for (picks the layout).
+cudaError_t launch_prep(int type, int rows, const float* x, long ldx, int n_valid, int K,
+                        int tokens, const int* gather, float* xp, cudaStream_t stream);
 cudaError_t launch_gemv_prepped(int type, const void* W, size_t row_bytes, int rows, int K,
                                 const float* xp, int tokens, float* y, long ldy, int* status,
                                 cudaStream_t stream);
@@ -110,11 +112,21 @@ struct MoeWork {
   size_t bytes;
 };
 
+// 2-D tensor maps of the Q4_K gate/up matrices (routed rows this device owns,
+// shared rows) for the tensor-core gate/up pass; built once per layer.
+struct SlabMaps {
+  CUtensorMap gate, up, gate_sh, up_sh;
+  long row_base;  // global row (expert_begin * inter) of the routed maps' row 0
+  int ready;      // 0: not a Q4_K layer, or nothing to compute here
+};
+cudaError_t moe_maps_build(const MoeDevice& m, SlabMaps* maps);
+
 size_t moe_work_bytes(const MoeDevice& m, int max_tokens);
 void moe_work_carve(const MoeDevice& m, int max_tokens, void* base, MoeWork* w);
 
-// out[t][h] for t < tokens.
+// out[t][h] for t < tokens.  maps: from moe_maps_build for this layer, or
+// null to build them for this call.
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int tokens,
-                       float* out, cudaStream_t stream);
+                       float* out, const SlabMaps* maps, cudaStream_t stream);
 
 }  // namespace lb

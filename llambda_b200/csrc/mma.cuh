@@ -408,20 +408,29 @@ __device__ __forceinline__ float s8_to_float(uint32_t w_xor80, int b) {
   return __uint_as_float(__byte_perm(w_xor80, 0x4B000000u, 0x7440u | b)) - 8388736.0f;
 }
 
-// Adds token t's (this lane's, t < nt) dot products over super-block sb of a
-// 16-row Q6_K block to y (.x row g, .y row g+8).  rg / rg8: the super-block
-// of rows g and g+8 in shared memory (2-byte aligned); m6[n]: the m6 buffers
-// of the group's tokens (n < nt valid; SMEM: staged in shared memory).
-template <bool SMEM>
+// Adds token t's (this lane's) dot products over super-block sb of a 16-row
+// Q6_K block to y[grp] (.x row g, .y row g+8) for NG groups of 4 tokens: token
+// 4*grp + t, if below nt.  rg / rg8: the super-block of rows g and g+8 in
+// shared memory (2-byte aligned); m6[n]: the m6 buffers of the tokens (n < nt
+// valid; SMEM: staged in shared memory).  The A fragments are decoded once
+// per k-step and serve every group.
+template <bool SMEM, int NG>
 __device__ __forceinline__ void q6k_sb_mma(const uint8_t* rg, const uint8_t* rg8, int sb,
-                                           const uint8_t* const (&m6)[4], int nt, int lane,
-                                           float2& y) {
+                                           const uint8_t* const (&m6)[4 * NG], int nt, int lane,
+                                           float2 (&y)[NG]) {
   const int g = lane >> 2, t = lane & 3;
   const int bn = g >> 1, part = g & 1;
-  const bool bval = bn < nt;
-  const uint4* bsrc =
-      reinterpret_cast<const uint4*>(m6[bn] + (size_t)sb * 1152) + (part * 4 + t) * 8;
-  const float4* msrc = reinterpret_cast<const float4*>(m6[t] + (size_t)sb * 1152 + 1024);
+  const uint4* bsrc[NG];
+  const float4* msrc[NG];
+  bool bval[NG], mval[NG];
+#pragma unroll
+  for (int grp = 0; grp < NG; ++grp) {
+    bval[grp] = 4 * grp + bn < nt;
+    mval[grp] = 4 * grp + t < nt;
+    bsrc[grp] = reinterpret_cast<const uint4*>(m6[4 * grp + bn] + (size_t)sb * 1152) +
+                (part * 4 + t) * 8;
+    msrc[grp] = reinterpret_cast<const float4*>(m6[4 * grp + t] + (size_t)sb * 1152 + 1024);
+  }
   const float d = half_bits_to_float(lds_u16(rg + 208));
   const float d8 = half_bits_to_float(lds_u16(rg8 + 208));
 #pragma unroll
@@ -452,37 +461,47 @@ __device__ __forceinline__ void q6k_sb_mma(const uint8_t* rg, const uint8_t* rg8
         q8[3] = ((B >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
       }
       const int q0 = (2 * c + h) * 4;  // first k-step of this (c, h)
-      uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
-      if (bval) {
-        b01 = ld_b16<SMEM>(bsrc + q0 / 2);
-        b23 = ld_b16<SMEM>(bsrc + q0 / 2 + 1);
-      }
-      float4 m01 = make_float4(0.f, 0.f, 0.f, 0.f), m23 = m01;
-      if (t < nt) {
-        const uint4 u01 = ld_b16<SMEM>(msrc + q0 / 2), u23 = ld_b16<SMEM>(msrc + q0 / 2 + 1);
-        m01 = make_float4(__uint_as_float(u01.x), __uint_as_float(u01.y), __uint_as_float(u01.z),
-                          __uint_as_float(u01.w));
-        m23 = make_float4(__uint_as_float(u23.x), __uint_as_float(u23.y), __uint_as_float(u23.z),
-                          __uint_as_float(u23.w));
+      uint4 b01[NG], b23[NG];
+      float4 m01[NG], m23[NG];
+#pragma unroll
+      for (int grp = 0; grp < NG; ++grp) {
+        b01[grp] = b23[grp] = make_uint4(0, 0, 0, 0);
+        if (bval[grp]) {
+          b01[grp] = ld_b16<SMEM>(bsrc[grp] + q0 / 2);
+          b23[grp] = ld_b16<SMEM>(bsrc[grp] + q0 / 2 + 1);
+        }
+        m01[grp] = m23[grp] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (mval[grp]) {
+          const uint4 u01 = ld_b16<SMEM>(msrc[grp] + q0 / 2);
+          const uint4 u23 = ld_b16<SMEM>(msrc[grp] + q0 / 2 + 1);
+          m01[grp] = make_float4(__uint_as_float(u01.x), __uint_as_float(u01.y),
+                                 __uint_as_float(u01.z), __uint_as_float(u01.w));
+          m23[grp] = make_float4(__uint_as_float(u23.x), __uint_as_float(u23.y),
+                                 __uint_as_float(u23.z), __uint_as_float(u23.w));
+        }
       }
 #pragma unroll
       for (int gg = 0; gg < 4; ++gg) {
-        float dv[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t b0 = gg == 0 ? b01.x : gg == 1 ? b01.z : gg == 2 ? b23.x : b23.z;
-        const uint32_t b1 = gg == 0 ? b01.y : gg == 1 ? b01.w : gg == 2 ? b23.y : b23.w;
-        mma_f16(dv, __byte_perm(qg[gg], 0, 0x4240), __byte_perm(q8[gg], 0, 0x4240),
-                __byte_perm(qg[gg], 0, 0x4341), __byte_perm(q8[gg], 0, 0x4341), b0, b1);
-        const float back = gg == 0 ? m01.x : gg == 1 ? m01.z : gg == 2 ? m23.x : m23.z;
-        const float off = gg == 0 ? m01.y : gg == 1 ? m01.w : gg == 2 ? m23.y : m23.w;
+        const uint32_t a0 = __byte_perm(qg[gg], 0, 0x4240), a1 = __byte_perm(q8[gg], 0, 0x4240);
+        const uint32_t a2 = __byte_perm(qg[gg], 0, 0x4341), a3 = __byte_perm(q8[gg], 0, 0x4341);
         // sub-block s = 8c + 2gg + h: scale byte 2gg + h of the chunk's 8
         const int sbyte = 2 * gg + h;
         const uint32_t wg = sbyte < 4 ? sg0 : sg1, w8 = sbyte < 4 ? s80 : s81;
         const float2 dsc = __fmul2_rn(make_float2(d, d8),
                                       make_float2(s8_to_float(wg, sbyte & 3),
                                                   s8_to_float(w8, sbyte & 3)));
-        float2 s2 = __fadd2_rn(make_float2(dv[0], dv[2]), make_float2(dv[1], dv[3]));
-        s2 = __ffma2_rn(s2, make_float2(back, back), make_float2(off, off));
-        y = __ffma2_rn(dsc, s2, y);
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+          float dv[4] = {0.f, 0.f, 0.f, 0.f};
+          const uint4& bl = gg < 2 ? b01[grp] : b23[grp];
+          const uint32_t b0 = (gg & 1) ? bl.z : bl.x, b1 = (gg & 1) ? bl.w : bl.y;
+          mma_f16(dv, a0, a1, a2, a3, b0, b1);
+          const float4& ml = gg < 2 ? m01[grp] : m23[grp];
+          const float back = (gg & 1) ? ml.z : ml.x, off = (gg & 1) ? ml.w : ml.y;
+          float2 s2 = __fadd2_rn(make_float2(dv[0], dv[2]), make_float2(dv[1], dv[3]));
+          s2 = __ffma2_rn(s2, make_float2(back, back), make_float2(off, off));
+          y[grp] = __ffma2_rn(dsc, s2, y[grp]);
+        }
       }
     }
   }

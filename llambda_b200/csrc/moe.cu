@@ -89,16 +89,14 @@ __device__ __forceinline__ uint32_t topk_key(float v) {
 
 // The k best scores of one token, in the order the reference's repeated
 // strict-> scan finds them (descending score, ties to the lower index).  The
-// k-th largest key is found by an 8-bit radix select (four passes of a
-// shared-memory histogram over the keys that match the bytes found so far);
-// every key above it is taken and the ties at it in index order, and the k
+// k-th largest key is found bit by bit from warp-wide counts; every key above
+// it is taken and the ties at it in index order, and the k
 // winners are ranked by (score, index).  PER: candidates per lane (E <= 32*PER).
 template <int PER>
 __global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T) {
   __shared__ float s_val[32];
   __shared__ uint32_t s_key[32];
   __shared__ int s_idx[32];
-  __shared__ int s_hist[256];
   const int t = blockIdx.x, lane = threadIdx.x;
   const int E = m.experts, k = m.top_k;
   const float* L = w.logits + (long)t * (E + 1);
@@ -118,56 +116,21 @@ __global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T)
     lv[q] = v;
     key[q] = kq;
   }
+  // the k-th largest key by a bitwise search over warp-wide counts (a byte
+  // histogram would serialise: the top bytes of nearby scores coincide)
+  auto count_ge = [&](uint32_t c) {
+    unsigned n = 0;
+#pragma unroll
+    for (int q = 0; q < PER; ++q) n += key[q] >= c ? 1u : 0u;
+    return (int)__reduce_add_sync(0xffffffffu, n);
+  };
   uint32_t th = 0u;  // the k-th largest key (0: fewer than k selectable scores)
-  int krem = k;      // its rank among the keys equal to it
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    const uint32_t hi = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s_hist[lane * 8 + j] = 0;
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < PER; ++q)
-      if (key[q] != 0u && (key[q] & hi) == th) atomicAdd(&s_hist[(key[q] >> shift) & 255], 1);
-    __syncwarp();
-    // lane l holds bins 255-8l .. 248-8l, highest first
-    int c[8], tot = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      c[j] = s_hist[255 - 8 * lane - j];
-      tot += c[j];
-    }
-    int incl = tot;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const bool here = incl - tot < krem && incl >= krem;
-    int bin = 0, above = 0;
-    if (here) {
-      int run = incl - tot;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (run + c[j] >= krem) {
-          bin = 255 - 8 * lane - j;
-          above = run;
-          break;
-        }
-        run += c[j];
-      }
-    }
-    const unsigned hm = __ballot_sync(0xffffffffu, here);
-    __syncwarp();
-    if (hm == 0u) {  // fewer than k selectable scores
-      th = 0u;
-      krem = 0;
-      break;
-    }
-    const int src = __ffs(hm) - 1;
-    th |= (uint32_t)__shfl_sync(0xffffffffu, bin, src) << shift;
-    krem -= __shfl_sync(0xffffffffu, above, src);
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t c = th | (1u << bit);
+    if (count_ge(c) >= k) th = c;
   }
+  // its rank among the keys equal to it (keys of valid scores are >= 1)
+  int krem = th == 0u ? 0 : k - (th == 0xFFFFFFFFu ? 0 : count_ge(th + 1u));
   const int need = krem;  // ties at th to take, lowest index first
   int nsel = 0, tie_base = 0;
 #pragma unroll
@@ -647,16 +610,23 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     bool shared;
   };
   ExpertView view;
-  int a_hint = 0;  // active index of the previous item (items are visited in order)
+  int a_hint = -1;  // active index of the previous item (items are visited in order)
   auto unit_at = [&](int u) {
     Unit x;
     if (u < n_routed) {
-      int a = a_hint;  // first a with pass_off[a + 1] * per_r > u, searched from the hint
-      if (w.pass_off[a] * per_r > u) a = 0;
-      int hi = nact;
-      while (hi - a > 1) {
-        const int mid = (a + hi) >> 1;
-        if (w.pass_off[mid] * per_r <= u) a = mid; else hi = mid;
+      // the active expert a with pass_off[a] * per_r <= u < pass_off[a + 1] * per_r:
+      // items come in order, so step on from the previous item's expert; the
+      // first item of a CTA searches
+      int a = a_hint;
+      if (a < 0) {
+        a = 0;
+        int hi = nact;
+        while (hi - a > 1) {
+          const int mid = (a + hi) >> 1;
+          if (w.pass_off[mid] * per_r <= u) a = mid; else hi = mid;
+        }
+      } else {
+        while (w.pass_off[a + 1] * per_r <= u) ++a;
       }
       a_hint = a;
       view_expert(m, w, T, a, view);
@@ -684,14 +654,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   if (warp == CW) {  // ---------------- producer
     if (lane == 0) {
       int q = 0;
+      RingPos rp;
       bool ok = true;
       for (int i = 0; i < n_my && ok; ++i) {
         const Unit x = unit_at(u0 + i);
         for (int t0 = x.t_begin; t0 < x.t_end && ok; t0 += NT) {
-          for (int sb = 0; sb < nsb; ++sb, ++q) {
-            const int s = q % stages;
-            if (q >= stages &&
-                !mbar_wait_or_abort(&sync->empty[s], ((q / stages) - 1) & 1, w.status, abort)) {
+          for (int sb = 0; sb < nsb; ++sb, ++q, rp.next(stages)) {
+            const int s = rp.s;
+            if (q >= stages && !mbar_wait_or_abort(&sync->empty[s], rp.phase ^ 1u, w.status, abort)) {
               ok = false;
               break;
             }
@@ -728,7 +698,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   const int mat = warp / RBM, rb = warp % RBM;
   const int g = lane >> 2, t = lane & 3;
   const long ld_dn = down_ld_floats(m);
-  int q = 0, pass = 0;
+  RingPos rp;
+  int pass = 0;
   bool ok = true;
   for (int i = 0; i < n_my && ok; ++i) {
     const Unit x = unit_at(u0 + i);
@@ -746,9 +717,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int r = 0; r < 2; ++r) acc[n][r] = make_float2(0.f, 0.f);
-      for (int sb = 0; sb < nsb; ++sb, ++q) {
-        const int s = q % stages;
-        if (!mbar_wait_or_abort(&sync->full[s], (q / stages) & 1, w.status, abort)) {
+      for (int sb = 0; sb < nsb; ++sb, rp.next(stages)) {
+        const int s = rp.s;
+        if (!mbar_wait_or_abort(&sync->full[s], rp.phase, w.status, abort)) {
           ok = false;
           break;
         }
@@ -926,16 +897,20 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     const uint8_t* src;  // row row0 of the slab in global memory
   };
   ExpertView view;
-  int a_hint = 0;
+  int a_hint = -1;
   auto unit_at = [&](int u) {
     Unit x;
     if (!shared_pass) {
-      int a = a_hint;
-      if (w.pass_off_dn[a] * per > u) a = 0;
-      int hi = nact;
-      while (hi - a > 1) {
-        const int mid = (a + hi) >> 1;
-        if (w.pass_off_dn[mid] * per <= u) a = mid; else hi = mid;
+      int a = a_hint;  // as in the gate/up kernel: step on, search only first
+      if (a < 0) {
+        a = 0;
+        int hi = nact;
+        while (hi - a > 1) {
+          const int mid = (a + hi) >> 1;
+          if (w.pass_off_dn[mid] * per <= u) a = mid; else hi = mid;
+        }
+      } else {
+        while (w.pass_off_dn[a + 1] * per <= u) ++a;
       }
       a_hint = a;
       view_expert(m, w, T, a, view);
@@ -958,11 +933,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   if (warp == CW) {  // ---------------- producer
     if (lane == 0) {
       int q = 0;
-      for (int i = 0; i < n_my; ++i, ++q) {
+      RingPos rp;
+      for (int i = 0; i < n_my; ++i, ++q, rp.next(stages)) {
         const Unit x = unit_at(u0 + i);
-        const int s = q % stages;
-        if (q >= stages &&
-            !mbar_wait_or_abort(&sync->empty[s], ((q / stages) - 1) & 1, w.status, abort))
+        const int s = rp.s;
+        if (q >= stages && !mbar_wait_or_abort(&sync->empty[s], rp.phase ^ 1u, w.status, abort))
           break;
         const int nblk = min(NB, (H - x.row0) / kTileRows);  // H % 16 == 0
         const int nt = x.t_end - x.t_begin;
@@ -988,10 +963,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   const int b = warp / KSPLIT, kp = warp % KSPLIT;
   const int sb0 = kp * nsb / KSPLIT, sb1 = (kp + 1) * nsb / KSPLIT;
   const int g = lane >> 2, t = lane & 3;
-  for (int i = 0, q = 0; i < n_my; ++i, ++q) {
+  RingPos rp;
+  for (int i = 0; i < n_my; ++i, rp.next(stages)) {
     const Unit x = unit_at(u0 + i);
-    const int s = q % stages;
-    if (!mbar_wait_or_abort(&sync->full[s], (q / stages) & 1, w.status, abort)) break;
+    const int s = rp.s;
+    if (!mbar_wait_or_abort(&sync->full[s], rp.phase, w.status, abort)) break;
     const int nt = x.t_end - x.t_begin;
     const int row_blk = x.row0 + b * kTileRows;
     int ids[NT];
@@ -1003,26 +979,26 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       m6[n] = SB ? smem + (size_t)s * stage_bytes + stage_w + min(n, nt - 1) * m6_bytes(K)
                  : reinterpret_cast<const uint8_t*>(w.xp_down + ids[n] * ld_dn);
     }
-    float2 y = make_float2(0.f, 0.f);
+    float2 y[1] = {make_float2(0.f, 0.f)};
     if (row_blk < H) {
       const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
       for (int sb = sb0; sb < sb1; ++sb)
-        q6k_sb_mma<SB>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, m6, nt,
-                       lane, y);
+        q6k_sb_mma<SB, 1>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, m6,
+                          nt, lane, y);
     }
     if (KSPLIT > 1) {
       float2* rs = red + ((size_t)s * CW) * 32;
       if (kp != 0) {
-        rs[warp * 32 + lane] = y;
+        rs[warp * 32 + lane] = y[0];
         __syncwarp();
         if (lane == 0) mbar_arrive(&sync->red[s]);
       } else {
-        if (!mbar_wait_or_abort(&sync->red[s], (q / stages) & 1, w.status, abort)) break;
+        if (!mbar_wait_or_abort(&sync->red[s], rp.phase, w.status, abort)) break;
 #pragma unroll
         for (int p = 1; p < KSPLIT; ++p) {
           const float2 o = rs[(warp + p) * 32 + lane];
-          y.x += o.x;
-          y.y += o.y;
+          y[0].x += o.x;
+          y[0].y += o.y;
         }
       }
     }
@@ -1036,8 +1012,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       const int tok = shared_pass ? x.t_begin + t : id / k;
       const int slot = shared_pass ? k : id - tok * k;
       float* out = w.partial + ((long)tok * (k + 1) + slot) * H + row_blk;
-      out[g] = y.x;
-      out[g + 8] = y.y;
+      out[g] = y[0].x;
+      out[g + 8] = y[0].y;
     }
   }
 }
@@ -1271,11 +1247,6 @@ bool q4k_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t rb
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-struct SlabMaps {
-  CUtensorMap gate, up, gate_sh, up_sh;
-  long row_base;  // global row (expert_begin * inter) of the routed maps' row 0
-};
-
 template <int NT, bool PAIR, int DT, bool M6, int CW>
 cudaError_t launch_up_slab_cw(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
                               cudaStream_t s) {
@@ -1378,9 +1349,33 @@ int up_pass_tokens(const MoeDevice& m, int T) {
 
 // Routed and shared gate/up in one tensor-core launch.
 template <int DT>
-cudaError_t launch_up_mma(const MoeDevice& m, const MoeWork& w, int T, cudaStream_t s) {
+cudaError_t launch_up_mma(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps* cached,
+                          cudaStream_t s) {
+  SlabMaps local;
+  if (!cached) {
+    const cudaError_t e = moe_maps_build(m, &local);
+    if (e != cudaSuccess) return e;
+    cached = &local;
+  }
+  const SlabMaps& mp = *cached;
+  if (!mp.ready) return cudaSuccess;  // nothing owned here
+  switch (up_pass_tokens(m, T)) {
+    case 1:
+      return launch_up_slab_nt<1, DT>(m, w, T, mp, s);
+    case 2:
+      return launch_up_slab_nt<2, DT>(m, w, T, mp, s);
+    default:
+      return launch_up_slab_nt<4, DT>(m, w, T, mp, s);
+  }
+}
+
+}  // namespace
+
+cudaError_t moe_maps_build(const MoeDevice& m, SlabMaps* out) {
+  SlabMaps& mp = *out;
+  mp.ready = 0;
+  if (m.up_type != LB_TYPE_Q4_K) return cudaSuccess;
   const bool pair = m.arch == 0;
-  SlabMaps mp;
   mp.row_base = (long)m.expert_begin * m.inter;
   const uint64_t owned_rows = (uint64_t)std::max(0, m.expert_end - m.expert_begin) * m.inter;
   const bool shared = m.shared_here && m.inter_sh;
@@ -1407,21 +1402,18 @@ cudaError_t launch_up_mma(const MoeDevice& m, const MoeWork& w, int T, cudaStrea
     mp.up_sh = mp.up;
     mp.gate_sh = mp.gate;
   }
-  switch (up_pass_tokens(m, T)) {
-    case 1:
-      return launch_up_slab_nt<1, DT>(m, w, T, mp, s);
-    case 2:
-      return launch_up_slab_nt<2, DT>(m, w, T, mp, s);
-    default:
-      return launch_up_slab_nt<4, DT>(m, w, T, mp, s);
-  }
+  mp.ready = 1;
+  return cudaSuccess;
 }
 
+namespace {
+
 template <int UT, int DT>
-cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T, cudaStream_t s) {
+cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T,
+                                 const SlabMaps* maps, cudaStream_t s) {
   cudaError_t e;
   if constexpr (UT == LB_TYPE_Q4_K) {
-    e = launch_up_mma<DT>(m, w, T, s);
+    e = launch_up_mma<DT>(m, w, T, maps, s);
   } else {
     e = launch_up<UT, DT>(m, w, T, 0, s);
     if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_up<UT, DT>(m, w, T, 1, s);
@@ -1478,6 +1470,7 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
 }
 
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int T, float* out,
+                       const SlabMaps* maps,
                        cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (T > w.max_tokens || m.experts > kMaxExperts || m.top_k > 32 || T * m.top_k > 4 * 1024)
@@ -1513,13 +1506,13 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
   if (!gate_ok) return cudaErrorInvalidValue;
   if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q6_K)
-    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q6_K>(m, w, T, s);
+    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q6_K>(m, w, T, maps, s);
   else if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q4_K)
-    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q4_K>(m, w, T, s);
+    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q4_K>(m, w, T, maps, s);
   else if (m.up_type == LB_TYPE_Q6_K && m.down_type == LB_TYPE_Q6_K)
-    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q6_K>(m, w, T, s);
+    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q6_K>(m, w, T, maps, s);
   else if (m.up_type == LB_TYPE_Q6_K && m.down_type == LB_TYPE_Q4_K)
-    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q4_K>(m, w, T, s);
+    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q4_K>(m, w, T, maps, s);
   else
     return cudaErrorInvalidValue;
   if (e != cudaSuccess) return e;
