@@ -8,7 +8,10 @@ x <- x + MoE(rms_norm(x)) as in the qwen3next block (llambda.lisp
 L5738-5746).  Weights are synthetic (seeded generator, 50 GB at N=1), made on
 the device.  With --gpus N the 512 experts of every layer are split over N
 ranks (expert parallel, 512/N each), every rank holds the replicated
-activations, and the per-layer partial outputs meet in one NCCL all-reduce.
+activations, and the per-layer partial outputs are summed inside each
+layer's combine kernel over NVLink peer memory (--reduce peer, default; the
+step is then replayed from one CUDA graph) or by an NCCL all-reduce per layer
+(--reduce nccl).
 
 Reported:
   value         tokens/s of the whole job, device-resident, CUDA events,
@@ -63,6 +66,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-kernels", action="store_true")
+    p.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
+                   help="N > 1: sum the ranks' partial outputs in the combine kernel over "
+                        "peer memory, or with an NCCL all-reduce per layer")
     p.add_argument("--no-graph", action="store_true",
                    help="launch every layer from Python instead of replaying one CUDA graph")
     p.add_argument("--workload", default="stack",
@@ -174,12 +180,14 @@ def max_over_ranks(v, world):
 
 # ----------------------------------------------------------------- workload
 
-def build_stack(cfg, layers, rank, world, seed, max_tokens, torch):
+def build_stack(cfg, layers, rank, world, seed, max_tokens, torch, peer=False):
     """Device-resident synthetic layers; returns (sessions, owned bytes)."""
     import llambda_b200 as LB
     from llambda_b200 import configs as CF
+    from llambda_b200 import ep
     E = cfg.experts
-    eb, ee = rank * E // world, (rank + 1) * E // world
+    roles = ep.layer_roles(rank, world, E, peer)
+    eb, ee = roles["expert_range"]
     sessions, keep = [], []
     norm_w = torch.ones(cfg.hidden, dtype=torch.float32)  # post_attention_norm, unit weights
     for layer in range(layers):
@@ -203,8 +211,8 @@ def build_stack(cfg, layers, rank, world, seed, max_tokens, torch):
         sess = LB.MoeSession.create(
             cfg.arch, cfg.hidden, cfg.top_k, tensors, weight_scale=cfg.weight_scale,
             weights_norm=cfg.weights_norm, on_device=True, expert_range=(eb, ee),
-            shared_here=(rank == 0), max_tokens=max_tokens,
-            input_norm=norm_w.cuda(), norm_epsilon=1e-6, add_residual=(rank == 0))
+            shared_here=roles["shared_here"], max_tokens=max_tokens,
+            input_norm=norm_w.cuda(), norm_epsilon=1e-6, add_residual=roles["add_residual"])
         sessions.append(sess)
     torch.cuda.synchronize()
     return sessions, keep
@@ -342,7 +350,12 @@ def run_ours(args):
     cfg = CF.CONFIG3
     B, NL = args.batch, args.layers
     t_setup = time.time()
-    sessions, keep = build_stack(cfg, NL, rank, world, args.seed, max(B, 1), torch)
+    peer = world > 1 and args.reduce == "peer"
+    sessions, keep = build_stack(cfg, NL, rank, world, args.seed, max(B, 1), torch, peer=peer)
+    if peer:  # each layer's combine sums every rank's partial over NVLink
+        from llambda_b200 import ep
+        keep.append(ep.attach_peer_reduction(sessions))
+    collective = world > 1 and not peer
     setup_s = time.time() - t_setup
     x0 = torch.empty(B, cfg.hidden, device="cuda")
     LB.synth_fill_device(LB.TYPE_F32, args.seed, CF.S_ACT, 0, B * cfg.hidden, 1.0, x0)
@@ -359,7 +372,7 @@ def run_ours(args):
             if record is not None:
                 record[li][0].record(st)
             s.run_device(cur, out, B, stream=st)
-            if world > 1:
+            if collective:
                 dist.all_reduce(out)
             if record is not None:
                 record[li][1].record(st)
@@ -369,10 +382,10 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    # one CUDA graph replays the whole stack step (single GPU; with N > 1 the
-    # NCCL all-reduce stays outside graphs)
+    # one CUDA graph replays the whole stack step (not with an NCCL all-reduce
+    # per layer, which stays outside graphs)
     graph = None
-    if world == 1 and not args.no_graph:
+    if not collective and not args.no_graph:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step()
@@ -411,7 +424,7 @@ def run_ours(args):
     for li, s in enumerate(sessions):
         out = bufs[li % 2]
         s.run_device(cur, out, B, sel_dev=sel, stream=stream)
-        if world > 1:
+        if collective:
             dist.all_reduce(out)
         distinct.append(distinct_experts(sel.cpu().numpy(), cfg.experts))
         cur = out
@@ -422,7 +435,7 @@ def run_ours(args):
     for li, s in enumerate(sessions):
         out = bufs[li % 2]
         s.run_device(cur, out, B, sel_dev=sel, stream=stream)
-        if world > 1:
+        if collective:
             dist.all_reduce(out)
         ss = sel.cpu().numpy()
         own_distinct.append(int(np.unique(ss[(ss >= eb) & (ss < ee)]).size))
@@ -454,7 +467,7 @@ def run_ours(args):
             cur_h = x_host
             for s in sessions:
                 out_h = s.run(cur_h)
-                if world > 1:
+                if collective:
                     t = torch.from_numpy(out_h)
                     dist.all_reduce(t, group=gloo)
                     out_h = t.numpy()
@@ -505,7 +518,8 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"config5_qwen3next_moe_stack_{NL}L_decode_b{B}",
                        "batch": B, "layers": NL, "experts": cfg.experts, "top_k": cfg.top_k,
-                       "hidden": cfg.hidden, "parallelism": f"ep{world}",
+                       "hidden": cfg.hidden,
+                       "parallelism": f"ep{world}" + ("-peer" if peer else "-nccl" if world > 1 else ""),
                        "l2": "weights streamed per step exceed L2 (no flush needed)",
                        "setup_s": round(setup_s, 1)},
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,

@@ -212,6 +212,29 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_run_device(llambda_cuda_moe_sessio
  * a CUDA error. */
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_status(llambda_cuda_moe_session* session);
 
+/* Expert-parallel reduction over peer memory.  These entry points have no
+ * counterpart in the reference (llambda runs on one device).
+ *
+ * Bytes of the symmetric device buffer that `world` expert-parallel ranks of
+ * this session need (0 on a bad argument). */
+LLAMBDA_CUDA_API size_t llambda_cuda_moe_peer_bytes(const llambda_cuda_moe_session* session,
+                                                    int world);
+
+/* After this call every run of the session sums the partial outputs of all
+ * `world` ranks itself (each rank owning a range of experts,
+ * expert_begin/expert_end), so every rank ends with the whole layer output
+ * (plus the residual when add_residual is set, on every rank) and no
+ * all-reduce follows.  peer_buffers[r] is rank r's copy of one symmetric
+ * device buffer of `bytes` bytes (>= llambda_cuda_moe_peer_bytes), mapped
+ * into this process, 16-byte aligned and zero-filled before the first run;
+ * every session of a stack may share it.  Every rank must then run the same
+ * sessions in the same order.  A rank that waits more than two seconds for a
+ * peer sets bit 2 (value 4) of the session status. */
+LLAMBDA_CUDA_API int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_session* session,
+                                                           int rank, int world,
+                                                           void* const* peer_buffers,
+                                                           size_t bytes);
+
 /* One MoE layer without any device allocation.  This entry point has no
  * counterpart in the reference.
  *

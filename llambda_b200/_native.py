@@ -81,6 +81,9 @@ SIGNATURES = {
     "llambda_cuda_moe_session_run": (C.c_int, [_vp, _fp, _sz, _fp, _i32p, _fp]),
     "llambda_cuda_moe_session_run_device": (C.c_int, [_vp, _vp, _sz, _vp, _vp, _vp, _vp]),
     "llambda_cuda_moe_session_status": (C.c_int, [_vp]),
+    "llambda_cuda_moe_peer_bytes": (_sz, [_vp, C.c_int]),
+    "llambda_cuda_moe_session_attach_peers": (C.c_int, [_vp, C.c_int, C.c_int,
+                                                        C.POINTER(_vp), _sz]),
     "llambda_cuda_moe_forward_static_scratch": (C.c_int, [C.POINTER(MoeDesc), _vp, _sz, _vp, _vp]),
     "llambda_cuda_synth_fill_device": (C.c_int, [C.c_int, _u64, _u64, _u64, _sz, C.c_float, _vp,
                                                  _vp]),
@@ -322,6 +325,16 @@ class MoeSession:
             self._h, _dev_ptr(x_dev), tokens, _dev_ptr(out_dev),
             _dev_ptr(sel_dev) if sel_dev is not None else None,
             _dev_ptr(w_dev) if w_dev is not None else None, _stream_ptr(stream)))
+
+    def peer_bytes(self, world: int) -> int:
+        """Bytes of the symmetric buffer `world` expert-parallel ranks need."""
+        return int(lib().llambda_cuda_moe_peer_bytes(self._h, world))
+
+    def attach_peers(self, rank: int, world: int, peer_ptrs, nbytes: int) -> None:
+        """Sum every rank's partial output inside each run, over peer memory:
+        peer_ptrs[r] is rank r's copy of one zero-filled symmetric buffer."""
+        arr = (_vp * world)(*[int(p) for p in peer_ptrs])
+        _check(lib().llambda_cuda_moe_session_attach_peers(self._h, rank, world, arr, nbytes))
 
     def status(self) -> int:
         rc = lib().llambda_cuda_moe_session_status(self._h)

@@ -796,6 +796,40 @@ int llambda_cuda_moe_session_status(llambda_cuda_moe_session* s) {
   });
 }
 
+size_t llambda_cuda_moe_peer_bytes(const llambda_cuda_moe_session* s, int world) {
+  if (!s || world < 1 || world > lb::kEpMaxWorld) return 0;
+  return lb::ep_buffer_bytes(world, s->max_tokens, s->m.hidden);
+}
+
+int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_session* s, int rank, int world,
+                                          void* const* peer_buffers, size_t bytes) {
+  if (!s || !peer_buffers) {
+    set_error("A session and the peer buffer pointers are required.");
+    return -1;
+  }
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    if (world < 2 || world > lb::kEpMaxWorld || rank < 0 || rank >= world)
+      throw Failure("world must be 2.." + std::to_string(lb::kEpMaxWorld) +
+                    " and 0 <= rank < world.");
+    if (s->m.hidden % 4) throw Failure("The peer-memory reduction needs hidden % 4 == 0.");
+    if (bytes < lb::ep_buffer_bytes(world, s->max_tokens, s->m.hidden))
+      throw Failure("The peer buffer is smaller than llambda_cuda_moe_peer_bytes.");
+    for (int r = 0; r < world; ++r) require_aligned16(peer_buffers[r], "peer buffer");
+    void* dev = nullptr;
+    cuda_check(cudaMalloc(&dev, sizeof(void*) * world), "cudaMalloc peer table");
+    s->owned.push_back(dev);
+    cuda_check(cudaMemcpy(dev, peer_buffers, sizeof(void*) * world, cudaMemcpyHostToDevice),
+               "peer table copy");
+    s->m.ep_peers = static_cast<void* const*>(dev);
+    s->m.ep_rank = rank;
+    s->m.ep_world = world;
+    s->m.ep_max_tokens = s->max_tokens;
+    return 0;
+  });
+}
+
 }  // extern "C"
 
 // ------------------------------------------------- MoE layer, no allocation

@@ -86,7 +86,23 @@ struct MoeDevice {
   // Shared-expert gate row kept apart from `router` (router then has E rows);
   // null when the row is appended to `router` as row E.
   const float* router_extra_row;
+  // Expert-parallel reduction over peer memory (ep_world > 1): ep_peers is a
+  // device array of every rank's copy of one symmetric buffer (ep_layout()),
+  // and the combine step sums all ranks' partial outputs itself.
+  void* const* ep_peers;
+  int ep_rank, ep_world;
+  int ep_max_tokens;  // tokens per slot of the buffer (the same on every rank)
 };
+
+// Symmetric buffer of the peer-memory reduction, per rank copy:
+//   [0, 512)        per-CTA epoch counters of this rank (local use)
+//   [4096, 8192)    flags[rank q][CTA]: the last epoch rank q pushed for the CTA
+//   [8192, ...)     slots[parity][rank q][ep_max_tokens][hidden] floats
+constexpr int kEpGrid = 128;  // CTAs of the reduction (the same on every rank)
+constexpr int kEpMaxWorld = 8;
+inline size_t ep_buffer_bytes(int world, int max_tokens, int hidden) {
+  return 8192 + (size_t)2 * world * max_tokens * hidden * sizeof(float);
+}
 
 // Scratch for one layer call with up to max_tokens tokens.
 struct MoeWork {

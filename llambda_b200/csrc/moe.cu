@@ -1177,6 +1177,126 @@ __global__ void combine_kernel(MoeDevice m, MoeWork w, int T, const float* x, fl
   }
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Expert-parallel combine with the cross-rank reduction fused in, over peer
+// memory.  CTA c owns a fixed chunk of the T x H outputs on every rank:
+//   1. it forms this rank's partial (its routed experts in rank order, the
+//      shared expert if here) and stores it into slot `rank` of every rank's
+//      buffer (plain stores over NVLink, half of the slots by epoch parity);
+//   2. it raises its flag on every rank (system-scope release after a
+//      fence) and waits, with a bounded spin, for every rank's flag;
+//   3. it sums the slots in rank order, plus the residual when the layer
+//      carries it, so every rank ends with the whole layer output.
+// Epochs are per-CTA counters in device memory, so the kernel can be replayed
+// from a CUDA graph.  A rank can be at most one epoch ahead of another (to
+// push epoch e+2 it needs every flag of e+1, raised only after that rank's
+// sum of e), so two parities of slots suffice.
+__global__ void __launch_bounds__(256) combine_ep_kernel(MoeDevice m, MoeWork w, int T,
+                                                         const float* __restrict__ x,
+                                                         float* __restrict__ out) {
+  __shared__ uint32_t s_epoch;
+  const int H = m.hidden, k = m.top_k, world = m.ep_world, rank = m.ep_rank;
+  const int H4 = H >> 2;
+  uint8_t* self = static_cast<uint8_t*>(m.ep_peers[rank]);
+  if (threadIdx.x == 0) {
+    uint32_t* epochs = reinterpret_cast<uint32_t*>(self);
+    s_epoch = epochs[blockIdx.x] + 1u;
+    epochs[blockIdx.x] = s_epoch;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const size_t slot = (size_t)m.ep_max_tokens * H;  // floats per (parity, rank)
+  const size_t par = (size_t)(epoch & 1u) * world * slot;
+  const long n4 = (long)T * H4;
+  const long c0 = (long)blockIdx.x * n4 / gridDim.x, c1 = (long)(blockIdx.x + 1) * n4 / gridDim.x;
+  const bool shared = m.shared_here && m.inter_sh;
+  for (long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+    const int t = (int)(i / H4), h = (int)(i - (long)t * H4) * 4;
+    const float* p = w.partial + (long)t * (k + 1) * H + h;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int j = 0; j < k; ++j) {
+      const int e = w.sel[t * k + j];
+      const float wt = w.wts[t * k + j];
+      const float4 q = *reinterpret_cast<const float4*>(p + (long)j * H);
+      const bool own = e >= m.expert_begin && e < m.expert_end;
+      acc[0] = __fadd_rn(acc[0], own ? __fmul_rn(wt, q.x) : 0.f);
+      acc[1] = __fadd_rn(acc[1], own ? __fmul_rn(wt, q.y) : 0.f);
+      acc[2] = __fadd_rn(acc[2], own ? __fmul_rn(wt, q.z) : 0.f);
+      acc[3] = __fadd_rn(acc[3], own ? __fmul_rn(wt, q.w) : 0.f);
+    }
+    if (shared) {
+      const float sw = m.arch == 0 ? w.shw[t] : 1.0f;
+      const float4 q = *reinterpret_cast<const float4*>(p + (long)k * H);
+      const float sv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        acc[c] = m.arch == 0 ? __fadd_rn(acc[c], __fmul_rn(sw, sv[c])) : __fadd_rn(acc[c], sv[c]);
+    }
+    const float4 v = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    const size_t off = par + (size_t)rank * slot + (size_t)t * H + h;
+    for (int q = 0; q < world; ++q)
+      *reinterpret_cast<float4*>(static_cast<uint8_t*>(m.ep_peers[q]) + 8192 + off * 4) = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int q = 0; q < world; ++q)
+      st_release_sys(reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(m.ep_peers[q]) + 4096) +
+                         rank * kEpGrid + blockIdx.x,
+                     epoch);
+    const uint32_t* flags = reinterpret_cast<const uint32_t*>(self + 4096);
+    const uint64_t t_start = global_ns();
+    bool late = false;
+    for (int q = 0; q < world && !late; ++q) {
+      while ((int)(ld_acquire_sys(flags + q * kEpGrid + blockIdx.x) - epoch) < 0) {
+        if (global_ns() - t_start > 2000000000ull) {  // bounded: two seconds
+          late = true;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    if (late) atomicOr(w.status, 4);  // a peer never arrived: the output is not valid
+  }
+  __syncthreads();
+  const float* slots = reinterpret_cast<const float*>(self + 8192) + par;
+  for (long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+    const int t = (int)(i / H4), h = (int)(i - (long)t * H4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < world; ++q) {  // rank order; L2 reads (peers wrote them)
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(slots + (size_t)q * slot +
+                                                              (size_t)t * H + h));
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    const long o = (long)t * H + h;
+    if (m.add_residual) {
+      const float4 xv = *reinterpret_cast<const float4*>(x + o);
+      acc = make_float4(__fadd_rn(xv.x, acc.x), __fadd_rn(xv.y, acc.y), __fadd_rn(xv.z, acc.z),
+                        __fadd_rn(xv.w, acc.w));
+    }
+    *reinterpret_cast<float4*>(out + o) = acc;
+  }
+}
+
 template <typename Kern>
 cudaError_t launch_persistent(Kern kern, const UnitPlan& p, cudaStream_t s, MoeDevice m, MoeWork w,
                               int T, int shared_pass) {
@@ -1518,6 +1638,11 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   if (e != cudaSuccess) return e;
   const bool vec = (m.hidden & 3) == 0 &&
                    ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  if (m.ep_world > 1) {  // every rank's partial meets here (peer memory, NVLink)
+    if (!vec || T > m.ep_max_tokens) return cudaErrorInvalidValue;
+    combine_ep_kernel<<<kEpGrid, 256, 0, s>>>(m, w, T, x, out);
+    return cudaGetLastError();
+  }
   const long n = (long)T * m.hidden / (vec ? 4 : 1);
   const int grid = (int)std::min<long>((n + 255) / 256, (long)sm_count() * 8);
   if (vec)
