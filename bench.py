@@ -440,7 +440,9 @@ def run_ours(args):
         ss = sel.cpu().numpy()
         own_distinct.append(int(np.unique(ss[(ss >= eb) & (ss < ee)]).size))
         cur = out
-    layer_bytes = [cfg.router_bytes() + (cfg.shared_bytes() if rank == 0 else 0)
+    from llambda_b200 import ep as _ep
+    streams_shared = _ep.layer_roles(rank, world, cfg.experts, peer)["shared_here"]
+    layer_bytes = [cfg.router_bytes() + (cfg.shared_bytes() if streams_shared else 0)
                    + u * cfg.expert_bytes() + 2 * 4 * B * cfg.hidden for u in own_distinct]
     peak, peak_kind = hbm_peak()
     achieved = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
@@ -509,9 +511,9 @@ def run_ours(args):
                    "sample": f"{B} tokens through 1 qwen3next layer per sample "
                              f"({per_layer * 1e3:.1f} ms), scaled to {NL} layers"}
 
-    # prep, router GEMV, top-k, route, gate/up, routed down, shared down (the
-    # shared expert's rank only), combine
-    launches_per_layer = 8 if rank == 0 else 7
+    # rms-norm + router, top-k, route, gate/up, routed down, shared down (ranks
+    # that compute a share of the shared expert), combine
+    launches_per_layer = 6 + (1 if streams_shared else 0)
     line = {"metric": "MoE FFN decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",

@@ -224,7 +224,8 @@ LLAMBDA_CUDA_API size_t llambda_cuda_moe_peer_bytes(const llambda_cuda_moe_sessi
  * `world` ranks itself (each rank owning a range of experts,
  * expert_begin/expert_end), so every rank ends with the whole layer output
  * (plus the residual when add_residual is set, on every rank) and no
- * all-reduce follows.  peer_buffers[r] is rank r's copy of one symmetric
+ * all-reduce follows.  A rank created with shared_here computes the shared
+ * expert for its part [T*rank/world, T*(rank+1)/world) of the tokens only.  peer_buffers[r] is rank r's copy of one symmetric
  * device buffer of `bytes` bytes (>= llambda_cuda_moe_peer_bytes), mapped
  * into this process, 16-byte aligned and zero-filled before the first run;
  * every session of a stack may share it.  Every rank must then run the same

@@ -660,6 +660,7 @@ int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
         else
           cuda_check(cudaMemsetAsync(r + E * H, 0, H * 4, s->stream), "memset");
         m.router = r;
+        m.router_rows = E + 1;
       }
       if (d->router_bias) {
         if (qwen) throw Failure("A router bias is only defined for nemotron_h_moe.");
@@ -826,6 +827,9 @@ int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_session* s, int rank,
     s->m.ep_rank = rank;
     s->m.ep_world = world;
     s->m.ep_max_tokens = s->max_tokens;
+    // every rank holding the shared expert computes it for its part of the tokens
+    s->m.sh_part = rank;
+    s->m.sh_parts = world;
     return 0;
   });
 }
@@ -932,6 +936,7 @@ lb::MoeDevice static_layer(const llambda_cuda_moe_desc* d) {
                                        &d->up_shexp, &d->down_shexp})
     if (t->data) require_aligned16(t->data, "MoE tensor");
   m.router = static_cast<const float*>(d->router.data);
+  m.router_rows = (int)E;
   m.router_extra_row = qwen && shared ? d->shared_gate_inp : nullptr;
   m.router_bias = d->router_bias;
   m.gate_exps = qwen ? static_cast<const uint8_t*>(d->gate_exps.data) : nullptr;

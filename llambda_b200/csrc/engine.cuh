@@ -97,22 +97,38 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// A try_wait suspends the thread until the phase completes or this many
+// nanoseconds pass, so a waiting warp issues a handful of instructions
+// instead of a spin loop.
+constexpr uint32_t kSuspendNs = 200000;
+// Every wait gives up after this long (a lost copy cannot hang the GPU).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n "
+      "selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
 
 // Bounded wait: returns false (and sets bit 2 of *status) if the phase did
-// not complete within the spin limit, so a lost copy cannot hang the GPU.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// not complete within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  do {
     if (mbar_try_wait(bar, parity)) return true;
+  } while (global_ns() - t0 < kWaitLimitNs);
   if (status) atomicOr(status, 2);
   return false;
 }
@@ -134,10 +150,12 @@ struct RingPos {
 // raised *abort (after its own wait timed out).
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int* status,
                                                    volatile int* abort) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  do {
     if (*abort) return false;
-  }
+    if (mbar_try_wait(bar, parity)) return true;
+  } while (global_ns() - t0 < kWaitLimitNs);
   if (status) atomicOr(status, 2);
   *abort = 1;
   return false;

@@ -87,8 +87,10 @@ __global__ void __launch_bounds__(64) prep_kernel(const float* __restrict__ x, l
   }
 }
 
-// The Q6_K tensor-core layout (mma.cuh, "m6") of token rows: one block per
-// (super-block, token), two warps storing 8 of its 16 sub-blocks each.
+// The Q6_K tensor-core layouts (mma.cuh, "m6", or "i6" with SLOT) of token
+// rows: one block per (super-block, token), two warps storing 8 of its 16
+// sub-blocks each.
+template <bool SLOT>
 __global__ void __launch_bounds__(64) m6_prep_kernel(const float* __restrict__ x, long ldx,
                                                      int n_valid, int K,
                                                      const int* __restrict__ gather,
@@ -106,7 +108,10 @@ __global__ void __launch_bounds__(64) m6_prep_kernel(const float* __restrict__ x
       va = e0 + g < n_valid ? s[e0 + g] : 0.f;
       vb = e0 + g + 8 < n_valid ? s[e0 + g + 8] : 0.f;
     }
-    m6_store_subblock(dst, sb * 16 + sub, va, vb, lane);
+    if (SLOT)
+      i6_store_subblock(dst, sb * 16 + sub, va, vb, lane);
+    else
+      m6_store_subblock(dst, sb * 16 + sub, va, vb, lane);
   }
 }
 
@@ -118,13 +123,14 @@ __global__ void __launch_bounds__(64) m6_prep_kernel(const float* __restrict__ x
 // [w*nsb/CW, (w+1)*nsb/CW) of every block, and warp 0 adds the other warps'
 // sums (in warp order) and writes the rows.  NG groups of 4 tokens share the
 // decoded weights; the tokens' prepared inputs (m6) are read through L1.
+// SLOT: one or two tokens (NG of them) in the sub-block slot form (i6).
 struct DenseSync {
   uint64_t full[8], empty[8], red[8];
   int abort;
   int pad[3];
 };
 
-template <int NG, int CW>
+template <int NG, int CW, bool SLOT>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     gemv_q6k_slab_kernel(const uint8_t* __restrict__ W, size_t rb, int rows, int nsb,
                          const uint8_t* __restrict__ m6, int tokens, float* __restrict__ y,
@@ -178,9 +184,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     float2 acc[NG];
 #pragma unroll
     for (int grp = 0; grp < NG; ++grp) acc[grp] = make_float2(0.f, 0.f);
-    for (int sb = sb0; sb < sb1; ++sb)
-      q6k_sb_mma<false, NG>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, m6p,
-                            tokens, lane, acc);
+    if (SLOT) {
+      q6i_block<false, NG>(blk, rb, sb0, sb1, m6p, kZero32, lane, 0, acc[0]);
+    } else {
+      for (int sb = sb0; sb < sb1; ++sb)
+        q6k_sb_mma<false, NG>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb,
+                              m6p, tokens, lane, acc);
+    }
     float2* rs = red + (size_t)s * CW * 32 * NG;
     if (warp != 0) {
 #pragma unroll
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       if (lane == 0) mbar_arrive(&sync->empty[s]);
       const int row = (u0 + i) * kTileRows + g;
 #pragma unroll
-      for (int grp = 0; grp < NG; ++grp) {
+      for (int grp = 0; grp < (SLOT ? 1 : NG); ++grp) {
         const int n = 4 * grp + t;
         if (n < tokens) {
           y[(long)n * ldy + row] = acc[grp].x;
@@ -567,7 +577,7 @@ cudaError_t launch_q4k_mma(const void* W, size_t rb, int rows, int K, const floa
   return cudaGetLastError();
 }
 
-template <int NG>
+template <int NG, bool SLOT>
 cudaError_t launch_q6k_slab(const void* W, size_t rb, int rows, int K, const uint8_t* m6,
                             int tokens, float* y, long ldy, int* status, cudaStream_t stream) {
   const int nsb = K / 256;
@@ -581,12 +591,12 @@ cudaError_t launch_q6k_slab(const void* W, size_t rb, int rows, int K, const uin
   const int units = rows / kTileRows;
   const int grid = std::max(1, std::min(units, sm_count()));
   if (wide) {
-    auto kern = gemv_q6k_slab_kernel<NG, 16>;
+    auto kern = gemv_q6k_slab_kernel<NG, 16, SLOT>;
     if (prepared_occupancy(kern, 17 * 32, smem) < 1) return cudaErrorUnknown;
     kern<<<grid, 17 * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, nsb, m6,
                                           tokens, y, ldy, stages, stage_bytes, status);
   } else {
-    auto kern = gemv_q6k_slab_kernel<NG, 8>;
+    auto kern = gemv_q6k_slab_kernel<NG, 8, SLOT>;
     if (prepared_occupancy(kern, 9 * 32, smem) < 1) return cudaErrorUnknown;
     kern<<<grid, 9 * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, nsb, m6,
                                          tokens, y, ldy, stages, stage_bytes, status);
@@ -602,8 +612,10 @@ size_t xprep_floats(int K, int tokens) {
   return std::max({(size_t)xp_stride(K), mx_bytes(K) / 4, m6_bytes(K) / 4}) * tokens;
 }
 
-// Q6_K matrices of whole 16-row blocks run on the tensor cores.
+// Q6_K matrices of whole 16-row blocks run on the tensor cores, one or two
+// tokens in the sub-block slot form.
 static bool q6k_dense_mma(int rows) { return rows % kTileRows == 0; }
+static bool q6k_dense_slots(int tokens) { return tokens <= 2; }
 
 cudaError_t launch_prep(int type, int rows, const float* x, long ldx, int n_valid, int K,
                         int tokens, const int* gather, float* xp, cudaStream_t stream) {
@@ -612,9 +624,12 @@ cudaError_t launch_prep(int type, int rows, const float* x, long ldx, int n_vali
   dim3 grid(K / 256, tokens);
   if (type == LB_TYPE_Q4_K)
     prep_kernel<LB_TYPE_Q4_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
+  else if (type == LB_TYPE_Q6_K && q6k_dense_mma(rows) && q6k_dense_slots(tokens))
+    m6_prep_kernel<true><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather,
+                                                  reinterpret_cast<uint8_t*>(xp));
   else if (type == LB_TYPE_Q6_K && q6k_dense_mma(rows))
-    m6_prep_kernel<<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather,
-                                            reinterpret_cast<uint8_t*>(xp));
+    m6_prep_kernel<false><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather,
+                                                   reinterpret_cast<uint8_t*>(xp));
   else if (type == LB_TYPE_Q6_K)
     prep_kernel<LB_TYPE_Q6_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
   else
@@ -635,13 +650,16 @@ cudaError_t launch_gemv_prepped(int type, const void* W, size_t rb, int rows, in
   LB_DENSE(T, 16, 4) LB_DENSE(T, 32, 1) LB_DENSE(T, 32, 2) LB_DENSE(T, 32, 4)
   if (type == LB_TYPE_Q6_K && q6k_dense_mma(rows)) {
     const uint8_t* m6 = reinterpret_cast<const uint8_t*>(xp);
+    if (q6k_dense_slots(tokens))
+      return tokens == 1 ? launch_q6k_slab<1, true>(W, rb, rows, K, m6, 1, y, ldy, status, stream)
+                         : launch_q6k_slab<2, true>(W, rb, rows, K, m6, 2, y, ldy, status, stream);
     for (int t0 = 0; t0 < tokens; t0 += 8) {  // 8 tokens per pass over the weights
       const int nt = std::min(8, tokens - t0);
       const cudaError_t e =
-          nt <= 4 ? launch_q6k_slab<1>(W, rb, rows, K, m6 + (size_t)t0 * m6_bytes(K), nt,
-                                       y + (long)t0 * ldy, ldy, status, stream)
-                  : launch_q6k_slab<2>(W, rb, rows, K, m6 + (size_t)t0 * m6_bytes(K), nt,
-                                       y + (long)t0 * ldy, ldy, status, stream);
+          nt <= 4 ? launch_q6k_slab<1, false>(W, rb, rows, K, m6 + (size_t)t0 * m6_bytes(K), nt,
+                                              y + (long)t0 * ldy, ldy, status, stream)
+                  : launch_q6k_slab<2, false>(W, rb, rows, K, m6 + (size_t)t0 * m6_bytes(K), nt,
+                                              y + (long)t0 * ldy, ldy, status, stream);
       if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -68,7 +68,8 @@ struct MoeDevice {
   int k_in_sh;       // shared gate/up row width
   int gate_type, up_type, down_type;
   int gate_sh_type, up_sh_type, down_sh_type;
-  const float* router;      // [E (+1 for the qwen3next shared gate row)][H]
+  const float* router;      // [router_rows][H]
+  int router_rows;          // E, or E + 1 with the qwen3next shared-gate row appended
   const float* router_bias; // [E] or null
   const uint8_t* gate_exps; // null for nemotron
   const uint8_t* up_exps;
@@ -92,7 +93,22 @@ struct MoeDevice {
   void* const* ep_peers;
   int ep_rank, ep_world;
   int ep_max_tokens;  // tokens per slot of the buffer (the same on every rank)
+  // With shared_here, the shared expert is computed for tokens
+  // [T*sh_part/sh_parts, T*(sh_part+1)/sh_parts) only (sh_parts <= 1: all):
+  // expert-parallel ranks split its tokens, and the rank sum reunites them.
+  int sh_part, sh_parts;
 };
+
+// The tokens [t0, t1) of a T-token call the shared expert is computed for.
+__host__ __device__ inline void shared_tokens(const MoeDevice& m, int T, int& t0, int& t1) {
+  if (m.sh_parts <= 1) {
+    t0 = 0;
+    t1 = T;
+  } else {
+    t0 = (int)((long)T * m.sh_part / m.sh_parts);
+    t1 = (int)((long)T * (m.sh_part + 1) / m.sh_parts);
+  }
+}
 
 // Symmetric buffer of the peer-memory reduction, per rank copy:
 //   [0, 512)        per-CTA epoch counters of this rank (local use)

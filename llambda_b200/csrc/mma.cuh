@@ -161,6 +161,16 @@ __device__ __forceinline__ uint4 ld_b16(const void* p) {
   if (SMEM) return *reinterpret_cast<const uint4*>(p);
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
+template <bool SMEM>
+__device__ __forceinline__ uint2 ld_b8(const void* p) {
+  if (SMEM) return *reinterpret_cast<const uint2*>(p);
+  return __ldg(reinterpret_cast<const uint2*>(p));
+}
+
+// 32 zero bytes in global memory (the B source of the threads without a
+// column of their own when the inputs are read through L1).
+static __device__ __align__(16) const uint8_t kZero32[32] = {};
+
 
 // Adds to y[n][r] (r = 0: row g, r = 1: row g + 8 of a 16-row block; .x the
 // even sub-block of the lane's slot, .y the odd one) this lane's share of the
@@ -168,10 +178,11 @@ __device__ __forceinline__ uint4 ld_b16(const void* p) {
 // bs (SMEM: the slices are in shared memory).  rg / rg8: the super-block of
 // rows g and g+8 in shared memory (16-byte aligned; the 8 row groups must
 // fall in different bank groups, e.g. rows 144 bytes apart or a pitch of 16
-// mod 128).
+// mod 128).  bz: 32 zero bytes in the slices' memory, the B source of the
+// threads whose column cannot be non-zero.
 template <int NT, bool SMEM>
 __device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8,
-                                           const BSlice (&bs)[NT], int lane,
+                                           const BSlice (&bs)[NT], const uint8_t* bz, int lane,
                                            float2 (&y)[NT][2]) {
   const int g = lane >> 2, t = lane & 3;
   const bool bthread = t == (g >> 1);  // the lane whose B column g can be non-zero
@@ -192,12 +203,9 @@ __device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8
       uint4 be[NT], bo[NT];  // B of k-steps j, j+1 (even set, odd set)
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
-        be[n] = bo[n] = make_uint4(0, 0, 0, 0);
-        if (bthread) {
-          const uint4* fr = reinterpret_cast<const uint4*>(bs[n].frag) + g * 4;
-          be[n] = ld_b16<SMEM>(fr + j / 2);
-          bo[n] = ld_b16<SMEM>(fr + 32 + j / 2);
-        }
+        const uint4* fr = reinterpret_cast<const uint4*>(bs[n].frag) + g * 4;
+        be[n] = ld_b16<SMEM>(bthread ? reinterpret_cast<const uint8_t*>(fr + j / 2) : bz);
+        bo[n] = ld_b16<SMEM>(bthread ? reinterpret_cast<const uint8_t*>(fr + 32 + j / 2) : bz);
       }
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
@@ -241,15 +249,15 @@ __device__ __forceinline__ void q4k_sb_mma(const uint8_t* rg, const uint8_t* rg8
 // q4k_sb_mma for nt (1..NT) tokens: the first nt entries of bs and y.
 template <int NT, bool SMEM>
 __device__ __forceinline__ void q4k_sb_mma_n(int nt, const uint8_t* rg, const uint8_t* rg8,
-                                             const BSlice (&bs)[NT], int lane,
-                                             float2 (&y)[NT][2]) {
+                                             const BSlice (&bs)[NT], const uint8_t* bz,
+                                             int lane, float2 (&y)[NT][2]) {
   if constexpr (NT == 1) {
-    q4k_sb_mma<1, SMEM>(rg, rg8, bs, lane, y);
+    q4k_sb_mma<1, SMEM>(rg, rg8, bs, bz, lane, y);
   } else {
     if (nt >= NT)
-      q4k_sb_mma<NT, SMEM>(rg, rg8, bs, lane, y);
+      q4k_sb_mma<NT, SMEM>(rg, rg8, bs, bz, lane, y);
     else
-      q4k_sb_mma_n<NT - 1, SMEM>(nt, rg, rg8, reinterpret_cast<const BSlice(&)[NT - 1]>(bs),
+      q4k_sb_mma_n<NT - 1, SMEM>(nt, rg, rg8, reinterpret_cast<const BSlice(&)[NT - 1]>(bs), bz,
                                  lane, reinterpret_cast<float2(&)[NT - 1][2]>(y));
   }
 }
@@ -267,7 +275,7 @@ __device__ __forceinline__ void q4k_tile_mma(const uint8_t* tile, int pitch, int
     BSlice bs[NT];
 #pragma unroll
     for (int n = 0; n < NT; ++n) bs[n] = mx_slice(mx[n], sb, nsb);
-    q4k_sb_mma_n<NT, false>(nt, rg, rg + 8 * pitch, bs, lane, y);
+    q4k_sb_mma_n<NT, false>(nt, rg, rg + 8 * pitch, bs, kZero32, lane, y);
   }
 }
 
@@ -505,6 +513,215 @@ __device__ __forceinline__ void q6k_sb_mma(const uint8_t* rg, const uint8_t* rg8
       }
     }
   }
+}
+
+// ----------------------------------------------- Q6_K rows, sub-block slots
+//
+// With one or two tokens most of the eight B columns of the form above are
+// empty while every k-step still pays for a scale and three fp32 updates per
+// thread.  This form gives the four threads of a quad four different
+// sub-blocks instead (the Q4_K slot mapping): in k-step j of a group of four,
+// thread t supplies values 4j..4j+3 of its own sub-block at k = 2t, 2t+1,
+// 2t+8, 2t+9, and B column 2u + part carries slot u's activations at thread
+// u's positions and zeros elsewhere, so after four k-steps D columns 2t, 2t+1
+// hold thread t's whole sub-block sums (high and low part) for rows g and
+// g+8, and the scale work falls to once per sub-block.  One mma per token and
+// k-step; the decoded A serves every token.
+//
+// Thread t owns sub-blocks 4i + t of each super-block: in 64-byte chunk c it
+// reads ql run t (bytes 64c + 16t.., low nibbles: sub-block 8c + t, high
+// nibbles: 8c + 4 + t) and qh run t & 1 (bytes 128 + 32c + 16(t & 1).., bits
+// 2(t >> 1) and 4 + 2(t >> 1)), with the chunk's scale bytes 8c + t and
+// 8c + 4 + t.  The quad's four partial sums are added once per row block.
+//
+// Prepared input of one entry ("i6", i6_bytes(K), 1152 bytes per 256 values):
+//   frag[s][part][j] : uint2, halves (x[4j], x[4j+2]) and (x[4j+1], x[4j+3])
+//       of sub-block s, scaled, part 0 = high, 1 = low (1024 bytes);
+//   meta[s] : float2 (back, -32 * sum(x)) of sub-block s (128 bytes).
+__host__ __device__ __forceinline__ size_t i6_bytes(int K) { return (size_t)(K / 256) * 1152; }
+
+// Stores sub-block s_glob of one entry: lane (g, 0) holds value g in va and
+// value g + 8 in vb; the other lanes pass zeros.  Whole warp.
+__device__ __forceinline__ void i6_store_subblock(uint8_t* xi, int s_glob, float va, float vb,
+                                                  int lane) {
+  float amax = fmaxf(fabsf(va), fabsf(vb)), sum = va + vb;
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  int ex = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 126;  // as in mx_store4
+  ex = min(max(ex, -100), 100);
+  const float f = pow2f(11 - ex);
+  uint8_t* base = xi + (size_t)(s_glob >> 4) * 1152;
+  const int sl = s_glob & 15;
+  if ((lane & 3) == 0) {
+    const int g = lane >> 2;
+    __half* h = reinterpret_cast<__half*>(base);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = g + 8 * r;
+      const float xs = (r ? vb : va) * f;
+      const __half hi = __float2half_rn(xs);
+      const __half lo = __float2half_rn(xs - __half2float(hi));
+      const int j = i >> 2, pos = i & 3, hp = (pos & 1) * 2 + (pos >> 1);
+      h[(sl * 2 + 0) * 16 + j * 4 + hp] = hi;
+      h[(sl * 2 + 1) * 16 + j * 4 + hp] = lo;
+    }
+    if (g == 0)
+      reinterpret_cast<float2*>(base + 1024)[sl] = make_float2(pow2f(ex + 13), -32.0f * sum);
+  }
+}
+
+// Zeroes sub-block s_glob of an i6 buffer (padding past the matrix's rows).
+// 16 lanes; lane l < 8 writes 8 bytes of the fragments, lane 0 the meta.
+__device__ __forceinline__ void i6_zero_subblock(uint8_t* xi, int s_glob, int l) {
+  uint8_t* base = xi + (size_t)(s_glob >> 4) * 1152;
+  const int sl = s_glob & 15;
+  if (l < 8) reinterpret_cast<uint2*>(base)[sl * 8 + l] = make_uint2(0, 0);  // (part, j) = l
+  if (l == 0) reinterpret_cast<float2*>(base + 1024)[sl] = make_float2(0.f, 0.f);
+}
+
+// N little-endian words from a shared-memory address p that is 4-byte
+// aligned (MIS = 0), 2 past a multiple of 4 (MIS = 1: N + 1 aligned loads and
+// one byte permute per word) or either (MIS = 2: decided per thread).
+template <int MIS, int N>
+__device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t (&w)[N]) {
+  if (MIS == 0) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = reinterpret_cast<const uint32_t*>(p)[i];
+  } else {
+    const int mis = MIS == 1 ? 2 : (int)(reinterpret_cast<uintptr_t>(p) & 2);
+    const uint32_t* a = reinterpret_cast<const uint32_t*>(p - mis);  // keeps the address space
+    const uint32_t sel = mis ? 0x5432u : 0x3210u;
+    uint32_t v[N + 1];
+#pragma unroll
+    for (int i = 0; i <= N; ++i) v[i] = a[i];  // within the super-block: runs end by byte 208
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = __byte_perm(v[i], v[i + 1], sel);
+  }
+}
+
+// Adds this thread's share of the dot products of super-block sb of a 16-row
+// Q6_K block with NTOK tokens to y[n] (.x row g, .y row g+8): only sub-blocks
+// 4i + t enter, the caller adds the quad.  rg / rg8: the super-block of rows
+// g and g+8 in shared memory (alignment as MIS of lds_words); xi[n]: token
+// n's i6 buffer (SMEM: in shared memory); bz: 32 zero bytes in the same
+// memory, the B source of the threads that carry no column of theirs.
+template <bool SMEM, int NTOK, int MIS>
+__device__ __forceinline__ void q6i_sb_mma(const uint8_t* rg, const uint8_t* rg8, int sb,
+                                           const uint8_t* const (&xi)[NTOK], const uint8_t* bz,
+                                           int lane, float2 (&y)[NTOK]) {
+  const int g = lane >> 2, t = lane & 3;
+  const bool bcol = (g >> 1) == t;  // this thread carries B column g (slot t, part g & 1)
+  const uint32_t ssel = 0x7440u | (uint32_t)t;
+  const int hsh = 2 * (t >> 1);
+  const float d = half_bits_to_float(lds_u16(rg + 208));
+  const float d8 = half_bits_to_float(lds_u16(rg8 + 208));
+  const size_t sbo = (size_t)sb * 1152;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t lg[4], l8[4], hg[4], h8[4], sw[2], s8w[2];
+    lds_words<MIS>(rg + 64 * c + 16 * t, lg);
+    lds_words<MIS>(rg8 + 64 * c + 16 * t, l8);
+    lds_words<MIS>(rg + 128 + 32 * c + 16 * (t & 1), hg);
+    lds_words<MIS>(rg8 + 128 + 32 * c + 16 * (t & 1), h8);
+    lds_words<MIS>(rg + 192 + 8 * c, sw);
+    lds_words<MIS>(rg8 + 192 + 8 * c, s8w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      hg[j] >>= hsh;
+      h8[j] >>= hsh;
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {  // n = 0: low nibbles, sub-block 8c + t; 1: high, 8c + 4 + t
+      // scale byte 8c + 4n + t of rows g and g+8 (int8, exactly)
+      const float2 dsc = __fmul2_rn(
+          make_float2(d, d8),
+          __fadd2_rn(
+              make_float2(__uint_as_float(__byte_perm(sw[n] ^ 0x80808080u, 0x4B000000u, ssel)),
+                          __uint_as_float(__byte_perm(s8w[n] ^ 0x80808080u, 0x4B000000u, ssel))),
+              make_float2(-8388736.0f, -8388736.0f)));
+      const int so = (8 * c + 4 * n) * 64;  // first fragment byte of the four sub-blocks
+      uint4 b01[NTOK], b23[NTOK];
+      float2 mt[NTOK];
+#pragma unroll
+      for (int k = 0; k < NTOK; ++k) {
+        const uint8_t* pb = bcol ? xi[k] + sbo + so + g * 32 : bz;
+        b01[k] = ld_b16<SMEM>(pb);
+        b23[k] = ld_b16<SMEM>(pb + 16);
+        const uint2 mu = ld_b8<SMEM>(xi[k] + sbo + 1024 + (8 * c + 4 * n + t) * 8);
+        mt[k] = make_float2(__uint_as_float(mu.x), __uint_as_float(mu.y));
+      }
+      float acc[NTOK][4];
+#pragma unroll
+      for (int k = 0; k < NTOK; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t qg, q8;
+        if (n == 0) {
+          qg = (lg[j] & 0x0F0F0F0Fu) | ((hg[j] << 4) & 0x30303030u);
+          q8 = (l8[j] & 0x0F0F0F0Fu) | ((h8[j] << 4) & 0x30303030u);
+        } else {
+          qg = ((lg[j] >> 4) & 0x0F0F0F0Fu) | (hg[j] & 0x30303030u);
+          q8 = ((l8[j] >> 4) & 0x0F0F0F0Fu) | (h8[j] & 0x30303030u);
+        }
+        const uint32_t a0 = __byte_perm(qg, 0, 0x4240), a1 = __byte_perm(q8, 0, 0x4240);
+        const uint32_t a2 = __byte_perm(qg, 0, 0x4341), a3 = __byte_perm(q8, 0, 0x4341);
+#pragma unroll
+        for (int k = 0; k < NTOK; ++k) {
+          const uint4& bl = j < 2 ? b01[k] : b23[k];
+          mma_f16(acc[k], a0, a1, a2, a3, (j & 1) ? bl.z : bl.x, (j & 1) ? bl.w : bl.y);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < NTOK; ++k) {
+        float2 s2 = __fadd2_rn(make_float2(acc[k][0], acc[k][2]), make_float2(acc[k][1], acc[k][3]));
+        s2 = __ffma2_rn(s2, make_float2(mt[k].x, mt[k].x), make_float2(mt[k].y, mt[k].y));
+        y[k] = __ffma2_rn(dsc, s2, y[k]);
+      }
+    }
+  }
+}
+
+// One 16-row Q6_K block (rows of rb bytes from blk, 16-byte aligned in shared
+// memory) times NTOK tokens xin[0..NTOK) over super-blocks [sb0, sb1):
+// returns, in thread t of quad g, rows g and g+8 for token t - tok0 (the
+// quad's threads summed), r unchanged where that is not one of the NTOK.
+template <bool SMEM, int NTOK>
+__device__ __forceinline__ void q6i_block(const uint8_t* blk, size_t rb, int sb0, int sb1,
+                                          const uint8_t* const* xin, const uint8_t* bz, int lane,
+                                          int tok0, float2& r) {
+  const uint8_t* xi[NTOK];
+#pragma unroll
+  for (int n = 0; n < NTOK; ++n) xi[n] = xin[n];
+  float2 y[NTOK];
+#pragma unroll
+  for (int n = 0; n < NTOK; ++n) y[n] = make_float2(0.f, 0.f);
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* rg = blk + g * rb;
+  const uint8_t* rg8 = blk + (g + 8) * rb;
+  if ((rb & 3) == 0) {  // rows 4-byte aligned: super-blocks at 0 and 2 mod 4 in turn
+    for (int sb = sb0; sb < sb1; ++sb) {
+      if (sb & 1)
+        q6i_sb_mma<SMEM, NTOK, 1>(rg + sb * LB_Q6K, rg8 + sb * LB_Q6K, sb, xi, bz, lane, y);
+      else
+        q6i_sb_mma<SMEM, NTOK, 0>(rg + sb * LB_Q6K, rg8 + sb * LB_Q6K, sb, xi, bz, lane, y);
+    }
+  } else {
+    for (int sb = sb0; sb < sb1; ++sb)
+      q6i_sb_mma<SMEM, NTOK, 2>(rg + sb * LB_Q6K, rg8 + sb * LB_Q6K, sb, xi, bz, lane, y);
+  }
+#pragma unroll
+  for (int n = 0; n < NTOK; ++n)
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+      y[n].x += __shfl_xor_sync(0xffffffffu, y[n].x, o);
+      y[n].y += __shfl_xor_sync(0xffffffffu, y[n].y, o);
+    }
+#pragma unroll
+  for (int n = 0; n < NTOK; ++n)
+    if (t == tok0 + n) r = y[n];
 }
 
 // ------------------------------------------------------------ tile staging

@@ -50,10 +50,10 @@ __host__ __device__ __forceinline__ long up_ld_floats(int K) {
 }
 
 // Floats per entry of the prepared down input: room for the warp engine's
-// layout and for the Q6_K tensor-core layout (m6, mma.cuh).
+// layout and for the Q6_K tensor-core layout (i6, mma.cuh).
 __host__ __device__ __forceinline__ long down_ld_floats(const MoeDevice& m) {
   const int K = m.k_down > m.k_down_sh ? m.k_down : m.k_down_sh;
-  const long a = xp_stride(K), b = (long)(m6_bytes(K) / 4);
+  const long a = xp_stride(K), b = (long)(i6_bytes(K) / 4);
   return a > b ? a : b;
 }
 
@@ -88,19 +88,18 @@ __device__ __forceinline__ uint32_t topk_key(float v) {
 }
 
 // The k best scores of one token, in the order the reference's repeated
-// strict-> scan finds them (descending score, ties to the lower index).  The
-// k-th largest key is found bit by bit from warp-wide counts; every key above
-// it is taken and the ties at it in index order, and the k
-// winners are ranked by (score, index).  PER: candidates per lane (E <= 32*PER).
+// strict-> scan finds them (descending score, ties to the lower index), by k
+// rounds of a warp-wide argmax: every lane keeps the best of its own PER
+// candidates (the lowest index among equal keys), the round's winner is the
+// highest key and, among lanes holding it, the lowest index (two warp
+// reductions), and only the winning lane rescans its candidates.  PER:
+// candidates per lane (E <= 32*PER); key 0 marks a score that is never
+// selected (NaN, -inf, -FLT_MAX and below).
 template <int PER>
 __global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T) {
-  __shared__ float s_val[32];
-  __shared__ uint32_t s_key[32];
-  __shared__ int s_idx[32];
   const int t = blockIdx.x, lane = threadIdx.x;
   const int E = m.experts, k = m.top_k;
   const float* L = w.logits + (long)t * (E + 1);
-  const unsigned lt_mask = (1u << lane) - 1u;
   float lv[PER];
   uint32_t key[PER];
 #pragma unroll
@@ -116,63 +115,44 @@ __global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T)
     lv[q] = v;
     key[q] = kq;
   }
-  // the k-th largest key by a bitwise search over warp-wide counts (a byte
-  // histogram would serialise: the top bytes of nearby scores coincide)
-  auto count_ge = [&](uint32_t c) {
-    unsigned n = 0;
+  uint32_t bk = 0u;  // this lane's best key, its slot and score
+  int bq = 0;
+  float bv = 0.f;
+  auto rescan = [&]() {
+    bk = 0u;
+    bq = 0;
+    bv = 0.f;
 #pragma unroll
-    for (int q = 0; q < PER; ++q) n += key[q] >= c ? 1u : 0u;
-    return (int)__reduce_add_sync(0xffffffffu, n);
+    for (int q = 0; q < PER; ++q)
+      if (key[q] > bk) {
+        bk = key[q];
+        bq = q;
+        bv = lv[q];
+      }
   };
-  uint32_t th = 0u;  // the k-th largest key (0: fewer than k selectable scores)
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t c = th | (1u << bit);
-    if (count_ge(c) >= k) th = c;
-  }
-  // its rank among the keys equal to it (keys of valid scores are >= 1)
-  int krem = th == 0u ? 0 : k - (th == 0xFFFFFFFFu ? 0 : count_ge(th + 1u));
-  const int need = krem;  // ties at th to take, lowest index first
-  int nsel = 0, tie_base = 0;
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const bool eq = th != 0u && key[q] == th;
-    const unsigned eqm = __ballot_sync(0xffffffffu, eq);
-    const bool take = key[q] > th || (eq && tie_base + __popc(eqm & lt_mask) < need);
-    tie_base += __popc(eqm);
-    const unsigned tm = __ballot_sync(0xffffffffu, take);
-    if (take && nsel + __popc(tm & lt_mask) < 32) {
-      const int pos = nsel + __popc(tm & lt_mask);
-      s_val[pos] = lv[q];
-      s_key[pos] = key[q];
-      s_idx[pos] = lane + 32 * q;
-    }
-    nsel += __popc(tm);
-  }
-  nsel = min(nsel, k);
-  __syncwarp();
+  rescan();
+  // lane r keeps round r's expert and score (-1: fewer than k selectable)
   float my_v = 0.f;
   int my_i = -1;
-  uint32_t my_k = 0u;
-  if (lane < nsel) {
-    my_v = s_val[lane];
-    my_k = s_key[lane];
-    my_i = s_idx[lane];
+  for (int r = 0; r < k; ++r) {
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+    if (mk == 0u) break;  // uniform: no selectable score left
+    const uint32_t win =
+        __reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)(lane + 32 * bq) : 0xffffffffu);
+    const int wl = (int)(win & 31u);
+    const float v = __shfl_sync(0xffffffffu, bv, wl);
+    if (lane == r) {
+      my_i = (int)win;
+      my_v = v;
+    }
+    if (lane == wl) {
+      const int wq = (int)(win >> 5);
+#pragma unroll
+      for (int q = 0; q < PER; ++q)
+        if (q == wq) key[q] = 0u;
+      rescan();
+    }
   }
-  int rank = 0;
-  for (int j = 0; j < nsel; ++j) {
-    const uint32_t kj = s_key[j];
-    const int ij = s_idx[j];
-    rank += (kj > my_k || (kj == my_k && ij < my_i)) ? 1 : 0;
-  }
-  __syncwarp();
-  if (lane < nsel) {
-    s_val[rank] = my_v;
-    s_idx[rank] = my_i;
-  }
-  __syncwarp();
-  // lane j keeps rank j's expert and score (-1: fewer than k selectable)
-  my_v = lane < nsel ? s_val[lane] : 0.f;
-  my_i = lane < nsel ? s_idx[lane] : -1;
   // sigmoid per rank in parallel; the sum runs in rank order, as in L5367-5372
   float wv = lane < k ? sigmoid_ref(my_v) : 0.f;
   float wsum = 0.f;
@@ -329,7 +309,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
   const float* xt = x + (long)blockIdx.x * H;
   const int nchunk = (K + 1023) >> 10;
   if (threadIdx.x == 0) {  // the router GEMV that follows finds its weights in L2
-    const int rows = m.experts + (m.arch == 0 && !m.router_extra_row ? 1 : 0);
+    const int rows = m.router_rows;
     const size_t bytes = (size_t)rows * H * sizeof(float);
     const size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
     const size_t lo = (size_t)blockIdx.x * per;
@@ -404,6 +384,128 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
     const int e = c * 1024 + 4 * threadIdx.x;
     if (e < K) emit(e, load4(e));
   }
+}
+
+// Prep and router in one kernel (Q4_K gate/up): a CTA takes 8 tokens and 16
+// router rows, which arrive by two bulk copies; the token tile is
+// rms-normalised in shared memory (rms-norm-into, L859-879), the warps of
+// all row tiles share the writes of the tokens' prepared gate/up input (one
+// super-block of one token each), and every CTA forms its 16 x 8 logits (dot-product-with-f32-tensor-data, L4096-4107) with
+// packed fp32x2 FMAs and a 31-shuffle butterfly.  Row E of qwen3next (the
+// shared-expert gate) comes from router_extra_row when it is kept apart.
+constexpr int kRouterTok = 8, kRouterRows = 16;
+__global__ void __launch_bounds__(128) moe_router_kernel(MoeDevice m, MoeWork w,
+                                                         const float* __restrict__ x, int T,
+                                                         int router_rows) {
+  extern __shared__ float4 rs4[];  // [8][H/4] tokens, then [16][H/4] router rows
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float s_scale[kRouterTok];
+  const int H = m.hidden, H4 = H >> 2, E = m.experts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * kRouterTok, nt = min(kRouterTok, T - t0);
+  const int crow0 = blockIdx.x * kRouterRows, crows = min(kRouterRows, router_rows - crow0);
+  const int main_end = m.router_rows;  // rows of m.router; then router_extra_row
+  const int main_rows = max(0, min(crows, main_end - crow0));
+  float4* xs4 = rs4;
+  float4* ws4 = rs4 + kRouterTok * H4;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    const uint32_t rowb = (uint32_t)H * 4u;
+    mbar_expect_tx(&bar, rowb * (uint32_t)(nt + crows));
+    tma_load_1d(xs4, x + (long)t0 * H, rowb * nt, &bar);
+    if (main_rows > 0) tma_load_1d(ws4, m.router + (size_t)crow0 * H, rowb * main_rows, &bar);
+    if (main_rows < crows)  // row E, the last row of the last tile
+      tma_load_1d(ws4 + (size_t)main_rows * H4, m.router_extra_row, rowb, &bar);
+  }
+  for (int i = nt * H4 + threadIdx.x; i < kRouterTok * H4; i += blockDim.x)
+    xs4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  mbar_wait(&bar, 0, w.status);
+  if (m.input_norm) {
+    for (int tok = warp; tok < nt; tok += 4) {
+      float acc = 0.f;
+      for (int c = lane; c < H4; c += 32) {
+        const float4 v = xs4[tok * H4 + c];
+        acc = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, acc))));
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) {
+        const float ms = __fdiv_rn(acc, (float)H);
+        s_scale[tok] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, m.norm_epsilon)));
+      }
+    }
+    __syncthreads();
+    const float4* nw4 = reinterpret_cast<const float4*>(m.input_norm);
+    for (int i = threadIdx.x; i < nt * H4; i += blockDim.x) {
+      const int tok = i / H4;
+      const float sc = s_scale[tok];
+      const float4 v = xs4[i], g = __ldg(nw4 + (i - tok * H4));
+      xs4[i] = make_float4(__fmul_rn(__fmul_rn(v.x, g.x), sc), __fmul_rn(__fmul_rn(v.y, g.y), sc),
+                           __fmul_rn(__fmul_rn(v.z, g.z), sc), __fmul_rn(__fmul_rn(v.w, g.w), sc));
+    }
+    __syncthreads();
+  }
+  {  // the experts' prepared input (zero-padded from H to k_in): the row tiles'
+     // warps share the tokens' (token, super-block) items
+    const int K = m.k_in, nsb = K >> 8;
+    const long ld_up = up_ld_floats(K);
+    for (int it = blockIdx.x * 4 + warp; it < nt * nsb; it += gridDim.x * 4) {
+      const int tok = it / nsb, sb = it - tok * nsb;
+      uint8_t* mx = reinterpret_cast<uint8_t*>(w.xp_up + (long)(t0 + tok) * ld_up);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = sb * 256 + h * 128 + lane * 4;
+        mx_store4(mx, K, e, e < H ? xs4[tok * H4 + (e >> 2)] : make_float4(0.f, 0.f, 0.f, 0.f));
+      }
+    }
+  }
+  const int row0 = warp * 4;  // this warp's 4 rows of the tile
+  if (row0 >= crows) return;
+  float2 acc[4][kRouterTok / 2];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int p = 0; p < kRouterTok / 2; ++p) acc[r][p] = make_float2(0.f, 0.f);
+  const float4* wr[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) wr[r] = ws4 + (size_t)min(row0 + r, crows - 1) * H4;
+  for (int c = lane; c < H4; c += 32) {
+    float4 wv[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) wv[r] = wr[r][c];
+#pragma unroll
+    for (int p = 0; p < kRouterTok / 2; ++p) {
+      const float4 xa = xs4[(2 * p) * H4 + c], xb = xs4[(2 * p + 1) * H4 + c];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].x, wv[r].x), make_float2(xa.x, xb.x), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].y, wv[r].y), make_float2(xa.y, xb.y), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].z, wv[r].z), make_float2(xa.z, xb.z), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].w, wv[r].w), make_float2(xa.w, xb.w), acc[r][p]);
+      }
+    }
+  }
+  float v[32];  // value r * 8 + n ends on lane r * 8 + n
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int p = 0; p < kRouterTok / 2; ++p) {
+      v[r * 8 + 2 * p] = acc[r][p].x;
+      v[r * 8 + 2 * p + 1] = acc[r][p].y;
+    }
+#pragma unroll
+  for (int h = 16; h >= 1; h >>= 1) {
+    const bool upper = (lane & h) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = upper ? v[i] : v[i + h];
+      const float keep = upper ? v[i + h] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  const int r = lane >> 3, n = lane & 7;
+  if (row0 + r < crows && n < nt) w.logits[(long)(t0 + n) * (E + 1) + crow0 + row0 + r] = v[0];
 }
 
 // Routing metadata of the expert owning a run of units, cached per warp.
@@ -557,9 +659,10 @@ struct SlabSync {
   uint64_t xempty[2];
   int abort;
   int pad[3];
+  uint4 zero[2];  // the B source of the threads whose column cannot be non-zero
 };
 
-template <int NT, bool PAIR, int DT, bool M6, int CW>
+template <int NT, bool PAIR, int DT, bool I6, int CW>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_up_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, long map_row_base,
                        const __grid_constant__ CUtensorMap tm_gate,
@@ -587,13 +690,16 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       mbar_init(&sync->xempty[p], RBM);
     }
     sync->abort = 0;
+    sync->zero[0] = sync->zero[1] = make_uint4(0, 0, 0, 0);
     fence_mbar_init();
   }
   __syncthreads();
   const int k = m.top_k;
   const int per_r = (m.inter + RU - 1) / RU;
   const int per_s = (m.inter_sh + RU - 1) / RU;
-  const int passes_s = (T + NT - 1) / NT;
+  int sh_t0, sh_t1;
+  shared_tokens(m, T, sh_t0, sh_t1);
+  const int passes_s = (sh_t1 - sh_t0 + NT - 1) / NT;
   const int nact = w.active[m.experts];
   // work items: (slab, pass of up to NT tokens), all of one cost; routed ones
   // expert-major (passes of expert a: pass_off[a] ..), then slab, then pass
@@ -643,8 +749,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       x.shared = true;
       x.rows_e = m.inter_sh;
       x.row0 = slab * RU;
-      x.t_begin = p * NT;
-      x.t_end = min(T, x.t_begin + NT);
+      x.t_begin = sh_t0 + p * NT;
+      x.t_end = min(sh_t1, x.t_begin + NT);
       x.map_row = x.row0;
     }
     return x;
@@ -729,7 +835,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
 #pragma unroll
         for (int n = 0; n < NT; ++n)
           bs[n] = BSlice{st + STAGE_W + n * 1088, st + STAGE_W + n * 1088 + 1024};
-        q4k_sb_mma_n<NT, true>(nt, blk + g * LB_Q4K, blk + (g + 8) * LB_Q4K, bs, lane, acc);
+        q4k_sb_mma_n<NT, true>(nt, blk + g * LB_Q4K, blk + (g + 8) * LB_Q4K, bs,
+                               reinterpret_cast<const uint8_t*>(sync->zero), lane, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sync->empty[s]);
       }
@@ -798,12 +905,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
           }
       }
       if (writer) {
-        if (M6) {  // the block's 16 rows are one Q6_K sub-block of the down input
+        if (I6) {  // the block's 16 rows are one Q6_K sub-block of the down input
           const int s_glob = (x.row0 + rb * kTileRows) >> 4;
 #pragma unroll
           for (int n = 0; n < NT; ++n)
             if (n < nt)
-              m6_store_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(n) * ld_dn),
+              i6_store_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(n) * ld_dn),
                                 s_glob, hv[0][n], hv[1][n], lane);
         } else if (t == 0) {
 #pragma unroll
@@ -817,11 +924,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
         }
       }
       if (warp == 0 && x.row0 + RU >= x.rows_e) {  // last slab: zero the padding up to kd
-        if (M6) {  // sub-blocks past the slab (the slab's own are written above)
+        if (I6) {  // sub-blocks past the slab (the slab's own are written above)
           const int s_from = (x.row0 + RU) >> 4, s_to = kd >> 4;
           for (int qq = lane >> 4; qq < nt * (s_to - s_from); qq += 2) {
             const int nn = qq / (s_to - s_from), sg = s_from + (qq - nn * (s_to - s_from));
-            m6_zero_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(nn) * ld_dn), sg,
+            i6_zero_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(nn) * ld_dn), sg,
                              lane & 15);
           }
         } else {
@@ -837,7 +944,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
 }
 
 // ---------------------------------------------------------------- down (slabs)
-// Q6_K down rows on the tensor cores (mma.cuh, Q6_K rows): a work item is a
+// Q6_K down rows on the tensor cores (mma.cuh, Q6_K rows in sub-block slots,
+// one mma per entry and k-step): a work item is a
 // slab of RU = 16 * CW / KSPLIT rows of one routed expert's down matrix (or
 // the shared expert's) for one pass of up to 4 entries.  A stage holds the
 // slab's 16-row blocks whole (16 rows x row bytes is a multiple of 16 bytes,
@@ -846,16 +954,28 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
 // other parts' sums reach the part-0 warp through shared memory, guarded by
 // a per-stage barrier.  Lane (g, t) ends with rows g, g+8 of its block for
 // the pass's entry t and writes them to `partial`.
+// What a stage holds, written by the producer before it arms the stage's
+// barrier (whose arrive releases it to the consumers): the slab's first row
+// and, per entry of the pass, its prepared-input id and output row of
+// `partial` (token * (k + 1) + slot).
+struct __align__(16) DownUnit {
+  int row0, nt, pad[2];
+  int id[4];
+  int orow[4];
+};
+
 struct DownSync {
   uint64_t full[kSlabMaxStages];
   uint64_t empty[kSlabMaxStages];
   uint64_t red[kSlabMaxStages];
+  DownUnit unit[kSlabMaxStages];
   int abort;
   int pad[3];
+  uint4 zero[2];  // the B source of the threads without a column of their own
 };
 
 // SB: the pass's entries' prepared inputs are staged with the weights (at
-// stage_w, m6_bytes(K) each) instead of being read through L1.
+// stage_w, i6_bytes(K) each) instead of being read through L1.
 template <int KSPLIT, int CW, bool SB>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_down_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, int stage_bytes,
@@ -875,83 +995,85 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       mbar_init(&sync->red[s], CW - NB);
     }
     sync->abort = 0;
+    sync->zero[0] = sync->zero[1] = make_uint4(0, 0, 0, 0);
     fence_mbar_init();
   }
   __syncthreads();
   const int k = m.top_k, H = m.hidden;
   const int per = (H + RU - 1) / RU;
-  const int passes_s = (T + NT - 1) / NT;
-  const int nact = w.active[m.experts];
-  const int n_routed = shared_pass ? 0 : w.pass_off_dn[nact] * per;
-  const int n_shared = (shared_pass && m.shared_here && m.inter_sh) ? per * passes_s : 0;
-  const int units = n_routed + n_shared;
-  const int u0 = (int)((long)blockIdx.x * units / gridDim.x);
-  const int n_my = (int)((long)(blockIdx.x + 1) * units / gridDim.x) - u0;
   const int K = shared_pass ? m.k_down_sh : m.k_down;
   const int nsb = K >> 8;
   const size_t rb = shared_pass ? m.down_sh_rb : m.down_rb;
   const long ld_dn = down_ld_floats(m);
+  const uint32_t xib = (uint32_t)i6_bytes(K);
 
-  struct Unit {
-    int row0, t_begin, t_end;
-    const uint8_t* src;  // row row0 of the slab in global memory
-  };
-  ExpertView view;
-  int a_hint = -1;
-  auto unit_at = [&](int u) {
-    Unit x;
-    if (!shared_pass) {
-      int a = a_hint;  // as in the gate/up kernel: step on, search only first
-      if (a < 0) {
-        a = 0;
-        int hi = nact;
-        while (hi - a > 1) {
-          const int mid = (a + hi) >> 1;
-          if (w.pass_off_dn[mid] * per <= u) a = mid; else hi = mid;
-        }
-      } else {
-        while (w.pass_off_dn[a + 1] * per <= u) ++a;
-      }
-      a_hint = a;
-      view_expert(m, w, T, a, view);
-      const int np = w.pass_off_dn[a + 1] - w.pass_off_dn[a];
-      const int local = u - w.pass_off_dn[a] * per, slab = local / np, p = local - slab * np;
-      x.row0 = slab * RU;
-      x.t_begin = p * NT;
-      x.t_end = min(view.ntok, x.t_begin + NT);
-      x.src = m.down_exps + ((size_t)view.e * H + x.row0) * rb;
-    } else {
-      const int slab = u / passes_s, p = u - slab * passes_s;
-      x.row0 = slab * RU;
-      x.t_begin = p * NT;
-      x.t_end = min(T, x.t_begin + NT);
-      x.src = m.down_sh + (size_t)x.row0 * rb;
-    }
-    return x;
-  };
-
-  if (warp == CW) {  // ---------------- producer
+  if (warp == CW) {  // ---------------- producer: enumerates the units, stages them
     if (lane == 0) {
+      int sh_t0, sh_t1;
+      shared_tokens(m, T, sh_t0, sh_t1);
+      const int passes_s = (sh_t1 - sh_t0 + NT - 1) / NT;
+      const int nact = w.active[m.experts];
+      const int n_routed = shared_pass ? 0 : w.pass_off_dn[nact] * per;
+      const int n_shared = (shared_pass && m.shared_here && m.inter_sh) ? per * passes_s : 0;
+      const int units = n_routed + n_shared;
+      const int u0 = (int)((long)blockIdx.x * units / gridDim.x);
+      const int n_my = (int)((long)(blockIdx.x + 1) * units / gridDim.x) - u0;
+      ExpertView view;
+      int a = -1;
       int q = 0;
       RingPos rp;
       for (int i = 0; i < n_my; ++i, ++q, rp.next(stages)) {
-        const Unit x = unit_at(u0 + i);
+        const int u = u0 + i;
+        int row0, t_begin, t_end;
+        const uint8_t* src;
+        if (!shared_pass) {
+          if (a < 0) {  // search once, then step on
+            a = 0;
+            int hi = nact;
+            while (hi - a > 1) {
+              const int mid = (a + hi) >> 1;
+              if (w.pass_off_dn[mid] * per <= u) a = mid; else hi = mid;
+            }
+          } else {
+            while (w.pass_off_dn[a + 1] * per <= u) ++a;
+          }
+          view_expert(m, w, T, a, view);
+          const int np = w.pass_off_dn[a + 1] - w.pass_off_dn[a];
+          const int local = u - w.pass_off_dn[a] * per, slab = local / np, p = local - slab * np;
+          row0 = slab * RU;
+          t_begin = p * NT;
+          t_end = min(view.ntok, t_begin + NT);
+          src = m.down_exps + ((size_t)view.e * H + row0) * rb;
+        } else {
+          const int slab = u / passes_s, p = u - slab * passes_s;
+          row0 = slab * RU;
+          t_begin = sh_t0 + p * NT;
+          t_end = min(sh_t1, t_begin + NT);
+          src = m.down_sh + (size_t)row0 * rb;
+        }
         const int s = rp.s;
         if (q >= stages && !mbar_wait_or_abort(&sync->empty[s], rp.phase ^ 1u, w.status, abort))
           break;
-        const int nblk = min(NB, (H - x.row0) / kTileRows);  // H % 16 == 0
-        const int nt = x.t_end - x.t_begin;
-        const uint32_t m6b = (uint32_t)m6_bytes(K);
-        mbar_expect_tx(&sync->full[s], (uint32_t)(nblk * kTileRows * rb) + (SB ? nt * m6b : 0u));
+        const int nblk = min(NB, (H - row0) / kTileRows);  // H % 16 == 0
+        const int nt = t_end - t_begin;
+        DownUnit& du = sync->unit[s];
+        du.row0 = row0;
+        du.nt = nt;
+        for (int n = 0; n < NT; ++n) {
+          const int tt = t_begin + min(n, nt - 1);
+          const int id = shared_pass ? T * k + tt : view.list[tt];
+          const int tok = shared_pass ? tt : id / k;
+          du.id[n] = id;
+          du.orow[n] = tok * (k + 1) + (shared_pass ? k : id - tok * k);
+        }
+        mbar_expect_tx(&sync->full[s], (uint32_t)(nblk * kTileRows * rb) + (SB ? nt * xib : 0u));
         uint8_t* st = smem + (size_t)s * stage_bytes;
         for (int b = 0; b < nblk; ++b)
-          tma_load_1d(st + (size_t)b * kTileRows * rb, x.src + (size_t)b * kTileRows * rb,
+          tma_load_1d(st + (size_t)b * kTileRows * rb, src + (size_t)b * kTileRows * rb,
                       (uint32_t)(kTileRows * rb), &sync->full[s]);
         if (SB)
-          for (int n = 0; n < nt; ++n) {
-            const int id = shared_pass ? T * k + x.t_begin + n : view.list[x.t_begin + n];
-            tma_load_1d(st + stage_w + n * m6b, w.xp_down + id * ld_dn, m6b, &sync->full[s]);
-          }
+          for (int n = 0; n < nt; ++n)
+            tma_load_1d(st + stage_w + n * xib, w.xp_down + du.id[n] * ld_dn, xib, &sync->full[s]);
       }
       for (int r = max(0, q - stages); r < q; ++r)
         mbar_wait(&sync->full[r % stages], (r / stages) & 1, nullptr);
@@ -959,32 +1081,43 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     return;
   }
 
-  // ---------------- consumers
+  // ---------------- consumers: the same units, in the same order
+  int units_c;
+  {
+    int sh_t0, sh_t1;
+    shared_tokens(m, T, sh_t0, sh_t1);
+    const int passes_s = (sh_t1 - sh_t0 + NT - 1) / NT;
+    const int n_routed = shared_pass ? 0 : w.pass_off_dn[w.active[m.experts]] * per;
+    const int n_shared = (shared_pass && m.shared_here && m.inter_sh) ? per * passes_s : 0;
+    units_c = n_routed + n_shared;
+  }
+  const int u0 = (int)((long)blockIdx.x * units_c / gridDim.x);
+  const int n_my = (int)((long)(blockIdx.x + 1) * units_c / gridDim.x) - u0;
   const int b = warp / KSPLIT, kp = warp % KSPLIT;
   const int sb0 = kp * nsb / KSPLIT, sb1 = (kp + 1) * nsb / KSPLIT;
   const int g = lane >> 2, t = lane & 3;
+  const uint8_t* bz = SB ? reinterpret_cast<const uint8_t*>(sync->zero) : kZero32;
   RingPos rp;
   for (int i = 0; i < n_my; ++i, rp.next(stages)) {
-    const Unit x = unit_at(u0 + i);
     const int s = rp.s;
     if (!mbar_wait_or_abort(&sync->full[s], rp.phase, w.status, abort)) break;
-    const int nt = x.t_end - x.t_begin;
-    const int row_blk = x.row0 + b * kTileRows;
-    int ids[NT];
-    const uint8_t* m6[NT];
+    const DownUnit du = sync->unit[s];
+    const int nt = du.nt;
+    const int row_blk = du.row0 + b * kTileRows;
+    const uint8_t* xin[NT];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const int tt = x.t_begin + min(n, nt - 1);
-      ids[n] = shared_pass ? T * k + tt : view.list[tt];
-      m6[n] = SB ? smem + (size_t)s * stage_bytes + stage_w + min(n, nt - 1) * m6_bytes(K)
-                 : reinterpret_cast<const uint8_t*>(w.xp_down + ids[n] * ld_dn);
-    }
+    for (int n = 0; n < NT; ++n)
+      xin[n] = SB ? smem + (size_t)s * stage_bytes + stage_w + min(n, nt - 1) * xib
+                  : reinterpret_cast<const uint8_t*>(w.xp_down + (long)du.id[n] * ld_dn);
     float2 y[1] = {make_float2(0.f, 0.f)};
     if (row_blk < H) {
       const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
-      for (int sb = sb0; sb < sb1; ++sb)
-        q6k_sb_mma<SB, 1>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, m6,
-                          nt, lane, y);
+      switch (nt) {
+        case 1: q6i_block<SB, 1>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
+        case 2: q6i_block<SB, 2>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
+        case 3: q6i_block<SB, 3>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
+        default: q6i_block<SB, 4>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
+      }
     }
     if (KSPLIT > 1) {
       float2* rs = red + ((size_t)s * CW) * 32;
@@ -1005,13 +1138,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&sync->empty[s]);
     if (kp == 0 && row_blk < H && t < nt) {
-      int id = ids[0];
+      int orow = du.orow[0];
 #pragma unroll
       for (int n2 = 1; n2 < NT; ++n2)
-        if (n2 == t) id = ids[n2];
-      const int tok = shared_pass ? x.t_begin + t : id / k;
-      const int slot = shared_pass ? k : id - tok * k;
-      float* out = w.partial + ((long)tok * (k + 1) + slot) * H + row_blk;
+        if (n2 == t) orow = du.orow[n2];
+      float* out = w.partial + (long)orow * H + row_blk;
       out[g] = y[0].x;
       out[g + 8] = y[0].y;
     }
@@ -1136,6 +1267,8 @@ __global__ void combine_kernel(MoeDevice m, MoeWork w, int T, const float* x, fl
   const int H = m.hidden, k = m.top_k, HV = H / V;
   const long n = (long)T * HV;
   const bool shared = m.shared_here && m.inter_sh;
+  int sh_t0, sh_t1;
+  shared_tokens(m, T, sh_t0, sh_t1);
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const int t = (int)(i / HV), h = (int)(i - (long)t * HV) * V;
     const float* p = w.partial + (long)t * (k + 1) * H + h;
@@ -1162,7 +1295,7 @@ __global__ void combine_kernel(MoeDevice m, MoeWork w, int T, const float* x, fl
 #pragma unroll
       for (int c = 0; c < V; ++c) acc[c] = __fadd_rn(acc[c], own ? __fmul_rn(wt, pv[c]) : 0.f);
     }
-    if (shared) {
+    if (shared && t >= sh_t0 && t < sh_t1) {
       const float sw = m.arch == 0 ? w.shw[t] : 1.0f;
 #pragma unroll
       for (int c = 0; c < V; ++c) {
@@ -1177,11 +1310,6 @@ __global__ void combine_kernel(MoeDevice m, MoeWork w, int T, const float* x, fl
   }
 }
 
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -1225,6 +1353,8 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(MoeDevice m, MoeWork w,
   const long n4 = (long)T * H4;
   const long c0 = (long)blockIdx.x * n4 / gridDim.x, c1 = (long)(blockIdx.x + 1) * n4 / gridDim.x;
   const bool shared = m.shared_here && m.inter_sh;
+  int sh_t0, sh_t1;
+  shared_tokens(m, T, sh_t0, sh_t1);
   for (long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
     const int t = (int)(i / H4), h = (int)(i - (long)t * H4) * 4;
     const float* p = w.partial + (long)t * (k + 1) * H + h;
@@ -1240,7 +1370,7 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(MoeDevice m, MoeWork w,
       acc[2] = __fadd_rn(acc[2], own ? __fmul_rn(wt, q.z) : 0.f);
       acc[3] = __fadd_rn(acc[3], own ? __fmul_rn(wt, q.w) : 0.f);
     }
-    if (shared) {
+    if (shared && t >= sh_t0 && t < sh_t1) {
       const float sw = m.arch == 0 ? w.shw[t] : 1.0f;
       const float4 q = *reinterpret_cast<const float4*>(p + (long)k * H);
       const float sv[4] = {q.x, q.y, q.z, q.w};
@@ -1367,10 +1497,10 @@ bool q4k_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t rb
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT, bool PAIR, int DT, bool M6, int CW>
+template <int NT, bool PAIR, int DT, bool I6, int CW>
 cudaError_t launch_up_slab_cw(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
                               cudaStream_t s) {
-  auto kern = moe_up_slab_kernel<NT, PAIR, DT, M6, CW>;
+  auto kern = moe_up_slab_kernel<NT, PAIR, DT, I6, CW>;
   constexpr int RU = CW / (PAIR ? 2 : 1) * kTileRows;
   const size_t stage = up_stage_bytes(CW, NT);
   const size_t extra = sizeof(SlabSync) + (size_t)2 * RU * NT * 4;
@@ -1384,12 +1514,12 @@ cudaError_t launch_up_slab_cw(const MoeDevice& m, const MoeWork& w, int T, const
 }
 
 // Shape of the Q6_K down slabs for rows of rb bytes: the most 16-row blocks
-// (8, 4, 2 or 1) whose stage fits 56 KiB, K split over 16 / blocks warps.
+// (8, 4, 2 or 1) whose stage fits 56 KiB, K split over 8 / blocks warps.
 struct DownPlan {
   int nb, stages, stage_bytes, stage_w;
   bool staged;  // entries' inputs staged with the weights
 };
-constexpr int kDownWarps = 16;
+constexpr int kDownWarps = 8;
 
 bool down_plan(size_t rb, int K, DownPlan* p) {
   const size_t block = (size_t)kTileRows * rb;
@@ -1397,17 +1527,17 @@ bool down_plan(size_t rb, int K, DownPlan* p) {
   while (nb > 1 && nb * block > 56 * 1024) nb >>= 1;
   p->nb = nb;
   p->stage_w = (int)((nb * block + 127) & ~size_t(127));
-  p->staged = 4 * m6_bytes(K) <= 24 * 1024;
-  p->stage_bytes = p->stage_w + (p->staged ? (int)(4 * m6_bytes(K)) : 0);
+  p->staged = 4 * i6_bytes(K) <= 24 * 1024;
+  p->stage_bytes = p->stage_w + (p->staged ? (int)(4 * i6_bytes(K)) : 0);
   const size_t per_stage = (size_t)p->stage_bytes + (size_t)kDownWarps * 32 * sizeof(float2);
   p->stages = (int)std::min<size_t>(kSlabMaxStages, (kTileSmemBudget - sizeof(DownSync)) / per_stage);
   return p->stages >= 2;
 }
 
-// The down input is written in the m6 layout and the down pass runs on the
+// The down input is written in the i6 layout and the down pass runs on the
 // Q6_K tensor-core slabs when the gate/up pass is the tensor-core one, the
 // down rows are Q6_K, the hidden size is a multiple of 16 and the slabs fit.
-bool down_uses_m6(const MoeDevice& m) {
+bool down_uses_i6(const MoeDevice& m) {
   DownPlan p;
   if (m.up_type != LB_TYPE_Q4_K || m.down_type != LB_TYPE_Q6_K || m.hidden % kTileRows) return false;
   if (!down_plan(m.down_rb, m.k_down, &p)) return false;
@@ -1436,10 +1566,10 @@ cudaError_t launch_down_slab(const MoeDevice& m, const MoeWork& w, int T, int sh
   return p.staged ? launch_down_slab_k<KS, true>(m, w, T, shared_pass, p, s)              \
                   : launch_down_slab_k<KS, false>(m, w, T, shared_pass, p, s);
   switch (kDownWarps / p.nb) {
+    case 1: LB_DOWN_SLAB(1)
     case 2: LB_DOWN_SLAB(2)
     case 4: LB_DOWN_SLAB(4)
-    case 8: LB_DOWN_SLAB(8)
-    default: LB_DOWN_SLAB(16)
+    default: LB_DOWN_SLAB(8)
   }
 #undef LB_DOWN_SLAB
 }
@@ -1450,7 +1580,7 @@ cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const
   // 16 consumer warps where their registers fit (120 each), else 8
   constexpr int CW = NT <= 2 ? 16 : 8;
   const bool pair = m.arch == 0;
-  if (DT == LB_TYPE_Q6_K && down_uses_m6(m))
+  if (DT == LB_TYPE_Q6_K && down_uses_i6(m))
     return pair ? launch_up_slab_cw<NT, true, DT, true, CW>(m, w, T, mp, s)
                 : launch_up_slab_cw<NT, false, DT, true, CW>(m, w, T, mp, s);
   return pair ? launch_up_slab_cw<NT, true, DT, false, CW>(m, w, T, mp, s)
@@ -1543,7 +1673,7 @@ cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T,
     moe_down_sums_kernel<<<std::min(T * m.top_k + T, sm_count() * 4), 128, 0, s>>>(m, w, T);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  if (DT == LB_TYPE_Q6_K && down_uses_m6(m)) {
+  if (DT == LB_TYPE_Q6_K && down_uses_i6(m)) {
     e = launch_down_slab(m, w, T, 0, s);
     if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_down_slab(m, w, T, 1, s);
     return e;
@@ -1597,20 +1727,33 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     return cudaErrorInvalidValue;
   if (m.inter_sh && m.k_in_sh != m.k_in) return cudaErrorInvalidValue;
   const int E = m.experts;
-  const int router_rows = E + (m.arch == 0 && !m.router_extra_row ? 1 : 0);
   cudaError_t e;
-  if (m.up_type == LB_TYPE_Q4_K)
-    moe_prep_kernel<LB_TYPE_Q4_K><<<T, 256, 0, s>>>(m, w, x);
-  else
-    moe_prep_kernel<LB_TYPE_Q6_K><<<T, 256, 0, s>>>(m, w, x);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  const float* xr = m.input_norm ? w.xn : x;
-  if (m.arch == 0 && m.router_extra_row) {  // shared-expert gate logit into column E
-    e = launch_gemv_f32(m.router_extra_row, 1, m.hidden, xr, m.hidden, T, w.logits + E, E + 1, s);
+  const size_t router_smem = (size_t)(kRouterTok + kRouterRows) * m.hidden * sizeof(float);
+  const uintptr_t align =
+      reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(m.router) |
+      reinterpret_cast<uintptr_t>(m.router_extra_row) | reinterpret_cast<uintptr_t>(m.input_norm);
+  const int all_rows = m.router_rows + (m.router_extra_row ? 1 : 0);  // column E: shared gate
+  if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
+      router_smem <= 192 * 1024 &&
+      prepared_occupancy(moe_router_kernel, 128, router_smem) >= 1) {
+    dim3 grid((all_rows + kRouterRows - 1) / kRouterRows, (T + kRouterTok - 1) / kRouterTok);
+    moe_router_kernel<<<grid, 128, router_smem, s>>>(m, w, x, T, all_rows);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  } else {
+    if (m.up_type == LB_TYPE_Q4_K)
+      moe_prep_kernel<LB_TYPE_Q4_K><<<T, 256, 0, s>>>(m, w, x);
+    else
+      moe_prep_kernel<LB_TYPE_Q6_K><<<T, 256, 0, s>>>(m, w, x);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const float* xr = m.input_norm ? w.xn : x;
+    if (m.arch == 0 && m.router_extra_row) {  // shared-expert gate logit into column E
+      e = launch_gemv_f32(m.router_extra_row, 1, m.hidden, xr, m.hidden, T, w.logits + E, E + 1,
+                          s);
+      if (e != cudaSuccess) return e;
+    }
+    e = launch_gemv_f32(m.router, m.router_rows, m.hidden, xr, m.hidden, T, w.logits, E + 1, s);
     if (e != cudaSuccess) return e;
   }
-  e = launch_gemv_f32(m.router, router_rows, m.hidden, xr, m.hidden, T, w.logits, E + 1, s);
-  if (e != cudaSuccess) return e;
   {
     const int per = (E + 31) / 32;
     if (per <= 1) topk_kernel<1><<<T, 32, 0, s>>>(m, w, T);

@@ -32,13 +32,19 @@ def shared_rank(world: int) -> int:
 
 
 def layer_roles(rank: int, world: int, experts: int, peer_reduction: bool) -> dict:
-    """Session arguments of one rank: its expert range, whether it computes the
-    shared expert, and whether its output carries the residual (every rank
-    with the peer-memory reduction, which sums all partials on every rank;
-    one rank with an all-reduce, so that x is added once)."""
+    """Session arguments of one rank: its expert range, whether it holds the
+    shared expert, and whether its output carries the residual.  With the
+    peer-memory reduction every rank holds the shared expert and computes it
+    for its part of the tokens (the rank sum reunites them), and every rank
+    adds the residual to the sum of all partials it forms itself; with an
+    all-reduce one rank computes the shared expert and adds x, so both count
+    once."""
+    if peer_reduction:
+        return {"expert_range": expert_range(rank, world, experts), "shared_here": True,
+                "add_residual": True}
     return {"expert_range": expert_range(rank, world, experts),
             "shared_here": rank == shared_rank(world),
-            "add_residual": True if peer_reduction else rank == shared_rank(world)}
+            "add_residual": rank == shared_rank(world)}
 
 
 def attach_peer_reduction(sessions, group=None):

@@ -48,7 +48,7 @@ def test_layer_roles():
     assert [r["add_residual"] for r in roles] == [True, False, False, False]  # x added once
     peer = [ep.layer_roles(r, 4, 512, peer_reduction=True) for r in range(4)]
     assert all(r["add_residual"] for r in peer)  # every rank sums all partials itself
-    assert [r["shared_here"] for r in peer] == [True, False, False, False]
+    assert all(r["shared_here"] for r in peer)  # each for its part of the tokens
 
 
 def _rank_tensors(cfg, tensors, rank, world):
@@ -165,3 +165,42 @@ def test_peer_reduction_two_gpus():
     for rank, status, err in got:
         assert status == 0, (rank, status)
         assert err < 1e-5, (rank, err)
+
+
+@pytest.mark.gpu
+def test_peer_wait_gives_up_when_a_peer_never_arrives():
+    """Rank 0 of a world of two whose peer never runs (its "peer" buffer is a
+    second buffer on the same GPU that nothing writes flags into): the
+    combine's bounded wait gives up after two seconds, the session reports
+    status bit 4, and the device stays usable."""
+    import time
+
+    import llambda_b200 as LB
+    from tests.helpers import gpu_tensors
+
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    tensors = host_layer(SMALL, seed=4)
+    T = 4
+    roles = ep.layer_roles(0, 2, SMALL.experts, peer_reduction=True)
+    s = LB.MoeSession.create(SMALL.arch, SMALL.hidden, SMALL.top_k, gpu_tensors(tensors),
+                             weight_scale=SMALL.weight_scale, weights_norm=SMALL.weights_norm,
+                             max_tokens=T, expert_range=roles["expert_range"],
+                             shared_here=roles["shared_here"],
+                             add_residual=roles["add_residual"])
+    try:
+        nbytes = s.peer_bytes(2)
+        bufs = [torch.zeros(nbytes, dtype=torch.uint8, device="cuda") for _ in range(2)]
+        s.attach_peers(0, 2, [b.data_ptr() for b in bufs], nbytes)
+        x = O.synth_f32(4, CF.S_ACT, 0, T * SMALL.hidden, 1.0).reshape(T, SMALL.hidden)
+        xs = torch.from_numpy(x).cuda()
+        y = torch.empty_like(xs)
+        t0 = time.time()
+        s.run_device(xs, y, T)
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 60
+        assert s.status() & 4
+        z = torch.arange(8, device="cuda", dtype=torch.float32)
+        assert float(z.sum().item()) == 28.0
+    finally:
+        s.close()
