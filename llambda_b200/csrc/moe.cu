@@ -87,76 +87,102 @@ __device__ __forceinline__ uint32_t topk_key(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Inverse of topk_key for a selectable key (-0.0 comes back as +0.0, which
+// every later use treats alike).
+__device__ __forceinline__ float topk_value(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
 // The k best scores of one token, in the order the reference's repeated
 // strict-> scan finds them (descending score, ties to the lower index), by k
-// rounds of a warp-wide argmax: every lane keeps the best of its own PER
-// candidates (the lowest index among equal keys), the round's winner is the
-// highest key and, among lanes holding it, the lowest index (two warp
-// reductions), and only the winning lane rescans its candidates.  PER:
-// candidates per lane (E <= 32*PER); key 0 marks a score that is never
-// selected (NaN, -inf, -FLT_MAX and below).
+// rounds of a warp-wide arg-max: every lane keeps the best of its own PER
+// candidates (the lowest index among equal keys), a round's winner is the
+// highest key (one warp max) held by one lane (a ballot; several lanes only
+// on exactly equal scores, where a warp min picks the lowest index), and
+// only the winning lane re-derives its best, by a tree over its candidates.
+// PER: candidates per lane (E <= 32*PER); key 0 marks a score that is never
+// selected (NaN, -inf, -FLT_MAX and below).  One warp per token t.
 template <int PER>
-__global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T) {
-  const int t = blockIdx.x, lane = threadIdx.x;
+__device__ __forceinline__ void topk_token(const MoeDevice& m, const MoeWork& w, int t,
+                                           int lane) {
   const int E = m.experts, k = m.top_k;
   const float* L = w.logits + (long)t * (E + 1);
+  // Every load goes out before any is used: addresses are clamped into the
+  // row (E + 1 entries) rather than guarded, as a guarded load per candidate
+  // would wait for the one before it.
   float lv[PER];
-  uint32_t key[PER];
 #pragma unroll
   for (int q = 0; q < PER; ++q) {
-    const int i = lane + 32 * q;
-    float v = 0.f;
-    uint32_t kq = 0u;
-    if (i < E) {
-      v = L[i];
-      if (m.router_bias) v = v + m.router_bias[i];
-      kq = topk_key(v);
-    }
-    lv[q] = v;
-    key[q] = kq;
+    const float* p = L + min(lane + 32 * q, E);
+    lv[q] = __ldg(p);
   }
-  uint32_t bk = 0u;  // this lane's best key, its slot and score
-  int bq = 0;
-  float bv = 0.f;
-  auto rescan = [&]() {
-    bk = 0u;
-    bq = 0;
-    bv = 0.f;
+  const float gate_logit = __ldg(L + E);
+  if (m.router_bias) {
+    float bs[PER];
 #pragma unroll
-    for (int q = 0; q < PER; ++q)
-      if (key[q] > bk) {
-        bk = key[q];
-        bq = q;
-        bv = lv[q];
+    for (int q = 0; q < PER; ++q) bs[q] = __ldg(m.router_bias + min(lane + 32 * q, E - 1));
+#pragma unroll
+    for (int q = 0; q < PER; ++q) lv[q] = lv[q] + bs[q];
+  }
+  uint32_t key[PER];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) key[q] = lane + 32 * q < E ? topk_key(lv[q]) : 0u;
+  // this lane's best key and its slot, by a tree whose left halves hold the
+  // lower slots (a strict > keeps the lower slot on equal keys)
+  uint32_t bk = 0u;
+  int bq = 0;
+  auto best = [&]() {
+    uint32_t kk[PER];
+    int qq[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      kk[q] = key[q];
+      qq[q] = q;
+    }
+#pragma unroll
+    for (int h = 1; h < PER; h <<= 1)
+#pragma unroll
+      for (int q = 0; q < PER; q += 2 * h) {
+        const bool take = kk[q + h] > kk[q];
+        kk[q] = take ? kk[q + h] : kk[q];
+        qq[q] = take ? qq[q + h] : qq[q];
       }
+    bk = kk[0];
+    bq = qq[0];
   };
-  rescan();
-  // lane r keeps round r's expert and score (-1: fewer than k selectable)
-  float my_v = 0.f;
+  best();
+  // round r: the highest key, and among lanes holding it the lowest index;
+  // lane r keeps the round's expert and key (-1: fewer than k selectable)
   int my_i = -1;
+  uint32_t my_k = 0u;
   for (int r = 0; r < k; ++r) {
     const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
     if (mk == 0u) break;  // uniform: no selectable score left
-    const uint32_t win =
-        __reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)(lane + 32 * bq) : 0xffffffffu);
-    const int wl = (int)(win & 31u);
-    const float v = __shfl_sync(0xffffffffu, bv, wl);
+    const unsigned holders = __ballot_sync(0xffffffffu, bk == mk);
+    int wl = __ffs(holders) - 1;
+    if (holders & (holders - 1u))  // equal keys on several lanes (rare)
+      wl = (int)(__reduce_min_sync(0xffffffffu,
+                                   bk == mk ? (uint32_t)(lane + 32 * bq) : 0xffffffffu) & 31u);
+    const int wq = __shfl_sync(0xffffffffu, bq, wl);
     if (lane == r) {
-      my_i = (int)win;
-      my_v = v;
+      my_i = wl + 32 * wq;
+      my_k = mk;
     }
     if (lane == wl) {
-      const int wq = (int)(win >> 5);
 #pragma unroll
       for (int q = 0; q < PER; ++q)
-        if (q == wq) key[q] = 0u;
-      rescan();
+        if (q == bq) key[q] = 0u;
+      best();
     }
   }
   // sigmoid per rank in parallel; the sum runs in rank order, as in L5367-5372
-  float wv = lane < k ? sigmoid_ref(my_v) : 0.f;
+  float wv = lane < k && my_i >= 0 ? sigmoid_ref(topk_value(my_k)) : 0.f;
   float wsum = 0.f;
-  for (int j = 0; j < k; ++j) wsum = wsum + __shfl_sync(0xffffffffu, wv, j);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float o = __shfl_sync(0xffffffffu, wv, j);
+    if (j < k) wsum = wsum + o;
+  }
   int bad = __any_sync(0xffffffffu, lane < k && my_i < 0);
   if (m.arch == 0 || m.weights_norm) {
     if (!(wsum > 0.f)) bad = 1;
@@ -168,14 +194,21 @@ __global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T)
     w.wts[t * k + lane] = wv;
   }
   if (lane == 0) {
-    w.shw[t] = (m.arch == 0) ? sigmoid_ref(L[E]) : 1.0f;
+    w.shw[t] = (m.arch == 0) ? sigmoid_ref(gate_logit) : 1.0f;
     if (bad) atomicOr(w.status, 1);
   }
 }
 
-// Groups the (token, rank) entries by owned expert, stably.
-// pass_nt: tokens per pass of the up kernel; pass_off counts passes.
-__global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int T, int pass_nt) {
+template <int PER>
+__global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T) {
+  topk_token<PER>(m, w, blockIdx.x, threadIdx.x);
+}
+
+// Groups the (token, rank) entries by owned expert, stably.  One CTA of up to
+// 8 warps.  pass_nt: tokens per pass of the up kernel; pass_off counts
+// passes.
+__device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
+                                            int pass_nt) {
   __shared__ int s_count[kMaxExperts];
   __shared__ int s_offset[kMaxExperts + 1];
   const int E = m.experts, k = m.top_k;
@@ -192,8 +225,10 @@ __global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int 
       if (u == 0)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const int idj = c + 32 * j + lane;
-          ev[j] = idj < n ? w.sel[idj] : -1;
+          const int idj = c + 32 * j + lane;  // clamped, not guarded: the loads overlap
+          const int* p = w.sel + min(idj, n - 1);
+          const int v = __ldg(p);
+          ev[j] = idj < n ? v : -1;
         }
       const int id = c + lane;
       int e = ev[0];
@@ -293,6 +328,10 @@ __global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int 
     const int pos = w.entries[id];
     if (pos >= 0) w.entries[T * k + s_offset[w.sel[id]] + pos] = id;
   }
+}
+
+__global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int T, int pass_nt) {
+  route_block(m, w, T, pass_nt);
 }
 
 // ---------------------------------------------------------------- prep
@@ -461,51 +500,52 @@ __global__ void __launch_bounds__(128) moe_router_kernel(MoeDevice m, MoeWork w,
     }
   }
   const int row0 = warp * 4;  // this warp's 4 rows of the tile
-  if (row0 >= crows) return;
-  float2 acc[4][kRouterTok / 2];
+  if (row0 < crows) {
+    float2 acc[4][kRouterTok / 2];
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int p = 0; p < kRouterTok / 2; ++p) acc[r][p] = make_float2(0.f, 0.f);
-  const float4* wr[4];
+      for (int p = 0; p < kRouterTok / 2; ++p) acc[r][p] = make_float2(0.f, 0.f);
+    const float4* wr[4];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) wr[r] = ws4 + (size_t)min(row0 + r, crows - 1) * H4;
-  for (int c = lane; c < H4; c += 32) {
-    float4 wv[4];
+    for (int r = 0; r < 4; ++r) wr[r] = ws4 + (size_t)min(row0 + r, crows - 1) * H4;
+    for (int c = lane; c < H4; c += 32) {
+      float4 wv[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) wv[r] = wr[r][c];
+      for (int r = 0; r < 4; ++r) wv[r] = wr[r][c];
 #pragma unroll
-    for (int p = 0; p < kRouterTok / 2; ++p) {
-      const float4 xa = xs4[(2 * p) * H4 + c], xb = xs4[(2 * p + 1) * H4 + c];
+      for (int p = 0; p < kRouterTok / 2; ++p) {
+        const float4 xa = xs4[(2 * p) * H4 + c], xb = xs4[(2 * p + 1) * H4 + c];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        acc[r][p] = __ffma2_rn(make_float2(wv[r].x, wv[r].x), make_float2(xa.x, xb.x), acc[r][p]);
-        acc[r][p] = __ffma2_rn(make_float2(wv[r].y, wv[r].y), make_float2(xa.y, xb.y), acc[r][p]);
-        acc[r][p] = __ffma2_rn(make_float2(wv[r].z, wv[r].z), make_float2(xa.z, xb.z), acc[r][p]);
-        acc[r][p] = __ffma2_rn(make_float2(wv[r].w, wv[r].w), make_float2(xa.w, xb.w), acc[r][p]);
+        for (int r = 0; r < 4; ++r) {
+          acc[r][p] = __ffma2_rn(make_float2(wv[r].x, wv[r].x), make_float2(xa.x, xb.x), acc[r][p]);
+          acc[r][p] = __ffma2_rn(make_float2(wv[r].y, wv[r].y), make_float2(xa.y, xb.y), acc[r][p]);
+          acc[r][p] = __ffma2_rn(make_float2(wv[r].z, wv[r].z), make_float2(xa.z, xb.z), acc[r][p]);
+          acc[r][p] = __ffma2_rn(make_float2(wv[r].w, wv[r].w), make_float2(xa.w, xb.w), acc[r][p]);
+        }
       }
     }
-  }
-  float v[32];  // value r * 8 + n ends on lane r * 8 + n
+    float v[32];  // value r * 8 + n ends on lane r * 8 + n
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int p = 0; p < kRouterTok / 2; ++p) {
-      v[r * 8 + 2 * p] = acc[r][p].x;
-      v[r * 8 + 2 * p + 1] = acc[r][p].y;
+      for (int p = 0; p < kRouterTok / 2; ++p) {
+        v[r * 8 + 2 * p] = acc[r][p].x;
+        v[r * 8 + 2 * p + 1] = acc[r][p].y;
+      }
+#pragma unroll
+    for (int h = 16; h >= 1; h >>= 1) {
+      const bool upper = (lane & h) != 0;
+#pragma unroll
+      for (int i = 0; i < h; ++i) {
+        const float send = upper ? v[i] : v[i + h];
+        const float keep = upper ? v[i + h] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+      }
     }
-#pragma unroll
-  for (int h = 16; h >= 1; h >>= 1) {
-    const bool upper = (lane & h) != 0;
-#pragma unroll
-    for (int i = 0; i < h; ++i) {
-      const float send = upper ? v[i] : v[i + h];
-      const float keep = upper ? v[i + h] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
-    }
+    const int r = lane >> 3, n = lane & 7;
+    if (row0 + r < crows && n < nt) w.logits[(long)(t0 + n) * (E + 1) + crow0 + row0 + r] = v[0];
   }
-  const int r = lane >> 3, n = lane & 7;
-  if (row0 + r < crows && n < nt) w.logits[(long)(t0 + n) * (E + 1) + crow0 + row0 + r] = v[0];
 }
 
 // Routing metadata of the expert owning a run of units, cached per warp.
@@ -1112,11 +1152,16 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     float2 y[1] = {make_float2(0.f, 0.f)};
     if (row_blk < H) {
       const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
-      switch (nt) {
-        case 1: q6i_block<SB, 1>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
-        case 2: q6i_block<SB, 2>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
-        case 3: q6i_block<SB, 3>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
-        default: q6i_block<SB, 4>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]); break;
+      if (nt == 1) {
+        q6i_block<SB, 1>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]);
+      } else if (nt == 2 || CW > 8) {  // at most two entries per decode (registers)
+        q6i_block<SB, 2>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]);
+        if (nt == 3) q6i_block<SB, 1>(blk, rb, sb0, sb1, xin + 2, bz, lane, 2, y[0]);
+        if (nt == 4) q6i_block<SB, 2>(blk, rb, sb0, sb1, xin + 2, bz, lane, 2, y[0]);
+      } else if (nt == 3) {
+        q6i_block<SB, 3>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]);
+      } else {
+        q6i_block<SB, 4>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]);
       }
     }
     if (KSPLIT > 1) {
@@ -1261,8 +1306,11 @@ __global__ void __launch_bounds__(128) moe_down_kernel(MoeDevice m, MoeWork w, i
 
 // ---------------------------------------------------------------- combine
 // VEC: four hidden values per thread (H % 4 == 0, x / out 16-byte aligned).
-template <bool VEC>
-__global__ void combine_kernel(MoeDevice m, MoeWork w, int T, const float* x, float* out) {
+// KMAX >= top_k: the rank loop is unrolled whole over clamped (not guarded)
+// addresses, so all of a thread's loads are in flight at once.
+template <bool VEC, int KMAX>
+__global__ void __launch_bounds__(128) combine_kernel(MoeDevice m, MoeWork w, int T,
+                                                      const float* x, float* out) {
   constexpr int V = VEC ? 4 : 1;
   const int H = m.hidden, k = m.top_k, HV = H / V;
   const long n = (long)T * HV;
@@ -1275,19 +1323,21 @@ __global__ void combine_kernel(MoeDevice m, MoeWork w, int T, const float* x, fl
     float acc[V];
 #pragma unroll
     for (int c = 0; c < V; ++c) acc[c] = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < k; ++j) {
-      const int e = w.sel[t * k + j];
-      const float wt = w.wts[t * k + j];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      const int jc = min(j, k - 1);
+      const int es = w.sel[t * k + jc];
+      const int e = j < k ? es : -1;
+      const float wt = w.wts[t * k + jc];
       float pv[V];  // loaded unconditionally (a valid address), so all loads go out at once
       if (VEC) {
-        const float4 q = *reinterpret_cast<const float4*>(p + (long)j * H);
+        const float4 q = *reinterpret_cast<const float4*>(p + (long)jc * H);
         pv[0] = q.x;
         pv[V > 1 ? 1 : 0] = q.y;
         pv[V > 2 ? 2 : 0] = q.z;
         pv[V > 3 ? 3 : 0] = q.w;
       } else {
-        pv[0] = p[(long)j * H];
+        pv[0] = p[(long)jc * H];
       }
       // experts of other devices add +0.0, which leaves a sum that starts at
       // +0.0 unchanged (it can never be -0.0)
@@ -1527,10 +1577,14 @@ bool down_plan(size_t rb, int K, DownPlan* p) {
   while (nb > 1 && nb * block > 56 * 1024) nb >>= 1;
   p->nb = nb;
   p->stage_w = (int)((nb * block + 127) & ~size_t(127));
-  p->staged = 4 * i6_bytes(K) <= 24 * 1024;
+  // the entries' inputs ride in the stage when three stages still fit
+  const size_t red = nb < kDownWarps ? (size_t)kDownWarps * 32 * sizeof(float2) : 0;
+  const size_t room = kTileSmemBudget - sizeof(DownSync);
+  p->staged = 4 * i6_bytes(K) <= 24 * 1024 &&
+              room / (p->stage_w + 4 * i6_bytes(K) + red) >= 3;
   p->stage_bytes = p->stage_w + (p->staged ? (int)(4 * i6_bytes(K)) : 0);
-  const size_t per_stage = (size_t)p->stage_bytes + (size_t)kDownWarps * 32 * sizeof(float2);
-  p->stages = (int)std::min<size_t>(kSlabMaxStages, (kTileSmemBudget - sizeof(DownSync)) / per_stage);
+  const size_t per_stage = (size_t)p->stage_bytes + red;
+  p->stages = (int)std::min<size_t>(kSlabMaxStages, room / per_stage);
   return p->stages >= 2;
 }
 
@@ -1549,7 +1603,7 @@ cudaError_t launch_down_slab_k(const MoeDevice& m, const MoeWork& w, int T, int 
                                const DownPlan& p, cudaStream_t s) {
   auto kern = moe_down_slab_kernel<KSPLIT, kDownWarps, SB>;
   const size_t smem = (size_t)p.stages * p.stage_bytes + sizeof(DownSync) +
-                      (size_t)p.stages * kDownWarps * 32 * sizeof(float2);
+                      (KSPLIT > 1 ? (size_t)p.stages * kDownWarps * 32 * sizeof(float2) : 0);
   if (prepared_occupancy(kern, (kDownWarps + 1) * 32, smem) < 1) return cudaErrorUnknown;
   kern<<<sm_count(), (kDownWarps + 1) * 32, smem, s>>>(m, w, T, p.stages, p.stage_bytes,
                                                         p.stage_w, shared_pass);
@@ -1577,7 +1631,7 @@ cudaError_t launch_down_slab(const MoeDevice& m, const MoeWork& w, int T, int sh
 template <int NT, int DT>
 cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
                               cudaStream_t s) {
-  // 16 consumer warps where their registers fit (120 each), else 8
+  // 16 consumer warps where their registers fit (96 each), else 8
   constexpr int CW = NT <= 2 ? 16 : 8;
   const bool pair = m.arch == 0;
   if (DT == LB_TYPE_Q6_K && down_uses_i6(m))
@@ -1736,6 +1790,7 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
       router_smem <= 192 * 1024 &&
       prepared_occupancy(moe_router_kernel, 128, router_smem) >= 1) {
+    // top-k and routing ride on the router launch (its last CTAs)
     dim3 grid((all_rows + kRouterRows - 1) / kRouterRows, (T + kRouterTok - 1) / kRouterTok);
     moe_router_kernel<<<grid, 128, router_smem, s>>>(m, w, x, T, all_rows);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1762,10 +1817,10 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     else if (per <= 8) topk_kernel<8><<<T, 32, 0, s>>>(m, w, T);
     else if (per <= 16) topk_kernel<16><<<T, 32, 0, s>>>(m, w, T);
     else topk_kernel<32><<<T, 32, 0, s>>>(m, w, T);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    route_kernel<<<1, 256, 0, s>>>(m, w, T, up_pass_tokens(m, T));
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  route_kernel<<<1, 256, 0, s>>>(m, w, T, up_pass_tokens(m, T));
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
   if (!gate_ok) return cudaErrorInvalidValue;
   if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q6_K)
@@ -1787,11 +1842,13 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     return cudaGetLastError();
   }
   const long n = (long)T * m.hidden / (vec ? 4 : 1);
-  const int grid = (int)std::min<long>((n + 255) / 256, (long)sm_count() * 8);
-  if (vec)
-    combine_kernel<true><<<std::max(grid, 1), 256, 0, s>>>(m, w, T, x, out);
+  const int grid = std::max(1, (int)std::min<long>((n + 127) / 128, (long)sm_count() * 16));
+  if (vec && m.top_k <= 16)
+    combine_kernel<true, 16><<<grid, 128, 0, s>>>(m, w, T, x, out);
+  else if (vec)
+    combine_kernel<true, 32><<<grid, 128, 0, s>>>(m, w, T, x, out);
   else
-    combine_kernel<false><<<std::max(grid, 1), 256, 0, s>>>(m, w, T, x, out);
+    combine_kernel<false, 32><<<grid, 128, 0, s>>>(m, w, T, x, out);
   return cudaGetLastError();
 }
 
