@@ -35,6 +35,9 @@ namespace {
 
 constexpr int kMaxExperts = 1024;
 constexpr int kSlabMaxStages = 10;
+// Rows of one 2-D tensor copy of the gate/up slabs (the slabs' rows per
+// matrix are multiples of it).
+constexpr int kUpBoxRows = 64;
 
 // Bytes of one gate/up slab stage: CW boxes of 16 Q4_K rows x one super-block
 // and NT tokens' activation slices (1024 fragment + 64 meta bytes each).
@@ -712,6 +715,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   constexpr int MATS = PAIR ? 2 : 1;
   constexpr int RBM = CW / MATS;       // row blocks per matrix
   constexpr int RU = RBM * kTileRows;  // rows per matrix per slab
+  static_assert(RU % kUpBoxRows == 0, "slab rows must be whole copy boxes");
   constexpr int BOX = kTileRows * LB_Q4K;
   constexpr int STAGE_W = CW * BOX;  // weights; then NT activation slices of 1088 bytes
   constexpr int STAGE = up_stage_bytes(CW, NT);
@@ -814,14 +818,18 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
             const int nt = min(NT, x.t_end - t0);
             mbar_expect_tx(&sync->full[s], STAGE_W + nt * 1088);
             uint8_t* st = smem + (size_t)s * STAGE;
+            // one box of kUpBoxRows rows per copy (the slab's blocks lie
+            // back to back, 144 bytes per row, in the stage as in the matrix)
 #pragma unroll
-            for (int b = 0; b < CW; ++b) {
-              const bool gate = PAIR && b < RBM;
-              const CUtensorMap* tm = x.shared ? (gate ? &tm_gate_sh : &tm_up_sh)
-                                               : (gate ? &tm_gate : &tm_up);
-              tma_load_2d(st + b * BOX, tm, sb * LB_Q4K, (int)(x.map_row + (b % RBM) * kTileRows),
-                          &sync->full[s]);
-            }
+            for (int mt = 0; mt < MATS; ++mt)
+#pragma unroll
+              for (int b = 0; b < RU / kUpBoxRows; ++b) {
+                const bool gate = PAIR && mt == 0;
+                const CUtensorMap* tm = x.shared ? (gate ? &tm_gate_sh : &tm_up_sh)
+                                                 : (gate ? &tm_gate : &tm_up);
+                tma_load_2d(st + (mt * RU + b * kUpBoxRows) * LB_Q4K, tm, sb * LB_Q4K,
+                            (int)(x.map_row + b * kUpBoxRows), &sync->full[s]);
+              }
             // the pass's tokens' activation slices for this super-block
             for (int n = 0; n < nt; ++n) {
               const int tok = x.shared ? t0 + n : view.list[t0 + n] / k;
@@ -922,14 +930,32 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
           ok = false;
           break;
         }
+        // the quad's 2 * NT values (all four lanes hold every sum) are shared
+        // out: lane t takes pairs (r, n) with 2n + r = t, t + 4, ..., and the
+        // products come back to lane t == 0
+        constexpr int PER_LANE = (2 * NT + 3) / 4;
+        float hq[PER_LANE];
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) {
+          const int pr = t + 4 * i, r = pr & 1, n = pr >> 1;
+          float gv = v[0][0];
+#pragma unroll
+          for (int r2 = 0; r2 < 2; ++r2)
+#pragma unroll
+            for (int n2 = 0; n2 < NT; ++n2)
+              if (r2 == r && n2 == n) gv = v[r2][n2];
+          const int row = x.row0 + rb * kTileRows + g + 8 * r;
+          const bool live = n < NT && n < nt && row < x.rows_e;
+          const float uv = xb[(rb * kTileRows + g + 8 * r) * NT + min(n, NT - 1)];
+          hq[i] = live ? __fmul_rn(silu_ref(gv), uv) : 0.f;
+        }
 #pragma unroll
         for (int r = 0; r < 2; ++r)
 #pragma unroll
           for (int n = 0; n < NT; ++n) {
-            const int row = x.row0 + rb * kTileRows + g + 8 * r;
-            hv[r][n] = (t == 0 && row < x.rows_e && n < nt)
-                           ? __fmul_rn(silu_ref(v[r][n]), xb[(rb * kTileRows + g + 8 * r) * NT + n])
-                           : 0.f;
+            const int pr = 2 * n + r;
+            const float o = __shfl_sync(0xffffffffu, hq[pr >> 2], (lane & ~3) | (pr & 3));
+            hv[r][n] = t == 0 ? o : 0.f;
           }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sync->xempty[par]);
@@ -1108,9 +1134,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
         }
         mbar_expect_tx(&sync->full[s], (uint32_t)(nblk * kTileRows * rb) + (SB ? nt * xib : 0u));
         uint8_t* st = smem + (size_t)s * stage_bytes;
-        for (int b = 0; b < nblk; ++b)
-          tma_load_1d(st + (size_t)b * kTileRows * rb, src + (size_t)b * kTileRows * rb,
-                      (uint32_t)(kTileRows * rb), &sync->full[s]);
+        // the slab's blocks are contiguous rows: one copy
+        tma_load_1d(st, src, (uint32_t)(nblk * kTileRows * rb), &sync->full[s]);
         if (SB)
           for (int n = 0; n < nt; ++n)
             tma_load_1d(st + stage_w + n * xib, w.xp_down + du.id[n] * ld_dn, xib, &sync->full[s]);
@@ -1539,7 +1564,7 @@ bool q4k_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t rb
   if (!encode || rows == 0) return false;
   const cuuint64_t dims[2] = {rb, rows};
   const cuuint64_t strides[1] = {rb};
-  const cuuint32_t box[2] = {LB_Q4K, kTileRows};
+  const cuuint32_t box[2] = {LB_Q4K, kUpBoxRows};
   const cuuint32_t elem[2] = {1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
                 elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
