@@ -224,6 +224,135 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   }
 }
 
+// Q6_K rows times 3..8 tokens (m6 layout) with the tokens' inputs resident
+// in shared memory.  K is cut into slices of 8 super-blocks (1680-byte row
+// pieces, 16-byte aligned); CTA c keeps slice c % slices of every token's
+// input (tokens x 9216 bytes, loaded once) and streams that slice of a run of
+// 16-row blocks, one block per stage by 16 row copies.  Consumer warp w takes
+// super-block w of the slice; warp 0 adds the others' sums (in warp order).
+// With two slices the halves meet in y (zeroed first) by atomic adds, whose
+// two-term sum is the same in either order.
+constexpr int kSliceSb = 8;
+struct SliceSync {
+  uint64_t full[8], empty[8], red[8], act;
+  int abort;
+  int pad[3];
+};
+
+template <int NG>
+__global__ void __launch_bounds__((kSliceSb + 1) * 32, 1)
+    gemv_q6k_slice_kernel(const uint8_t* __restrict__ W, size_t rb, int rows, int slices,
+                          const uint8_t* __restrict__ m6, int tokens, float* __restrict__ y,
+                          long ldy, int stages, int* status) {
+  constexpr int CW = kSliceSb;
+  constexpr uint32_t kPiece = kSliceSb * LB_Q6K;  // 1680 bytes of a row
+  constexpr uint32_t kStage = kTileRows * kPiece;
+  constexpr uint32_t kActTok = kSliceSb * 1152;
+  constexpr uint32_t kActPitch = kActTok + 16;  // tokens 4 banks apart (meta loads)
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* act = smem + (size_t)stages * kStage;  // [tokens][kActPitch]
+  SliceSync* sync = reinterpret_cast<SliceSync*>(act + (size_t)4 * NG * kActPitch);
+  float2* red = reinterpret_cast<float2*>(sync + 1);  // [stages][CW][32][NG]
+  volatile int* abort = &sync->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&sync->full[s], 1);
+      mbar_init(&sync->empty[s], CW);
+      mbar_init(&sync->red[s], CW - 1);
+    }
+    mbar_init(&sync->act, 1);
+    sync->abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int slice = blockIdx.x % slices, ctas = gridDim.x / slices, cta = blockIdx.x / slices;
+  const int units = rows / kTileRows;  // rows % 16 == 0
+  const int u0 = (int)((long)cta * units / ctas);
+  const int n_my = cta < ctas ? (int)((long)(cta + 1) * units / ctas) - u0 : 0;
+  const size_t m6b = m6_bytes((int)(rb / LB_Q6K) * 256);
+  if (warp == CW) {  // ---------------- producer
+    if (lane == 0) {
+      mbar_expect_tx(&sync->act, (uint32_t)tokens * kActTok);
+      for (int n = 0; n < tokens; ++n)
+        tma_load_1d(act + (size_t)n * kActPitch, m6 + n * m6b + (size_t)slice * kActTok, kActTok,
+                    &sync->act);
+    }
+    RingPos rp;
+    int q = 0;
+    for (int i = 0; i < n_my; ++i, ++q, rp.next(stages)) {
+      bool ok = true;
+      if (lane == 0 && q >= stages)
+        ok = mbar_wait_or_abort(&sync->empty[rp.s], rp.phase ^ 1u, status, abort);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      if (lane == 0) mbar_expect_tx(&sync->full[rp.s], kStage);
+      __syncwarp();
+      if (lane < kTileRows)  // one row piece per lane
+        tma_load_1d(smem + (size_t)rp.s * kStage + lane * kPiece,
+                    W + ((size_t)(u0 + i) * kTileRows + lane) * rb + (size_t)slice * kPiece,
+                    kPiece, &sync->full[rp.s]);
+    }
+    if (lane == 0) {
+      for (int r = max(0, q - stages); r < q; ++r)
+        mbar_wait(&sync->full[r % stages], (r / stages) & 1, nullptr);
+      mbar_wait(&sync->act, 0, nullptr);
+    }
+    return;
+  }
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* m6p[4 * NG];
+#pragma unroll
+  for (int n = 0; n < 4 * NG; ++n) m6p[n] = act + (size_t)min(n, tokens - 1) * kActPitch;
+  if (!mbar_wait_or_abort(&sync->act, 0, status, abort)) return;
+  RingPos rp;
+  for (int i = 0; i < n_my; ++i, rp.next(stages)) {
+    const int s = rp.s;
+    if (!mbar_wait_or_abort(&sync->full[s], rp.phase, status, abort)) break;
+    const uint8_t* blk = smem + (size_t)s * kStage;
+    float2 acc[NG];
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) acc[grp] = make_float2(0.f, 0.f);
+    q6k_sb_mma<true, NG>(blk + g * kPiece + warp * LB_Q6K, blk + (g + 8) * kPiece + warp * LB_Q6K,
+                         warp, m6p, tokens, lane, acc);
+    float2* rs = red + (size_t)s * CW * 32 * NG;
+    if (warp != 0) {
+#pragma unroll
+      for (int grp = 0; grp < NG; ++grp) rs[(warp * 32 + lane) * NG + grp] = acc[grp];
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sync->red[s]);
+        mbar_arrive(&sync->empty[s]);
+      }
+    } else {
+      if (!mbar_wait_or_abort(&sync->red[s], rp.phase, status, abort)) break;
+      for (int w2 = 1; w2 < CW; ++w2)
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+          const float2 o = rs[(w2 * 32 + lane) * NG + grp];
+          acc[grp].x += o.x;
+          acc[grp].y += o.y;
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sync->empty[s]);
+      const int row = (u0 + i) * kTileRows + g;
+#pragma unroll
+      for (int grp = 0; grp < NG; ++grp) {
+        const int n = 4 * grp + t;
+        if (n < tokens) {
+          float* o = y + (long)n * ldy + row;
+          if (slices > 1) {
+            atomicAdd(o, acc[grp].x);
+            atomicAdd(o + 8, acc[grp].y);
+          } else {
+            o[0] = acc[grp].x;
+            o[8] = acc[grp].y;
+          }
+        }
+      }
+    }
+  }
+}
+
 // Each warp owns a contiguous run of units (RU rows each), streams them
 // through its TMA ring and computes every token against each staged unit.
 template <int TYPE, int LPR, int RL>
@@ -582,7 +711,7 @@ cudaError_t launch_q6k_slab(const void* W, size_t rb, int rows, int K, const uin
                             int tokens, float* y, long ldy, int* status, cudaStream_t stream) {
   const int nsb = K / 256;
   const int stage_bytes = (int)((kTileRows * rb + 127) & ~size_t(127));
-  const bool wide = nsb >= 16;
+  const bool wide = nsb >= 16 && NG == 1;  // two groups need more than 96 registers
   const int cw = wide ? 16 : 8;
   const size_t per_stage = (size_t)stage_bytes + (size_t)cw * 32 * NG * sizeof(float2);
   const int stages = (int)std::min<size_t>(8, (kTileSmemBudget - sizeof(DenseSync)) / per_stage);
@@ -602,6 +731,33 @@ cudaError_t launch_q6k_slab(const void* W, size_t rb, int rows, int K, const uin
                                          tokens, y, ldy, stages, stage_bytes, status);
   }
   return cudaGetLastError();
+}
+
+// The sliced kernel for 3..8 tokens when K is 8 or 16 super-blocks; false
+// when it does not apply (the caller takes the streamed path).
+template <int NG>
+bool launch_q6k_slice(const void* W, size_t rb, int rows, int K, const uint8_t* m6, int tokens,
+                      float* y, long ldy, int* status, cudaStream_t stream, cudaError_t* err) {
+  const int nsb = K / 256, slices = nsb / kSliceSb;
+  if (nsb % kSliceSb || slices < 1 || slices > 2 || tokens > 4 * NG) return false;
+  const size_t per_stage = (size_t)kTileRows * kSliceSb * LB_Q6K +
+                           (size_t)kSliceSb * 32 * NG * sizeof(float2);
+  const size_t fixed = (size_t)4 * NG * (kSliceSb * 1152 + 16) + sizeof(SliceSync);
+  if (fixed + 3 * per_stage > kTileSmemBudget) return false;
+  const int stages = (int)std::min<size_t>(8, (kTileSmemBudget - fixed) / per_stage);
+  const size_t smem = fixed + (size_t)stages * per_stage;
+  auto kern = gemv_q6k_slice_kernel<NG>;
+  if (prepared_occupancy(kern, (kSliceSb + 1) * 32, smem) < 1) return false;
+  if (slices > 1) {
+    *err = cudaMemset2DAsync(y, (size_t)ldy * sizeof(float), 0, (size_t)rows * sizeof(float),
+                             tokens, stream);
+    if (*err != cudaSuccess) return true;
+  }
+  const int grid = std::max(slices, sm_count() / slices * slices);
+  kern<<<grid, (kSliceSb + 1) * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows,
+                                                     slices, m6, tokens, y, ldy, stages, status);
+  *err = cudaGetLastError();
+  return true;
 }
 
 }  // namespace
@@ -655,6 +811,14 @@ cudaError_t launch_gemv_prepped(int type, const void* W, size_t rb, int rows, in
                          : launch_q6k_slab<2, true>(W, rb, rows, K, m6, 2, y, ldy, status, stream);
     for (int t0 = 0; t0 < tokens; t0 += 8) {  // 8 tokens per pass over the weights
       const int nt = std::min(8, tokens - t0);
+      cudaError_t se = cudaSuccess;
+      const uint8_t* m6t = m6 + (size_t)t0 * m6_bytes(K);
+      float* yt = y + (long)t0 * ldy;
+      if (nt <= 4 ? launch_q6k_slice<1>(W, rb, rows, K, m6t, nt, yt, ldy, status, stream, &se)
+                  : launch_q6k_slice<2>(W, rb, rows, K, m6t, nt, yt, ldy, status, stream, &se)) {
+        if (se != cudaSuccess) return se;
+        continue;
+      }
       const cudaError_t e =
           nt <= 4 ? launch_q6k_slab<1, false>(W, rb, rows, K, m6 + (size_t)t0 * m6_bytes(K), nt,
                                               y + (long)t0 * ldy, ldy, status, stream)

@@ -357,10 +357,12 @@ __host__ __device__ __forceinline__ int tile_red_floats() {
 // 64c + 32(gg%2) + 16h + i (low nibble for gg < 2, high nibble otherwise)
 // and its high 2 bits in qh byte 128 + 32c + 16h + i, bits 2gg and 2gg+1.
 
-// Prepared down-projection input of one entry (token, rank) for Q6_K rows
-// ("m6"), m6_bytes(K) bytes (16-byte aligned), per super-block (1152 bytes):
-//   frag[part][t][q] : uint2, halves (x[4t], x[4t+2]) and (x[4t+1], x[4t+3])
-//       of k-step q's sub-block, scaled, part 0 = high, 1 = low (1024 bytes);
+// Prepared input of one token for Q6_K rows ("m6"), m6_bytes(K) bytes
+// (16-byte aligned), per super-block (1152 bytes):
+//   frag[q / 2][part][t][q % 2] : uint2, halves (x[4t], x[4t+2]) and
+//       (x[4t+1], x[4t+3]) of k-step q's sub-block, scaled, part 0 = high,
+//       1 = low (1024 bytes): the eight threads that load one k-step pair
+//       of a token read 128 consecutive bytes (no bank conflicts);
 //   meta[q] : float2 (back, -32 * sum(x)) of k-step q's sub-block (128 bytes).
 __host__ __device__ __forceinline__ size_t m6_bytes(int K) { return (size_t)(K / 256) * 1152; }
 
@@ -394,21 +396,12 @@ __device__ __forceinline__ void m6_store_subblock(uint8_t* m6, int s_glob, float
       const __half hi = __float2half_rn(xs);
       const __half lo = __float2half_rn(xs - __half2float(hi));
       const int t4 = i >> 2, pos = i & 3, hp = (pos & 1) * 2 + (pos >> 1);
-      h[((0 * 4 + t4) * 16 + q) * 4 + hp] = hi;
-      h[((1 * 4 + t4) * 16 + q) * 4 + hp] = lo;
+      h[((((q >> 1) * 2 + 0) * 4 + t4) * 2 + (q & 1)) * 4 + hp] = hi;
+      h[((((q >> 1) * 2 + 1) * 4 + t4) * 2 + (q & 1)) * 4 + hp] = lo;
     }
     if (g == 0)
       reinterpret_cast<float2*>(base + 1024)[q] = make_float2(pow2f(ex + 13), -32.0f * sum);
   }
-}
-
-// Zeroes sub-block s_glob of an m6 buffer (padding past the matrix's rows).
-// 16 lanes; lane l < 16 writes 8 bytes of the fragments, lane 0 the meta.
-__device__ __forceinline__ void m6_zero_subblock(uint8_t* m6, int s_glob, int l) {
-  uint8_t* base = m6 + (size_t)(s_glob >> 4) * 1152;
-  const int q = q6_step_of(s_glob & 15);
-  if (l < 8) reinterpret_cast<uint2*>(base)[l * 16 + q] = make_uint2(0, 0);  // (part, t) = l
-  if (l == 0) reinterpret_cast<float2*>(base + 1024)[q] = make_float2(0.f, 0.f);
 }
 
 // int8 byte b of w as a float, exactly (2^23 + 128 + v, minus 2^23 + 128).
@@ -435,9 +428,15 @@ __device__ __forceinline__ void q6k_sb_mma(const uint8_t* rg, const uint8_t* rg8
   for (int grp = 0; grp < NG; ++grp) {
     bval[grp] = 4 * grp + bn < nt;
     mval[grp] = 4 * grp + t < nt;
-    bsrc[grp] = reinterpret_cast<const uint4*>(m6[4 * grp + bn] + (size_t)sb * 1152) +
-                (part * 4 + t) * 8;
-    msrc[grp] = reinterpret_cast<const float4*>(m6[4 * grp + t] + (size_t)sb * 1152 + 1024);
+    const uint8_t* pb = m6[4 * grp];  // m6[4 grp + bn], m6[4 grp + t] without indexing
+    const uint8_t* pm = m6[4 * grp];  // the pointer array by a register (local memory)
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+      if (bn == i) pb = m6[4 * grp + i];
+      if (t == i) pm = m6[4 * grp + i];
+    }
+    bsrc[grp] = reinterpret_cast<const uint4*>(pb + (size_t)sb * 1152) + part * 4 + t;
+    msrc[grp] = reinterpret_cast<const float4*>(pm + (size_t)sb * 1152 + 1024);
   }
   const float d = half_bits_to_float(lds_u16(rg + 208));
   const float d8 = half_bits_to_float(lds_u16(rg8 + 208));
@@ -475,8 +474,8 @@ __device__ __forceinline__ void q6k_sb_mma(const uint8_t* rg, const uint8_t* rg8
       for (int grp = 0; grp < NG; ++grp) {
         b01[grp] = b23[grp] = make_uint4(0, 0, 0, 0);
         if (bval[grp]) {
-          b01[grp] = ld_b16<SMEM>(bsrc[grp] + q0 / 2);
-          b23[grp] = ld_b16<SMEM>(bsrc[grp] + q0 / 2 + 1);
+          b01[grp] = ld_b16<SMEM>(bsrc[grp] + (q0 / 2) * 8);
+          b23[grp] = ld_b16<SMEM>(bsrc[grp] + (q0 / 2 + 1) * 8);
         }
         m01[grp] = m23[grp] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (mval[grp]) {

@@ -42,6 +42,7 @@ def test_known_answer_blocks(kind):  # tests.lisp T2257-2322
     (LB.TYPE_Q4_K, 2816, 100), (LB.TYPE_Q4_K, 4096, 300),
     (LB.TYPE_Q6_K, 256, 5), (LB.TYPE_Q6_K, 512, 2048), (LB.TYPE_Q6_K, 768, 77),
     (LB.TYPE_Q6_K, 2048, 129), (LB.TYPE_Q6_K, 3840, 64), (LB.TYPE_Q6_K, 4096, 300),
+    (LB.TYPE_Q6_K, 2048, 160), (LB.TYPE_Q6_K, 4096, 96),  # K slices of 8 super-blocks
 ])
 @pytest.mark.parametrize("tokens", [1, 2, 3, 8, 11])
 def test_gemv_matches_oracle(type_tag, K, rows, tokens):
