@@ -19,9 +19,11 @@ Reported:
   e2e           the same through the C ABI with host buffers: one
                 llambda_cuda_moe_session_run per layer per step, host copies
                 inside the timed region
-  roofline      the MoE layer (router + experts + combine) as the unit:
-                algorithmic bytes (router + shared + distinct experts) per
-                layer / measured layer time, against the measured HBM peak
+  roofline      the dominant kernel, the gate/up pass: its algorithmic bytes
+                (gate and up rows of every distinct routed expert, plus the
+                shared expert's) / its duration from CUDA events the sessions
+                record around it on the launch stream, against the measured
+                HBM peak; the routed down pass and the whole layer beside it
   kernels       dense dequant-GEMV roofline (configs 1 and 2) timed alone
   cpu_baseline  the CPU oracle (a C restatement of the reference path, AVX2,
                 all host threads) on a bounded sample, rank 0 only
@@ -49,9 +51,13 @@ sys.path.insert(0, ROOT)
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 NOMINAL_HBM_GBS = 8000.0
-# ncu DRAM traffic of one config-5 b32 layer on one GPU: gate/up 286.8 MB +
-# routed down 209.6 MB + router, shared down and small kernels ~5.6 MB
-LAYER_TRAFFIC_BYTES_N1 = 502_000_000
+# ncu DRAM traffic (read + write) of one config-5 b32 layer's gate/up launch
+# and routed down launch on one GPU
+GATE_UP_TRAFFIC_BYTES_N1 = 279_900_000
+DOWN_TRAFFIC_BYTES_N1 = 202_500_000
+# the same for one dense GEMV launch (workload, tokens)
+DENSE_TRAFFIC_BYTES = {("config1", 1): 33_100_000, ("config2", 1): 438_600_000,
+                       ("config2", 8): 444_700_000}
 
 
 def parse():
@@ -71,8 +77,9 @@ def parse():
                         "peer memory, or with an NCCL all-reduce per layer")
     p.add_argument("--no-graph", action="store_true",
                    help="launch every layer from Python instead of replaying one CUDA graph")
-    p.add_argument("--workload", default="stack",
-                   choices=["stack", "config1", "config2", "config3", "config4"])
+    p.add_argument("--workload", default="stack", choices=["stack", "config1", "config2"],
+                   help="stack: the config-5 MoE decode stack (the headline line); "
+                        "config1/config2: one dense dequant-GEMV of --batch tokens")
     return p.parse_args()
 
 
@@ -340,10 +347,35 @@ def run_reference(args):
     return 0
 
 
+def run_dense(args, torch, LB, CF):
+    """--workload config1|config2: one dense dequant-GEMV (rank 0 only) with
+    --batch tokens; value = algorithmic HBM GB/s (weights + inputs + outputs)."""
+    cfg = CF.CONFIG1 if args.workload == "config1" else CF.CONFIG2
+    r = time_dense_gemv(torch, LB, cfg, args.batch, reps=max(args.steps, 1))
+    peak, peak_kind = hbm_peak()
+    line = {"metric": "dequant-GEMV HBM GB/s", "value": round(r["achieved_gbs"], 1),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": 3,
+            "ms_per_step": round(r["us_per_launch"] / 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": r["workload"], "tokens": args.batch,
+                       "l2": f"{r['weight_copies_rotated']} weight copies rotated past L2"},
+            "roofline": {"bound": "hbm", "achieved": round(r["achieved_gbs"], 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(r["achieved_gbs"] / peak, 4),
+                         "peak_kind": peak_kind,
+                         "traffic": DENSE_TRAFFIC_BYTES.get((args.workload, args.batch))},
+            "e2e": None, "cpu_baseline": None, "gpu_launches": 2 * max(args.steps, 1)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     import llambda_b200 as LB
     from llambda_b200 import configs as CF
+    if args.workload in ("config1", "config2"):
+        if LB.probe() != 1:
+            raise SystemExit("CUDA backend unavailable: " + LB._native.last_error())
+        return run_dense(args, torch, LB, CF)
     rank, world, local = dist_setup(args.gpus)
     if LB.probe() != 1:
         raise SystemExit("CUDA backend unavailable: " + LB._native.last_error())
@@ -413,9 +445,16 @@ def run_ours(args):
     ms = e0.elapsed_time(e1) / args.steps
     ms = max_over_ranks(ms, world)
     value = B / (ms * 1e-3)
-    step(layer_ev)  # per-layer times (launched eagerly) for the roofline
+    # per-layer times and, from CUDA events the sessions record on the same
+    # stream, the gate/up and routed down kernels of every layer (launched eagerly)
+    for s in sessions:
+        s.time_kernels(True)
+    step(layer_ev)
     torch.cuda.synchronize()
     layer_ms = [a.elapsed_time(b) for a, b in layer_ev]
+    kern_ms = [s.kernel_ms() for s in sessions]
+    for s in sessions:
+        s.time_kernels(False)
 
     # routing of the timed steps (identical every step: same x0) -> algorithmic bytes
     sel = torch.empty(B, cfg.top_k, dtype=torch.int32, device="cuda")
@@ -445,17 +484,29 @@ def run_ours(args):
     layer_bytes = [cfg.router_bytes() + (cfg.shared_bytes() if streams_shared else 0)
                    + u * cfg.expert_bytes() + 2 * 4 * B * cfg.hidden for u in own_distinct]
     peak, peak_kind = hbm_peak()
-    achieved = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "moe_layer (rms_norm+router+route+up+down+combine)",
+    # the dominant kernel: the gate/up pass (its rows of every distinct routed
+    # expert this rank owns, plus the shared expert's where it runs here)
+    gu_bytes = [u * cfg.gate_up_bytes() + (cfg.shared_gate_up_bytes() if streams_shared else 0)
+                for u in own_distinct]
+    gu_ms = statistics.mean(k[0] for k in kern_ms)
+    dn_bytes = [u * cfg.down_bytes() for u in own_distinct]
+    dn_ms = statistics.mean(k[1] for k in kern_ms)
+    achieved = (sum(gu_bytes) / NL) / (gu_ms * 1e-3) / 1e9
+    layer_gbs = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "moe_up_slab_kernel (gate/up pass, Q4_K)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
-                "algorithmic_bytes_per_layer": int(sum(layer_bytes) / NL),
-                "layer_us_mean": round(statistics.mean(layer_ms) * 1e3, 2),
-                # DRAM read+write bytes of one layer at N=1, from one ncu capture of
-                # the layer's kernels (profiles/moe_slab_kernels_config5_b32.md)
-                "traffic": LAYER_TRAFFIC_BYTES_N1 if world == 1 else None,
-                "traffic_unit": "bytes per layer (ncu dram__bytes_read+write)"}
+                "algorithmic_bytes_per_launch": int(sum(gu_bytes) / NL),
+                "launch_us_mean": round(gu_ms * 1e3, 2),
+                # DRAM read+write bytes of one gate/up launch at N=1 (ncu capture)
+                "traffic": GATE_UP_TRAFFIC_BYTES_N1 if world == 1 else None,
+                "down": {"kernel": "moe_down_slab_kernel (routed, Q6_K)",
+                         "achieved": round((sum(dn_bytes) / NL) / (dn_ms * 1e-3) / 1e9, 1),
+                         "launch_us_mean": round(dn_ms * 1e3, 2),
+                         "traffic": DOWN_TRAFFIC_BYTES_N1 if world == 1 else None},
+                "layer": {"achieved": round(layer_gbs, 1), "frac": round(layer_gbs / peak, 4),
+                          "algorithmic_bytes": int(sum(layer_bytes) / NL),
+                          "us_mean": round(statistics.mean(layer_ms) * 1e3, 2)}}
 
     # e2e through the C ABI with host buffers (one call per layer per step)
     e2e = None
@@ -493,8 +544,6 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1:
         if not args.no_kernels:
-            for s in sessions:
-                pass
             kernels = {}
             try:
                 kernels["config1_b1"] = time_dense_gemv(torch, LB, CF.CONFIG1, 1)

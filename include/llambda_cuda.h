@@ -212,6 +212,16 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_run_device(llambda_cuda_moe_sessio
  * a CUDA error. */
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_status(llambda_cuda_moe_session* session);
 
+/* Kernel timing (a measurement aid with no counterpart in the reference):
+ * with enable != 0 every later run records CUDA events around the gate/up
+ * pass and the routed down pass on the run's stream;
+ * llambda_cuda_moe_session_kernel_ms waits for the last run's events and
+ * returns the two durations in milliseconds.  0 on success, -1 on failure. */
+LLAMBDA_CUDA_API int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_session* session,
+                                                           int enable);
+LLAMBDA_CUDA_API int llambda_cuda_moe_session_kernel_ms(llambda_cuda_moe_session* session,
+                                                        float* gate_up_ms, float* down_ms);
+
 /* Expert-parallel reduction over peer memory.  These entry points have no
  * counterpart in the reference (llambda runs on one device).
  *

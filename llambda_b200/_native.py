@@ -81,6 +81,9 @@ SIGNATURES = {
     "llambda_cuda_moe_session_run": (C.c_int, [_vp, _fp, _sz, _fp, _i32p, _fp]),
     "llambda_cuda_moe_session_run_device": (C.c_int, [_vp, _vp, _sz, _vp, _vp, _vp, _vp]),
     "llambda_cuda_moe_session_status": (C.c_int, [_vp]),
+    "llambda_cuda_moe_session_time_kernels": (C.c_int, [_vp, C.c_int]),
+    "llambda_cuda_moe_session_kernel_ms": (C.c_int, [_vp, C.POINTER(C.c_float),
+                                                      C.POINTER(C.c_float)]),
     "llambda_cuda_moe_peer_bytes": (_sz, [_vp, C.c_int]),
     "llambda_cuda_moe_session_attach_peers": (C.c_int, [_vp, C.c_int, C.c_int,
                                                         C.POINTER(_vp), _sz]),
@@ -335,6 +338,17 @@ class MoeSession:
         peer_ptrs[r] is rank r's copy of one zero-filled symmetric buffer."""
         arr = (_vp * world)(*[int(p) for p in peer_ptrs])
         _check(lib().llambda_cuda_moe_session_attach_peers(self._h, rank, world, arr, nbytes))
+
+    def time_kernels(self, enable: bool = True) -> None:
+        """Record CUDA events around the gate/up and routed down passes of
+        every later run (a measurement aid)."""
+        _check(lib().llambda_cuda_moe_session_time_kernels(self._h, int(bool(enable))))
+
+    def kernel_ms(self) -> tuple[float, float]:
+        """(gate/up, routed down) milliseconds of the last run (timing on)."""
+        a, b = C.c_float(), C.c_float()
+        _check(lib().llambda_cuda_moe_session_kernel_ms(self._h, C.byref(a), C.byref(b)))
+        return float(a.value), float(b.value)
 
     def status(self) -> int:
         rc = lib().llambda_cuda_moe_session_status(self._h)

@@ -88,6 +88,17 @@ class MoeConfig:
         down = row_bytes(self.down_type, self.k_down) * self.hidden
         return gate + up + down
 
+    def gate_up_bytes(self) -> int:
+        up = row_bytes(self.up_type, self.k_in) * self.inter
+        return up * (2 if self.has_gate else 1)
+
+    def down_bytes(self) -> int:
+        return row_bytes(self.down_type, self.k_down) * self.hidden
+
+    def shared_gate_up_bytes(self) -> int:
+        up = row_bytes(self.up_type, self.k_in) * self.inter_sh
+        return up * (2 if self.has_gate else 1)
+
     def shared_bytes(self) -> int:
         up = row_bytes(self.up_type, self.k_in) * self.inter_sh
         gate = up if self.has_gate else 0

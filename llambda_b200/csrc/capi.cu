@@ -227,7 +227,11 @@ struct llambda_cuda_moe_session {
   void* work = nullptr;
   Pinned hx, hout, hsel, hw;
   DevBuf dx, dout, dsel, dw;
+  cudaEvent_t marks[3] = {nullptr, nullptr, nullptr};  // kernel timing, when enabled
+  bool timing = false;
   ~llambda_cuda_moe_session() {
+    for (cudaEvent_t e : marks)
+      if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
     for (void* p : owned) cudaFree(p);
     if (work) cudaFree(work);
@@ -741,7 +745,9 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
     int status = 0;
     cuda_check(cudaMemsetAsync(s->w.status, 0, 4, s->stream), "memset");
     cuda_check(cudaMemcpyAsync(dx, hx, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
-    cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, &s->maps, s->stream), "MoE launch");
+    cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, &s->maps, s->stream,
+                              s->timing ? s->marks : nullptr),
+               "MoE launch");
     cuda_check(cudaMemcpyAsync(hout, dout, xb, cudaMemcpyDeviceToHost, s->stream), "output copy");
     int32_t* hsel = selected ? static_cast<int32_t*>(s->hsel.get(sb)) : nullptr;
     float* hw = weights ? static_cast<float*>(s->hw.get(sb)) : nullptr;
@@ -771,13 +777,47 @@ int llambda_cuda_moe_session_run_device(llambda_cuda_moe_session* s, const float
     DeviceGuard g(s->device);
     if ((int64_t)tokens > s->max_tokens) throw Failure("Token count exceeds max_tokens.");
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    cuda_check(lb::launch_moe(s->m, s->w, device_x, (int)tokens, device_out, &s->maps, st),
+    cuda_check(lb::launch_moe(s->m, s->w, device_x, (int)tokens, device_out, &s->maps, st,
+                              s->timing ? s->marks : nullptr),
                "MoE launch");
     const size_t sb = tokens * s->m.top_k * 4;
     if (device_selected)
       cuda_check(cudaMemcpyAsync(device_selected, s->w.sel, sb, cudaMemcpyDeviceToDevice, st), "copy");
     if (device_weights)
       cuda_check(cudaMemcpyAsync(device_weights, s->w.wts, sb, cudaMemcpyDeviceToDevice, st), "copy");
+    return 0;
+  });
+}
+
+int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_session* s, int enable) {
+  if (!s) {
+    set_error("A session is required.");
+    return -1;
+  }
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    if (enable)
+      for (cudaEvent_t& e : s->marks)
+        if (!e) cuda_check(cudaEventCreate(&e), "create timing event");
+    s->timing = enable != 0;
+    return 0;
+  });
+}
+
+int llambda_cuda_moe_session_kernel_ms(llambda_cuda_moe_session* s, float* gate_up_ms,
+                                       float* down_ms) {
+  if (!s || !gate_up_ms || !down_ms) {
+    set_error("A session and two outputs are required.");
+    return -1;
+  }
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    if (!s->timing) throw Failure("Kernel timing is not enabled on this session.");
+    cuda_check(cudaEventSynchronize(s->marks[2]), "timing events");
+    cuda_check(cudaEventElapsedTime(gate_up_ms, s->marks[0], s->marks[1]), "gate/up time");
+    cuda_check(cudaEventElapsedTime(down_ms, s->marks[1], s->marks[2]), "down time");
     return 0;
   });
 }

@@ -158,7 +158,10 @@ void moe_work_carve(const MoeDevice& m, int max_tokens, void* base, MoeWork* w);
 
 // out[t][h] for t < tokens.  maps: from moe_maps_build for this layer, or
 // null to build them for this call.
+// marks (optional, three events): recorded before the gate/up pass, after it
+// and after the routed down pass, for timing those kernels.
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int tokens,
-                       float* out, const SlabMaps* maps, cudaStream_t stream);
+                       float* out, const SlabMaps* maps, cudaStream_t stream,
+                       const cudaEvent_t* marks = nullptr);
 
 }  // namespace lb

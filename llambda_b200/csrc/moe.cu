@@ -1739,25 +1739,29 @@ namespace {
 
 template <int UT, int DT>
 cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T,
-                                 const SlabMaps* maps, cudaStream_t s) {
+                                 const SlabMaps* maps, cudaStream_t s, const cudaEvent_t* marks) {
   cudaError_t e;
+  auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
+  if ((e = mark(0)) != cudaSuccess) return e;
   if constexpr (UT == LB_TYPE_Q4_K) {
     e = launch_up_mma<DT>(m, w, T, maps, s);
   } else {
     e = launch_up<UT, DT>(m, w, T, 0, s);
     if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_up<UT, DT>(m, w, T, 1, s);
   }
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || (e = mark(1)) != cudaSuccess) return e;
   if (DT == LB_TYPE_Q4_K) {
     moe_down_sums_kernel<<<std::min(T * m.top_k + T, sm_count() * 4), 128, 0, s>>>(m, w, T);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (DT == LB_TYPE_Q6_K && down_uses_i6(m)) {
     e = launch_down_slab(m, w, T, 0, s);
+    if (e == cudaSuccess) e = mark(2);
     if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_down_slab(m, w, T, 1, s);
     return e;
   }
   e = launch_down<DT>(m, w, T, 0, s);
+  if (e == cudaSuccess) e = mark(2);
   if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_down<DT>(m, w, T, 1, s);
   return e;
 }
@@ -1799,8 +1803,7 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
 }
 
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int T, float* out,
-                       const SlabMaps* maps,
-                       cudaStream_t s) {
+                       const SlabMaps* maps, cudaStream_t s, const cudaEvent_t* marks) {
   if (T <= 0) return cudaSuccess;
   if (T > w.max_tokens || m.experts > kMaxExperts || m.top_k > 32 || T * m.top_k > 4 * 1024)
     return cudaErrorInvalidValue;
@@ -1849,13 +1852,13 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
   if (!gate_ok) return cudaErrorInvalidValue;
   if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q6_K)
-    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q6_K>(m, w, T, maps, s);
+    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q6_K>(m, w, T, maps, s, marks);
   else if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q4_K)
-    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q4_K>(m, w, T, maps, s);
+    e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q4_K>(m, w, T, maps, s, marks);
   else if (m.up_type == LB_TYPE_Q6_K && m.down_type == LB_TYPE_Q6_K)
-    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q6_K>(m, w, T, maps, s);
+    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q6_K>(m, w, T, maps, s, marks);
   else if (m.up_type == LB_TYPE_Q6_K && m.down_type == LB_TYPE_Q4_K)
-    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q4_K>(m, w, T, maps, s);
+    e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q4_K>(m, w, T, maps, s, marks);
   else
     return cudaErrorInvalidValue;
   if (e != cudaSuccess) return e;
