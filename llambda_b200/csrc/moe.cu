@@ -435,12 +435,11 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
 // super-block of one token each), and every CTA forms its 16 x 8 logits (dot-product-with-f32-tensor-data, L4096-4107) with
 // packed fp32x2 FMAs and a 31-shuffle butterfly.  Row E of qwen3next (the
 // shared-expert gate) comes from router_extra_row when it is kept apart.
-constexpr int kRouterTok = 8, kRouterRows = 16;
-__global__ void __launch_bounds__(128) moe_router_kernel(MoeDevice m, MoeWork w,
-                                                         const float* __restrict__ x, int T,
-                                                         int router_rows) {
+constexpr int kRouterTok = 8, kRouterRows = 16, kRouterWarps = 8;
+__global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
+    MoeDevice m, MoeWork w, const float* __restrict__ x, int T, int router_rows) {
   extern __shared__ float4 rs4[];  // [8][H/4] tokens, then [16][H/4] router rows
-  __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t bar_x, bar_w;
   __shared__ float s_scale[kRouterTok];
   const int H = m.hidden, H4 = H >> 2, E = m.experts;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -450,22 +449,24 @@ __global__ void __launch_bounds__(128) moe_router_kernel(MoeDevice m, MoeWork w,
   const int main_rows = max(0, min(crows, main_end - crow0));
   float4* xs4 = rs4;
   float4* ws4 = rs4 + kRouterTok * H4;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
+  if (threadIdx.x == 0) {  // the token tile and the rows complete on separate barriers, so
+    mbar_init(&bar_x, 1);  // the norm and the prepared input overlap the rows' copy
+    mbar_init(&bar_w, 1);
     fence_mbar_init();
     const uint32_t rowb = (uint32_t)H * 4u;
-    mbar_expect_tx(&bar, rowb * (uint32_t)(nt + crows));
-    tma_load_1d(xs4, x + (long)t0 * H, rowb * nt, &bar);
-    if (main_rows > 0) tma_load_1d(ws4, m.router + (size_t)crow0 * H, rowb * main_rows, &bar);
+    mbar_expect_tx(&bar_x, rowb * (uint32_t)nt);
+    tma_load_1d(xs4, x + (long)t0 * H, rowb * nt, &bar_x);
+    mbar_expect_tx(&bar_w, rowb * (uint32_t)crows);
+    if (main_rows > 0) tma_load_1d(ws4, m.router + (size_t)crow0 * H, rowb * main_rows, &bar_w);
     if (main_rows < crows)  // row E, the last row of the last tile
-      tma_load_1d(ws4 + (size_t)main_rows * H4, m.router_extra_row, rowb, &bar);
+      tma_load_1d(ws4 + (size_t)main_rows * H4, m.router_extra_row, rowb, &bar_w);
   }
   for (int i = nt * H4 + threadIdx.x; i < kRouterTok * H4; i += blockDim.x)
     xs4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
-  mbar_wait(&bar, 0, w.status);
+  mbar_wait(&bar_x, 0, w.status);
   if (m.input_norm) {
-    for (int tok = warp; tok < nt; tok += 4) {
+    for (int tok = warp; tok < nt; tok += kRouterWarps) {
       float acc = 0.f;
       for (int c = lane; c < H4; c += 32) {
         const float4 v = xs4[tok * H4 + c];
@@ -492,7 +493,8 @@ __global__ void __launch_bounds__(128) moe_router_kernel(MoeDevice m, MoeWork w,
      // warps share the tokens' (token, super-block) items
     const int K = m.k_in, nsb = K >> 8;
     const long ld_up = up_ld_floats(K);
-    for (int it = blockIdx.x * 4 + warp; it < nt * nsb; it += gridDim.x * 4) {
+    for (int it = blockIdx.x * kRouterWarps + warp; it < nt * nsb;
+         it += gridDim.x * kRouterWarps) {
       const int tok = it / nsb, sb = it - tok * nsb;
       uint8_t* mx = reinterpret_cast<uint8_t*>(w.xp_up + (long)(t0 + tok) * ld_up);
 #pragma unroll
@@ -502,53 +504,60 @@ __global__ void __launch_bounds__(128) moe_router_kernel(MoeDevice m, MoeWork w,
       }
     }
   }
-  const int row0 = warp * 4;  // this warp's 4 rows of the tile
-  if (row0 < crows) {
-    float2 acc[4][kRouterTok / 2];
+  mbar_wait(&bar_w, 0, w.status);
+  constexpr int R = kRouterRows / kRouterWarps;  // this warp's rows of the tile
+  const int row0 = warp * R;
+  if (row0 >= crows) return;
+  float2 acc[R][kRouterTok / 2];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+  for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int p = 0; p < kRouterTok / 2; ++p) acc[r][p] = make_float2(0.f, 0.f);
-    const float4* wr[4];
+    for (int p = 0; p < kRouterTok / 2; ++p) acc[r][p] = make_float2(0.f, 0.f);
+  const float4* wr[R];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) wr[r] = ws4 + (size_t)min(row0 + r, crows - 1) * H4;
-    for (int c = lane; c < H4; c += 32) {
-      float4 wv[4];
+  for (int r = 0; r < R; ++r) wr[r] = ws4 + (size_t)min(row0 + r, crows - 1) * H4;
+  for (int c = lane; c < H4; c += 32) {
+    float4 wv[R];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) wv[r] = wr[r][c];
+    for (int r = 0; r < R; ++r) wv[r] = wr[r][c];
 #pragma unroll
-      for (int p = 0; p < kRouterTok / 2; ++p) {
-        const float4 xa = xs4[(2 * p) * H4 + c], xb = xs4[(2 * p + 1) * H4 + c];
+    for (int p = 0; p < kRouterTok / 2; ++p) {
+      const float4 xa = xs4[(2 * p) * H4 + c], xb = xs4[(2 * p + 1) * H4 + c];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          acc[r][p] = __ffma2_rn(make_float2(wv[r].x, wv[r].x), make_float2(xa.x, xb.x), acc[r][p]);
-          acc[r][p] = __ffma2_rn(make_float2(wv[r].y, wv[r].y), make_float2(xa.y, xb.y), acc[r][p]);
-          acc[r][p] = __ffma2_rn(make_float2(wv[r].z, wv[r].z), make_float2(xa.z, xb.z), acc[r][p]);
-          acc[r][p] = __ffma2_rn(make_float2(wv[r].w, wv[r].w), make_float2(xa.w, xb.w), acc[r][p]);
-        }
+      for (int r = 0; r < R; ++r) {
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].x, wv[r].x), make_float2(xa.x, xb.x), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].y, wv[r].y), make_float2(xa.y, xb.y), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].z, wv[r].z), make_float2(xa.z, xb.z), acc[r][p]);
+        acc[r][p] = __ffma2_rn(make_float2(wv[r].w, wv[r].w), make_float2(xa.w, xb.w), acc[r][p]);
       }
     }
-    float v[32];  // value r * 8 + n ends on lane r * 8 + n
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int p = 0; p < kRouterTok / 2; ++p) {
-        v[r * 8 + 2 * p] = acc[r][p].x;
-        v[r * 8 + 2 * p + 1] = acc[r][p].y;
-      }
-#pragma unroll
-    for (int h = 16; h >= 1; h >>= 1) {
-      const bool upper = (lane & h) != 0;
-#pragma unroll
-      for (int i = 0; i < h; ++i) {
-        const float send = upper ? v[i] : v[i + h];
-        const float keep = upper ? v[i + h] : v[i];
-        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
-      }
-    }
-    const int r = lane >> 3, n = lane & 7;
-    if (row0 + r < crows && n < nt) w.logits[(long)(t0 + n) * (E + 1) + crow0 + row0 + r] = v[0];
   }
+  // transpose-reduce of the warp's R * 8 sums over the 32 lanes: value
+  // r * 8 + n ends on lanes 2(r * 8 + n) and 2(r * 8 + n) + 1
+  constexpr int NV = R * kRouterTok;
+  static_assert(NV == 16, "two rows of eight tokens per warp");
+  float v[NV];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int p = 0; p < kRouterTok / 2; ++p) {
+      v[r * 8 + 2 * p] = acc[r][p].x;
+      v[r * 8 + 2 * p + 1] = acc[r][p].y;
+    }
+#pragma unroll
+  for (int h = 16, cnt = NV / 2; h >= 2; h >>= 1, cnt >>= 1) {
+    const bool upper = (lane & h) != 0;
+#pragma unroll
+    for (int i = 0; i < cnt; ++i) {
+      const float send = upper ? v[i] : v[i + cnt];
+      const float keep = upper ? v[i + cnt] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  const int idx = (lane >> 1) & (NV - 1), r = idx >> 3, n = idx & 7;
+  if ((lane & 1) == 0 && row0 + r < crows && n < nt)
+    w.logits[(long)(t0 + n) * (E + 1) + crow0 + row0 + r] = v[0];
 }
 
 // Routing metadata of the expert owning a run of units, cached per warp.
@@ -1817,10 +1826,10 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   const int all_rows = m.router_rows + (m.router_extra_row ? 1 : 0);  // column E: shared gate
   if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
       router_smem <= 192 * 1024 &&
-      prepared_occupancy(moe_router_kernel, 128, router_smem) >= 1) {
+      prepared_occupancy(moe_router_kernel, kRouterWarps * 32, router_smem) >= 1) {
     // top-k and routing ride on the router launch (its last CTAs)
     dim3 grid((all_rows + kRouterRows - 1) / kRouterRows, (T + kRouterTok - 1) / kRouterTok);
-    moe_router_kernel<<<grid, 128, router_smem, s>>>(m, w, x, T, all_rows);
+    moe_router_kernel<<<grid, kRouterWarps * 32, router_smem, s>>>(m, w, x, T, all_rows);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   } else {
     if (m.up_type == LB_TYPE_Q4_K)
