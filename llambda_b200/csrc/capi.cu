@@ -1039,7 +1039,7 @@ int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
     lb::moe_work_carve(m, T, base, &w);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     int status = 0;
-    cuda_check(cudaMemsetAsync(w.status, 0, sizeof(int), st), "clear status");
+    cuda_check(cudaMemsetAsync(w.status, 0, 2 * sizeof(int), st), "clear status and ticket");
     cuda_check(lb::launch_moe(m, w, device_x, T, device_out, nullptr, st), "MoE launch");
     cuda_check(cudaMemcpyAsync(&status, w.status, sizeof(int), cudaMemcpyDeviceToHost, st),
                "status copy");

@@ -136,6 +136,8 @@ struct MoeWork {
   int* pass_off_dn;   // [E+1] the same for the down pass (4 entries per pass)
   int* status;        // [1] device status word (bit 0: non-positive weight sum,
                       //  bit 1: a TMA stage wait timed out)
+  int* tickets;       // [1] arrival counter of the top-k launch (zero between
+                      //  launches; right after the status word)
   float* xn;          // [T][H] normalised input (when input_norm is set)
   float* xp_up;       // [T] prepared gate/up inputs (stride xp_stride(k_in))
   float* xp_down;     // [T*k + T] prepared down inputs: routed entry ids, then

@@ -202,14 +202,35 @@ __device__ __forceinline__ void topk_token(const MoeDevice& m, const MoeWork& w,
   }
 }
 
+// Declared here, defined with the routing below.
+template <bool CG>
+__device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
+                                            int pass_nt);
+
+// Top-k (warp 0 of each CTA, one token per CTA) with the routing on the last
+// CTA to finish (an arrival counter; its eight warps group the entries), so
+// the grouping needs no launch of its own.  The counter is zero between
+// launches: the last CTA resets it.
 template <int PER>
-__global__ void __launch_bounds__(32) topk_kernel(MoeDevice m, MoeWork w, int T) {
-  topk_token<PER>(m, w, blockIdx.x, threadIdx.x);
+__global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w, int T,
+                                                         int pass_nt) {
+  __shared__ int s_last;
+  if (threadIdx.x < 32) topk_token<PER>(m, w, blockIdx.x, threadIdx.x);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(w.tickets, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // every CTA's selections are visible from here
+  route_block<true>(m, w, T, pass_nt);
+  if (threadIdx.x == 0) *w.tickets = 0;
 }
 
 // Groups the (token, rank) entries by owned expert, stably.  One CTA of up to
 // 8 warps.  pass_nt: tokens per pass of the up kernel; pass_off counts
-// passes.
+// passes.  CG: the selections were written by other CTAs of the same launch
+// (read through L2).
+template <bool CG>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
                                             int pass_nt) {
   __shared__ int s_count[kMaxExperts];
@@ -230,7 +251,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
         for (int j = 0; j < 8; ++j) {
           const int idj = c + 32 * j + lane;  // clamped, not guarded: the loads overlap
           const int* p = w.sel + min(idj, n - 1);
-          const int v = __ldg(p);
+          const int v = CG ? __ldcg(p) : __ldg(p);
           ev[j] = idj < n ? v : -1;
         }
       const int id = c + lane;
@@ -329,13 +350,10 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
   // the first half holds each entry's position within its expert).
   for (int id = threadIdx.x; id < n; id += blockDim.x) {
     const int pos = w.entries[id];
-    if (pos >= 0) w.entries[T * k + s_offset[w.sel[id]] + pos] = id;
+    if (pos >= 0) w.entries[T * k + s_offset[CG ? __ldcg(w.sel + id) : w.sel[id]] + pos] = id;
   }
 }
 
-__global__ void __launch_bounds__(256) route_kernel(MoeDevice m, MoeWork w, int T, int pass_nt) {
-  route_block(m, w, T, pass_nt);
-}
 
 // ---------------------------------------------------------------- prep
 // Per token: optional rms-norm (rms-norm-into, llambda.lisp L859-879:
@@ -1802,7 +1820,8 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
   w->active = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
   w->pass_off = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
   w->pass_off_dn = reinterpret_cast<int*>(take((size_t)(E + 1) * 4));
-  w->status = reinterpret_cast<int*>(take(4));
+  w->status = reinterpret_cast<int*>(take(8));  // the status word, then the ticket
+  w->tickets = w->status ? w->status + 1 : nullptr;
   w->xn = reinterpret_cast<float*>(take(m.input_norm ? (size_t)T * m.hidden * 4 : 4));
   w->xp_up = reinterpret_cast<float*>(take((size_t)T * up_ld_floats(m.k_in) * 4));
   w->xp_down = reinterpret_cast<float*>(
@@ -1846,16 +1865,14 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     e = launch_gemv_f32(m.router, m.router_rows, m.hidden, xr, m.hidden, T, w.logits, E + 1, s);
     if (e != cudaSuccess) return e;
   }
-  {
-    const int per = (E + 31) / 32;
-    if (per <= 1) topk_kernel<1><<<T, 32, 0, s>>>(m, w, T);
-    else if (per <= 2) topk_kernel<2><<<T, 32, 0, s>>>(m, w, T);
-    else if (per <= 4) topk_kernel<4><<<T, 32, 0, s>>>(m, w, T);
-    else if (per <= 8) topk_kernel<8><<<T, 32, 0, s>>>(m, w, T);
-    else if (per <= 16) topk_kernel<16><<<T, 32, 0, s>>>(m, w, T);
-    else topk_kernel<32><<<T, 32, 0, s>>>(m, w, T);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    route_kernel<<<1, 256, 0, s>>>(m, w, T, up_pass_tokens(m, T));
+  {  // top-k per token, the routing on the last CTA
+    const int per = (E + 31) / 32, pnt = up_pass_tokens(m, T);
+    if (per <= 1) topk_route_kernel<1><<<T, 256, 0, s>>>(m, w, T, pnt);
+    else if (per <= 2) topk_route_kernel<2><<<T, 256, 0, s>>>(m, w, T, pnt);
+    else if (per <= 4) topk_route_kernel<4><<<T, 256, 0, s>>>(m, w, T, pnt);
+    else if (per <= 8) topk_route_kernel<8><<<T, 256, 0, s>>>(m, w, T, pnt);
+    else if (per <= 16) topk_route_kernel<16><<<T, 256, 0, s>>>(m, w, T, pnt);
+    else topk_route_kernel<32><<<T, 256, 0, s>>>(m, w, T, pnt);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
