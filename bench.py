@@ -560,9 +560,9 @@ def run_ours(args):
                    "sample": f"{B} tokens through 1 qwen3next layer per sample "
                              f"({per_layer * 1e3:.1f} ms), scaled to {NL} layers"}
 
-    # rms-norm + router, top-k, route, gate/up, routed down, shared down (ranks
-    # that compute a share of the shared expert), combine
-    launches_per_layer = 6 + (1 if streams_shared else 0)
+    # rms-norm + router, top-k with routing, gate/up, routed down, shared down
+    # (ranks that compute a share of the shared expert), combine
+    launches_per_layer = 5 + (1 if streams_shared else 0)
     line = {"metric": "MoE FFN decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",

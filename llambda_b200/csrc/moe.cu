@@ -722,11 +722,20 @@ __global__ void __launch_bounds__(128) moe_up_kernel(MoeDevice m, MoeWork w, int
 // With gate and up, the up warps hand their row sums to the gate warps once
 // per slab through a double-buffered exchange guarded by two more barriers.
 // Every wait is bounded; a timeout raises a CTA-wide abort flag.
+// A gate/up work item as the producer publishes it with the item's first
+// stage (before it arms that stage's barrier): the slab's first row, the
+// matrix's rows, the pass's entries and their ids.
+struct __align__(16) UpUnit {
+  int row0, rows_e, nt, shared;
+  int ids[4];
+};
+
 struct SlabSync {
   uint64_t full[kSlabMaxStages];
   uint64_t empty[kSlabMaxStages];
   uint64_t xfull[2];
   uint64_t xempty[2];
+  UpUnit unit[kSlabMaxStages];
   int abort;
   int pad[3];
   uint4 zero[2];  // the B source of the threads whose column cannot be non-zero
@@ -843,6 +852,17 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
               break;
             }
             const int nt = min(NT, x.t_end - t0);
+            if (sb == 0) {  // the item's rows and entries travel with its first stage
+              UpUnit& uu = sync->unit[s];
+              uu.row0 = x.row0;
+              uu.rows_e = x.rows_e;
+              uu.nt = nt;
+              uu.shared = x.shared ? 1 : 0;
+              for (int n = 0; n < NT; ++n) {
+                const int tt = min(t0 + n, x.t_end - 1);
+                uu.ids[n] = x.shared ? T * k + tt : view.list[tt];
+              }
+            }
             mbar_expect_tx(&sync->full[s], STAGE_W + nt * 1088);
             uint8_t* st = smem + (size_t)s * STAGE;
             // one box of kUpBoxRows rows per copy (the slab's blocks lie
@@ -882,154 +902,150 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   RingPos rp;
   int pass = 0;
   bool ok = true;
-  for (int i = 0; i < n_my && ok; ++i) {
-    const Unit x = unit_at(u0 + i);
-    const int kd = x.shared ? m.k_down_sh : m.k_down, tasks_d = kd >> 6;
-    for (int t0 = x.t_begin; t0 < x.t_end && ok; t0 += NT, ++pass) {
-      const int nt = min(NT, x.t_end - t0);
-      int ids[NT];
+  for (int i = 0; i < n_my && ok; ++i, ++pass) {
+    UpUnit x;  // read with the item's first stage
+    int nt = 0;
+    float2 acc[NT][2];
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const int tt = min(t0 + n, x.t_end - 1);
-        ids[n] = x.shared ? T * k + tt : view.list[tt];
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) acc[n][r] = make_float2(0.f, 0.f);
+    for (int sb = 0; sb < nsb; ++sb, rp.next(stages)) {
+      const int s = rp.s;
+      if (!mbar_wait_or_abort(&sync->full[s], rp.phase, w.status, abort)) {
+        ok = false;
+        break;
       }
-      float2 acc[NT][2];
+      if (sb == 0) {  // the item, as the producer published it with this stage
+        x = sync->unit[s];
+        nt = x.nt;
+      }
+      const uint8_t* st = smem + (size_t)s * STAGE;
+      const uint8_t* blk = st + warp * BOX;
+      BSlice bs[NT];
 #pragma unroll
       for (int n = 0; n < NT; ++n)
+        bs[n] = BSlice{st + STAGE_W + n * 1088, st + STAGE_W + n * 1088 + 1024};
+      q4k_sb_mma_n<NT, true>(nt, blk + g * LB_Q4K, blk + (g + 8) * LB_Q4K, bs,
+                             reinterpret_cast<const uint8_t*>(sync->zero), lane, acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sync->empty[s]);
+    }
+    if (!ok) break;
+    const int kd = x.shared ? m.k_down_sh : m.k_down, tasks_d = kd >> 6;
+    // row sums of rows g and g+8 of this block on lane t == 0 of each quad
+    float v[2][NT];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) acc[n][r] = make_float2(0.f, 0.f);
-      for (int sb = 0; sb < nsb; ++sb, rp.next(stages)) {
-        const int s = rp.s;
-        if (!mbar_wait_or_abort(&sync->full[s], rp.phase, w.status, abort)) {
-          ok = false;
-          break;
-        }
-        const uint8_t* st = smem + (size_t)s * STAGE;
-        const uint8_t* blk = st + warp * BOX;
-        BSlice bs[NT];
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-          bs[n] = BSlice{st + STAGE_W + n * 1088, st + STAGE_W + n * 1088 + 1024};
-        q4k_sb_mma_n<NT, true>(nt, blk + g * LB_Q4K, blk + (g + 8) * LB_Q4K, bs,
-                               reinterpret_cast<const uint8_t*>(sync->zero), lane, acc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sync->empty[s]);
+      for (int n = 0; n < NT; ++n) {
+        float s = acc[n][r].x + acc[n][r].y;
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        v[r][n] = s;
       }
-      if (!ok) break;
-      // row sums of rows g and g+8 of this block on lane t == 0 of each quad
-      float v[2][NT];
+    const int par = pass & 1, use = pass >> 1;
+    float* xb = xch + (size_t)par * RU * NT;
+    auto id_of = [&](int nn) {  // ids[nn] without indexing registers dynamically
+      int id = x.ids[0];
+#pragma unroll
+      for (int n2 = 1; n2 < NT; ++n2)
+        if (n2 == nn) id = x.ids[n2];
+      return id;
+    };
+    // h = silu(gate) * up or relu(up)^2 of rows g, g+8 (zero past rows_e),
+    // on lane t == 0 of each quad; zero elsewhere
+    float hv[2][NT];
+    bool writer = !PAIR;
+    if (PAIR && mat == 1) {  // up warps: hand the sums to the gate warps
+      if (use > 0 && !mbar_wait_or_abort(&sync->xempty[par], (use - 1) & 1, w.status, abort)) {
+        ok = false;
+        break;
+      }
+      if (t == 0)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int n = 0; n < NT; ++n) xb[(rb * kTileRows + g + 8 * r) * NT + n] = v[r][n];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sync->xfull[par]);
+    } else if (PAIR) {  // gate warps: silu(gate) * up
+      if (!mbar_wait_or_abort(&sync->xfull[par], use & 1, w.status, abort)) {
+        ok = false;
+        break;
+      }
+      // the quad's 2 * NT values (all four lanes hold every sum) are shared
+      // out: lane t takes pairs (r, n) with 2n + r = t, t + 4, ..., and the
+      // products come back to lane t == 0
+      constexpr int PER_LANE = (2 * NT + 3) / 4;
+      float hq[PER_LANE];
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i) {
+        const int pr = t + 4 * i, r = pr & 1, n = pr >> 1;
+        float gv = v[0][0];
+#pragma unroll
+        for (int r2 = 0; r2 < 2; ++r2)
+#pragma unroll
+          for (int n2 = 0; n2 < NT; ++n2)
+            if (r2 == r && n2 == n) gv = v[r2][n2];
+        const int row = x.row0 + rb * kTileRows + g + 8 * r;
+        const bool live = n < NT && n < nt && row < x.rows_e;
+        const float uv = xb[(rb * kTileRows + g + 8 * r) * NT + min(n, NT - 1)];
+        hq[i] = live ? __fmul_rn(silu_ref(gv), uv) : 0.f;
+      }
 #pragma unroll
       for (int r = 0; r < 2; ++r)
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
-          float s = acc[n][r].x + acc[n][r].y;
-          s += __shfl_xor_sync(0xffffffffu, s, 1);
-          s += __shfl_xor_sync(0xffffffffu, s, 2);
-          v[r][n] = s;
+          const int pr = 2 * n + r;
+          const float o = __shfl_sync(0xffffffffu, hq[pr >> 2], (lane & ~3) | (pr & 3));
+          hv[r][n] = t == 0 ? o : 0.f;
         }
-      const int par = pass & 1, use = pass >> 1;
-      float* xb = xch + (size_t)par * RU * NT;
-      auto id_of = [&](int nn) {  // ids[nn] without indexing registers dynamically
-        int id = ids[0];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sync->xempty[par]);
+      writer = true;
+    }
+    if (!PAIR) {  // up only: relu(up)^2
 #pragma unroll
-        for (int n2 = 1; n2 < NT; ++n2)
-          if (n2 == nn) id = ids[n2];
-        return id;
-      };
-      // h = silu(gate) * up or relu(up)^2 of rows g, g+8 (zero past rows_e),
-      // on lane t == 0 of each quad; zero elsewhere
-      float hv[2][NT];
-      bool writer = !PAIR;
-      if (PAIR && mat == 1) {  // up warps: hand the sums to the gate warps
-        if (use > 0 && !mbar_wait_or_abort(&sync->xempty[par], (use - 1) & 1, w.status, abort)) {
-          ok = false;
-          break;
-        }
-        if (t == 0)
+      for (int r = 0; r < 2; ++r)
 #pragma unroll
-          for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int n = 0; n < NT; ++n) xb[(rb * kTileRows + g + 8 * r) * NT + n] = v[r][n];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sync->xfull[par]);
-      } else if (PAIR) {  // gate warps: silu(gate) * up
-        if (!mbar_wait_or_abort(&sync->xfull[par], use & 1, w.status, abort)) {
-          ok = false;
-          break;
-        }
-        // the quad's 2 * NT values (all four lanes hold every sum) are shared
-        // out: lane t takes pairs (r, n) with 2n + r = t, t + 4, ..., and the
-        // products come back to lane t == 0
-        constexpr int PER_LANE = (2 * NT + 3) / 4;
-        float hq[PER_LANE];
-#pragma unroll
-        for (int i = 0; i < PER_LANE; ++i) {
-          const int pr = t + 4 * i, r = pr & 1, n = pr >> 1;
-          float gv = v[0][0];
-#pragma unroll
-          for (int r2 = 0; r2 < 2; ++r2)
-#pragma unroll
-            for (int n2 = 0; n2 < NT; ++n2)
-              if (r2 == r && n2 == n) gv = v[r2][n2];
+        for (int n = 0; n < NT; ++n) {
           const int row = x.row0 + rb * kTileRows + g + 8 * r;
-          const bool live = n < NT && n < nt && row < x.rows_e;
-          const float uv = xb[(rb * kTileRows + g + 8 * r) * NT + min(n, NT - 1)];
-          hq[i] = live ? __fmul_rn(silu_ref(gv), uv) : 0.f;
+          hv[r][n] = (t == 0 && row < x.rows_e && n < nt) ? relu_sq_ref(v[r][n]) : 0.f;
         }
+    }
+    if (writer) {
+      if (I6) {  // the block's 16 rows are one Q6_K sub-block of the down input
+        const int s_glob = (x.row0 + rb * kTileRows) >> 4;
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int n = 0; n < NT; ++n)
+          if (n < nt)
+            i6_store_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(n) * ld_dn),
+                              s_glob, hv[0][n], hv[1][n], lane);
+      } else if (t == 0) {
 #pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            const int pr = 2 * n + r;
-            const float o = __shfl_sync(0xffffffffu, hq[pr >> 2], (lane & ~3) | (pr & 3));
-            hv[r][n] = t == 0 ? o : 0.f;
-          }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sync->xempty[par]);
-        writer = true;
-      }
-      if (!PAIR) {  // up only: relu(up)^2
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            const int row = x.row0 + rb * kTileRows + g + 8 * r;
-            hv[r][n] = (t == 0 && row < x.rows_e && n < nt) ? relu_sq_ref(v[r][n]) : 0.f;
-          }
-      }
-      if (writer) {
-        if (I6) {  // the block's 16 rows are one Q6_K sub-block of the down input
-          const int s_glob = (x.row0 + rb * kTileRows) >> 4;
+        for (int r = 0; r < 2; ++r) {
+          const int row = x.row0 + rb * kTileRows + g + 8 * r;
 #pragma unroll
           for (int n = 0; n < NT; ++n)
-            if (n < nt)
-              i6_store_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(n) * ld_dn),
-                                s_glob, hv[0][n], hv[1][n], lane);
-        } else if (t == 0) {
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const int row = x.row0 + rb * kTileRows + g + 8 * r;
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-              if (row < x.rows_e && n < nt)
-                w.xp_down[(long)id_of(n) * ld_dn + xp_index<DT>(row, tasks_d)] = hv[r][n];
-          }
+            if (row < x.rows_e && n < nt)
+              w.xp_down[(long)id_of(n) * ld_dn + xp_index<DT>(row, tasks_d)] = hv[r][n];
         }
       }
-      if (warp == 0 && x.row0 + RU >= x.rows_e) {  // last slab: zero the padding up to kd
-        if (I6) {  // sub-blocks past the slab (the slab's own are written above)
-          const int s_from = (x.row0 + RU) >> 4, s_to = kd >> 4;
-          for (int qq = lane >> 4; qq < nt * (s_to - s_from); qq += 2) {
-            const int nn = qq / (s_to - s_from), sg = s_from + (qq - nn * (s_to - s_from));
-            i6_zero_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(nn) * ld_dn), sg,
-                             lane & 15);
-          }
-        } else {
-          const int pad = kd - x.rows_e;
-          for (int qq = lane; qq < nt * pad; qq += 32) {
-            const int nn = qq / pad, pe = x.rows_e + (qq - nn * pad);
-            w.xp_down[(long)id_of(nn) * ld_dn + xp_index<DT>(pe, tasks_d)] = 0.f;
-          }
+    }
+    if (warp == 0 && x.row0 + RU >= x.rows_e) {  // last slab: zero the padding up to kd
+      if (I6) {  // sub-blocks past the slab (the slab's own are written above)
+        const int s_from = (x.row0 + RU) >> 4, s_to = kd >> 4;
+        for (int qq = lane >> 4; qq < nt * (s_to - s_from); qq += 2) {
+          const int nn = qq / (s_to - s_from), sg = s_from + (qq - nn * (s_to - s_from));
+          i6_zero_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(nn) * ld_dn), sg,
+                           lane & 15);
+        }
+      } else {
+        const int pad = kd - x.rows_e;
+        for (int qq = lane; qq < nt * pad; qq += 32) {
+          const int nn = qq / pad, pe = x.rows_e + (qq - nn * pad);
+          w.xp_down[(long)id_of(nn) * ld_dn + xp_index<DT>(pe, tasks_d)] = 0.f;
         }
       }
     }
