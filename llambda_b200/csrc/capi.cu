@@ -592,8 +592,8 @@ int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
     int eb = d->expert_begin, ee = d->expert_end;
     if (eb == 0 && ee == 0) ee = (int)E;
     if (eb < 0 || ee > (int)E || eb >= ee) throw Failure("Invalid owned expert range.");
-    if (d->max_tokens < 1 || (int64_t)d->max_tokens * top_k > 4096)
-      throw Failure("max_tokens must be positive and max_tokens * top_k at most 4096.");
+    if (d->max_tokens < 1 || (int64_t)d->max_tokens * top_k > 65536)
+      throw Failure("max_tokens must be positive and max_tokens * top_k at most 65536.");
 
     auto s = new llambda_cuda_moe_session();
     try {
@@ -1025,8 +1025,8 @@ int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
   }
   return guarded([&] {
     const lb::MoeDevice m = static_layer(desc);
-    if ((int64_t)tokens * m.top_k > 4096)
-      throw Failure("tokens * top_k must be at most 4096.");
+    if ((int64_t)tokens * m.top_k > 65536)
+      throw Failure("tokens * top_k must be at most 65536.");
     const int T = (int)tokens;
     const size_t need = lb::moe_work_bytes(m, T);
     if (need > LLAMBDA_CUDA_STATIC_SCRATCH_BYTES)

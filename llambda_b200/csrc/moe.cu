@@ -34,6 +34,8 @@ namespace lb {
 namespace {
 
 constexpr int kMaxExperts = 1024;
+// (token, rank) entries of one layer call (prefill batches included)
+constexpr int kMaxEntries = 64 * 1024;
 constexpr int kSlabMaxStages = 10;
 // Rows of one 2-D tensor copy of the gate/up slabs (the slabs' rows per
 // matrix are multiples of it).
@@ -1849,7 +1851,7 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int T, float* out,
                        const SlabMaps* maps, cudaStream_t s, const cudaEvent_t* marks) {
   if (T <= 0) return cudaSuccess;
-  if (T > w.max_tokens || m.experts > kMaxExperts || m.top_k > 32 || T * m.top_k > 4 * 1024)
+  if (T > w.max_tokens || m.experts > kMaxExperts || m.top_k > 32 || T * m.top_k > kMaxEntries)
     return cudaErrorInvalidValue;
   if (m.inter_sh && m.k_in_sh != m.k_in) return cudaErrorInvalidValue;
   const int E = m.experts;

@@ -156,26 +156,26 @@ def test_non_positive_weight_sum_is_an_error():
         _session(cfg, tensors, 2).run(x)
 
 
-@pytest.mark.parametrize("tokens", [1, 16])
+@pytest.mark.parametrize("tokens", [1, 16, 512])  # decode and a prefill batch (config 3)
 def test_config3_full_layer(tokens):
     cfg = CF.CONFIG3
     tensors = host_layer(cfg, seed=0)
     x = O.synth_f32(0, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
     ref, sel_ref, w_ref = O.moe_forward(oracle_layer(cfg, tensors), x, tokens, cfg.top_k)
-    out, sel, w = _session(cfg, tensors, 64).run(x, with_routing=True)
+    out, sel, w = _session(cfg, tensors, max(64, tokens)).run(x, with_routing=True)
     _check_selection(cfg, tensors, x, sel, sel_ref)
     same = np.all(sel == sel_ref, axis=1)
     assert max_rel(out[same], ref[same]) < MAX_REL
     assert max_rel(out[same], ref[same]) < 1e-5
 
 
-@pytest.mark.parametrize("tokens", [1, 64])
+@pytest.mark.parametrize("tokens", [1, 64, 1024])  # decode and a prefill batch (config 4)
 def test_config4_full_layer(tokens):
     cfg = CF.CONFIG4
     tensors = host_layer(cfg, seed=0)
     x = O.synth_f32(0, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
     ref, sel_ref, w_ref = O.moe_forward(oracle_layer(cfg, tensors), x, tokens, cfg.top_k)
-    out, sel, w = _session(cfg, tensors, 64).run(x, with_routing=True)
+    out, sel, w = _session(cfg, tensors, max(64, tokens)).run(x, with_routing=True)
     _check_selection(cfg, tensors, x, sel, sel_ref)
     same = np.all(sel == sel_ref, axis=1)
     assert max_rel(out[same], ref[same]) < MAX_REL
