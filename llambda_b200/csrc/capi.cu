@@ -198,6 +198,12 @@ void session_launch(llambda_cuda_session* s, const uint8_t* W, const float* din,
                "GEMV launch");
     return;
   }
+  cudaError_t fe = cudaSuccess;
+  if (lb::launch_gemv_fused(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, din, (long)s->ne0,
+                            (int)tokens, dout, (long)s->ne1, s->status, st, &fe)) {
+    cuda_check(fe, "GEMV launch");
+    return;
+  }
   float* xp = static_cast<float*>(s->dxp.get(lb::xprep_floats((int)s->ne0, (int)tokens) * 4));
   cuda_check(lb::launch_prep(s->type, (int)s->ne1, din, (long)s->ne0, (int)s->ne0, (int)s->ne0,
                              (int)tokens,

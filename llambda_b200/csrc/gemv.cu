@@ -482,6 +482,79 @@ __global__ void __launch_bounds__(NW * 32, 1)
     for (int q = i; q < issued; ++q) mbar_wait(&full[q % plan.stages], (q / plan.stages) & 1, nullptr);
 }
 
+// The same tile pipeline for up to NT tokens with the activation prep fused
+// in: every CTA forms the tokens' mx layout of the raw input in shared memory
+// while its first tiles stream in (the input is a few KB per token), so the
+// call is one launch and the B fragments are shared-memory reads.
+template <int NT, int NW>
+__global__ void __launch_bounds__(NW * 32, 1)
+    gemv_q4k_fused_kernel(const uint8_t* __restrict__ W, size_t rb, int rows, int nsb,
+                          const float* __restrict__ x, long ldx, int tokens,
+                          float* __restrict__ y, long ldy, TilePlan plan, int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = nsb * 256;
+  const size_t mxb = mx_bytes(K);
+  uint8_t* act = smem + (size_t)plan.stages * plan.stage_bytes;  // [NT][mxb]
+  uint8_t* bz = act + NT * mxb;                                  // 32 zero bytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(bz + 32);
+  float* red = reinterpret_cast<float*>(full + 8);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < plan.stages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x < 8) reinterpret_cast<uint32_t*>(bz)[threadIdx.x] = 0u;
+  __syncthreads();
+  const int tiles = (rows + kTileRows - 1) / kTileRows;
+  const int u0 = (int)((long)blockIdx.x * tiles / gridDim.x);
+  const int n_my = (int)((long)(blockIdx.x + 1) * tiles / gridDim.x) - u0;
+  auto issue = [&](int idx) {
+    const int row0 = (u0 + idx) * kTileRows, s = idx % plan.stages;
+    tile_issue(smem + (size_t)s * plan.stage_bytes, &full[s], plan.pitch,
+               min(kTileRows, rows - row0), rb, W + (size_t)row0 * rb, nullptr, lane);
+  };
+  int issued = 0;  // meaningful in warp 0 (the producer)
+  if (warp == 0)
+    for (; issued < plan.stages && issued < n_my; ++issued) issue(issued);
+  // the tokens' prepared input, 128 values per warp item (mx_store4 wants the
+  // 8 lanes of each 32-value sub-block together)
+  for (int it = warp; it < tokens * (K >> 7); it += NW) {
+    const int tok = it / (K >> 7), e = (it - tok * (K >> 7)) * 128 + lane * 4;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x + (long)tok * ldx + e));
+    mx_store4(act + tok * mxb, K, e, v);
+  }
+  __syncthreads();
+  const uint8_t* mxp[NT];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) mxp[n] = act + (size_t)min(n, tokens - 1) * mxb;
+  int i = 0;
+  bool stop = false;
+  for (; i < n_my; ++i) {
+    const int s = i % plan.stages;
+    const bool ok = mbar_wait(&full[s], (i / plan.stages) & 1, status);
+    const int row0 = (u0 + i) * kTileRows, nr = min(kTileRows, rows - row0);
+    const uint8_t* st = smem + (size_t)s * plan.stage_bytes;
+    float2 acc[1][NT][2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) acc[0][n][r] = make_float2(0.f, 0.f);
+    if (ok) tile_items<NT, 1, NW, true>(st, plan.pitch, nsb, warp, lane, mxp, tokens, acc, bz);
+    float* rbuf = red + (i & 1) * (tile_red_floats<NT, 1, NW>() / 2);
+    tile_partials_store<NT, 1>(rbuf, warp, lane, acc);
+    stop = __syncthreads_or(!ok);  // also: every warp is done with this stage
+    if (stop) break;
+    const int r = threadIdx.x & 15, n = threadIdx.x >> 4;
+    if (n < tokens && r < nr) y[(long)n * ldy + row0 + r] = tile_row_sum<NT, 1, NW>(rbuf, 0, r, n);
+    if (warp == 0 && issued < n_my) {
+      issue(issued);
+      ++issued;
+    }
+  }
+  if (stop && threadIdx.x == 0)  // drain copies still in flight before the CTA exits
+    for (int q = i; q < issued; ++q) mbar_wait(&full[q % plan.stages], (q / plan.stages) & 1, nullptr);
+}
+
 // F32 rows (the MoE router, ffn_gate_inp), tiled: a CTA of 4 warps takes 16
 // rows (4 per warp) and up to kF32Tok tokens, whose activations it first
 // copies into shared memory, so that each weight float4 read from global
@@ -706,6 +779,23 @@ cudaError_t launch_q4k_mma(const void* W, size_t rb, int rows, int K, const floa
   return cudaGetLastError();
 }
 
+template <int NT, int NW>
+cudaError_t launch_q4k_fused(const void* W, size_t rb, int rows, int K, const float* x, long ldx,
+                             int tokens, float* y, long ldy, int* status, cudaStream_t stream) {
+  auto kern = gemv_q4k_fused_kernel<NT, NW>;
+  const size_t extra =
+      (size_t)NT * mx_bytes(K) + 32 + 64 + (size_t)tile_red_floats<NT, 1, NW>() * 4;
+  const TilePlan plan = tile_plan(rb, 1, kTileSmemBudget - extra);
+  if (plan.stages < 2) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)plan.stages * plan.stage_bytes + extra;
+  if (prepared_occupancy(kern, NW * 32, smem) < 1) return cudaErrorUnknown;
+  const int tiles = (rows + kTileRows - 1) / kTileRows;
+  const int grid = std::min(tiles, sm_count());
+  kern<<<grid, NW * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, K / 256, x, ldx,
+                                        tokens, y, ldy, plan, status);
+  return cudaGetLastError();
+}
+
 template <int NG, bool SLOT>
 cudaError_t launch_q6k_slab(const void* W, size_t rb, int rows, int K, const uint8_t* m6,
                             int tokens, float* y, long ldy, int* status, cudaStream_t stream) {
@@ -837,6 +927,17 @@ cudaError_t launch_gemv_prepped(int type, const void* W, size_t rb, int rows, in
 #undef LB_DENSE_T
 #undef LB_DENSE
   return cudaErrorInvalidValue;
+}
+
+bool launch_gemv_fused(int type, const void* W, size_t rb, int rows, int K, const float* x,
+                       long ldx, int tokens, float* y, long ldy, int* status, cudaStream_t stream,
+                       cudaError_t* err) {
+  if (type != LB_TYPE_Q4_K || tokens < 1 || tokens > 2 || K % 256 || (ldx & 3) ||
+      (reinterpret_cast<uintptr_t>(x) & 15))
+    return false;
+  *err = tokens == 1 ? launch_q4k_fused<1, 16>(W, rb, rows, K, x, ldx, 1, y, ldy, status, stream)
+                     : launch_q4k_fused<2, 16>(W, rb, rows, K, x, ldx, 2, y, ldy, status, stream);
+  return true;
 }
 
 cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long ldx, int tokens,

@@ -33,6 +33,11 @@ size_t xprep_floats(int K, int tokens);
 // rows: the matrix the prepared input is for (picks the layout).
 cudaError_t launch_prep(int type, int rows, const float* x, long ldx, int n_valid, int K,
                         int tokens, const int* gather, float* xp, cudaStream_t stream);
+// Q4_K rows times one or two raw input vectors in one launch (the prep fused
+// in); false when the shape does not apply (then prep + launch_gemv_prepped).
+bool launch_gemv_fused(int type, const void* W, size_t row_bytes, int rows, int K, const float* x,
+                       long ldx, int tokens, float* y, long ldy, int* status, cudaStream_t stream,
+                       cudaError_t* err);
 cudaError_t launch_gemv_prepped(int type, const void* W, size_t row_bytes, int rows, int K,
                                 const float* xp, int tokens, float* y, long ldy, int* status,
                                 cudaStream_t stream);

@@ -264,35 +264,38 @@ __device__ __forceinline__ void q4k_sb_mma_n(int nt, const uint8_t* rg, const ui
 
 // q4k_sb_mma over super-blocks [sb0, sb1) of a 16-row tile whose row 0 is
 // `tile`, rows `pitch` bytes apart (pitch % 128 == 16), with nt tokens whose
-// prepared activations (global memory) start at mx[n].
-template <int NT>
+// prepared activations start at mx[n] (SMEM: in shared memory, with the
+// 32 zero bytes bz there too; else global memory).
+template <int NT, bool SMEM = false>
 __device__ __forceinline__ void q4k_tile_mma(const uint8_t* tile, int pitch, int sb0, int sb1,
                                              const uint8_t* const (&mx)[NT], int nt, int nsb,
-                                             int lane, float2 (&y)[NT][2]) {
+                                             int lane, float2 (&y)[NT][2],
+                                             const uint8_t* bz = kZero32) {
   const int g = lane >> 2;
   for (int sb = sb0; sb < sb1; ++sb) {
     const uint8_t* rg = tile + g * pitch + sb * LB_Q4K;
     BSlice bs[NT];
 #pragma unroll
     for (int n = 0; n < NT; ++n) bs[n] = mx_slice(mx[n], sb, nsb);
-    q4k_sb_mma_n<NT, false>(nt, rg, rg + 8 * pitch, bs, kZero32, lane, y);
+    q4k_sb_mma_n<NT, SMEM>(nt, rg, rg + 8 * pitch, bs, bz, lane, y);
   }
 }
 
 // This warp's share of a staged tile: the (matrix, super-block) items
 // [warp*I/W, (warp+1)*I/W) of I = MATS * nsb.
-template <int NT, int MATS, int W>
+template <int NT, int MATS, int W, bool SMEM = false>
 __device__ __forceinline__ void tile_items(const uint8_t* stage, int pitch, int nsb, int warp,
                                            int lane, const uint8_t* const (&mx)[NT], int nt,
-                                           float2 (&y)[MATS][NT][2]) {
+                                           float2 (&y)[MATS][NT][2],
+                                           const uint8_t* bz = kZero32) {
   const int items = MATS * nsb;
   const int i0 = warp * items / W, i1 = (warp + 1) * items / W;
 #pragma unroll
   for (int mat = 0; mat < MATS; ++mat) {
     const int sb0 = max(i0 - mat * nsb, 0), sb1 = min(i1 - mat * nsb, nsb);
     if (sb0 < sb1)
-      q4k_tile_mma<NT>(stage + (size_t)mat * kTileRows * pitch, pitch, sb0, sb1, mx, nt, nsb,
-                       lane, y[mat]);
+      q4k_tile_mma<NT, SMEM>(stage + (size_t)mat * kTileRows * pitch, pitch, sb0, sb1, mx, nt,
+                             nsb, lane, y[mat], bz);
   }
 }
 
