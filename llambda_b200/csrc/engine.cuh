@@ -104,6 +104,33 @@ constexpr uint32_t kSuspendNs = 200000;
 // Every wait gives up after this long (a lost copy cannot hang the GPU).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Programmatic dependent launch: a kernel launched with launch_pdl may start
+// while the kernel before it in the stream is still running; it calls
+// griddep_wait() before it reads anything that kernel wrote or writes
+// anything it still reads (all of the earlier kernel's work is then done and
+// visible), and griddep_launch() once its own CTAs are resident, so the next
+// kernel can be scheduled early.  Both are no-ops without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

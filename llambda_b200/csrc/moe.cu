@@ -217,6 +217,8 @@ template <int PER>
 __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w, int T,
                                                          int pass_nt) {
   __shared__ int s_last;
+  griddep_wait();
+  griddep_launch();
   if (threadIdx.x < 32) topk_token<PER>(m, w, blockIdx.x, threadIdx.x);
   __threadfence();
   __syncthreads();
@@ -474,13 +476,16 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     mbar_init(&bar_w, 1);
     fence_mbar_init();
     const uint32_t rowb = (uint32_t)H * 4u;
-    mbar_expect_tx(&bar_x, rowb * (uint32_t)nt);
-    tma_load_1d(xs4, x + (long)t0 * H, rowb * nt, &bar_x);
+    // the router rows do not depend on the kernel before: fetched first
     mbar_expect_tx(&bar_w, rowb * (uint32_t)crows);
     if (main_rows > 0) tma_load_1d(ws4, m.router + (size_t)crow0 * H, rowb * main_rows, &bar_w);
     if (main_rows < crows)  // row E, the last row of the last tile
       tma_load_1d(ws4 + (size_t)main_rows * H4, m.router_extra_row, rowb, &bar_w);
+    griddep_wait();  // x is the previous kernel's output
+    mbar_expect_tx(&bar_x, rowb * (uint32_t)nt);
+    tma_load_1d(xs4, x + (long)t0 * H, rowb * nt, &bar_x);
   }
+  griddep_launch();
   for (int i = nt * H4 + threadIdx.x; i < kRouterTok * H4; i += blockDim.x)
     xs4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
@@ -776,6 +781,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();  // the routing and prepared inputs of the kernels before
+  griddep_launch();
   const int k = m.top_k;
   const int per_r = (m.inter + RU - 1) / RU;
   const int per_s = (m.inter_sh + RU - 1) / RU;
@@ -1110,6 +1117,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();  // the routing and the gate/up pass's output
+  griddep_launch();
   const int k = m.top_k, H = m.hidden;
   const int per = (H + RU - 1) / RU;
   const int K = shared_pass ? m.k_down_sh : m.k_down;
@@ -1382,6 +1391,8 @@ template <bool VEC, int KMAX>
 __global__ void __launch_bounds__(128) combine_kernel(MoeDevice m, MoeWork w, int T,
                                                       const float* x, float* out) {
   constexpr int V = VEC ? 4 : 1;
+  griddep_wait();
+  griddep_launch();
   const int H = m.hidden, k = m.top_k, HV = H / V;
   const long n = (long)T * HV;
   const bool shared = m.shared_here && m.inter_sh;
@@ -1458,6 +1469,8 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(MoeDevice m, MoeWork w,
                                                          const float* __restrict__ x,
                                                          float* __restrict__ out) {
   __shared__ uint32_t s_epoch;
+  griddep_wait();
+  griddep_launch();
   const int H = m.hidden, k = m.top_k, world = m.ep_world, rank = m.ep_rank;
   const int H4 = H >> 2;
   uint8_t* self = static_cast<uint8_t*>(m.ep_peers[rank]);
@@ -1628,9 +1641,8 @@ cudaError_t launch_up_slab_cw(const MoeDevice& m, const MoeWork& w, int T, const
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = (size_t)stages * stage + extra;
   if (prepared_occupancy(kern, (CW + 1) * 32, smem) < 1) return cudaErrorUnknown;
-  kern<<<sm_count(), (CW + 1) * 32, smem, s>>>(m, w, T, stages, mp.row_base, mp.gate,
-                                                mp.up, mp.gate_sh, mp.up_sh);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(sm_count()), dim3((CW + 1) * 32), smem, s, m, w, T, stages,
+                    mp.row_base, mp.gate, mp.up, mp.gate_sh, mp.up_sh);
 }
 
 // Shape of the Q6_K down slabs for rows of rb bytes: the most 16-row blocks
@@ -1675,9 +1687,8 @@ cudaError_t launch_down_slab_k(const MoeDevice& m, const MoeWork& w, int T, int 
   const size_t smem = (size_t)p.stages * p.stage_bytes + sizeof(DownSync) +
                       (KSPLIT > 1 ? (size_t)p.stages * kDownWarps * 32 * sizeof(float2) : 0);
   if (prepared_occupancy(kern, (kDownWarps + 1) * 32, smem) < 1) return cudaErrorUnknown;
-  kern<<<sm_count(), (kDownWarps + 1) * 32, smem, s>>>(m, w, T, p.stages, p.stage_bytes,
-                                                        p.stage_w, shared_pass);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(sm_count()), dim3((kDownWarps + 1) * 32), smem, s, m, w, T,
+                    p.stages, p.stage_bytes, p.stage_w, shared_pass);
 }
 
 cudaError_t launch_down_slab(const MoeDevice& m, const MoeWork& w, int T, int shared_pass,
@@ -1866,7 +1877,9 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
       prepared_occupancy(moe_router_kernel, kRouterWarps * 32, router_smem) >= 1) {
     // top-k and routing ride on the router launch (its last CTAs)
     dim3 grid((all_rows + kRouterRows - 1) / kRouterRows, (T + kRouterTok - 1) / kRouterTok);
-    moe_router_kernel<<<grid, kRouterWarps * 32, router_smem, s>>>(m, w, x, T, all_rows);
+    e = launch_pdl(moe_router_kernel, grid, dim3(kRouterWarps * 32), router_smem, s, m, w, x, T,
+                   all_rows);
+    if (e != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   } else {
     if (m.up_type == LB_TYPE_Q4_K)
@@ -1885,12 +1898,11 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   }
   {  // top-k per token, the routing on the last CTA
     const int per = (E + 31) / 32, pnt = up_pass_tokens(m, T);
-    if (per <= 1) topk_route_kernel<1><<<T, 256, 0, s>>>(m, w, T, pnt);
-    else if (per <= 2) topk_route_kernel<2><<<T, 256, 0, s>>>(m, w, T, pnt);
-    else if (per <= 4) topk_route_kernel<4><<<T, 256, 0, s>>>(m, w, T, pnt);
-    else if (per <= 8) topk_route_kernel<8><<<T, 256, 0, s>>>(m, w, T, pnt);
-    else if (per <= 16) topk_route_kernel<16><<<T, 256, 0, s>>>(m, w, T, pnt);
-    else topk_route_kernel<32><<<T, 256, 0, s>>>(m, w, T, pnt);
+    auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
+              : per <= 4 ? topk_route_kernel<4> : per <= 8 ? topk_route_kernel<8>
+              : per <= 16 ? topk_route_kernel<16> : topk_route_kernel<32>;
+    e = launch_pdl(kern, dim3(T), dim3(256), 0, s, m, w, T, pnt);
+    if (e != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
@@ -1910,18 +1922,13 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
                    ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
   if (m.ep_world > 1) {  // every rank's partial meets here (peer memory, NVLink)
     if (!vec || T > m.ep_max_tokens) return cudaErrorInvalidValue;
-    combine_ep_kernel<<<kEpGrid, 256, 0, s>>>(m, w, T, x, out);
-    return cudaGetLastError();
+    return launch_pdl(combine_ep_kernel, dim3(kEpGrid), dim3(256), 0, s, m, w, T, x, out);
   }
   const long n = (long)T * m.hidden / (vec ? 4 : 1);
   const int grid = std::max(1, (int)std::min<long>((n + 127) / 128, (long)sm_count() * 16));
-  if (vec && m.top_k <= 16)
-    combine_kernel<true, 16><<<grid, 128, 0, s>>>(m, w, T, x, out);
-  else if (vec)
-    combine_kernel<true, 32><<<grid, 128, 0, s>>>(m, w, T, x, out);
-  else
-    combine_kernel<false, 32><<<grid, 128, 0, s>>>(m, w, T, x, out);
-  return cudaGetLastError();
+  auto kern = vec && m.top_k <= 16 ? combine_kernel<true, 16>
+              : vec ? combine_kernel<true, 32> : combine_kernel<false, 32>;
+  return launch_pdl(kern, dim3(grid), dim3(128), 0, s, m, w, T, x, out);
 }
 
 }  // namespace lb
