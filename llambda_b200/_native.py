@@ -311,6 +311,16 @@ class MoeSession:
         d.add_residual = int(bool(add_residual))
         return cls(d, keep)
 
+    def run_into(self, dest: np.ndarray, x: np.ndarray) -> np.ndarray:
+        """The layer output of x written into dest (a C-contiguous float32
+        array of x's shape), as the reference's run-into functions do."""
+        x = _f32(x).reshape(-1, self.hidden)
+        if dest.dtype != np.float32 or not dest.flags.c_contiguous or dest.size != x.size:
+            raise ValueError("dest must be a C-contiguous float32 array of x's size")
+        _check(lib().llambda_cuda_moe_session_run(self._h, _fptr(x), x.shape[0], _fptr(dest),
+                                                  None, None))
+        return dest
+
     def run(self, x: np.ndarray, with_routing: bool = False):
         x = _f32(x).reshape(-1, self.hidden)
         T = x.shape[0]

@@ -235,7 +235,21 @@ struct llambda_cuda_moe_session {
   DevBuf dx, dout, dsel, dw;
   cudaEvent_t marks[3] = {nullptr, nullptr, nullptr};  // kernel timing, when enabled
   bool timing = false;
+  // The host-buffer call (copies in, the layer's kernels, copies out, status)
+  // as one CUDA graph, captured for one token count and replayed while the
+  // staging buffers stay where they are.
+  Pinned hstatus;
+  cudaGraphExec_t graph = nullptr;
+  int graph_tokens = 0;
+  int eager_tokens = 0;  // the first call of a token count runs eagerly (fills the caches)
+  const void* graph_key[2] = {nullptr, nullptr};
+  void drop_graph() {
+    if (graph) cudaGraphExecDestroy(graph);
+    graph = nullptr;
+    graph_tokens = 0;
+  }
   ~llambda_cuda_moe_session() {
+    drop_graph();
     for (cudaEvent_t e : marks)
       if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
@@ -747,22 +761,54 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
     float* hout = static_cast<float*>(s->hout.get(xb));
     float* dx = static_cast<float*>(s->dx.get(xb));
     float* dout = static_cast<float*>(s->dout.get(xb));
+    int* hstatus = static_cast<int*>(s->hstatus.get(4));
     std::memcpy(hx, x, xb);
-    int status = 0;
-    cuda_check(cudaMemsetAsync(s->w.status, 0, 4, s->stream), "memset");
-    cuda_check(cudaMemcpyAsync(dx, hx, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
-    cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, &s->maps, s->stream,
-                              s->timing ? s->marks : nullptr),
-               "MoE launch");
-    cuda_check(cudaMemcpyAsync(hout, dout, xb, cudaMemcpyDeviceToHost, s->stream), "output copy");
+    auto enqueue = [&]() {
+      cuda_check(cudaMemsetAsync(s->w.status, 0, 4, s->stream), "memset");
+      cuda_check(cudaMemcpyAsync(dx, hx, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
+      cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, &s->maps, s->stream,
+                                s->timing ? s->marks : nullptr),
+                 "MoE launch");
+      cuda_check(cudaMemcpyAsync(hout, dout, xb, cudaMemcpyDeviceToHost, s->stream),
+                 "output copy");
+      cuda_check(cudaMemcpyAsync(hstatus, s->w.status, 4, cudaMemcpyDeviceToHost, s->stream),
+                 "copy");
+    };
+    const bool same = s->graph && s->graph_tokens == T && s->graph_key[0] == hx &&
+                      s->graph_key[1] == hout;
+    if (s->timing || selected || weights || (!same && s->eager_tokens != T)) {
+      enqueue();  // timed or checked calls, and a new token count's first call
+      s->eager_tokens = T;
+    } else {
+      if (!same) {
+        s->drop_graph();
+        cudaGraph_t g = nullptr;
+        cuda_check(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal),
+                   "begin capture");
+        try {
+          enqueue();
+        } catch (...) {
+          cudaStreamEndCapture(s->stream, &g);
+          if (g) cudaGraphDestroy(g);
+          throw;
+        }
+        cuda_check(cudaStreamEndCapture(s->stream, &g), "end capture");
+        const cudaError_t ie = cudaGraphInstantiate(&s->graph, g, 0);
+        cudaGraphDestroy(g);
+        cuda_check(ie, "graph instantiate");
+        s->graph_tokens = T;
+        s->graph_key[0] = hx;
+        s->graph_key[1] = hout;
+      }
+      cuda_check(cudaGraphLaunch(s->graph, s->stream), "graph launch");
+    }
     int32_t* hsel = selected ? static_cast<int32_t*>(s->hsel.get(sb)) : nullptr;
     float* hw = weights ? static_cast<float*>(s->hw.get(sb)) : nullptr;
     if (hsel)
       cuda_check(cudaMemcpyAsync(hsel, s->w.sel, sb, cudaMemcpyDeviceToHost, s->stream), "copy");
     if (hw) cuda_check(cudaMemcpyAsync(hw, s->w.wts, sb, cudaMemcpyDeviceToHost, s->stream), "copy");
-    cuda_check(cudaMemcpyAsync(&status, s->w.status, 4, cudaMemcpyDeviceToHost, s->stream), "copy");
     cuda_check(cudaStreamSynchronize(s->stream), "MoE layer");
-    if (status)
+    if (*hstatus)
       throw Failure("MoE router produced non-positive top-k weight sum.");
     std::memcpy(out, hout, xb);
     if (hsel) std::memcpy(selected, hsel, sb);
@@ -857,6 +903,8 @@ int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_session* s, int rank,
   return guarded([&] {
     std::lock_guard<std::mutex> lock(s->mu);
     DeviceGuard g(s->device);
+    s->drop_graph();  // the layer's launches change with the reduction
+    s->eager_tokens = 0;
     if (world < 2 || world > lb::kEpMaxWorld || rank < 0 || rank >= world)
       throw Failure("world must be 2.." + std::to_string(lb::kEpMaxWorld) +
                     " and 0 <= rank < world.");

@@ -129,6 +129,30 @@ def test_norm_and_residual():
     assert max_rel(out[same], ref[same]) < 1e-5
 
 
+def test_repeated_host_calls_replay_one_graph():
+    """Host-buffer calls of one token count run eagerly once, are then captured
+    into a CUDA graph and replayed: every call must see its own input."""
+    cfg = SMALL_QWEN
+    tensors = host_layer(cfg, seed=5)
+    xs = [O.synth_f32(5, CF.S_ACT, i, 6 * cfg.hidden, 1.0).reshape(6, cfg.hidden)
+          for i in range(3)]
+    refs = [O.moe_forward(oracle_layer(cfg, tensors), x, 6, cfg.top_k)[0] for x in xs]
+    s = _session(cfg, tensors, 8)
+    try:
+        for i in (0, 1, 1, 2, 0, 2):  # eager, capture, replays with new inputs
+            out = s.run(xs[i])
+            assert max_rel(out, refs[i]) < 1e-5, i
+        out3 = s.run(xs[0][:3])  # another token count: eager, then its own graph
+        assert max_rel(out3, O.moe_forward(oracle_layer(cfg, tensors), xs[0][:3], 3,
+                                           cfg.top_k)[0]) < 1e-5
+        assert max_rel(s.run(xs[1]), refs[1]) < 1e-5
+        dest = np.empty_like(xs[2])  # the run-into form writes the caller's buffer
+        assert s.run_into(dest, xs[2]) is dest
+        assert max_rel(dest, refs[2]) < 1e-5
+    finally:
+        s.close()
+
+
 def test_expert_parallel_split_sums_to_full():
     """Expert-parallel shards (owned expert ranges, shared expert on one
     shard) add up to the whole layer."""
