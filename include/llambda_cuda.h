@@ -222,6 +222,19 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_sess
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_kernel_ms(llambda_cuda_moe_session* session,
                                                         float* gate_up_ms, float* down_ms);
 
+/* Prefill path (a tuning knob with no counterpart in the reference; the
+ * reference runs every token through the same per-token code,
+ * qwen3next-moe-into L5321-5426 / nemotron-h-moe-ffn-into L5827-5949).
+ * MoE runs of at least `tokens` tokens (default 128; values below 64 act as
+ * 64) compute the expert products as bf16 grouped GEMMs on the tensor cores:
+ * weights decoded once per 128-row block and 64 tokens, inputs and the
+ * gate/up activations rounded to bf16, fp32 sums (results within 2e-2
+ * relative of the fp32 path).  Smaller runs use the fp32 decode kernels.
+ * Process-wide; later runs use the new value.  0 on success, -1 on a
+ * non-positive value. */
+LLAMBDA_CUDA_API int llambda_cuda_set_prefill_min_tokens(int tokens);
+LLAMBDA_CUDA_API int llambda_cuda_prefill_min_tokens(void);
+
 /* Expert-parallel reduction over peer memory.  These entry points have no
  * counterpart in the reference (llambda runs on one device).
  *

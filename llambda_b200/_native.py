@@ -84,6 +84,8 @@ SIGNATURES = {
     "llambda_cuda_moe_session_time_kernels": (C.c_int, [_vp, C.c_int]),
     "llambda_cuda_moe_session_kernel_ms": (C.c_int, [_vp, C.POINTER(C.c_float),
                                                       C.POINTER(C.c_float)]),
+    "llambda_cuda_set_prefill_min_tokens": (C.c_int, [C.c_int]),
+    "llambda_cuda_prefill_min_tokens": (C.c_int, []),
     "llambda_cuda_moe_peer_bytes": (_sz, [_vp, C.c_int]),
     "llambda_cuda_moe_session_attach_peers": (C.c_int, [_vp, C.c_int, C.c_int,
                                                         C.POINTER(_vp), _sz]),
@@ -383,3 +385,13 @@ def synth_fill_device(type_tag: int, seed: int, stream_id: int, first: int, coun
                       scale: float, out_dev, stream=None) -> None:
     _check(lib().llambda_cuda_synth_fill_device(type_tag, seed, stream_id, first, count, scale,
                                                 _dev_ptr(out_dev), _stream_ptr(stream)))
+
+
+def set_prefill_min_tokens(tokens: int) -> None:
+    """MoE runs of at least `tokens` tokens take the bf16 tensor-core prefill
+    path (process-wide; values below 64 act as 64)."""
+    _check(lib().llambda_cuda_set_prefill_min_tokens(int(tokens)))
+
+
+def prefill_min_tokens() -> int:
+    return int(lib().llambda_cuda_prefill_min_tokens())

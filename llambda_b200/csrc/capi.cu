@@ -243,6 +243,7 @@ struct llambda_cuda_moe_session {
   int graph_tokens = 0;
   int eager_tokens = 0;  // the first call of a token count runs eagerly (fills the caches)
   const void* graph_key[2] = {nullptr, nullptr};
+  int graph_prefill_min = 0;  // the prefill threshold the graph was captured under
   void drop_graph() {
     if (graph) cudaGraphExecDestroy(graph);
     graph = nullptr;
@@ -775,7 +776,7 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
                  "copy");
     };
     const bool same = s->graph && s->graph_tokens == T && s->graph_key[0] == hx &&
-                      s->graph_key[1] == hout;
+                      s->graph_key[1] == hout && s->graph_prefill_min == lb::prefill_min_tokens();
     if (s->timing || selected || weights || (!same && s->eager_tokens != T)) {
       enqueue();  // timed or checked calls, and a new token count's first call
       s->eager_tokens = T;
@@ -799,6 +800,7 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
         s->graph_tokens = T;
         s->graph_key[0] = hx;
         s->graph_key[1] = hout;
+        s->graph_prefill_min = lb::prefill_min_tokens();
       }
       cuda_check(cudaGraphLaunch(s->graph, s->stream), "graph launch");
     }
@@ -840,6 +842,17 @@ int llambda_cuda_moe_session_run_device(llambda_cuda_moe_session* s, const float
     return 0;
   });
 }
+
+int llambda_cuda_set_prefill_min_tokens(int tokens) {
+  if (tokens < 1) {
+    set_error("The prefill threshold must be positive.");
+    return -1;
+  }
+  lb::set_prefill_min_tokens(tokens);
+  return 0;
+}
+
+int llambda_cuda_prefill_min_tokens(void) { return lb::prefill_min_tokens(); }
 
 int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_session* s, int enable) {
   if (!s) {

@@ -148,6 +148,13 @@ struct MoeWork {
   float* xp_down;     // [T*k + T] prepared down inputs: routed entry ids, then
                       // shared token rows (stride xp_stride(max(k_down, k_down_sh)))
   float* partial;     // [T][k+1][H] unscaled down outputs per (token, rank)
+  // Prefill path (carved when max_tokens >= 64, null otherwise):
+  uint16_t* pf_xs;    // [T*k + T][k_in] bf16 inputs grouped by expert, then shared rows
+  uint16_t* pf_hs;    // [T*k + T][max(k_down, k_down_sh)] bf16 intermediates, same rows
+  int* pf_prow;       // [T*k + T] partial-output row of each grouped row
+  int4* pf_tiles;     // gate/up tiles [pf_max_up], then down tiles
+  int* pf_count;      // [2] tiles of the gate/up and the down pass
+  long pf_max_up;
   size_t bytes;
 };
 
@@ -170,5 +177,17 @@ void moe_work_carve(const MoeDevice& m, int max_tokens, void* base, MoeWork* w);
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int tokens,
                        float* out, const SlabMaps* maps, cudaStream_t stream,
                        const cudaEvent_t* marks = nullptr);
+
+// Prefill path (prefill.cu): the expert products of batches of at least
+// prefill_min_tokens() tokens as tcgen05 bf16 grouped GEMMs.
+void set_prefill_min_tokens(int n);
+int prefill_min_tokens();
+size_t prefill_work_bytes(const MoeDevice& m, int max_tokens, size_t* parts /* [5] */);
+long prefill_max_up_tiles(const MoeDevice& m, int max_tokens);
+bool prefill_applies(const MoeDevice& m, const MoeWork& w, int T);
+// Gather, plan, gate/up and down passes; partial outputs land in w.partial
+// as in the decode path.  marks as in launch_moe.
+cudaError_t launch_prefill_passes(const MoeDevice& m, const MoeWork& w, const float* x, int T,
+                                  cudaStream_t stream, const cudaEvent_t* marks);
 
 }  // namespace lb

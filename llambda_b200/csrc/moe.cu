@@ -1856,6 +1856,20 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
   w->xp_down = reinterpret_cast<float*>(
       take((size_t)(T * k + T) * down_ld_floats(m) * 4));
   w->partial = reinterpret_cast<float*>(take((size_t)T * (k + 1) * m.hidden * 4));
+  size_t pf[5];
+  if (prefill_work_bytes(m, T, pf)) {
+    w->pf_xs = reinterpret_cast<uint16_t*>(take(pf[0]));
+    w->pf_hs = reinterpret_cast<uint16_t*>(take(pf[1]));
+    w->pf_prow = reinterpret_cast<int*>(take(pf[2]));
+    w->pf_tiles = reinterpret_cast<int4*>(take(pf[3]));
+    w->pf_count = reinterpret_cast<int*>(take(pf[4]));
+    w->pf_max_up = prefill_max_up_tiles(m, T);
+  } else {
+    w->pf_xs = w->pf_hs = nullptr;
+    w->pf_prow = w->pf_count = nullptr;
+    w->pf_tiles = nullptr;
+    w->pf_max_up = 0;
+  }
   w->bytes = off;
 }
 
@@ -1907,7 +1921,9 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   }
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
   if (!gate_ok) return cudaErrorInvalidValue;
-  if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q6_K)
+  if (prefill_applies(m, w, T))
+    e = launch_prefill_passes(m, w, x, T, s, marks);
+  else if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q6_K)
     e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q6_K>(m, w, T, maps, s, marks);
   else if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q4_K)
     e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q4_K>(m, w, T, maps, s, marks);

@@ -1,0 +1,874 @@
+// Expert products of prefill-sized batches on the fifth-generation tensor
+// cores (tcgen05, sm_100a).
+//
+// The decode kernels take an expert's tokens two to four at a time and decode
+// its weights again for every pass.  A prefill batch routes tens of tokens to
+// every expert, so this path decodes each 128-row block of an expert's
+// weights ONCE per 64 tokens, into bf16 in shared memory, and multiplies it
+// against all of those tokens with tcgen05.mma (accumulators in tensor
+// memory):
+//
+//   gather   x (rms-normed when the layer has input_norm) -> bf16 rows grouped
+//            by expert (xs: the routed entries in expert order, then the
+//            shared expert's tokens), and the partial-output row of each
+//   plan     tile lists: (expert, 64-token chunk, 128-row block) per pass
+//   gate/up  D[128 rows x tokens] = W (decoded) . xs^T per tile; epilogue
+//            silu(gate) * up (qwen3next-moe-into, llambda.lisp L5321-5426) or
+//            relu(up)^2 (nemotron-h-moe-ffn-into, L5827-5949) -> bf16 rows hs
+//   down     D = W_down (decoded) . hs^T -> fp32 partial outputs per (token,
+//            rank), which the combine kernel weights and sums exactly as in
+//            the decode path (L5380-5426, L5940-5949)
+//
+// Weight decode follows the reference's formulas: Q4_K w = (d*sc)*q - dmin*m
+// (expand-q4-k-body, L4145-4201; get-scale-min-k4-at, L4316-4336), Q6_K
+// w = d*sc*(q - 32) (q6-quant-1..4, L4115-4137; expand-q6-k-group,
+// L4203-4310), each rounded once to bf16; tokens are rounded to bf16; all
+// sums are fp32 in the tensor cores.
+//
+// One CTA per SM (persistent; tiles i, i + grid, ...), 10 warps:
+//   warps 0-7  decode: thread (row r = tid % 128, half h = tid / 128) turns
+//              32 weights of its row into bf16 per 64-wide K chunk, written
+//              in the 128-byte-swizzled K-major layout the MMA reads; then
+//              the epilogue (tensor-memory lanes of warp w are rows
+//              32*(w%4)..+31; warps 0-3 take tokens 0-31, warps 4-7 32-63)
+//   warp 8     producer: per super-block, one bulk copy per weight row
+//              (rounded out to 16-byte bounds) and four TMA tensor loads of
+//              the tokens' bf16 rows (64 x 64, 128-byte swizzle)
+//   warp 9     MMA: one thread issues tcgen05.mma (M=128, N = tokens rounded
+//              up to 16, K=16, bf16 x bf16 -> fp32) and tcgen05.commit
+// Pipelines (mbarriers, every wait bounded in time):
+//   full/empty[2]     weight + token stages (producer -> decoders, MMA)
+//   afull/aempty[4]   decoded 128 x 64 chunks (decoders -> MMA)
+//   tfull/tempty      the tile's accumulators (MMA -> epilogue -> MMA)
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <mutex>
+
+#include "engine.cuh"
+#include "kernels.h"
+
+namespace lb {
+
+namespace {
+
+constexpr int kPfM = 128;       // weight rows per tile (the MMA's M)
+constexpr int kPfN = 64;        // tokens per tile
+constexpr int kPfRing = 4;      // decoded chunks in flight
+constexpr int kPfStages = 2;    // weight + token stages
+constexpr int kPfDecWarps = 8;
+constexpr int kPfThreads = (kPfDecWarps + 2) * 32;
+constexpr uint32_t kPfChunkBytes = kPfM * 128;   // 128 rows x 64 bf16
+constexpr uint32_t kPfBoxBytes = kPfN * 128;     // 64 tokens x 64 bf16
+constexpr uint32_t kPfBStage = 4 * kPfBoxBytes;  // one super-block of K
+constexpr int kPfCarveMin = 64;                  // smallest max_tokens given prefill buffers
+
+__host__ __device__ constexpr int pf_block_bytes(int wt) { return wt == LB_TYPE_Q4_K ? LB_Q4K : LB_Q6K; }
+// Bytes of one staged row (the inner box of the weights' tensor map): a Q4_K
+// super-block (144 bytes, always 16-byte aligned), or a Q6_K super-block with
+// the 0-14 bytes before it down to a 16-byte boundary (210 + 14 = 224).
+__host__ __device__ constexpr int pf_pitch(int wt) { return wt == LB_TYPE_Q4_K ? LB_Q4K : 224; }
+__host__ __device__ constexpr uint32_t pf_wstage(int wt, int nmat) {
+  return (uint32_t)(nmat * kPfM * pf_pitch(wt));
+}
+
+struct PfSync {
+  uint64_t full[kPfStages], empty[kPfStages];
+  uint64_t afull[kPfRing], aempty[kPfRing];
+  uint64_t tfull, tempty, done;
+  uint32_t tmem;
+  int abort;
+};
+
+__host__ __device__ constexpr size_t pf_smem_bytes(int wt, int nmat) {
+  return 1024 /* alignment slack */ + (size_t)kPfRing * kPfChunkBytes +
+         (size_t)kPfStages * kPfBStage + (size_t)kPfStages * pf_wstage(wt, nmat) +
+         sizeof(PfSync);
+}
+
+// Tensor maps of one pass: the tokens' bf16 rows (64 x 64 boxes, 128-byte
+// swizzle) and the weights (routed gate or up / down, routed up, the shared
+// expert's), each viewed as a byte matrix whose rows are g weight rows, so
+// the row pitch g * rb is a multiple of 16; a box is one super-block column
+// (pf_pitch bytes from a 16-byte boundary) of 128 / g map rows.
+struct PfMaps {
+  CUtensorMap b, w0, w1, s0, s1;
+};
+
+// One pass (gate/up or down) of the prefill path.
+struct PfPass {
+  int g, g_sh;        // weight rows per tensor-map row
+  long rb, rb_sh;     // row bytes
+  int rows, rows_sh;  // rows of one expert matrix (valid rows of a tile)
+  int nsb, nsb_sh;    // super-blocks per row
+  const int4* tiles;  // {first grouped row, tokens, expert (-1 shared), row block}
+  const int* ntiles;
+  uint16_t* hs;       // gate/up output: bf16 [grouped row][ld_h]
+  long ld_h;
+  float* partial;     // down output: [T][k+1][H]
+  const int* prow;    // partial row of each grouped row
+  int H;
+  int* status;
+};
+
+// ------------------------------------------------------------ tcgen05 PTX
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(dst)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+               : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, both K-major, kind::f16 (bf16 operands).
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrives on bar once every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+// 16 consecutive fp32 columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;"  // the registers are defined only after the wait
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte
+// swizzled layout: rows of 128 bytes (64 bf16), groups of 8 rows 1024 bytes
+// apart; p must be 1024-byte aligned (the swizzle phase is taken from the
+// address).  Start address >> 4 in bits 0-13, stride-dimension offset
+// (1024 >> 4) in bits 32-45, descriptor version 1 (bits 46-47), layout type
+// 2 = 128-byte swizzle (bits 61-63).  Advancing K by 16 bf16 adds 32 bytes
+// (2 in the start field).
+__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
+  const uint32_t a = smem_addr(p);
+  return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and
+// B bf16 (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 in bits 17-22,
+// M >> 4 in bits 24-28.
+__device__ __forceinline__ uint32_t mma_idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(kPfM >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Offset of 16-byte chunk `chunk` (0..7) of row r in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int chunk) {
+  return (uint32_t)r * 128u + ((uint32_t)(chunk ^ (r & 7)) << 4);
+}
+
+// N little-endian words from a 2-byte-aligned shared-memory address: N + 1
+// aligned loads and a funnel shift each (the word after the run is read; the
+// callers' runs end at least 4 bytes before the end of the staged row).
+template <int N>
+__device__ __forceinline__ void lds_run(const uint8_t* p, uint32_t* out) {
+  const uint32_t a = smem_addr(p);
+  const uint32_t s = (a & 3u) * 8u;
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(p - (a & 3u));
+  uint32_t v[N + 1];
+#pragma unroll
+  for (int i = 0; i <= N; ++i) v[i] = w[i];
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(v[i], v[i + 1], s);
+}
+
+// Four weights of one word of 4-bit or 6-bit values (bytes below 128) to
+// bf16 pairs: w = ds * (2^23 + 2^16 q) - off, the PRMT magic float of each
+// byte (see magic_q).
+__device__ __forceinline__ void decode_word(uint32_t v, float ds, float off, uint32_t& p0,
+                                            uint32_t& p1) {
+  const float f0 = fmaf(ds, magic_q<0>(v), -off), f1 = fmaf(ds, magic_q<1>(v), -off);
+  const float f2 = fmaf(ds, magic_q<2>(v), -off), f3 = fmaf(ds, magic_q<3>(v), -off);
+  p0 = bf16x2(f0, f1);
+  p1 = bf16x2(f2, f3);
+}
+
+// 32 weights (K [64c + 32h, +32) of the super-block at b) as bf16 into row r
+// of a decoded chunk.
+template <int WT>
+__device__ __forceinline__ void decode_chunk(const uint8_t* b, int c, int h, int r, uint8_t* a) {
+  uint32_t o[16];
+  if (WT == LB_TYPE_Q4_K) {
+    // sub-block j = 2c + h: qs bytes [32c, 32c + 32), low nibbles (h = 0) or
+    // high nibbles (h = 1); w = (d*sc)*q - dmin*m
+    const uint4 hdr = *reinterpret_cast<const uint4*>(b);
+    const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
+    int sc, mn;
+    q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + h, sc, mn);
+    const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+    const float ds = d1 * kMagicUnscale, off = fmaf(d1, kMagicBias, m1);
+    const uint4 q0 = *reinterpret_cast<const uint4*>(b + 16 + 32 * c);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(b + 32 + 32 * c);
+    const uint32_t wd[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const int sh = 4 * h;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      decode_word((wd[i] >> sh) & 0x0F0F0F0Fu, ds, off, o[2 * i], o[2 * i + 1]);
+  } else {
+    // 128-half n = c / 2, quarter qd = 2 (c % 2) + h: ql bytes
+    // [64n + 32 (qd % 2), +32) (low nibbles for qd < 2, high otherwise),
+    // qh bytes [128 + 32n, +32) bits 2qd..2qd+1, scales 8n + 2qd + l/16;
+    // w = d * sc * (q - 32)
+    const int n = c >> 1, qd = (c & 1) * 2 + h;
+    uint32_t ql[8], qh[8];
+    lds_run<8>(b + 64 * n + 32 * (qd & 1), ql);
+    lds_run<8>(b + 128 + 32 * n, qh);
+    const uint32_t scw = lds_u16(b + 192 + 8 * n + 2 * qd);
+    const float d = half_bits_to_float(lds_u16(b + 208));
+    const float d0 = d * (float)(int)(int8_t)(scw & 0xFFu);
+    const float d1 = d * (float)(int)(int8_t)(scw >> 8);
+    const float ds0 = d0 * kMagicUnscale, off0 = d0 * (kMagicBias + 32.0f);
+    const float ds1 = d1 * kMagicUnscale, off1 = d1 * (kMagicBias + 32.0f);
+    const int shl = 4 * (qd >> 1), shh = 2 * qd;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t v = ((ql[i] >> shl) & 0x0F0F0F0Fu) | (((qh[i] >> shh) & 0x03030303u) << 4);
+      decode_word(v, i < 4 ? ds0 : ds1, i < 4 ? off0 : off1, o[2 * i], o[2 * i + 1]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(a + sw128_off(r, 4 * h + j)) =
+        make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+}
+
+__device__ __forceinline__ void zero_chunk(int h, int r, uint8_t* a) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(a + sw128_off(r, 4 * h + j)) = make_uint4(0, 0, 0, 0);
+}
+
+// ------------------------------------------------------------ GEMM kernel
+//
+// PAIR: two weight matrices (gate, up) share the tokens; DOWN: the epilogue
+// writes fp32 partial outputs instead of bf16 activations.
+template <int WT, bool PAIR, bool DOWN>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    pf_gemm_kernel(const __grid_constant__ PfMaps maps, const PfPass p) {
+  constexpr int NMAT = PAIR ? 2 : 1;
+  constexpr int BB = pf_block_bytes(WT), PITCH = pf_pitch(WT);
+  constexpr uint32_t WSTAGE = pf_wstage(WT, NMAT);
+  constexpr uint32_t TCOLS = NMAT * kPfN;  // 64 or 128 tensor-memory columns
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint8_t* a_ring = smem;
+  uint8_t* b_st = a_ring + kPfRing * kPfChunkBytes;
+  uint8_t* w_st = b_st + kPfStages * kPfBStage;
+  PfSync* sy = reinterpret_cast<PfSync*>(w_st + kPfStages * WSTAGE);
+  volatile int* abort = &sy->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&sy->full[s], 1);
+      mbar_init(&sy->empty[s], kPfDecWarps + 1);
+    }
+    for (int i = 0; i < kPfRing; ++i) {
+      mbar_init(&sy->afull[i], kPfDecWarps);
+      mbar_init(&sy->aempty[i], 1);
+    }
+    mbar_init(&sy->tfull, 1);
+    mbar_init(&sy->tempty, kPfDecWarps);
+    mbar_init(&sy->done, 1);
+    sy->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kPfDecWarps + 1) tmem_alloc(&sy->tmem, TCOLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sy->tmem;
+  const int ntiles = *p.ntiles;
+
+  if (warp == kPfDecWarps) {  // ------------------------------------ producer
+    RingPos rp;
+    int q = 0;
+    uint32_t last_phase[kPfStages] = {};
+    for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
+      const int4 tl = p.tiles[tile];
+      const bool sh = tl.z < 0;
+      const int nsb = sh ? p.nsb_sh : p.nsb, rows = sh ? p.rows_sh : p.rows;
+      const int g = sh ? p.g_sh : p.g, rows_g = kPfM / g;
+      const long rb = sh ? p.rb_sh : p.rb;
+      // this lane's box: matrix lane / g, weight rows j, j + g, ... (j = lane % g)
+      const int mat = lane / g, j = lane - mat * g;
+      const CUtensorMap* wm = mat == 0 ? (sh ? &maps.s0 : &maps.w0) : (sh ? &maps.s1 : &maps.w1);
+      const int y = (int)(((sh ? 0L : (long)tl.z * rows) + (long)tl.w * kPfM) / g);
+      for (int sb = 0; sb < nsb; ++sb) {
+        if (q >= kPfStages &&
+            !mbar_wait_or_abort(&sy->empty[rp.s], rp.phase ^ 1u, p.status, abort))
+          break;
+        uint8_t* wst = w_st + rp.s * WSTAGE;
+        if (lane == 0) mbar_expect_tx(&sy->full[rp.s], WSTAGE + kPfBStage);
+        __syncwarp();
+        if (lane < NMAT * g) {
+          const long x = (long)j * rb + (long)sb * BB;
+          tma_load_2d(wst + (size_t)(mat * kPfM + j * rows_g) * PITCH, wm, (int)(x & ~15L), y,
+                      &sy->full[rp.s]);
+        }
+        if (lane == 0)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tma_load_2d(b_st + rp.s * kPfBStage + c * kPfBoxBytes, &maps.b, sb * 256 + c * 64,
+                        tl.x, &sy->full[rp.s]);
+        last_phase[rp.s] = rp.phase;
+        ++q;
+        rp.next(kPfStages);
+      }
+    }
+    // copies still in flight land before the CTA exits (bounded)
+    for (int s = 0; s < kPfStages && s < q; ++s) mbar_wait(&sy->full[s], last_phase[s], nullptr);
+  } else if (warp == kPfDecWarps + 1) {  // ---------------------------- MMA
+    if (lane == 0) {
+      RingPos rp;
+      int auses = 0, it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x, ++it) {
+        const int4 tl = p.tiles[tile];
+        const int nsb = tl.z < 0 ? p.nsb_sh : p.nsb;
+        const uint32_t idesc = mma_idesc((tl.y + 15) & ~15);
+        if (it > 0 && !mbar_wait_or_abort(&sy->tempty, (it - 1) & 1, p.status, abort)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int sb = 0; sb < nsb && ok; ++sb) {
+          if (!mbar_wait_or_abort(&sy->full[rp.s], rp.phase, p.status, abort)) {
+            ok = false;
+            break;
+          }
+          for (int c = 0; c < 4 && ok; ++c)
+#pragma unroll
+            for (int mat = 0; mat < NMAT; ++mat) {
+              const int slot = auses & (kPfRing - 1);
+              if (!mbar_wait_or_abort(&sy->afull[slot], (auses / kPfRing) & 1, p.status, abort)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t ad = sw128_desc(a_ring + slot * kPfChunkBytes);
+              const uint64_t bd = sw128_desc(b_st + rp.s * kPfBStage + c * kPfBoxBytes);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                tc_mma(tmem + mat * kPfN, ad + 2 * j, bd + 2 * j, idesc, (sb | c | j) != 0);
+              tc_commit(&sy->aempty[slot]);
+              ++auses;
+            }
+          if (!ok) break;
+          tc_commit(&sy->empty[rp.s]);
+          rp.next(kPfStages);
+        }
+        if (!ok) break;
+        tc_commit(&sy->tfull);
+      }
+      // every MMA issued has completed before the tensor memory is freed
+      tc_commit(&sy->done);
+      mbar_wait(&sy->done, 0, nullptr);
+    }
+    __syncwarp();
+  } else {  // ------------------------------------------------ decode + epilogue
+    const int tid = threadIdx.x, r = tid & (kPfM - 1), h = tid >> 7;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    RingPos rp;
+    int auses = 0, it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      const int4 tl = p.tiles[tile];
+      const bool sh = tl.z < 0;
+      const int nsb = sh ? p.nsb_sh : p.nsb, rows = sh ? p.rows_sh : p.rows;
+      const long rb = sh ? p.rb_sh : p.rb;
+      const int r0 = tl.w * kPfM;
+      const bool valid = r0 + r < rows;
+      const int g = sh ? p.g_sh : p.g;
+      const int jr = r % g;  // this row's box and its place in it
+      const uint32_t srow = (uint32_t)(jr * (kPfM / g) + r / g) * PITCH;
+      for (int sb = 0; sb < nsb && ok; ++sb) {
+        if (!mbar_wait_or_abort(&sy->full[rp.s], rp.phase, p.status, abort)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* wst = w_st + rp.s * WSTAGE;
+        // the super-block's offset in its box row (the box starts 16-byte aligned)
+        const uint32_t mis = (uint32_t)(((long)jr * rb + (long)sb * BB) & 15L);
+        for (int c = 0; c < 4 && ok; ++c)
+#pragma unroll
+          for (int mat = 0; mat < NMAT; ++mat) {
+            const int slot = auses & (kPfRing - 1);
+            if (auses >= kPfRing &&
+                !mbar_wait_or_abort(&sy->aempty[slot], ((auses / kPfRing) - 1) & 1, p.status,
+                                    abort)) {
+              ok = false;
+              break;
+            }
+            uint8_t* a = a_ring + slot * kPfChunkBytes;
+            if (valid)
+              decode_chunk<WT>(wst + (size_t)mat * kPfM * PITCH + srow + mis, c, h, r, a);
+            else
+              zero_chunk(h, r, a);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sy->afull[slot]);
+            ++auses;
+          }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sy->empty[rp.s]);
+        rp.next(kPfStages);
+      }
+      if (!ok) break;
+      // ---- epilogue: this warp's 32 rows, tokens [32 h, 32 h + 32)
+      if (!mbar_wait_or_abort(&sy->tfull, it & 1, p.status, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int ntok = tl.y;
+      const int row = r0 + r;
+#pragma unroll 1
+      for (int c16 = 0; c16 < 2; ++c16) {
+        const int n0 = 32 * h + 16 * c16;
+        if (n0 >= ntok) break;  // warp-uniform
+        float y0[16], y1[16];
+        tmem_ld16(tmem + lane_base + n0, y0);
+        if (PAIR) tmem_ld16(tmem + lane_base + kPfN + n0, y1);
+        if (DOWN) {
+          if (row < p.H)
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (n0 + j < ntok)
+                p.partial[(long)__ldg(p.prow + tl.x + n0 + j) * p.H + row] = y0[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (n0 + j < ntok) {
+              float hv = 0.f;
+              if (row < rows) {
+                if (PAIR) {
+                  hv = __fmul_rn(y0[j] / (1.0f + __expf(-y0[j])), y1[j]);
+                } else {
+                  const float u = y0[j] > 0.f ? y0[j] : 0.f;
+                  hv = __fmul_rn(u, u);
+                }
+              }
+              const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
+              p.hs[(long)(tl.x + n0 + j) * p.ld_h + row] = *reinterpret_cast<const uint16_t*>(&hb);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sy->tempty);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kPfDecWarps + 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TCOLS);
+  }
+}
+
+// ------------------------------------------------------------ gather + plan
+
+// One CTA per token: the token's bf16 row (rms-normed when the layer has
+// input_norm: rms-norm-into, llambda.lisp L859-879) copied to each grouped
+// row it is routed to on this device, zero-padded from H to k_in.
+__global__ void __launch_bounds__(256) pf_gather_kernel(MoeDevice m, MoeWork w,
+                                                        const float* __restrict__ x, int T) {
+  __shared__ int s_dst[33], s_prow[33], s_n;
+  __shared__ float s_red[8];
+  const int t = blockIdx.x, H = m.hidden, K = m.k_in, k = m.top_k;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* xt = x + (long)t * H;
+  if (warp == 0) {
+    int dst = -1;
+    if (lane < k) {
+      const int id = t * k + lane;
+      const int e = w.sel[id];
+      if (e >= m.expert_begin && e < m.expert_end) dst = w.offsets[e] + w.entries[id];
+    }
+    const unsigned own = __ballot_sync(0xffffffffu, dst >= 0);
+    const int slot = __popc(own & ((1u << lane) - 1u));
+    if (dst >= 0) {
+      s_dst[slot] = dst;
+      s_prow[slot] = t * (k + 1) + lane;
+    }
+    if (lane == 0) {
+      int n = __popc(own);
+      int t0, t1;
+      shared_tokens(m, T, t0, t1);
+      if (m.shared_here && m.inter_sh && t >= t0 && t < t1) {
+        s_dst[n] = T * k + t;
+        s_prow[n] = t * (k + 1) + k;
+        ++n;
+      }
+      s_n = n;
+    }
+  }
+  float scale = 1.f;
+  if (m.input_norm) {
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) acc = fmaf(xt[i], xt[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) s_red[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+      for (int i = 0; i < 8; ++i) s += s_red[i];
+      s_red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), m.norm_epsilon)));
+    }
+  }
+  __syncthreads();
+  if (m.input_norm) scale = s_red[0];
+  const int nd = s_n;
+  uint16_t* xs = w.pf_xs;
+  for (int c0 = threadIdx.x * 8; c0 < K; c0 += blockDim.x * 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = c0 + j;
+      float xv = i < H ? xt[i] : 0.f;
+      if (m.input_norm && i < H) xv = __fmul_rn(__fmul_rn(xv, m.input_norm[i]), scale);
+      v[j] = xv;
+    }
+    const uint4 pk = make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]),
+                                bf16x2(v[6], v[7]));
+    for (int d = 0; d < nd; ++d)
+      *reinterpret_cast<uint4*>(xs + (long)s_dst[d] * K + c0) = pk;
+  }
+  if (threadIdx.x < nd) w.pf_prow[s_dst[threadIdx.x]] = s_prow[threadIdx.x];
+}
+
+// Tile lists of both passes, in expert order (then the shared expert): for
+// each active expert, its row blocks, each with its 64-token chunks in a row,
+// so CTAs running side by side read the same weight rows.
+__global__ void __launch_bounds__(1024) pf_plan_kernel(MoeDevice m, MoeWork w, int T) {
+  __shared__ int s_warp[32];
+  const int E = m.experts, na = w.active[E];
+  const int a = threadIdx.x, warp = a >> 5, lane = a & 31;
+  int e = -1, cnt = 0, nch = 0;
+  if (a < na) {
+    e = w.active[a];
+    cnt = w.counts[e];
+    nch = (cnt + kPfN - 1) / kPfN;
+  }
+  int incl = nch;  // inclusive scan over the block
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int v = s_warp[lane], iv = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, iv, o);
+      if (lane >= o) iv += u;
+    }
+    s_warp[lane] = iv - v;  // exclusive
+  }
+  __syncthreads();
+  const int base = s_warp[warp] + incl - nch;  // chunks of the active experts before a
+  __shared__ int s_total;
+  if (a == blockDim.x - 1) s_total = base + nch;
+  __syncthreads();
+  const int routed = s_total;
+  const int mbu = m.k_down / kPfM, mbd = (m.hidden + kPfM - 1) / kPfM;
+  int4* up = w.pf_tiles;
+  int4* dn = w.pf_tiles + w.pf_max_up;
+  if (a < na) {
+    const int off = w.offsets[e];
+    for (int mb = 0; mb < mbu; ++mb)
+      for (int ch = 0; ch < nch; ++ch)
+        up[(long)base * mbu + mb * nch + ch] =
+            make_int4(off + ch * kPfN, min(kPfN, cnt - ch * kPfN), e, mb);
+    for (int mb = 0; mb < mbd; ++mb)
+      for (int ch = 0; ch < nch; ++ch)
+        dn[(long)base * mbd + mb * nch + ch] =
+            make_int4(off + ch * kPfN, min(kPfN, cnt - ch * kPfN), e, mb);
+  }
+  int nsh = 0, mbu_sh = 0, t0 = 0, t1 = 0;
+  if (m.shared_here && m.inter_sh) {
+    shared_tokens(m, T, t0, t1);
+    nsh = (t1 - t0 + kPfN - 1) / kPfN;
+    mbu_sh = m.k_down_sh / kPfM;
+  }
+  for (int i = a; i < nsh * mbu_sh; i += blockDim.x) {
+    const int mb = i / nsh, ch = i - mb * nsh;
+    up[(long)routed * mbu + i] =
+        make_int4(T * m.top_k + t0 + ch * kPfN, min(kPfN, t1 - t0 - ch * kPfN), -1, mb);
+  }
+  for (int i = a; i < nsh * mbd; i += blockDim.x) {
+    const int mb = i / nsh, ch = i - mb * nsh;
+    dn[(long)routed * mbd + i] =
+        make_int4(T * m.top_k + t0 + ch * kPfN, min(kPfN, t1 - t0 - ch * kPfN), -1, mb);
+  }
+  if (a == 0) {
+    w.pf_count[0] = routed * mbu + nsh * mbu_sh;
+    w.pf_count[1] = (routed + nsh) * mbd;
+  }
+}
+
+// ------------------------------------------------------------ host side
+
+std::atomic<int> g_prefill_min{128};
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return encode;
+}
+
+// bf16 rows [rows][cols] (row pitch cols * 2 bytes), 64 x 64 boxes with the
+// 128-byte swizzle; rows past the end read as zeros.
+bool bf16_rows_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows) {
+  const auto encode = tensor_map_encoder();
+  if (!encode || rows == 0 || (cols * 2) % 16) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kPfN};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int pf_down_ld(const MoeDevice& m) {
+  return std::max(m.k_down, m.shared_here && m.inter_sh ? m.k_down_sh : 0);
+}
+
+void pf_tile_bounds(const MoeDevice& m, int T, long* max_up, long* max_dn) {
+  const long entries = (long)T * m.top_k;
+  const long owned = std::max(1, m.expert_end - m.expert_begin);
+  const long chunks_r = entries / kPfN + std::min(owned, entries) + 1;
+  const long chunks_sh = m.shared_here && m.inter_sh ? (T + kPfN - 1) / kPfN : 0;
+  const long mbu = m.k_down / kPfM, mbd = (m.hidden + kPfM - 1) / kPfM;
+  const long mbu_sh = m.shared_here && m.inter_sh ? m.k_down_sh / kPfM : 0;
+  *max_up = chunks_r * mbu + chunks_sh * mbu_sh;
+  *max_dn = (chunks_r + chunks_sh) * mbd;
+}
+
+bool q_type(int t) { return t == LB_TYPE_Q4_K || t == LB_TYPE_Q6_K; }
+
+// Weight rows per tensor-map row: the smallest g in 1, 2, 4, 8 with g * rb a
+// multiple of 16 bytes that divides the tensor's rows and one expert's rows
+// (a Q6_K row of n super-blocks is 2n mod 16 bytes); 0 if none.
+int pf_group(long rb, long rows_total, long rows_e) {
+  for (int g = 1; g <= 8; g *= 2)
+    if ((g * rb) % 16 == 0 && rows_total % g == 0 && rows_e % g == 0) return g;
+  return 0;
+}
+
+bool pf_weight_map(CUtensorMap* map, const uint8_t* base, long rb, long rows_total, int g,
+                   int pitch) {
+  const auto encode = tensor_map_encoder();
+  if (!encode || !base || !g || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)(g * rb), (cuuint64_t)(rows_total / g)};
+  const cuuint64_t strides[1] = {(cuuint64_t)(g * rb)};
+  const cuuint32_t box[2] = {(cuuint32_t)pitch, (cuuint32_t)(kPfM / g)};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides,
+                box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool weights_ok(const uint8_t* base, long rb, long rows_total, long rows_e) {
+  return base && (reinterpret_cast<uintptr_t>(base) & 15) == 0 &&
+         pf_group(rb, rows_total, rows_e) != 0;
+}
+
+template <int WT, bool PAIR, bool DOWN>
+cudaError_t launch_pf_gemm(const PfMaps& maps, const PfPass& p, cudaStream_t s) {
+  auto kern = pf_gemm_kernel<WT, PAIR, DOWN>;
+  const size_t smem = pf_smem_bytes(WT, PAIR ? 2 : 1);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kern<<<sm_count(), kPfThreads, smem, s>>>(maps, p);
+  return cudaGetLastError();
+}
+
+template <bool DOWN>
+cudaError_t launch_pf_pass(int wt, bool pair, const PfMaps& maps, const PfPass& p,
+                           cudaStream_t s) {
+  if (wt == LB_TYPE_Q4_K)
+    return pair ? launch_pf_gemm<LB_TYPE_Q4_K, true, DOWN>(maps, p, s)
+                : launch_pf_gemm<LB_TYPE_Q4_K, false, DOWN>(maps, p, s);
+  return pair ? launch_pf_gemm<LB_TYPE_Q6_K, true, DOWN>(maps, p, s)
+              : launch_pf_gemm<LB_TYPE_Q6_K, false, DOWN>(maps, p, s);
+}
+
+}  // namespace
+
+void set_prefill_min_tokens(int n) { g_prefill_min.store(std::max(kPfCarveMin, n)); }
+int prefill_min_tokens() { return g_prefill_min.load(); }
+
+size_t prefill_work_bytes(const MoeDevice& m, int T, size_t* parts) {
+  if (T < kPfCarveMin) {
+    for (int i = 0; i < 5; ++i) parts[i] = 0;
+    return 0;
+  }
+  const long rows = (long)T * m.top_k + T;
+  long max_up, max_dn;
+  pf_tile_bounds(m, T, &max_up, &max_dn);
+  parts[0] = (size_t)rows * m.k_in * 2;          // xs
+  parts[1] = (size_t)rows * pf_down_ld(m) * 2;   // hs
+  parts[2] = (size_t)rows * 4;                   // prow
+  parts[3] = (size_t)(max_up + max_dn) * 16;     // tiles
+  parts[4] = 16;                                 // counts
+  size_t total = 0;
+  for (int i = 0; i < 5; ++i) total += (parts[i] + 255) & ~size_t(255);
+  return total;
+}
+
+long prefill_max_up_tiles(const MoeDevice& m, int T) {
+  long max_up, max_dn;
+  pf_tile_bounds(m, T, &max_up, &max_dn);
+  return max_up;
+}
+
+bool prefill_applies(const MoeDevice& m, const MoeWork& w, int T) {
+  if (T < g_prefill_min.load() || !w.pf_xs || T > w.max_tokens) return false;
+  if (m.ep_world > 1) return false;
+  if (!q_type(m.up_type) || !q_type(m.down_type)) return false;
+  const bool pair = m.arch == 0;
+  if (pair && m.gate_type != m.up_type) return false;
+  const long E = m.experts;
+  if (!weights_ok(m.up_exps, (long)m.up_rb, E * m.inter, m.inter)) return false;
+  if (pair && !weights_ok(m.gate_exps, (long)m.gate_rb, E * m.inter, m.inter)) return false;
+  if (!weights_ok(m.down_exps, (long)m.down_rb, E * m.hidden, m.hidden)) return false;
+  if (m.shared_here && m.inter_sh) {
+    if (m.up_sh_type != m.up_type || m.down_sh_type != m.down_type) return false;
+    if (pair && m.gate_sh_type != m.gate_type) return false;
+    if (m.k_in_sh != m.k_in) return false;
+    if (!weights_ok(m.up_sh, (long)m.up_sh_rb, m.inter_sh, m.inter_sh)) return false;
+    if (pair && !weights_ok(m.gate_sh, (long)m.gate_sh_rb, m.inter_sh, m.inter_sh)) return false;
+    if (!weights_ok(m.down_sh, (long)m.down_sh_rb, m.hidden, m.hidden)) return false;
+  }
+  constexpr size_t kSmemMax = 227 * 1024;
+  if (pf_smem_bytes(m.up_type, pair ? 2 : 1) > kSmemMax || pf_smem_bytes(m.down_type, 1) > kSmemMax)
+    return false;
+  return (m.k_in % 256) == 0 && (m.k_down % 256) == 0;
+}
+
+cudaError_t launch_prefill_passes(const MoeDevice& m, const MoeWork& w, const float* x, int T,
+                                  cudaStream_t s, const cudaEvent_t* marks) {
+  cudaError_t e;
+  auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
+  if (m.experts > 1024) return cudaErrorInvalidValue;
+  pf_gather_kernel<<<T, 256, 0, s>>>(m, w, x, T);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  pf_plan_kernel<<<1, 1024, 0, s>>>(m, w, T);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  const long rows = (long)T * m.top_k + T;
+  const int ld_h = pf_down_ld(m);
+  const bool pair = m.arch == 0;
+  const bool shared = m.shared_here && m.inter_sh;
+  const long E = m.experts;
+  const int pq_up = pf_pitch(m.up_type), pq_dn = pf_pitch(m.down_type);
+  PfMaps um, dm;
+  PfPass up{}, dn{};
+  up.g = pf_group((long)m.up_rb, E * m.inter, m.inter);
+  dn.g = pf_group((long)m.down_rb, E * m.hidden, m.hidden);
+  if (!bf16_rows_map(&um.b, w.pf_xs, m.k_in, rows) || !bf16_rows_map(&dm.b, w.pf_hs, ld_h, rows) ||
+      !pf_weight_map(&um.w0, pair ? m.gate_exps : m.up_exps, (long)m.up_rb, E * m.inter, up.g,
+                     pq_up) ||
+      !pf_weight_map(&um.w1, m.up_exps, (long)m.up_rb, E * m.inter, up.g, pq_up) ||
+      !pf_weight_map(&dm.w0, m.down_exps, (long)m.down_rb, E * m.hidden, dn.g, pq_dn))
+    return cudaErrorInvalidValue;
+  dm.w1 = dm.w0;
+  if (shared) {
+    up.g_sh = pf_group((long)m.up_sh_rb, m.inter_sh, m.inter_sh);
+    dn.g_sh = pf_group((long)m.down_sh_rb, m.hidden, m.hidden);
+    if (!pf_weight_map(&um.s0, pair ? m.gate_sh : m.up_sh, (long)m.up_sh_rb, m.inter_sh, up.g_sh,
+                       pq_up) ||
+        !pf_weight_map(&um.s1, m.up_sh, (long)m.up_sh_rb, m.inter_sh, up.g_sh, pq_up) ||
+        !pf_weight_map(&dm.s0, m.down_sh, (long)m.down_sh_rb, m.hidden, dn.g_sh, pq_dn))
+      return cudaErrorInvalidValue;
+    dm.s1 = dm.s0;
+  } else {  // no shared tiles: the maps are never read
+    up.g_sh = up.g;
+    dn.g_sh = dn.g;
+    um.s0 = um.w0;
+    um.s1 = um.w1;
+    dm.s0 = dm.s1 = dm.w0;
+  }
+  if ((e = mark(0)) != cudaSuccess) return e;
+  up.rb = (long)m.up_rb;
+  up.rb_sh = shared ? (long)m.up_sh_rb : 0;
+  up.rows = m.inter;
+  up.rows_sh = shared ? m.inter_sh : 0;
+  up.nsb = m.k_in / 256;
+  up.nsb_sh = m.k_in / 256;
+  up.tiles = w.pf_tiles;
+  up.ntiles = w.pf_count;
+  up.hs = w.pf_hs;
+  up.ld_h = ld_h;
+  up.H = m.hidden;
+  up.status = w.status;
+  if ((e = launch_pf_pass<false>(m.up_type, pair, um, up, s)) != cudaSuccess) return e;
+  if ((e = mark(1)) != cudaSuccess) return e;
+  dn.rb = (long)m.down_rb;
+  dn.rb_sh = shared ? (long)m.down_sh_rb : 0;
+  dn.rows = m.hidden;
+  dn.rows_sh = m.hidden;
+  dn.nsb = m.k_down / 256;
+  dn.nsb_sh = shared ? m.k_down_sh / 256 : 0;
+  dn.tiles = w.pf_tiles + w.pf_max_up;
+  dn.ntiles = w.pf_count + 1;
+  dn.partial = w.partial;
+  dn.prow = w.pf_prow;
+  dn.H = m.hidden;
+  dn.status = w.status;
+  if ((e = launch_pf_pass<true>(m.down_type, false, dm, dn, s)) != cudaSuccess) return e;
+  return mark(2);
+}
+
+}  // namespace lb

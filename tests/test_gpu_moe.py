@@ -180,8 +180,17 @@ def test_non_positive_weight_sum_is_an_error():
         _session(cfg, tensors, 2).run(x)
 
 
+@pytest.fixture
+def decode_kernels_only():
+    """Every batch through the fp32 decode kernels (no bf16 prefill path)."""
+    old = LB.prefill_min_tokens()
+    LB.set_prefill_min_tokens(1 << 30)
+    yield
+    LB.set_prefill_min_tokens(old)
+
+
 @pytest.mark.parametrize("tokens", [1, 16, 512])  # decode and a prefill batch (config 3)
-def test_config3_full_layer(tokens):
+def test_config3_full_layer(tokens, decode_kernels_only):
     cfg = CF.CONFIG3
     tensors = host_layer(cfg, seed=0)
     x = O.synth_f32(0, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
@@ -194,7 +203,7 @@ def test_config3_full_layer(tokens):
 
 
 @pytest.mark.parametrize("tokens", [1, 64, 1024])  # decode and a prefill batch (config 4)
-def test_config4_full_layer(tokens):
+def test_config4_full_layer(tokens, decode_kernels_only):
     cfg = CF.CONFIG4
     tensors = host_layer(cfg, seed=0)
     x = O.synth_f32(0, CF.S_ACT, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
