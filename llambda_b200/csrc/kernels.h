@@ -185,6 +185,9 @@ int prefill_min_tokens();
 size_t prefill_work_bytes(const MoeDevice& m, int max_tokens, size_t* parts /* [5] */);
 long prefill_max_up_tiles(const MoeDevice& m, int max_tokens);
 bool prefill_applies(const MoeDevice& m, const MoeWork& w, int T);
+// rms-norm (into w.xn) and the fp32 router GEMM of a prefill batch.
+cudaError_t launch_prefill_router(const MoeDevice& m, const MoeWork& w, const float* x, int T,
+                                  cudaStream_t stream);
 // Gather, plan, gate/up and down passes; partial outputs land in w.partial
 // as in the decode path.  marks as in launch_moe.
 cudaError_t launch_prefill_passes(const MoeDevice& m, const MoeWork& w, const float* x, int T,

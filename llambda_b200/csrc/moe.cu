@@ -36,6 +36,11 @@ namespace {
 constexpr int kMaxExperts = 1024;
 // (token, rank) entries of one layer call (prefill batches included)
 constexpr int kMaxEntries = 64 * 1024;
+// The routing CTA splits the grouping of entries over its warps from
+// 8 * kRouteSplitChunks chunks of 32 entries on (prefill batches), with
+// per-warp expert counters in kRouteSplitSlots ints of shared memory.
+constexpr int kRouteSplitChunks = 4;
+constexpr int kRouteSplitSlots = 8192;
 constexpr int kSlabMaxStages = 10;
 // Rows of one 2-D tensor copy of the gate/up slabs (the slabs' rows per
 // matrix are multiples of it).
@@ -241,22 +246,36 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
   __shared__ int s_offset[kMaxExperts + 1];
   const int E = m.experts, k = m.top_k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) s_count[e] = 0;
-  __syncthreads();
+  const int nw = blockDim.x >> 5;
   // Stable grouping of entries (token-major, rank-minor) by owned expert.
+  // Small batches: warp 0 walks all entries.  Large batches: warp q walks
+  // the q-th contiguous range of 32-entry chunks with its own per-expert
+  // counters, and each entry's position is then offset by the entries the
+  // warps before it gave the same expert, which keeps the order stable.
   const int n = T * k;
-  if (warp == 0) {
+  const int nchunk = (n + 31) >> 5;
+  const bool split = nchunk >= 8 * kRouteSplitChunks && E * nw <= kRouteSplitSlots;
+  __shared__ int s_wcount[kRouteSplitSlots];  // [warp][expert] when split
+  const int walkers = split ? nw : 1;
+  int* my_count = split ? s_wcount + warp * E : s_count;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_count[e] = 0;
+  if (split)
+    for (int i = threadIdx.x; i < E * nw; i += blockDim.x) s_wcount[i] = 0;
+  __syncthreads();
+  const int c_lo = (int)((long)nchunk * warp / walkers), c_hi = (int)((long)nchunk * (warp + 1) / walkers);
+  if (warp < walkers) {
     const unsigned lt_mask = (1u << lane) - 1u;
     int ev[8];  // selections of the next 8 chunks, loaded ahead of the serial part
-    for (int c = 0; c < n; c += 32) {
-      const int u = (c >> 5) & 7;
+    for (int ci = c_lo; ci < c_hi; ++ci) {
+      const int c = ci << 5;
+      const int u = (ci - c_lo) & 7;
       if (u == 0)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int idj = c + 32 * j + lane;  // clamped, not guarded: the loads overlap
           const int* p = w.sel + min(idj, n - 1);
           const int v = CG ? __ldcg(p) : __ldg(p);
-          ev[j] = idj < n ? v : -1;
+          ev[j] = idj < n && ci + j < c_hi ? v : -1;
         }
       const int id = c + lane;
       int e = ev[0];
@@ -271,14 +290,33 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
         grp = __match_any_sync(act, e);
         rank = __popc(grp & lt_mask);
       }
-      int base = own ? s_count[e] : 0;
+      int base = own ? my_count[e] : 0;
       __syncwarp();
-      if (own && rank == 0) s_count[e] = base + __popc(grp);
+      if (own && rank == 0) my_count[e] = base + __popc(grp);
       __syncwarp();
       if (id < n) w.entries[id] = own ? (base + rank) : -1;  // position, fixed below
     }
   }
   __syncthreads();
+  if (split) {
+    // per expert: the total, and each warp's start among the expert's entries
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int run = 0;
+      for (int q = 0; q < nw; ++q) {
+        const int v = s_wcount[q * E + e];
+        s_wcount[q * E + e] = run;
+        run += v;
+      }
+      s_count[e] = run;
+    }
+    __syncthreads();
+    if (warp > 0)  // warp 0's positions already start at 0
+      for (int id = (c_lo << 5) + lane; id < min(n, c_hi << 5); id += 32) {
+        const int pos = w.entries[id];
+        if (pos >= 0) w.entries[id] = pos + s_wcount[warp * E + (CG ? __ldcg(w.sel + id) : w.sel[id])];
+      }
+    __syncthreads();
+  }
   // Exclusive scans over experts (entries, up passes, down passes) and the
   // active list in increasing expert id: warp wp takes experts
   // [wp*per_w, (wp+1)*per_w); pass 1 sums each warp's range, pass 2 scans it
@@ -1886,7 +1924,10 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
       reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(m.router) |
       reinterpret_cast<uintptr_t>(m.router_extra_row) | reinterpret_cast<uintptr_t>(m.input_norm);
   const int all_rows = m.router_rows + (m.router_extra_row ? 1 : 0);  // column E: shared gate
-  if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
+  const bool prefill = prefill_applies(m, w, T);
+  if (prefill) {
+    if ((e = launch_prefill_router(m, w, x, T, s)) != cudaSuccess) return e;
+  } else if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
       router_smem <= 192 * 1024 &&
       prepared_occupancy(moe_router_kernel, kRouterWarps * 32, router_smem) >= 1) {
     // top-k and routing ride on the router launch (its last CTAs)
@@ -1921,7 +1962,7 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   }
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
   if (!gate_ok) return cudaErrorInvalidValue;
-  if (prefill_applies(m, w, T))
+  if (prefill)
     e = launch_prefill_passes(m, w, x, T, s, marks);
   else if (m.up_type == LB_TYPE_Q4_K && m.down_type == LB_TYPE_Q6_K)
     e = launch_expert_passes<LB_TYPE_Q4_K, LB_TYPE_Q6_K>(m, w, T, maps, s, marks);

@@ -211,58 +211,78 @@ __device__ __forceinline__ void lds_run(const uint8_t* p, uint32_t* out) {
   for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(v[i], v[i + 1], s);
 }
 
-// Four weights of one word of 4-bit or 6-bit values (bytes below 128) to
-// bf16 pairs: w = ds * (2^23 + 2^16 q) - off, the PRMT magic float of each
-// byte (see magic_q).
-__device__ __forceinline__ void decode_word(uint32_t v, float ds, float off, uint32_t& p0,
-                                            uint32_t& p1) {
-  const float f0 = fmaf(ds, magic_q<0>(v), -off), f1 = fmaf(ds, magic_q<1>(v), -off);
-  const float f2 = fmaf(ds, magic_q<2>(v), -off), f3 = fmaf(ds, magic_q<3>(v), -off);
-  p0 = bf16x2(f0, f1);
-  p1 = bf16x2(f2, f3);
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) {
+  __nv_bfloat162 r;
+  memcpy(&r, &u, 4);
+  return r;
+}
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 v) {
+  uint32_t r;
+  memcpy(&r, &v, 4);
+  return r;
+}
+
+// Four 6- or 4-bit values q (bytes of v, each below 128) to two bf16 pairs
+// (q0, q1), (q2, q3) minus `bias`, exactly: one PRMT puts a byte under the
+// exponent byte 0x43, the bf16 number 128 + q, and a bf16 subtract of bias
+// (128, or 160 = 128 + 32 for Q6_K's offset) leaves the small integer, which
+// bf16 holds exactly.
+__device__ __forceinline__ void q_pairs(uint32_t v, __nv_bfloat162 bias, __nv_bfloat162& a,
+                                        __nv_bfloat162& b) {
+  a = __hsub2(as_bf2(__byte_perm(v, 0x43434343u, 0x4140u)), bias);
+  b = __hsub2(as_bf2(__byte_perm(v, 0x43434343u, 0x4342u)), bias);
 }
 
 // 32 weights (K [64c + 32h, +32) of the super-block at b) as bf16 into row r
-// of a decoded chunk.
+// of a decoded chunk.  Q4_K: w = (d*sc)*q - dmin*m with d*sc and dmin*m
+// rounded to bf16 and one bf16 FMA per pair; Q6_K: w = (d*sc)*(q - 32) with
+// d*sc rounded to bf16 and one bf16 multiply per pair.
 template <int WT>
 __device__ __forceinline__ void decode_chunk(const uint8_t* b, int c, int h, int r, uint8_t* a) {
   uint32_t o[16];
   if (WT == LB_TYPE_Q4_K) {
     // sub-block j = 2c + h: qs bytes [32c, 32c + 32), low nibbles (h = 0) or
-    // high nibbles (h = 1); w = (d*sc)*q - dmin*m
+    // high nibbles (h = 1)
     const uint4 hdr = *reinterpret_cast<const uint4*>(b);
     const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
     int sc, mn;
     q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + h, sc, mn);
-    const float d1 = d * (float)sc, m1 = dmin * (float)mn;
-    const float ds = d1 * kMagicUnscale, off = fmaf(d1, kMagicBias, m1);
+    const __nv_bfloat162 d1 = __float2bfloat162_rn(d * (float)sc);
+    const __nv_bfloat162 nm1 = __float2bfloat162_rn(-(dmin * (float)mn));
+    const __nv_bfloat162 k128 = as_bf2(0x43004300u);
     const uint4 q0 = *reinterpret_cast<const uint4*>(b + 16 + 32 * c);
     const uint4 q1 = *reinterpret_cast<const uint4*>(b + 32 + 32 * c);
     const uint32_t wd[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const int sh = 4 * h;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      decode_word((wd[i] >> sh) & 0x0F0F0F0Fu, ds, off, o[2 * i], o[2 * i + 1]);
+    for (int i = 0; i < 8; ++i) {
+      __nv_bfloat162 x0, x1;
+      q_pairs((wd[i] >> sh) & 0x0F0F0F0Fu, k128, x0, x1);
+      o[2 * i] = as_u32(__hfma2(x0, d1, nm1));
+      o[2 * i + 1] = as_u32(__hfma2(x1, d1, nm1));
+    }
   } else {
     // 128-half n = c / 2, quarter qd = 2 (c % 2) + h: ql bytes
     // [64n + 32 (qd % 2), +32) (low nibbles for qd < 2, high otherwise),
-    // qh bytes [128 + 32n, +32) bits 2qd..2qd+1, scales 8n + 2qd + l/16;
-    // w = d * sc * (q - 32)
+    // qh bytes [128 + 32n, +32) bits 2qd..2qd+1, scales 8n + 2qd + l/16
     const int n = c >> 1, qd = (c & 1) * 2 + h;
     uint32_t ql[8], qh[8];
     lds_run<8>(b + 64 * n + 32 * (qd & 1), ql);
     lds_run<8>(b + 128 + 32 * n, qh);
     const uint32_t scw = lds_u16(b + 192 + 8 * n + 2 * qd);
     const float d = half_bits_to_float(lds_u16(b + 208));
-    const float d0 = d * (float)(int)(int8_t)(scw & 0xFFu);
-    const float d1 = d * (float)(int)(int8_t)(scw >> 8);
-    const float ds0 = d0 * kMagicUnscale, off0 = d0 * (kMagicBias + 32.0f);
-    const float ds1 = d1 * kMagicUnscale, off1 = d1 * (kMagicBias + 32.0f);
+    const __nv_bfloat162 s0 = __float2bfloat162_rn(d * (float)(int)(int8_t)(scw & 0xFFu));
+    const __nv_bfloat162 s1 = __float2bfloat162_rn(d * (float)(int)(int8_t)(scw >> 8));
+    const __nv_bfloat162 k160 = as_bf2(0x43204320u);
     const int shl = 4 * (qd >> 1), shh = 2 * qd;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t v = ((ql[i] >> shl) & 0x0F0F0F0Fu) | (((qh[i] >> shh) & 0x03030303u) << 4);
-      decode_word(v, i < 4 ? ds0 : ds1, i < 4 ? off0 : off1, o[2 * i], o[2 * i + 1]);
+      // q = ql nibble | qh 2 bits << 4 (below 64): no carry crosses a byte
+      const uint32_t v = ((ql[i] >> shl) & 0x0F0F0F0Fu) + ((qh[i] >> shh) & 0x03030303u) * 16u;
+      __nv_bfloat162 x0, x1;
+      q_pairs(v, k160, x0, x1);
+      o[2 * i] = as_u32(__hmul2(x0, i < 4 ? s0 : s1));
+      o[2 * i + 1] = as_u32(__hmul2(x1, i < 4 ? s0 : s1));
     }
   }
 #pragma unroll
@@ -479,7 +499,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               float hv = 0.f;
               if (row < rows) {
                 if (PAIR) {
-                  hv = __fmul_rn(y0[j] / (1.0f + __expf(-y0[j])), y1[j]);
+                  hv = __fmul_rn(__fdividef(y0[j], 1.0f + __expf(-y0[j])), y1[j]);
                 } else {
                   const float u = y0[j] > 0.f ? y0[j] : 0.f;
                   hv = __fmul_rn(u, u);
@@ -506,16 +526,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
 // ------------------------------------------------------------ gather + plan
 
-// One CTA per token: the token's bf16 row (rms-normed when the layer has
-// input_norm: rms-norm-into, llambda.lisp L859-879) copied to each grouped
-// row it is routed to on this device, zero-padded from H to k_in.
+// One CTA per token: the token's bf16 row (the rms-normed row when the layer
+// has input_norm) copied to each grouped row it is routed to on this device,
+// zero-padded from H to k_in.
 __global__ void __launch_bounds__(256) pf_gather_kernel(MoeDevice m, MoeWork w,
                                                         const float* __restrict__ x, int T) {
   __shared__ int s_dst[33], s_prow[33], s_n;
-  __shared__ float s_red[8];
   const int t = blockIdx.x, H = m.hidden, K = m.k_in, k = m.top_k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* xt = x + (long)t * H;
+  const float* xt = (m.input_norm ? w.xn : x) + (long)t * H;  // rms-normed by pf_norm_kernel
   if (warp == 0) {
     int dst = -1;
     if (lane < k) {
@@ -541,21 +560,7 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(MoeDevice m, MoeWork w,
       s_n = n;
     }
   }
-  float scale = 1.f;
-  if (m.input_norm) {
-    float acc = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) acc = fmaf(xt[i], xt[i], acc);
-    acc = warp_sum(acc);
-    if (lane == 0) s_red[warp] = acc;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float s = 0.f;
-      for (int i = 0; i < 8; ++i) s += s_red[i];
-      s_red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), m.norm_epsilon)));
-    }
-  }
   __syncthreads();
-  if (m.input_norm) scale = s_red[0];
   const int nd = s_n;
   uint16_t* xs = w.pf_xs;
   for (int c0 = threadIdx.x * 8; c0 < K; c0 += blockDim.x * 8) {
@@ -563,9 +568,7 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(MoeDevice m, MoeWork w,
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int i = c0 + j;
-      float xv = i < H ? xt[i] : 0.f;
-      if (m.input_norm && i < H) xv = __fmul_rn(__fmul_rn(xv, m.input_norm[i]), scale);
-      v[j] = xv;
+      v[j] = i < H ? xt[i] : 0.f;
     }
     const uint4 pk = make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]),
                                 bf16x2(v[6], v[7]));
@@ -644,6 +647,93 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(MoeDevice m, MoeWork w, i
   if (a == 0) {
     w.pf_count[0] = routed * mbu + nsh * mbu_sh;
     w.pf_count[1] = (routed + nsh) * mbd;
+  }
+}
+
+// ------------------------------------------------------------ router
+
+// rms-norm-into (llambda.lisp L859-879) of every token into w.xn: scale =
+// 1/sqrt(mean(x^2) + eps), xn = (x * weight) * scale.  One warp per token.
+__global__ void __launch_bounds__(256) pf_norm_kernel(MoeDevice m, MoeWork w,
+                                                      const float* __restrict__ x, int T) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int H = m.hidden;
+  const float* xt = x + (long)t * H;
+  float acc = 0.f;
+  for (int i = lane; i < H; i += 32) acc = fmaf(xt[i], xt[i], acc);
+  acc = warp_sum(acc);
+  const float scale =
+      __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)H), m.norm_epsilon)));
+  float* o = w.xn + (long)t * H;
+  for (int i = lane; i < H; i += 32) o[i] = __fmul_rn(__fmul_rn(xt[i], m.input_norm[i]), scale);
+}
+
+constexpr int kRtTok = 64, kRtRows = 64, kRtK = 32;
+
+// Router logits of a prefill batch (dot-product-with-f32-tensor-data,
+// L4096-4107, for every router row; row E of the logits is the qwen3next
+// shared-expert gate, L3491-3500): an fp32 register-blocked GEMM, 64 tokens x
+// 64 rows per CTA, K in chunks of 32 staged through shared memory (the next
+// chunk's loads in flight during the current one's FMAs), 4 x 4 outputs per
+// thread on packed fp32x2 FMA.  fp32 throughout, so the expert selection is
+// that of the decode path's router.
+__global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
+                                                        const float* __restrict__ xr, int T,
+                                                        int all_rows) {
+  __shared__ __align__(16) float xs[kRtK][kRtTok + 4];
+  __shared__ __align__(16) float ws[kRtK][kRtRows + 4];
+  const int t0 = blockIdx.y * kRtTok, r0 = blockIdx.x * kRtRows, H = m.hidden;
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int lr = tid >> 2, lk = (tid & 3) * 8;  // this thread's staged row and 8 k values
+  const float* xrow = xr + (long)min(t0 + lr, T - 1) * H;
+  const int rr = min(r0 + lr, all_rows - 1);
+  const float* wrow = rr < m.router_rows ? m.router + (long)rr * H : m.router_extra_row;
+  float2 acc[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+  float xv[8], wv[8];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int kk = k0 + lk + j;
+      xv[j] = kk < H ? __ldg(xrow + kk) : 0.f;
+      wv[j] = kk < H ? __ldg(wrow + kk) : 0.f;
+    }
+  };
+  fetch(0);
+  for (int k0 = 0; k0 < H; k0 += kRtK) {
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      xs[lk + j][lr] = xv[j];
+      ws[lk + j][lr] = wv[j];
+    }
+    __syncthreads();
+    if (k0 + kRtK < H) fetch(k0 + kRtK);
+#pragma unroll
+    for (int k = 0; k < kRtK; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[i][0] = __ffma2_rn(make_float2(av[i], av[i]), make_float2(b.x, b.y), acc[i][0]);
+        acc[i][1] = __ffma2_rn(make_float2(av[i], av[i]), make_float2(b.z, b.w), acc[i][1]);
+      }
+    }
+  }
+  const int E1 = m.experts + 1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty * 4 + i;
+    if (t >= T) continue;
+    const float v[4] = {acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = r0 + tx * 4 + j;
+      if (r < all_rows) w.logits[(long)t * E1 + r] = v[j];
+    }
   }
 }
 
@@ -772,6 +862,19 @@ long prefill_max_up_tiles(const MoeDevice& m, int T) {
   long max_up, max_dn;
   pf_tile_bounds(m, T, &max_up, &max_dn);
   return max_up;
+}
+
+cudaError_t launch_prefill_router(const MoeDevice& m, const MoeWork& w, const float* x, int T,
+                                  cudaStream_t s) {
+  cudaError_t e;
+  if (m.input_norm) {
+    pf_norm_kernel<<<(T + 7) / 8, 256, 0, s>>>(m, w, x, T);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  const int all_rows = m.router_rows + (m.router_extra_row ? 1 : 0);
+  dim3 grid((all_rows + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
+  pf_router_kernel<<<grid, 256, 0, s>>>(m, w, m.input_norm ? w.xn : x, T, all_rows);
+  return cudaGetLastError();
 }
 
 bool prefill_applies(const MoeDevice& m, const MoeWork& w, int T) {
