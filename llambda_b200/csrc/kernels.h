@@ -154,6 +154,7 @@ struct MoeWork {
   int* pf_prow;       // [T*k + T] partial-output row of each grouped row
   int4* pf_tiles;     // gate/up tiles [pf_max_up], then down tiles
   int* pf_count;      // [2] tiles of the gate/up and the down pass
+  float* pf_rlog;     // [slices][T][E+1] router logits per K slice
   long pf_max_up;
   size_t bytes;
 };
@@ -182,7 +183,7 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
 // prefill_min_tokens() tokens as tcgen05 bf16 grouped GEMMs.
 void set_prefill_min_tokens(int n);
 int prefill_min_tokens();
-size_t prefill_work_bytes(const MoeDevice& m, int max_tokens, size_t* parts /* [5] */);
+size_t prefill_work_bytes(const MoeDevice& m, int max_tokens, size_t* parts /* [6] */);
 long prefill_max_up_tiles(const MoeDevice& m, int max_tokens);
 bool prefill_applies(const MoeDevice& m, const MoeWork& w, int T);
 // rms-norm (into w.xn) and the fp32 router GEMM of a prefill batch.

@@ -212,7 +212,7 @@ __device__ __forceinline__ void topk_token(const MoeDevice& m, const MoeWork& w,
 // Declared here, defined with the routing below.
 template <bool CG>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
-                                            int pass_nt);
+                                            int pass_nt, bool grouped_ids);
 
 // Top-k (warp 0 of each CTA, one token per CTA) with the routing on the last
 // CTA to finish (an arrival counter; its eight warps group the entries), so
@@ -220,7 +220,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
 // launches: the last CTA resets it.
 template <int PER>
 __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w, int T,
-                                                         int pass_nt) {
+                                                         int pass_nt, int grouped_ids) {
   __shared__ int s_last;
   griddep_wait();
   griddep_launch();
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
   __syncthreads();
   if (!s_last) return;
   __threadfence();  // every CTA's selections are visible from here
-  route_block<true>(m, w, T, pass_nt);
+  route_block<true>(m, w, T, pass_nt, grouped_ids != 0);
   if (threadIdx.x == 0) *w.tickets = 0;
 }
 
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
 // (read through L2).
 template <bool CG>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
-                                            int pass_nt) {
+                                            int pass_nt, bool grouped_ids) {
   __shared__ int s_count[kMaxExperts];
   __shared__ int s_offset[kMaxExperts + 1];
   const int E = m.experts, k = m.top_k;
@@ -389,10 +389,23 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
   if (threadIdx.x == 0) w.offsets[E] = s_offset[E];
   __syncthreads();
   // Scatter entry ids into their expert-grouped slots (second half of entries;
-  // the first half holds each entry's position within its expert).
-  for (int id = threadIdx.x; id < n; id += blockDim.x) {
-    const int pos = w.entries[id];
-    if (pos >= 0) w.entries[T * k + s_offset[CG ? __ldcg(w.sel + id) : w.sel[id]] + pos] = id;
+  // the first half holds each entry's position within its expert).  The
+  // prefill path reads positions only and skips it.  Four entries' loads
+  // per thread are in flight at once.
+  if (!grouped_ids) return;
+  for (int id0 = threadIdx.x; id0 < n; id0 += 4 * blockDim.x) {
+    int pos[4], e[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int id = min(id0 + u * (int)blockDim.x, n - 1);
+      pos[u] = w.entries[id];
+      e[u] = CG ? __ldcg(w.sel + id) : w.sel[id];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int id = id0 + u * (int)blockDim.x;
+      if (id < n && pos[u] >= 0) w.entries[T * k + s_offset[e[u]] + pos[u]] = id;
+    }
   }
 }
 
@@ -1894,18 +1907,20 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
   w->xp_down = reinterpret_cast<float*>(
       take((size_t)(T * k + T) * down_ld_floats(m) * 4));
   w->partial = reinterpret_cast<float*>(take((size_t)T * (k + 1) * m.hidden * 4));
-  size_t pf[5];
+  size_t pf[6];
   if (prefill_work_bytes(m, T, pf)) {
     w->pf_xs = reinterpret_cast<uint16_t*>(take(pf[0]));
     w->pf_hs = reinterpret_cast<uint16_t*>(take(pf[1]));
     w->pf_prow = reinterpret_cast<int*>(take(pf[2]));
     w->pf_tiles = reinterpret_cast<int4*>(take(pf[3]));
     w->pf_count = reinterpret_cast<int*>(take(pf[4]));
+    w->pf_rlog = reinterpret_cast<float*>(take(pf[5]));
     w->pf_max_up = prefill_max_up_tiles(m, T);
   } else {
     w->pf_xs = w->pf_hs = nullptr;
     w->pf_prow = w->pf_count = nullptr;
     w->pf_tiles = nullptr;
+    w->pf_rlog = nullptr;
     w->pf_max_up = 0;
   }
   w->bytes = off;
@@ -1956,7 +1971,7 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
               : per <= 4 ? topk_route_kernel<4> : per <= 8 ? topk_route_kernel<8>
               : per <= 16 ? topk_route_kernel<16> : topk_route_kernel<32>;
-    e = launch_pdl(kern, dim3(T), dim3(256), 0, s, m, w, T, pnt);
+    e = launch_pdl(kern, dim3(T), dim3(256), 0, s, m, w, T, pnt, prefill ? 0 : 1);
     if (e != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }

@@ -66,6 +66,7 @@ constexpr uint32_t kPfChunkBytes = kPfM * 128;   // 128 rows x 64 bf16
 constexpr uint32_t kPfBoxBytes = kPfN * 128;     // 64 tokens x 64 bf16
 constexpr uint32_t kPfBStage = 4 * kPfBoxBytes;  // one super-block of K
 constexpr int kPfCarveMin = 64;                  // smallest max_tokens given prefill buffers
+constexpr int kPfRouterSlices = 8;               // most K slices of the router GEMM
 
 __host__ __device__ constexpr int pf_block_bytes(int wt) { return wt == LB_TYPE_Q4_K ? LB_Q4K : LB_Q6K; }
 // Bytes of one staged row (the inner box of the weights' tensor map): a Q4_K
@@ -653,20 +654,39 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(MoeDevice m, MoeWork w, i
 // ------------------------------------------------------------ router
 
 // rms-norm-into (llambda.lisp L859-879) of every token into w.xn: scale =
-// 1/sqrt(mean(x^2) + eps), xn = (x * weight) * scale.  One warp per token.
+// 1/sqrt(mean(x^2) + eps), xn = (x * weight) * scale.  One CTA per token,
+// the row held in registers between the sum and the scaling.
 __global__ void __launch_bounds__(256) pf_norm_kernel(MoeDevice m, MoeWork w,
                                                       const float* __restrict__ x, int T) {
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (t >= T) return;
-  const int H = m.hidden;
+  constexpr int kPer = 16;  // values per thread held in registers (H <= 4096)
+  __shared__ float s_red[8];
+  const int t = blockIdx.x, H = m.hidden, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* xt = x + (long)t * H;
+  float v[kPer];
   float acc = 0.f;
-  for (int i = lane; i < H; i += 32) acc = fmaf(xt[i], xt[i], acc);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * 256;
+    v[j] = i < H ? xt[i] : 0.f;
+    acc = fmaf(v[j], v[j], acc);
+  }
+  for (int i = threadIdx.x + kPer * 256; i < H; i += 256) acc = fmaf(xt[i], xt[i], acc);
   acc = warp_sum(acc);
+  if (lane == 0) s_red[warp] = acc;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) tot += s_red[q];
   const float scale =
-      __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)H), m.norm_epsilon)));
+      __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), m.norm_epsilon)));
   float* o = w.xn + (long)t * H;
-  for (int i = lane; i < H; i += 32) o[i] = __fmul_rn(__fmul_rn(xt[i], m.input_norm[i]), scale);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < H) o[i] = __fmul_rn(__fmul_rn(v[j], m.input_norm[i]), scale);
+  }
+  for (int i = threadIdx.x + kPer * 256; i < H; i += 256)
+    o[i] = __fmul_rn(__fmul_rn(xt[i], m.input_norm[i]), scale);
 }
 
 constexpr int kRtTok = 64, kRtRows = 64, kRtK = 32;
@@ -680,15 +700,18 @@ constexpr int kRtTok = 64, kRtRows = 64, kRtK = 32;
 // that of the decode path's router.
 __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
                                                         const float* __restrict__ xr, int T,
-                                                        int all_rows) {
+                                                        int all_rows, int kc) {
   __shared__ __align__(16) float xs[kRtK][kRtTok + 4];
   __shared__ __align__(16) float ws[kRtK][kRtRows + 4];
-  const int t0 = blockIdx.y * kRtTok, r0 = blockIdx.x * kRtRows, H = m.hidden;
+  const int t0 = blockIdx.y * kRtTok, r0 = blockIdx.x * kRtRows;
+  // K slice blockIdx.z of kc values (gridDim.z slices; one: the whole row)
+  const int kb = blockIdx.z * kc, H = min(m.hidden - kb, kc);
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const int lr = tid >> 2, lk = (tid & 3) * 8;  // this thread's staged row and 8 k values
-  const float* xrow = xr + (long)min(t0 + lr, T - 1) * H;
+  const float* xrow = xr + (long)min(t0 + lr, T - 1) * m.hidden + kb;
   const int rr = min(r0 + lr, all_rows - 1);
-  const float* wrow = rr < m.router_rows ? m.router + (long)rr * H : m.router_extra_row;
+  const float* wrow =
+      (rr < m.router_rows ? m.router + (long)rr * m.hidden : m.router_extra_row) + kb;
   float2 acc[4][2];
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
@@ -724,6 +747,7 @@ __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
     }
   }
   const int E1 = m.experts + 1;
+  float* dst = gridDim.z == 1 ? w.logits : w.pf_rlog + (long)blockIdx.z * T * E1;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int t = t0 + ty * 4 + i;
@@ -732,8 +756,21 @@ __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int r = r0 + tx * 4 + j;
-      if (r < all_rows) w.logits[(long)t * E1 + r] = v[j];
+      if (r < all_rows) dst[(long)t * E1 + r] = v[j];
     }
+  }
+}
+
+// logits = the K slices' partial logits summed in slice order.
+__global__ void __launch_bounds__(256) pf_router_sum_kernel(MoeDevice m, MoeWork w, int T,
+                                                            int all_rows, int slices) {
+  const int E1 = m.experts + 1;
+  const long n = (long)T * E1;
+  for (long i = blockIdx.x * 256L + threadIdx.x; i < n; i += (long)gridDim.x * 256) {
+    if ((int)(i % E1) >= all_rows) continue;
+    float v = w.pf_rlog[i];
+    for (int z = 1; z < slices; ++z) v = __fadd_rn(v, w.pf_rlog[(long)z * n + i]);
+    w.logits[i] = v;
   }
 }
 
@@ -842,7 +879,7 @@ int prefill_min_tokens() { return g_prefill_min.load(); }
 
 size_t prefill_work_bytes(const MoeDevice& m, int T, size_t* parts) {
   if (T < kPfCarveMin) {
-    for (int i = 0; i < 5; ++i) parts[i] = 0;
+    for (int i = 0; i < 6; ++i) parts[i] = 0;
     return 0;
   }
   const long rows = (long)T * m.top_k + T;
@@ -853,8 +890,9 @@ size_t prefill_work_bytes(const MoeDevice& m, int T, size_t* parts) {
   parts[2] = (size_t)rows * 4;                   // prow
   parts[3] = (size_t)(max_up + max_dn) * 16;     // tiles
   parts[4] = 16;                                 // counts
+  parts[5] = (size_t)kPfRouterSlices * T * (m.experts + 1) * 4;  // router K-slice logits
   size_t total = 0;
-  for (int i = 0; i < 5; ++i) total += (parts[i] + 255) & ~size_t(255);
+  for (int i = 0; i < 6; ++i) total += (parts[i] + 255) & ~size_t(255);
   return total;
 }
 
@@ -868,12 +906,24 @@ cudaError_t launch_prefill_router(const MoeDevice& m, const MoeWork& w, const fl
                                   cudaStream_t s) {
   cudaError_t e;
   if (m.input_norm) {
-    pf_norm_kernel<<<(T + 7) / 8, 256, 0, s>>>(m, w, x, T);
+    pf_norm_kernel<<<T, 256, 0, s>>>(m, w, x, T);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const int all_rows = m.router_rows + (m.router_extra_row ? 1 : 0);
-  dim3 grid((all_rows + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
-  pf_router_kernel<<<grid, 256, 0, s>>>(m, w, m.input_norm ? w.xn : x, T, all_rows);
+  const int tiles = ((all_rows + kRtRows - 1) / kRtRows) * ((T + kRtTok - 1) / kRtTok);
+  // K slices so that about four CTAs run per SM, each slice a multiple of 32
+  int slices = std::min(kPfRouterSlices, std::max(1, (4 * sm_count() + tiles - 1) / tiles));
+  int kc = (m.hidden + slices - 1) / slices;
+  kc = (kc + kRtK - 1) / kRtK * kRtK;
+  slices = (m.hidden + kc - 1) / kc;
+  dim3 grid((all_rows + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok, slices);
+  pf_router_kernel<<<grid, 256, 0, s>>>(m, w, m.input_norm ? w.xn : x, T, all_rows, kc);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (slices > 1) {
+    const long n = (long)T * (m.experts + 1);
+    pf_router_sum_kernel<<<(int)std::min<long>((n + 255) / 256, 4L * sm_count()), 256, 0, s>>>(
+        m, w, T, all_rows, slices);
+  }
   return cudaGetLastError();
 }
 
