@@ -25,21 +25,28 @@
 // L4203-4310), each rounded once to bf16; tokens are rounded to bf16; all
 // sums are fp32 in the tensor cores.
 //
-// One CTA per SM (persistent; tiles i, i + grid, ...), 10 warps:
-//   warps 0-7  decode: thread (row r = tid % 128, half h = tid / 128) turns
-//              32 weights of its row into bf16 per 64-wide K chunk, written
-//              in the 128-byte-swizzled K-major layout the MMA reads; then
-//              the epilogue (tensor-memory lanes of warp w are rows
-//              32*(w%4)..+31; warps 0-3 take tokens 0-31, warps 4-7 32-63)
-//   warp 8     producer: per super-block, one bulk copy per weight row
-//              (rounded out to 16-byte bounds) and four TMA tensor loads of
-//              the tokens' bf16 rows (64 x 64, 128-byte swizzle)
-//   warp 9     MMA: one thread issues tcgen05.mma (M=128, N = tokens rounded
-//              up to 16, K=16, bf16 x bf16 -> fp32) and tcgen05.commit
+// One CTA per SM (persistent; tiles i, i + grid, ...), 22 warps:
+//   warps 0-15 decode: thread (row r = tid % 128, part = tid / 128) turns
+//              16 weights of its row into bf16 per 64-wide K chunk and stores
+//              them (tcgen05.st) into its tensor-memory lane, where the MMA
+//              reads its A operand (row = lane, two bf16 per column)
+//   warps 18-21 epilogue: warp w reads tensor-memory lanes 32*(w%4)..+31
+//              (weight rows) for all of the tile's tokens
+//   warp 16    producer: per super-block, g tensor copies per weight matrix
+//              (boxes of 128/g map rows of g weight rows each, from a 16-byte
+//              boundary) and four of the tokens' bf16 rows (64 x 64,
+//              128-byte swizzle)
+//   warp 17    MMA: one thread issues tcgen05.mma (M=128, N = tokens rounded
+//              up to 16, K=16, bf16 x bf16 -> fp32; A from tensor memory, B
+//              from shared memory) and tcgen05.commit
+// Tensor memory (512 columns): two accumulator buffers (64 fp32 columns per
+// matrix), then a ring of 8 decoded 128 x 64 chunks (32 columns each).
 // Pipelines (mbarriers, every wait bounded in time):
-//   full/empty[2]     weight + token stages (producer -> decoders, MMA)
-//   afull/aempty[4]   decoded 128 x 64 chunks (decoders -> MMA)
-//   tfull/tempty      the tile's accumulators (MMA -> epilogue -> MMA)
+//   full/empty[3]     weight + token stages (producer -> decoders, MMA)
+//   afull/aempty[8]   decoded chunks (decoders -> MMA)
+//   tfull/tempty[2]   two accumulator buffers in tensor memory (MMA ->
+//                     epilogue -> MMA), so the next tile's products start
+//                     while the epilogue drains the last
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -58,11 +65,13 @@ namespace {
 
 constexpr int kPfM = 128;       // weight rows per tile (the MMA's M)
 constexpr int kPfN = 64;        // tokens per tile
-constexpr int kPfRing = 4;      // decoded chunks in flight
-constexpr int kPfStages = 2;    // weight + token stages
-constexpr int kPfDecWarps = 8;
-constexpr int kPfThreads = (kPfDecWarps + 2) * 32;
-constexpr uint32_t kPfChunkBytes = kPfM * 128;   // 128 rows x 64 bf16
+constexpr int kPfRing = 8;      // decoded chunks in flight (tensor memory)
+constexpr int kPfStages = 3;    // weight + token stages (shared memory)
+constexpr int kPfDecWarps = 16;
+constexpr int kPfEpiWarps = 4;
+constexpr int kPfThreads = (kPfDecWarps + 2 + kPfEpiWarps) * 32;
+constexpr uint32_t kPfChunkCols = 32;            // 128 lanes x 64 bf16 (two per column)
+constexpr uint32_t kPfTmemCols = 512;            // accumulators, then the decoded chunks
 constexpr uint32_t kPfBoxBytes = kPfN * 128;     // 64 tokens x 64 bf16
 constexpr uint32_t kPfBStage = 4 * kPfBoxBytes;  // one super-block of K
 constexpr int kPfCarveMin = 64;                  // smallest max_tokens given prefill buffers
@@ -80,15 +89,14 @@ __host__ __device__ constexpr uint32_t pf_wstage(int wt, int nmat) {
 struct PfSync {
   uint64_t full[kPfStages], empty[kPfStages];
   uint64_t afull[kPfRing], aempty[kPfRing];
-  uint64_t tfull, tempty, done;
+  uint64_t tfull[2], tempty[2], done;
   uint32_t tmem;
   int abort;
 };
 
 __host__ __device__ constexpr size_t pf_smem_bytes(int wt, int nmat) {
-  return 1024 /* alignment slack */ + (size_t)kPfRing * kPfChunkBytes +
-         (size_t)kPfStages * kPfBStage + (size_t)kPfStages * pf_wstage(wt, nmat) +
-         sizeof(PfSync);
+  return 1024 /* alignment slack */ + (size_t)kPfStages * kPfBStage +
+         (size_t)kPfStages * pf_wstage(wt, nmat) + sizeof(PfSync);
 }
 
 // Tensor maps of one pass: the tokens' bf16 rows (64 x 64 boxes, 128-byte
@@ -116,6 +124,34 @@ struct PfPass {
   int* status;
 };
 
+// Bounded wait for the MMA thread: polls without suspending (one thread, so
+// the polling costs one warp's issue slots), so a completed phase is seen at
+// once; the clock is read every 64 polls.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n "
+      "selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_spin_or_abort(uint64_t* bar, uint32_t parity, int* status,
+                                                   volatile int* abort) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_test(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_ns() - t0 >= kWaitLimitNs) break;
+  }
+  if (status) atomicOr(status, 2);
+  *abort = 1;
+  return false;
+}
+
 // ------------------------------------------------------------ tcgen05 PTX
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -135,14 +171,26 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
                : "memory");
 }
-// D[tmem] (+)= A[smem] . B[smem]^T, both K-major, kind::f16 (bf16 operands).
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                       uint32_t acc) {
+// D[tmem] (+)= A[tmem] . B[smem]^T: A's rows in tensor-memory lanes 0-127,
+// K along the columns (two bf16 per 32-bit column), K-major B.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
+}
+// 8 consecutive 32-bit columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+// Waits until this thread's tensor-memory stores are complete.
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 // Arrives on bar once every tcgen05.mma this thread issued before has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -192,11 +240,6 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// Offset of 16-byte chunk `chunk` (0..7) of row r in a 128-byte-swizzled tile.
-__device__ __forceinline__ uint32_t sw128_off(int r, int chunk) {
-  return (uint32_t)r * 128u + ((uint32_t)(chunk ^ (r & 7)) << 4);
-}
-
 // N little-endian words from a 2-byte-aligned shared-memory address: N + 1
 // aligned loads and a funnel shift each (the word after the run is read; the
 // callers' runs end at least 4 bytes before the end of the staged row).
@@ -234,68 +277,79 @@ __device__ __forceinline__ void q_pairs(uint32_t v, __nv_bfloat162 bias, __nv_bf
   b = __hsub2(as_bf2(__byte_perm(v, 0x43434343u, 0x4342u)), bias);
 }
 
-// 32 weights (K [64c + 32h, +32) of the super-block at b) as bf16 into row r
-// of a decoded chunk.  Q4_K: w = (d*sc)*q - dmin*m with d*sc and dmin*m
-// rounded to bf16 and one bf16 FMA per pair; Q6_K: w = (d*sc)*(q - 32) with
-// d*sc rounded to bf16 and one bf16 multiply per pair.
+// The scale factors of one thread's four chunks of a super-block (row part
+// `part`: sub-blocks 2c + part/2 for Q4_K; scales 4c + part for Q6_K),
+// computed once per super-block.  Q4_K: a = d*sc, b = -(dmin*m)
+// (get-scale-min-k4-at, L4316-4336); Q6_K: a = d*sc.  Rounded to bf16.
+struct SbScales {
+  __nv_bfloat162 a[4], b[4];
+};
+
 template <int WT>
-__device__ __forceinline__ void decode_chunk(const uint8_t* b, int c, int h, int r, uint8_t* a) {
-  uint32_t o[16];
+__device__ __forceinline__ void sb_scales(const uint8_t* blk, int part, SbScales& s) {
+  const int h = part >> 1;
   if (WT == LB_TYPE_Q4_K) {
-    // sub-block j = 2c + h: qs bytes [32c, 32c + 32), low nibbles (h = 0) or
-    // high nibbles (h = 1)
-    const uint4 hdr = *reinterpret_cast<const uint4*>(b);
+    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
     const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-    int sc, mn;
-    q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + h, sc, mn);
-    const __nv_bfloat162 d1 = __float2bfloat162_rn(d * (float)sc);
-    const __nv_bfloat162 nm1 = __float2bfloat162_rn(-(dmin * (float)mn));
-    const __nv_bfloat162 k128 = as_bf2(0x43004300u);
-    const uint4 q0 = *reinterpret_cast<const uint4*>(b + 16 + 32 * c);
-    const uint4 q1 = *reinterpret_cast<const uint4*>(b + 32 + 32 * c);
-    const uint32_t wd[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    const int sh = 4 * h;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      __nv_bfloat162 x0, x1;
-      q_pairs((wd[i] >> sh) & 0x0F0F0F0Fu, k128, x0, x1);
-      o[2 * i] = as_u32(__hfma2(x0, d1, nm1));
-      o[2 * i + 1] = as_u32(__hfma2(x1, d1, nm1));
+    for (int c = 0; c < 4; ++c) {
+      int sc, mn;
+      q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + h, sc, mn);
+      s.a[c] = __float2bfloat162_rn(d * (float)sc);
+      s.b[c] = __float2bfloat162_rn(-(dmin * (float)mn));
     }
   } else {
-    // 128-half n = c / 2, quarter qd = 2 (c % 2) + h: ql bytes
-    // [64n + 32 (qd % 2), +32) (low nibbles for qd < 2, high otherwise),
-    // qh bytes [128 + 32n, +32) bits 2qd..2qd+1, scales 8n + 2qd + l/16
+    const float d = half_bits_to_float(lds_u16(blk + 208));
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t w2 = lds_u16(blk + 192 + 4 * c + 2 * h);  // scales 4c + 2h, +1
+      s.a[c] = __float2bfloat162_rn(d * (float)(int)(int8_t)((w2 >> (8 * (part & 1))) & 0xFFu));
+      s.b[c] = s.a[c];
+    }
+  }
+}
+
+// 16 weights (K [64c + 16 part, +16) of the super-block at blk) as eight bf16
+// pairs.  Q4_K: w = (d*sc)*q - dmin*m, one bf16 FMA per pair; Q6_K:
+// w = (d*sc)*(q - 32), one bf16 multiply per pair.
+template <int WT>
+__device__ __forceinline__ void decode_chunk(const uint8_t* blk, int c, int part,
+                                             const SbScales& s, uint32_t* o) {
+  const int h = part >> 1, u = part & 1;
+  if (WT == LB_TYPE_Q4_K) {
+    // sub-block 2c + h: qs bytes [32c + 16u, +16), low nibbles (h = 0) or
+    // high nibbles (h = 1)
+    const __nv_bfloat162 k128 = as_bf2(0x43004300u);
+    const uint4 q = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c + 16 * u);
+    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+    const int sh = 4 * h;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 x0, x1;
+      q_pairs((wd[i] >> sh) & 0x0F0F0F0Fu, k128, x0, x1);
+      o[2 * i] = as_u32(__hfma2(x0, s.a[c], s.b[c]));
+      o[2 * i + 1] = as_u32(__hfma2(x1, s.a[c], s.b[c]));
+    }
+  } else {
+    // 128-half n = c / 2, quarter qd = 2 (c % 2) + h, l in [16u, 16u + 16):
+    // ql bytes 64n + 32 (qd % 2) + l (low nibbles for qd < 2, high
+    // otherwise), qh bytes 128 + 32n + l bits 2qd..2qd+1
     const int n = c >> 1, qd = (c & 1) * 2 + h;
-    uint32_t ql[8], qh[8];
-    lds_run<8>(b + 64 * n + 32 * (qd & 1), ql);
-    lds_run<8>(b + 128 + 32 * n, qh);
-    const uint32_t scw = lds_u16(b + 192 + 8 * n + 2 * qd);
-    const float d = half_bits_to_float(lds_u16(b + 208));
-    const __nv_bfloat162 s0 = __float2bfloat162_rn(d * (float)(int)(int8_t)(scw & 0xFFu));
-    const __nv_bfloat162 s1 = __float2bfloat162_rn(d * (float)(int)(int8_t)(scw >> 8));
+    uint32_t ql[4], qh[4];
+    lds_run<4>(blk + 64 * n + 32 * (qd & 1) + 16 * u, ql);
+    lds_run<4>(blk + 128 + 32 * n + 16 * u, qh);
     const __nv_bfloat162 k160 = as_bf2(0x43204320u);
     const int shl = 4 * (qd >> 1), shh = 2 * qd;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
       // q = ql nibble | qh 2 bits << 4 (below 64): no carry crosses a byte
       const uint32_t v = ((ql[i] >> shl) & 0x0F0F0F0Fu) + ((qh[i] >> shh) & 0x03030303u) * 16u;
       __nv_bfloat162 x0, x1;
       q_pairs(v, k160, x0, x1);
-      o[2 * i] = as_u32(__hmul2(x0, i < 4 ? s0 : s1));
-      o[2 * i + 1] = as_u32(__hmul2(x1, i < 4 ? s0 : s1));
+      o[2 * i] = as_u32(__hmul2(x0, s.a[c]));
+      o[2 * i + 1] = as_u32(__hmul2(x1, s.a[c]));
     }
   }
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    *reinterpret_cast<uint4*>(a + sw128_off(r, 4 * h + j)) =
-        make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-}
-
-__device__ __forceinline__ void zero_chunk(int h, int r, uint8_t* a) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    *reinterpret_cast<uint4*>(a + sw128_off(r, 4 * h + j)) = make_uint4(0, 0, 0, 0);
 }
 
 // ------------------------------------------------------------ GEMM kernel
@@ -308,11 +362,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   constexpr int NMAT = PAIR ? 2 : 1;
   constexpr int BB = pf_block_bytes(WT), PITCH = pf_pitch(WT);
   constexpr uint32_t WSTAGE = pf_wstage(WT, NMAT);
-  constexpr uint32_t TCOLS = NMAT * kPfN;  // 64 or 128 tensor-memory columns
+  constexpr uint32_t ACC = NMAT * kPfN;  // columns of one accumulator buffer
+  constexpr uint32_t ABASE = 2 * ACC;     // first column of the decoded-chunk ring
+  constexpr int RING = kPfRing / NMAT;   // items (one K chunk of every matrix) in flight
+  static_assert(ABASE + kPfRing * kPfChunkCols <= kPfTmemCols, "tensor memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  uint8_t* a_ring = smem;
-  uint8_t* b_st = a_ring + kPfRing * kPfChunkBytes;
+  uint8_t* b_st = smem;
   uint8_t* w_st = b_st + kPfStages * kPfBStage;
   PfSync* sy = reinterpret_cast<PfSync*>(w_st + kPfStages * WSTAGE);
   volatile int* abort = &sy->abort;
@@ -326,13 +382,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&sy->afull[i], kPfDecWarps);
       mbar_init(&sy->aempty[i], 1);
     }
-    mbar_init(&sy->tfull, 1);
-    mbar_init(&sy->tempty, kPfDecWarps);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sy->tfull[b], 1);
+      mbar_init(&sy->tempty[b], kPfEpiWarps);
+    }
     mbar_init(&sy->done, 1);
     sy->abort = 0;
     fence_mbar_init();
   }
-  if (warp == kPfDecWarps + 1) tmem_alloc(&sy->tmem, TCOLS);
+  if (warp == kPfDecWarps + 1) tmem_alloc(&sy->tmem, kPfTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -385,50 +443,55 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int4 tl = p.tiles[tile];
         const int nsb = tl.z < 0 ? p.nsb_sh : p.nsb;
         const uint32_t idesc = mma_idesc((tl.y + 15) & ~15);
-        if (it > 0 && !mbar_wait_or_abort(&sy->tempty, (it - 1) & 1, p.status, abort)) break;
+        const int buf = it & 1;
+        const uint32_t dacc = tmem + buf * ACC;
+        if (it >= 2 &&
+            !mbar_spin_or_abort(&sy->tempty[buf], ((it >> 1) - 1) & 1, p.status, abort))
+          break;
         tc_fence_after();
         bool ok = true;
         for (int sb = 0; sb < nsb && ok; ++sb) {
-          if (!mbar_wait_or_abort(&sy->full[rp.s], rp.phase, p.status, abort)) {
+          if (!mbar_spin_or_abort(&sy->full[rp.s], rp.phase, p.status, abort)) {
             ok = false;
             break;
           }
-          for (int c = 0; c < 4 && ok; ++c)
+          for (int c = 0; c < 4; ++c) {
+            const int slot = auses % RING;
+            if (!mbar_spin_or_abort(&sy->afull[slot], (auses / RING) & 1, p.status, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t bd = sw128_desc(b_st + rp.s * kPfBStage + c * kPfBoxBytes);
 #pragma unroll
             for (int mat = 0; mat < NMAT; ++mat) {
-              const int slot = auses & (kPfRing - 1);
-              if (!mbar_wait_or_abort(&sy->afull[slot], (auses / kPfRing) & 1, p.status, abort)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint64_t ad = sw128_desc(a_ring + slot * kPfChunkBytes);
-              const uint64_t bd = sw128_desc(b_st + rp.s * kPfBStage + c * kPfBoxBytes);
+              const uint32_t ad = tmem + ABASE + (slot * NMAT + mat) * kPfChunkCols;
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tc_mma(tmem + mat * kPfN, ad + 2 * j, bd + 2 * j, idesc, (sb | c | j) != 0);
-              tc_commit(&sy->aempty[slot]);
-              ++auses;
+              for (int j = 0; j < 4; ++j)  // K steps of 16: 8 columns of A, 32 bytes of B
+                tc_mma_ts(dacc + mat * kPfN, ad + 8 * j, bd + 2 * j, idesc, (sb | c | j) != 0);
             }
+            tc_commit(&sy->aempty[slot]);
+            ++auses;
+          }
           if (!ok) break;
           tc_commit(&sy->empty[rp.s]);
           rp.next(kPfStages);
         }
         if (!ok) break;
-        tc_commit(&sy->tfull);
+        tc_commit(&sy->tfull[buf]);
       }
       // every MMA issued has completed before the tensor memory is freed
       tc_commit(&sy->done);
       mbar_wait(&sy->done, 0, nullptr);
     }
     __syncwarp();
-  } else {  // ------------------------------------------------ decode + epilogue
-    const int tid = threadIdx.x, r = tid & (kPfM - 1), h = tid >> 7;
-    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+  } else if (warp < kPfDecWarps) {  // ------------------------------- decode
+    const int tid = threadIdx.x, r = tid & (kPfM - 1), part = tid >> 7;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;  // lanes r of this warp
     RingPos rp;
-    int auses = 0, it = 0;
+    int auses = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const int4 tl = p.tiles[tile];
       const bool sh = tl.z < 0;
       const int nsb = sh ? p.nsb_sh : p.nsb, rows = sh ? p.rows_sh : p.rows;
@@ -446,47 +509,56 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint8_t* wst = w_st + rp.s * WSTAGE;
         // the super-block's offset in its box row (the box starts 16-byte aligned)
         const uint32_t mis = (uint32_t)(((long)jr * rb + (long)sb * BB) & 15L);
-        for (int c = 0; c < 4 && ok; ++c)
+        SbScales scl[NMAT];
+        if (valid)
+#pragma unroll
+          for (int mat = 0; mat < NMAT; ++mat)
+            sb_scales<WT>(wst + (size_t)mat * kPfM * PITCH + srow + mis, part, scl[mat]);
+        for (int c = 0; c < 4; ++c) {
+          const int slot = auses % RING;
+          if (auses >= RING &&
+              !mbar_wait_or_abort(&sy->aempty[slot], ((auses / RING) - 1) & 1, p.status, abort)) {
+            ok = false;
+            break;
+          }
 #pragma unroll
           for (int mat = 0; mat < NMAT; ++mat) {
-            const int slot = auses & (kPfRing - 1);
-            if (auses >= kPfRing &&
-                !mbar_wait_or_abort(&sy->aempty[slot], ((auses / kPfRing) - 1) & 1, p.status,
-                                    abort)) {
-              ok = false;
-              break;
-            }
-            uint8_t* a = a_ring + slot * kPfChunkBytes;
+            uint32_t o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             if (valid)
-              decode_chunk<WT>(wst + (size_t)mat * kPfM * PITCH + srow + mis, c, h, r, a);
-            else
-              zero_chunk(h, r, a);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sy->afull[slot]);
-            ++auses;
+              decode_chunk<WT>(wst + (size_t)mat * kPfM * PITCH + srow + mis, c, part, scl[mat], o);
+            tmem_st8(tmem + lane_base + ABASE + (slot * NMAT + mat) * kPfChunkCols + 8 * part, o);
           }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sy->afull[slot]);
+          ++auses;
+        }
         if (!ok) break;
         __syncwarp();
         if (lane == 0) mbar_arrive(&sy->empty[rp.s]);
         rp.next(kPfStages);
       }
       if (!ok) break;
-      // ---- epilogue: this warp's 32 rows, tokens [32 h, 32 h + 32)
-      if (!mbar_wait_or_abort(&sy->tfull, it & 1, p.status, abort)) {
-        ok = false;
-        break;
-      }
+    }
+  } else {  // ------------------------------------------------------ epilogue
+    const int q = warp & 3, r = 32 * q + lane;  // tensor-memory lanes of this warp
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int4 tl = p.tiles[tile];
+      const int buf = it & 1;
+      if (!mbar_wait_or_abort(&sy->tfull[buf], (it >> 1) & 1, p.status, abort)) break;
       tc_fence_after();
       const int ntok = tl.y;
-      const int row = r0 + r;
+      const int rows = tl.z < 0 ? p.rows_sh : p.rows;
+      const int row = tl.w * kPfM + r;
+      const uint32_t acc = tmem + lane_base + buf * ACC;
 #pragma unroll 1
-      for (int c16 = 0; c16 < 2; ++c16) {
-        const int n0 = 32 * h + 16 * c16;
-        if (n0 >= ntok) break;  // warp-uniform
+      for (int n0 = 0; n0 < ntok; n0 += 16) {  // warp-uniform
         float y0[16], y1[16];
-        tmem_ld16(tmem + lane_base + n0, y0);
-        if (PAIR) tmem_ld16(tmem + lane_base + kPfN + n0, y1);
+        tmem_ld16(acc + n0, y0);
+        if (PAIR) tmem_ld16(acc + kPfN + n0, y1);
         if (DOWN) {
           if (row < p.H)
 #pragma unroll
@@ -514,14 +586,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sy->tempty);
+      if (lane == 0) mbar_arrive(&sy->tempty[buf]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == kPfDecWarps + 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TCOLS);
+    tmem_dealloc(tmem, kPfTmemCols);
   }
 }
 
