@@ -55,6 +55,10 @@ NOMINAL_HBM_GBS = 8000.0
 # and routed down launch on one GPU
 GATE_UP_TRAFFIC_BYTES_N1 = 279_900_000
 DOWN_TRAFFIC_BYTES_N1 = 202_500_000
+# the same for the prefill path's tcgen05 GEMM launches at batch 2048 (ncu,
+# 2-layer capture of the same workload: DRAM read + write of one launch)
+PF_GATE_UP_TRAFFIC_BYTES = {2048: 719_800_000}
+PF_DOWN_TRAFFIC_BYTES = {2048: 616_200_000}
 # the same for one dense GEMV launch (workload, tokens)
 DENSE_TRAFFIC_BYTES = {("config1", 1): 33_100_000, ("config2", 1): 438_600_000,
                        ("config2", 8): 444_700_000}
@@ -493,17 +497,28 @@ def run_ours(args):
     dn_ms = statistics.mean(k[1] for k in kern_ms)
     achieved = (sum(gu_bytes) / NL) / (gu_ms * 1e-3) / 1e9
     layer_gbs = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "moe_up_slab_kernel (gate/up pass, Q4_K)",
+    prefill = B >= LB.prefill_min_tokens()
+    if prefill:
+        gu_name = "pf_gemm_kernel<Q4_K, gate+up> (tcgen05 bf16 grouped GEMM, routed + shared)"
+        dn_name = "pf_gemm_kernel<Q6_K, down> (tcgen05 bf16 grouped GEMM, routed + shared)"
+        gu_traffic = PF_GATE_UP_TRAFFIC_BYTES.get(B) if world == 1 else None
+        dn_traffic = PF_DOWN_TRAFFIC_BYTES.get(B) if world == 1 else None
+    else:
+        gu_name = "moe_up_slab_kernel (gate/up pass, Q4_K)"
+        dn_name = "moe_down_slab_kernel (routed, Q6_K)"
+        gu_traffic = GATE_UP_TRAFFIC_BYTES_N1 if world == 1 else None
+        dn_traffic = DOWN_TRAFFIC_BYTES_N1 if world == 1 else None
+    roofline = {"bound": "hbm", "kernel": gu_name,
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "algorithmic_bytes_per_launch": int(sum(gu_bytes) / NL),
                 "launch_us_mean": round(gu_ms * 1e3, 2),
                 # DRAM read+write bytes of one gate/up launch at N=1 (ncu capture)
-                "traffic": GATE_UP_TRAFFIC_BYTES_N1 if world == 1 else None,
-                "down": {"kernel": "moe_down_slab_kernel (routed, Q6_K)",
+                "traffic": gu_traffic,
+                "down": {"kernel": dn_name,
                          "achieved": round((sum(dn_bytes) / NL) / (dn_ms * 1e-3) / 1e9, 1),
                          "launch_us_mean": round(dn_ms * 1e3, 2),
-                         "traffic": DOWN_TRAFFIC_BYTES_N1 if world == 1 else None},
+                         "traffic": dn_traffic},
                 "layer": {"achieved": round(layer_gbs, 1), "frac": round(layer_gbs / peak, 4),
                           "algorithmic_bytes": int(sum(layer_bytes) / NL),
                           "us_mean": round(statistics.mean(layer_ms) * 1e3, 2)}}
@@ -563,14 +578,17 @@ def run_ours(args):
                    "sample": f"{B} tokens through 1 qwen3next layer per sample "
                              f"({per_layer * 1e3:.1f} ms), scaled to {NL} layers"}
 
-    # rms-norm + router, top-k with routing, gate/up, routed down, shared down
-    # (ranks that compute a share of the shared expert), combine
-    launches_per_layer = 5 + (1 if streams_shared else 0)
-    line = {"metric": "MoE FFN decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
+    # decode: rms-norm + router, top-k with routing, gate/up, routed down, shared
+    # down (ranks that compute a share of the shared expert), combine.
+    # prefill: rms-norm, router K slices, their sum, top-k with routing, gather,
+    # tile plan, gate/up, down, combine.
+    launches_per_layer = 9 if prefill else 5 + (1 if streams_shared else 0)
+    phase = "prefill" if prefill else "decode"
+    line = {"metric": f"MoE FFN {phase} tokens/s", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"config5_qwen3next_moe_stack_{NL}L_decode_b{B}",
+            "vs_baseline": None, "dtype": "bf16" if prefill else "f32", "data": "synthetic",
+            "config": {"workload": f"config5_qwen3next_moe_stack_{NL}L_{phase}_b{B}",
                        "batch": B, "layers": NL, "experts": cfg.experts, "top_k": cfg.top_k,
                        "hidden": cfg.hidden,
                        "parallelism": f"ep{world}" + ("-peer" if peer else "-nccl" if world > 1 else ""),

@@ -761,15 +761,15 @@ __global__ void __launch_bounds__(256) pf_norm_kernel(MoeDevice m, MoeWork w,
     o[i] = __fmul_rn(__fmul_rn(xt[i], m.input_norm[i]), scale);
 }
 
-constexpr int kRtTok = 64, kRtRows = 64, kRtK = 32;
+constexpr int kRtTok = 128, kRtRows = 64, kRtK = 32;
 
 // Router logits of a prefill batch (dot-product-with-f32-tensor-data,
 // L4096-4107, for every router row; row E of the logits is the qwen3next
-// shared-expert gate, L3491-3500): an fp32 register-blocked GEMM, 64 tokens x
-// 64 rows per CTA, K in chunks of 32 staged through shared memory (the next
-// chunk's loads in flight during the current one's FMAs), 4 x 4 outputs per
-// thread on packed fp32x2 FMA.  fp32 throughout, so the expert selection is
-// that of the decode path's router.
+// shared-expert gate, L3491-3500): an fp32 register-blocked GEMM, 128 tokens
+// x 64 rows per CTA over one K slice, K in chunks of 32 staged through shared
+// memory (the next chunk's float4 loads in flight during the current one's
+// FMAs), 8 tokens x 4 rows per thread on packed fp32x2 FMA.  fp32
+// throughout, so the expert selection is that of the decode path's router.
 __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
                                                         const float* __restrict__ xr, int T,
                                                         int all_rows, int kc) {
@@ -777,42 +777,57 @@ __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
   __shared__ __align__(16) float ws[kRtK][kRtRows + 4];
   const int t0 = blockIdx.y * kRtTok, r0 = blockIdx.x * kRtRows;
   // K slice blockIdx.z of kc values (gridDim.z slices; one: the whole row)
-  const int kb = blockIdx.z * kc, H = min(m.hidden - kb, kc);
+  const int kb = blockIdx.z * kc, K = min(m.hidden - kb, kc);
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  const int lr = tid >> 2, lk = (tid & 3) * 8;  // this thread's staged row and 8 k values
-  const float* xrow = xr + (long)min(t0 + lr, T - 1) * m.hidden + kb;
-  const int rr = min(r0 + lr, all_rows - 1);
+  // staging: token row tid/2 (16 values from (tid&1)*16), router row tid/4 (8 from (tid&3)*8)
+  const int xr_row = tid >> 1, xk = (tid & 1) * 16, wr_row = tid >> 2, wk = (tid & 3) * 8;
+  const float* xrow = xr + (long)min(t0 + xr_row, T - 1) * m.hidden + kb;
+  const int rr = min(r0 + wr_row, all_rows - 1);
   const float* wrow =
       (rr < m.router_rows ? m.router + (long)rr * m.hidden : m.router_extra_row) + kb;
-  float2 acc[4][2];
+  const bool vec = ((m.hidden | kb) & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(m.router) |
+                     reinterpret_cast<uintptr_t>(m.router_extra_row)) & 15) == 0;
+  float2 acc[8][2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
-  float xv[8], wv[8];
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+  float xv[16], wv[8];
   auto fetch = [&](int k0) {
+    if (vec && k0 + kRtK <= K) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int kk = k0 + lk + j;
-      xv[j] = kk < H ? __ldg(xrow + kk) : 0.f;
-      wv[j] = kk < H ? __ldg(wrow + kk) : 0.f;
+      for (int j = 0; j < 4; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xrow + k0 + xk) + j);
+        xv[4 * j] = v.x, xv[4 * j + 1] = v.y, xv[4 * j + 2] = v.z, xv[4 * j + 3] = v.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(wrow + k0 + wk) + j);
+        wv[4 * j] = v.x, wv[4 * j + 1] = v.y, wv[4 * j + 2] = v.z, wv[4 * j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xv[j] = k0 + xk + j < K ? __ldg(xrow + k0 + xk + j) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[j] = k0 + wk + j < K ? __ldg(wrow + k0 + wk + j) : 0.f;
     }
   };
   fetch(0);
-  for (int k0 = 0; k0 < H; k0 += kRtK) {
+  for (int k0 = 0; k0 < K; k0 += kRtK) {
     __syncthreads();
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      xs[lk + j][lr] = xv[j];
-      ws[lk + j][lr] = wv[j];
-    }
+    for (int j = 0; j < 16; ++j) xs[xk + j][xr_row] = xv[j];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ws[wk + j][wr_row] = wv[j];
     __syncthreads();
-    if (k0 + kRtK < H) fetch(k0 + kRtK);
+    if (k0 + kRtK < K) fetch(k0 + kRtK);
 #pragma unroll
     for (int k = 0; k < kRtK; ++k) {
-      const float4 a = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+      const float4 a0 = *reinterpret_cast<const float4*>(&xs[k][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&xs[k][ty * 8 + 4]);
       const float4 b = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 8; ++i) {
         acc[i][0] = __ffma2_rn(make_float2(av[i], av[i]), make_float2(b.x, b.y), acc[i][0]);
         acc[i][1] = __ffma2_rn(make_float2(av[i], av[i]), make_float2(b.z, b.w), acc[i][1]);
       }
@@ -821,8 +836,8 @@ __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
   const int E1 = m.experts + 1;
   float* dst = gridDim.z == 1 ? w.logits : w.pf_rlog + (long)blockIdx.z * T * E1;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + ty * 4 + i;
+  for (int i = 0; i < 8; ++i) {
+    const int t = t0 + ty * 8 + i;
     if (t >= T) continue;
     const float v[4] = {acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y};
 #pragma unroll
