@@ -40,6 +40,7 @@ constexpr int kMaxEntries = 64 * 1024;
 // 8 * kRouteSplitChunks chunks of 32 entries on (prefill batches), with
 // per-warp expert counters in kRouteSplitSlots ints of shared memory.
 constexpr int kRouteSplitChunks = 4;
+constexpr int kTopkTokens = 8;  // tokens per CTA of the top-k launch (one per warp)
 constexpr int kRouteSplitSlots = 8192;
 constexpr int kSlabMaxStages = 10;
 // Rows of one 2-D tensor copy of the gate/up slabs (the slabs' rows per
@@ -214,17 +215,20 @@ template <bool CG>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
                                             int pass_nt, bool grouped_ids);
 
-// Top-k (warp 0 of each CTA, one token per CTA) with the routing on the last
-// CTA to finish (an arrival counter; its eight warps group the entries), so
-// the grouping needs no launch of its own.  The counter is zero between
-// launches: the last CTA resets it.
+// Top-k (one warp per token, kTopkTokens tokens per CTA) with the routing on
+// the last CTA to finish (an arrival counter; its eight warps group the
+// entries), so the grouping needs no launch of its own.  The counter is zero
+// between launches: the last CTA resets it.
 template <int PER>
 __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w, int T,
                                                          int pass_nt, int grouped_ids) {
   __shared__ int s_last;
   griddep_wait();
   griddep_launch();
-  if (threadIdx.x < 32) topk_token<PER>(m, w, blockIdx.x, threadIdx.x);
+  {
+    const int t = blockIdx.x * kTopkTokens + (threadIdx.x >> 5);
+    if (t < T) topk_token<PER>(m, w, t, threadIdx.x & 31);
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(w.tickets, 1) == (int)gridDim.x - 1;
@@ -310,11 +314,23 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
       s_count[e] = run;
     }
     __syncthreads();
-    if (warp > 0)  // warp 0's positions already start at 0
-      for (int id = (c_lo << 5) + lane; id < min(n, c_hi << 5); id += 32) {
-        const int pos = w.entries[id];
-        if (pos >= 0) w.entries[id] = pos + s_wcount[warp * E + (CG ? __ldcg(w.sel + id) : w.sel[id])];
+    if (warp > 0) {  // warp 0's positions already start at 0; 8 entries' loads in flight
+      const int id_end = min(n, c_hi << 5);
+      for (int id0 = (c_lo << 5) + lane; id0 < id_end; id0 += 8 * 32) {
+        int pos[8], e[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int id = min(id0 + 32 * u, id_end - 1);
+          pos[u] = w.entries[id];
+          e[u] = CG ? __ldcg(w.sel + id) : w.sel[id];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int id = id0 + 32 * u;
+          if (id < id_end && pos[u] >= 0) w.entries[id] = pos[u] + s_wcount[warp * E + e[u]];
+        }
       }
+    }
     __syncthreads();
   }
   // Exclusive scans over experts (entries, up passes, down passes) and the
@@ -1971,7 +1987,8 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
               : per <= 4 ? topk_route_kernel<4> : per <= 8 ? topk_route_kernel<8>
               : per <= 16 ? topk_route_kernel<16> : topk_route_kernel<32>;
-    e = launch_pdl(kern, dim3(T), dim3(256), 0, s, m, w, T, pnt, prefill ? 0 : 1);
+    e = launch_pdl(kern, dim3((T + kTopkTokens - 1) / kTopkTokens), dim3(256), 0, s, m, w, T, pnt,
+                   prefill ? 0 : 1);
     if (e != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }

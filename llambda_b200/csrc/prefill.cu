@@ -285,9 +285,16 @@ struct SbScales {
   __nv_bfloat162 a[4], b[4];
 };
 
-template <int WT>
+// Small non-negative integer to float without a conversion instruction.
+__device__ __forceinline__ float small_int_f(uint32_t v) {
+  return __uint_as_float(0x4B000000u | v) - 8388608.0f;
+}
+
+// H = part / 2 (warp-uniform), a template argument so the sub-block indices
+// and byte shifts are constants.
+template <int WT, int H>
 __device__ __forceinline__ void sb_scales(const uint8_t* blk, int part, SbScales& s) {
-  const int h = part >> 1;
+  constexpr int h = H;
   if (WT == LB_TYPE_Q4_K) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
     const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
@@ -295,8 +302,8 @@ __device__ __forceinline__ void sb_scales(const uint8_t* blk, int part, SbScales
     for (int c = 0; c < 4; ++c) {
       int sc, mn;
       q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + h, sc, mn);
-      s.a[c] = __float2bfloat162_rn(d * (float)sc);
-      s.b[c] = __float2bfloat162_rn(-(dmin * (float)mn));
+      s.a[c] = __float2bfloat162_rn(d * small_int_f((uint32_t)sc));
+      s.b[c] = __float2bfloat162_rn(-(dmin * small_int_f((uint32_t)mn)));
     }
   } else {
     const float d = half_bits_to_float(lds_u16(blk + 208));
@@ -365,6 +372,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   constexpr uint32_t ACC = NMAT * kPfN;  // columns of one accumulator buffer
   constexpr uint32_t ABASE = 2 * ACC;     // first column of the decoded-chunk ring
   constexpr int RING = kPfRing / NMAT;   // items (one K chunk of every matrix) in flight
+  constexpr int RING_LOG = RING == 8 ? 3 : RING == 4 ? 2 : 1;
+  static_assert((1 << RING_LOG) == RING, "ring of a power of two");
   static_assert(ABASE + kPfRing * kPfChunkCols <= kPfTmemCols, "tensor memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -456,8 +465,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             break;
           }
           for (int c = 0; c < 4; ++c) {
-            const int slot = auses % RING;
-            if (!mbar_spin_or_abort(&sy->afull[slot], (auses / RING) & 1, p.status, abort)) {
+            const int slot = auses & (RING - 1);
+            if (!mbar_spin_or_abort(&sy->afull[slot], (auses >> RING_LOG) & 1, p.status, abort)) {
               ok = false;
               break;
             }
@@ -512,27 +521,42 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         SbScales scl[NMAT];
         if (valid)
 #pragma unroll
-          for (int mat = 0; mat < NMAT; ++mat)
-            sb_scales<WT>(wst + (size_t)mat * kPfM * PITCH + srow + mis, part, scl[mat]);
-        for (int c = 0; c < 4; ++c) {
-          const int slot = auses % RING;
-          if (auses >= RING &&
-              !mbar_wait_or_abort(&sy->aempty[slot], ((auses / RING) - 1) & 1, p.status, abort)) {
+          for (int mat = 0; mat < NMAT; ++mat) {
+            const uint8_t* blk = wst + (size_t)mat * kPfM * PITCH + srow + mis;
+            if (part >> 1)  // warp-uniform
+              sb_scales<WT, 1>(blk, part, scl[mat]);
+            else
+              sb_scales<WT, 0>(blk, part, scl[mat]);
+          }
+        for (int c = 0; c < 4; c += 2) {  // two items per wait for the stores
+          const int slot = auses & (RING - 1);  // items auses, auses + 1: slots slot, slot + 1
+          // the later slot's last use ends after the earlier one's (commits complete in order)
+          if (auses + 1 >= RING &&
+              !mbar_wait_or_abort(&sy->aempty[slot + 1], (((auses + 1) >> RING_LOG) - 1) & 1,
+                                  p.status, abort)) {
             ok = false;
             break;
           }
 #pragma unroll
-          for (int mat = 0; mat < NMAT; ++mat) {
-            uint32_t o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (valid)
-              decode_chunk<WT>(wst + (size_t)mat * kPfM * PITCH + srow + mis, c, part, scl[mat], o);
-            tmem_st8(tmem + lane_base + ABASE + (slot * NMAT + mat) * kPfChunkCols + 8 * part, o);
-          }
+          for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int mat = 0; mat < NMAT; ++mat) {
+              uint32_t o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+              if (valid)
+                decode_chunk<WT>(wst + (size_t)mat * kPfM * PITCH + srow + mis, c + i, part,
+                                 scl[mat], o);
+              tmem_st8(tmem + lane_base + ABASE + ((slot + i) * NMAT + mat) * kPfChunkCols +
+                           8 * part,
+                       o);
+            }
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sy->afull[slot]);
-          ++auses;
+          if (lane == 0) {
+            mbar_arrive(&sy->afull[slot]);
+            mbar_arrive(&sy->afull[slot + 1]);
+          }
+          auses += 2;
         }
         if (!ok) break;
         __syncwarp();
