@@ -42,6 +42,10 @@ extern "C" {
 #endif
 
 #define LLAMBDA_CUDA_TYPE_F32 0
+/* 32-value blocks (llambda.lisp L26-27, sizes L2139-2140): projection
+ * sessions only, the formats of rows whose width is not a multiple of 256. */
+#define LLAMBDA_CUDA_TYPE_Q5_0 6
+#define LLAMBDA_CUDA_TYPE_Q8_0 8
 #define LLAMBDA_CUDA_TYPE_Q4_K 12
 #define LLAMBDA_CUDA_TYPE_Q6_K 14
 

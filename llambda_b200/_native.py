@@ -18,8 +18,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libllambda_cuda.so")
 
 TYPE_F32, TYPE_Q4_K, TYPE_Q6_K = 0, 12, 14
+TYPE_Q5_0, TYPE_Q8_0 = 6, 8  # 32-value blocks: projection sessions only
 ARCH_QWEN3NEXT, ARCH_NEMOTRON_H_MOE = 0, 1
 BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210}
+BLOCK32_BYTES = {TYPE_Q5_0: 22, TYPE_Q8_0: 34}
 
 
 class LlambdaCudaError(RuntimeError):
@@ -33,6 +35,10 @@ def row_bytes(type_tag: int, ne0: int) -> int:
         if ne0 % 256:
             raise ValueError(f"K-quant rows need a multiple of 256 columns, got {ne0}")
         return ne0 // 256 * BLOCK_BYTES[type_tag]
+    if type_tag in BLOCK32_BYTES:
+        if ne0 % 32:
+            raise ValueError(f"Q5_0/Q8_0 rows need a multiple of 32 columns, got {ne0}")
+        return ne0 // 32 * BLOCK32_BYTES[type_tag]
     raise ValueError(f"unsupported GGML type tag {type_tag}")
 
 

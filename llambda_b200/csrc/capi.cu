@@ -41,6 +41,8 @@ size_t row_bytes(int type, uint64_t ne0) {
     case LLAMBDA_CUDA_TYPE_F32: return ne0 * 4;
     case LLAMBDA_CUDA_TYPE_Q4_K: return ne0 % 256 ? 0 : ne0 / 256 * 144;
     case LLAMBDA_CUDA_TYPE_Q6_K: return ne0 % 256 ? 0 : ne0 / 256 * 210;
+    case LLAMBDA_CUDA_TYPE_Q5_0: return ne0 % 32 ? 0 : ne0 / 32 * 22;
+    case LLAMBDA_CUDA_TYPE_Q8_0: return ne0 % 32 ? 0 : ne0 / 32 * 34;
     default: return 0;
   }
 }
@@ -50,17 +52,25 @@ const char* type_name(int type) {
     case LLAMBDA_CUDA_TYPE_F32: return "F32";
     case LLAMBDA_CUDA_TYPE_Q4_K: return "Q4_K";
     case LLAMBDA_CUDA_TYPE_Q6_K: return "Q6_K";
+    case LLAMBDA_CUDA_TYPE_Q5_0: return "Q5_0";
+    case LLAMBDA_CUDA_TYPE_Q8_0: return "Q8_0";
     default: return "unsupported";
   }
 }
 
-void require_rows(int type, uint64_t ne0, const char* what) {
+bool block32(int type) {
+  return type == LLAMBDA_CUDA_TYPE_Q5_0 || type == LLAMBDA_CUDA_TYPE_Q8_0;
+}
+
+// Types of the MoE layer's tensors (the K-quants and the F32 router); a
+// projection session also takes Q5_0 and Q8_0 rows (projection = true).
+void require_rows(int type, uint64_t ne0, const char* what, bool projection = false) {
   if (type != LLAMBDA_CUDA_TYPE_F32 && type != LLAMBDA_CUDA_TYPE_Q4_K &&
-      type != LLAMBDA_CUDA_TYPE_Q6_K)
+      type != LLAMBDA_CUDA_TYPE_Q6_K && !(projection && block32(type)))
     throw Failure(std::string(what) + ": unsupported GGML type tag " + std::to_string(type));
   if (!row_bytes(type, ne0))
-    throw Failure(std::string(what) + ": " + type_name(type) + " rows need a multiple of 256 "
-                  "columns, got " + std::to_string(ne0));
+    throw Failure(std::string(what) + ": " + type_name(type) + " rows need a multiple of " +
+                  (block32(type) ? "32" : "256") + " columns, got " + std::to_string(ne0));
 }
 
 int current_device() {
@@ -87,8 +97,12 @@ void* dev_alloc(size_t bytes) {
 }
 
 void validate_scales(int type, const void* dev, size_t bytes, cudaStream_t s, const char* what) {
-  if (type != LLAMBDA_CUDA_TYPE_Q4_K && type != LLAMBDA_CUDA_TYPE_Q6_K) return;
-  const size_t blocks = bytes / (type == LLAMBDA_CUDA_TYPE_Q4_K ? 144 : 210);
+  if (type != LLAMBDA_CUDA_TYPE_Q4_K && type != LLAMBDA_CUDA_TYPE_Q6_K && !block32(type)) return;
+  const size_t blocks =
+      bytes / (type == LLAMBDA_CUDA_TYPE_Q4_K   ? 144
+               : type == LLAMBDA_CUDA_TYPE_Q6_K ? 210
+               : type == LLAMBDA_CUDA_TYPE_Q5_0 ? 22
+                                                : 34);
   unsigned* bad = nullptr;
   cuda_check(cudaMalloc(&bad, sizeof(unsigned)), "cudaMalloc");
   unsigned host = 0;
@@ -195,6 +209,12 @@ void session_launch(llambda_cuda_session* s, const uint8_t* W, const float* din,
   if (s->type == LLAMBDA_CUDA_TYPE_F32) {
     cuda_check(lb::launch_gemv_f32(W, (int)s->ne1, (int)s->ne0, din, (long)s->ne0, (int)tokens,
                                    dout, (long)s->ne1, st),
+               "GEMV launch");
+    return;
+  }
+  if (block32(s->type)) {
+    cuda_check(lb::launch_gemv_q32(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, din,
+                                   (long)s->ne0, (int)tokens, dout, (long)s->ne1, st),
                "GEMV launch");
     return;
   }
@@ -336,7 +356,7 @@ static int session_make(int type, uint64_t ne0, uint64_t ne1, uint64_t ne2, cons
     if (!data) throw Failure("Tensor data is required.");
     if (ne0 == 0 || ne1 == 0) throw Failure("Tensor dimensions must be positive.");
     if (ne2 == 0) ne2 = 1;
-    require_rows(type, ne0, "projection tensor");
+    require_rows(type, ne0, "projection tensor", true);
     const size_t rb = row_bytes(type, ne0);
     const size_t bytes = rb * ne1 * ne2;
     if (!on_device && data_size != bytes)
@@ -421,7 +441,7 @@ int llambda_cuda_session_create(const char* model_path, llambda_cuda_session** r
     ne1 = u64(24);
     ne2 = u64(32);
     const uint64_t nbytes = u64(40), offset = u64(48);
-    require_rows((int)type, ne0, "projection file");
+    require_rows((int)type, ne0, "projection file", true);
     if (nbytes != row_bytes((int)type, ne0) * ne1 * (ne2 ? ne2 : 1))
       throw Failure("Projection file data size does not match its dimensions.");
     if (offset < sizeof(hdr) || std::fseek(f, (long)offset, SEEK_SET) != 0)

@@ -16,8 +16,16 @@
 
 // GGML type tags (llambda.lisp L24-31).
 #define LB_TYPE_F32 0
+#define LB_TYPE_Q5_0 6
+#define LB_TYPE_Q8_0 8
 #define LB_TYPE_Q4_K 12
 #define LB_TYPE_Q6_K 14
+
+// 32-value block formats (llambda.lisp L2139-2140):
+//   Q5_0 (22 B): d:f16 @0, qh:u32 @2, qs[16] @6
+//   Q8_0 (34 B): d:f16 @0, qs:int8[32] @2
+#define LB_Q5_0 22
+#define LB_Q8_0 34
 
 namespace lb {
 

@@ -694,6 +694,80 @@ __global__ void __launch_bounds__(128) gemv_f32_kernel(const float* __restrict__
   }
 }
 
+// Q5_0 / Q8_0 rows (32-value blocks; dot-product-with-q5-0-tensor-data,
+// llambda.lisp L4037-4068, and -q8-0-, L4070-4094): one warp per row, lane l
+// takes blocks l, l + 32, ...; the tokens' inputs sit in shared memory, so a
+// block's bytes are read once for all of them.  Per block the integer values
+// times x are summed in fp32 and scaled by d once (the reference scales each
+// product; the values are exact, so only the rounding order differs).
+// Rows are 2-byte aligned (22- and 34-byte blocks): 16-bit loads.
+template <int TYPE>
+__global__ void __launch_bounds__(256) gemv_q32_kernel(const uint8_t* __restrict__ W, size_t rb,
+                                                       int rows, int K,
+                                                       const float* __restrict__ x, long ldx,
+                                                       int tokens, float* __restrict__ y,
+                                                       long ldy) {
+  constexpr int kMaxTok = 8;
+  constexpr int BB = TYPE == LB_TYPE_Q5_0 ? LB_Q5_0 : LB_Q8_0;
+  extern __shared__ float xs[];  // [tokens][K]
+  for (int i = threadIdx.x; i < tokens * K; i += blockDim.x) {
+    const int t = i / K;
+    xs[i] = x[(long)t * ldx + (i - t * K)];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nblk = K >> 5;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    const uint8_t* wr = W + (size_t)row * rb;
+    float acc[kMaxTok];
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) acc[t] = 0.f;
+    for (int b = lane; b < nblk; b += 32) {
+      const unsigned short* h = reinterpret_cast<const unsigned short*>(wr + (size_t)b * BB);
+      const float d = __half2float(__ushort_as_half(__ldg(h)));
+      float q[32];
+      if (TYPE == LB_TYPE_Q8_0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t v = __ldg(h + 1 + i);
+          q[2 * i] = (float)(int8_t)(v & 0xFFu);
+          q[2 * i + 1] = (float)(int8_t)(v >> 8);
+        }
+      } else {
+        const uint32_t qh = (uint32_t)__ldg(h + 1) | ((uint32_t)__ldg(h + 2) << 16);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t v = __ldg(h + 3 + i);  // qs bytes 2i, 2i + 1
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int j = 2 * i + k;
+            const uint32_t byte = (v >> (8 * k)) & 0xFFu;
+            q[j] = (float)((int)((byte & 15u) | (((qh >> j) & 1u) << 4)) - 16);
+            q[16 + j] = (float)((int)((byte >> 4) | (((qh >> (j + 16)) & 1u) << 4)) - 16);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kMaxTok; ++t) {
+        if (t < tokens) {
+          const float* xb = xs + t * K + b * 32;
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s = fmaf(q[j], xb[j], s);
+          acc[t] = fmaf(d, s, acc[t]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) {
+      if (t < tokens) {
+        const float v = warp_sum(acc[t]);
+        if (lane == 0) y[(long)t * ldy + row] = v;
+      }
+    }
+  }
+}
+
 __global__ void check_scales_kernel(int type, const uint8_t* __restrict__ W, size_t blocks,
                                     unsigned* bad) {
   unsigned local = 0;
@@ -703,6 +777,10 @@ __global__ void check_scales_kernel(int type, const uint8_t* __restrict__ W, siz
       const uint8_t* p = W + b * LB_Q4K;
       const uint32_t d = p[0] | (p[1] << 8), m = p[2] | (p[3] << 8);
       local += ((d & 0x7C00u) == 0x7C00u) || ((m & 0x7C00u) == 0x7C00u);
+    } else if (type == LB_TYPE_Q5_0 || type == LB_TYPE_Q8_0) {
+      const uint8_t* p = W + b * (type == LB_TYPE_Q5_0 ? LB_Q5_0 : LB_Q8_0);
+      const uint32_t d = p[0] | (p[1] << 8);
+      local += (d & 0x7C00u) == 0x7C00u;
     } else {
       const uint8_t* p = W + b * LB_Q6K + 208;
       const uint32_t d = p[0] | (p[1] << 8);
@@ -970,9 +1048,33 @@ cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long
   return cudaGetLastError();
 }
 
+cudaError_t launch_gemv_q32(int type, const void* W, size_t rb, int rows, int K, const float* x,
+                            long ldx, int tokens, float* y, long ldy, cudaStream_t stream) {
+  if (rows <= 0 || tokens <= 0) return cudaSuccess;
+  if ((type != LB_TYPE_Q5_0 && type != LB_TYPE_Q8_0) || K % 32) return cudaErrorInvalidValue;
+  // tokens per launch: up to 8 whose inputs fit in 192 KB of shared memory
+  const int per = std::max(1, std::min(8, (int)((192 * 1024) / ((size_t)K * 4))));
+  if ((size_t)K * 4 > 192 * 1024) return cudaErrorInvalidValue;
+  auto kern = type == LB_TYPE_Q5_0 ? gemv_q32_kernel<LB_TYPE_Q5_0> : gemv_q32_kernel<LB_TYPE_Q8_0>;
+  const int grid = std::max(1, std::min((rows + 7) / 8, sm_count() * 8));
+  for (int t0 = 0; t0 < tokens; t0 += per) {
+    const int nt = std::min(per, tokens - t0);
+    const size_t smem = (size_t)nt * K * 4;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)std::max<size_t>(smem, 1));
+    if (e != cudaSuccess) return e;
+    kern<<<grid, 256, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, K,
+                                      x + (long)t0 * ldx, ldx, nt, y + (long)t0 * ldy, ldy);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t check_fp16_scales(int type, const void* W, size_t blocks, unsigned* bad,
                               cudaStream_t stream) {
-  if (type != LB_TYPE_Q4_K && type != LB_TYPE_Q6_K) return cudaSuccess;
+  if (type != LB_TYPE_Q4_K && type != LB_TYPE_Q6_K && type != LB_TYPE_Q5_0 &&
+      type != LB_TYPE_Q8_0)
+    return cudaSuccess;
   const size_t grid = std::min<size_t>((blocks + 255) / 256, (size_t)sm_count() * 8);
   check_scales_kernel<<<(int)std::max<size_t>(grid, 1), 256, 0, stream>>>(
       type, static_cast<const uint8_t*>(W), blocks, bad);

@@ -41,6 +41,10 @@ bool launch_gemv_fused(int type, const void* W, size_t row_bytes, int rows, int 
 cudaError_t launch_gemv_prepped(int type, const void* W, size_t row_bytes, int rows, int K,
                                 const float* xp, int tokens, float* y, long ldy, int* status,
                                 cudaStream_t stream);
+// Q5_0 / Q8_0 rows (32-value blocks): x natural layout, no preparation.
+cudaError_t launch_gemv_q32(int type, const void* W, size_t row_bytes, int rows, int K,
+                            const float* x, long ldx, int tokens, float* y, long ldy,
+                            cudaStream_t stream);
 // F32 rows (router): x natural layout, no preparation.
 cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long ldx, int tokens,
                             float* y, long ldy, cudaStream_t stream);

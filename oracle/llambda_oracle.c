@@ -35,6 +35,8 @@
 #define OR_QK_K 256
 #define OR_Q4K_BLOCK 144 /* 4 + 12 + 128, L2142 */
 #define OR_Q6K_BLOCK 210 /* 2 + 16 + 192, L2144 */
+#define OR_Q5_0_BLOCK 22 /* 2 + 4 + 16, L2139 */
+#define OR_Q8_0_BLOCK 34 /* 2 + 32, L2140 */
 
 static __thread char or_error[512];
 static int or_workers = 24; /* *gemv-worker-count*, L36 */
@@ -239,6 +241,101 @@ int or_dot_q6_k(const uint8_t *row, const float *x, size_t count, float *out) {
 }
 
 /* dot-product-with-f32-tensor-data, L4096-4107: sequential, unfused. */
+/* The 5-bit value of position j (0..31) of a Q5_0 block: nibble j (low) or
+ * j-16 (high) of qs, bit j of qh as bit 4, minus 16 (L3978-3983). */
+static int or_q5_0_value(const uint8_t *blk, uint32_t qh, int j) {
+  int packed = blk[6 + (j & 15)];
+  int nib = j < 16 ? (packed & 0x0F) : (packed >> 4);
+  return (nib | (((qh >> j) & 1) << 4)) - 16;
+}
+
+static uint32_t or_read_u32(const uint8_t *p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+/* dequantize-q5-0, L3965-3990: w = d * q, rounded once. */
+int or_dequantize_q5_0(const uint8_t *p, size_t count, float *out) {
+  if (count % 32) {
+    or_fail("Q5_0 dequantization requires ELEMENT-COUNT to be a multiple of 32.%s", 0);
+    return -1;
+  }
+  for (size_t b = 0; b < count / 32; ++b) {
+    const uint8_t *blk = p + b * OR_Q5_0_BLOCK;
+    int err = 0;
+    float d = or_read_fp16(blk, &err);
+    if (err) return -1;
+    uint32_t qh = or_read_u32(blk + 2);
+    for (int j = 0; j < 32; ++j) out[b * 32 + j] = d * (float)or_q5_0_value(blk, qh, j);
+  }
+  return 0;
+}
+
+/* dequantize-q8-0, L3992-4009: w = d * q (signed bytes). */
+int or_dequantize_q8_0(const uint8_t *p, size_t count, float *out) {
+  if (count % 32) {
+    or_fail("Q8_0 dequantization requires ELEMENT-COUNT to be a multiple of 32.%s", 0);
+    return -1;
+  }
+  for (size_t b = 0; b < count / 32; ++b) {
+    const uint8_t *blk = p + b * OR_Q8_0_BLOCK;
+    int err = 0;
+    float d = or_read_fp16(blk, &err);
+    if (err) return -1;
+    for (int j = 0; j < 32; ++j) out[b * 32 + j] = d * (float)(int8_t)blk[2 + j];
+  }
+  return 0;
+}
+
+/* dot-product-with-q5-0-tensor-data, L4037-4068: per pair j of a block,
+ * sum += d * (q0 * x[j] + q1 * x[16 + j]), single-float steps in order. */
+int or_dot_q5_0(const uint8_t *row, const float *x, size_t count, float *out) {
+  if (count % 32) {
+    or_fail("Q5_0 dot product requires ELEMENT-COUNT to be a multiple of 32.%s", 0);
+    return -1;
+  }
+  float sum = 0.0f;
+  for (size_t b = 0; b < count / 32; ++b) {
+    const uint8_t *blk = row + b * OR_Q5_0_BLOCK;
+    int err = 0;
+    float d = or_read_fp16(blk, &err);
+    if (err) return -1;
+    uint32_t qh = or_read_u32(blk + 2);
+    const float *xb = x + b * 32;
+    for (int j = 0; j < 16; ++j) {
+      float p0 = (float)or_q5_0_value(blk, qh, j) * xb[j];
+      float p1 = (float)or_q5_0_value(blk, qh, j + 16) * xb[16 + j];
+      float pair = p0 + p1;
+      float term = d * pair;
+      sum = sum + term;
+    }
+  }
+  *out = sum;
+  return 0;
+}
+
+/* dot-product-with-q8-0-tensor-data, L4070-4094: sum += (d * q) * x[j]. */
+int or_dot_q8_0(const uint8_t *row, const float *x, size_t count, float *out) {
+  if (count % 32) {
+    or_fail("Q8_0 dot product requires ELEMENT-COUNT to be a multiple of 32.%s", 0);
+    return -1;
+  }
+  float sum = 0.0f;
+  for (size_t b = 0; b < count / 32; ++b) {
+    const uint8_t *blk = row + b * OR_Q8_0_BLOCK;
+    int err = 0;
+    float d = or_read_fp16(blk, &err);
+    if (err) return -1;
+    const float *xb = x + b * 32;
+    for (int j = 0; j < 32; ++j) {
+      float dq = d * (float)(int8_t)blk[2 + j];
+      float term = dq * xb[j];
+      sum = sum + term;
+    }
+  }
+  *out = sum;
+  return 0;
+}
+
 float or_dot_f32(const float *row, const float *x, size_t count) {
   float sum = 0.0f;
   for (size_t i = 0; i < count; ++i) {
@@ -264,6 +361,8 @@ size_t or_row_bytes(int type, size_t columns) {
     case OR_TYPE_F32: return columns * 4;
     case OR_TYPE_Q4_K: return columns % OR_QK_K ? 0 : columns / OR_QK_K * OR_Q4K_BLOCK;
     case OR_TYPE_Q6_K: return columns % OR_QK_K ? 0 : columns / OR_QK_K * OR_Q6K_BLOCK;
+    case OR_TYPE_Q5_0: return columns % 32 ? 0 : columns / 32 * OR_Q5_0_BLOCK;
+    case OR_TYPE_Q8_0: return columns % 32 ? 0 : columns / 32 * OR_Q8_0_BLOCK;
     default: return 0;
   }
 }
@@ -287,6 +386,14 @@ int or_gemv(const or_tensor *t, size_t start_row, size_t row_count,
   if (t->type == OR_TYPE_F32) {
     for (size_t r = 0; r < row_count; ++r)
       y[r] = or_dot_f32((const float *)(base + r * rb), x, cols);
+    return 0;
+  }
+  if (t->type == OR_TYPE_Q5_0 || t->type == OR_TYPE_Q8_0) { /* sequential rows, L4582-4593 */
+    for (size_t r = 0; r < row_count; ++r) {
+      int rc = t->type == OR_TYPE_Q5_0 ? or_dot_q5_0(base + r * rb, x, cols, &y[r])
+                                       : or_dot_q8_0(base + r * rb, x, cols, &y[r]);
+      if (rc) return -1;
+    }
     return 0;
   }
   int failed = 0;

@@ -19,6 +19,8 @@ extern "C" {
 enum {
   OR_TYPE_F32 = 0,
   OR_TYPE_F16 = 1,
+  OR_TYPE_Q5_0 = 6,
+  OR_TYPE_Q8_0 = 8,
   OR_TYPE_Q4_K = 12,
   OR_TYPE_Q6_K = 14
 };
@@ -58,6 +60,10 @@ int or_dequantize_q4_k(const uint8_t *blocks, size_t count, float *out);
 int or_dequantize_q6_k(const uint8_t *blocks, size_t count, float *out);
 int or_dot_q4_k(const uint8_t *row, const float *x, size_t count, float *out);
 int or_dot_q6_k(const uint8_t *row, const float *x, size_t count, float *out);
+int or_dequantize_q5_0(const uint8_t *blocks, size_t count, float *out);
+int or_dequantize_q8_0(const uint8_t *blocks, size_t count, float *out);
+int or_dot_q5_0(const uint8_t *row, const float *x, size_t count, float *out);
+int or_dot_q8_0(const uint8_t *row, const float *x, size_t count, float *out);
 float or_dot_f32(const float *row, const float *x, size_t count);
 float or_dot_product(const float *a, const float *b, size_t count);
 size_t or_row_bytes(int type, size_t columns);

@@ -144,3 +144,39 @@ def test_config2_full_size(tokens):
     rows = np.arange(0, c.rows, 97)  # oracle on a row sample keeps the test short
     r = np.stack([[O.dot_row(c.type, w[i * 3360:(i + 1) * 3360], xi) for i in rows] for xi in x])
     assert max_rel(y[:, rows], r) < 1e-5
+
+
+@pytest.mark.parametrize("kind", ["q5_0", "q8_0"])
+@pytest.mark.parametrize("K,rows,tokens", [(32, 5, 1), (1856, 300, 1), (2688, 129, 3),
+                                           (3712, 64, 9), (6144, 40, 2)])
+def test_block32_gemv_matches_oracle(kind, K, rows, tokens):
+    """Q5_0 / Q8_0 projection sessions (dot-product-with-q5-0/-q8-0-tensor-data,
+    L4037-4094) against the oracle: Nemotron-H widths that are not multiples
+    of 256, a single block, and more tokens than one launch takes."""
+    from tests import block32 as B
+    t = LB.TYPE_Q5_0 if kind == "q5_0" else LB.TYPE_Q8_0
+    blocks = B.random_blocks(t, rows * K // 32, seed=K + rows)
+    x = np.random.default_rng(K).standard_normal((tokens, K)).astype(np.float32)
+    s = LB.ProjectionSession.from_tensor(t, K, rows, blocks)
+    y = s.run_batch(x) if tokens > 1 else s.run(x[0])[None]
+    ref = _oracle_gemv(t, blocks, K, rows, x)
+    assert max_rel(y, ref) < MAX_REL
+    assert max_rel(y, ref) < 1e-5
+
+
+@pytest.mark.parametrize("kind", ["q5_0", "q8_0"])
+def test_block32_hand_blocks_through_the_gemv(kind):
+    from tests import block32 as B
+    t = LB.TYPE_Q5_0 if kind == "q5_0" else LB.TYPE_Q8_0
+    blk, want = B.hand_q5_0() if kind == "q5_0" else B.hand_q8_0()
+    s = LB.ProjectionSession.from_tensor(t, 32, 1, blk)
+    got = s.run_batch(np.eye(32, dtype=np.float32))[:, 0]  # unit vectors pick the weights
+    assert np.array_equal(got, want)
+
+
+def test_block32_rejects_fp16_specials():
+    from tests import block32 as B
+    blk, _ = B.hand_q8_0()
+    blk[0:2] = np.frombuffer(np.array([np.nan], np.float16).tobytes(), np.uint8)
+    with pytest.raises(LB.LlambdaCudaError, match="Inf/NaN"):
+        LB.ProjectionSession.from_tensor(LB.TYPE_Q8_0, 32, 1, blk)

@@ -225,3 +225,34 @@ def test_gemv_is_worker_count_independent():
     assert np.array_equal(a, b)
     # row-by-row equals the whole GEMV
     assert np.array_equal(a[5], np.float32(O.dot_row(O.TYPE_Q6_K, w[5 * 420:6 * 420], x)))
+
+
+@pytest.mark.parametrize("kind", ["q5_0", "q8_0"])
+def test_block32_dequantize_hand_blocks(kind):  # dequantize-q5-0 / -q8-0, L3965-4009
+    from tests import block32 as B
+    blk, want = B.hand_q5_0() if kind == "q5_0" else B.hand_q8_0()
+    t = O.TYPE_Q5_0 if kind == "q5_0" else O.TYPE_Q8_0
+    assert np.array_equal(O.dequantize(t, blk, 32), want)
+
+
+@pytest.mark.parametrize("kind", ["q5_0", "q8_0"])
+def test_block32_dot_matches_dequant_dot(kind):  # L4037-4094 against L3965-4009
+    from tests import block32 as B
+    t = O.TYPE_Q5_0 if kind == "q5_0" else O.TYPE_Q8_0
+    blocks = B.random_blocks(t, 64, seed=3)
+    x = np.random.default_rng(4).standard_normal(64 * 32).astype(np.float32)
+    deq = O.dequantize(t, blocks, 64 * 32).astype(np.float64)
+    ref = float(np.dot(deq, x))
+    got = O.dot_row(t, blocks, x)
+    assert abs(got - ref) <= 1e-4 * max(1.0, abs(ref))
+    # rows of a tensor through the GEMV (sequential rows, L4582-4593)
+    y = O.gemv(t, blocks, 1024, 2, x[:1024])
+    assert abs(float(y[1]) - O.dot_row(t, blocks[(len(blocks) // 2):], x[:1024])) == 0.0
+
+
+def test_block32_fp16_special_is_an_error():
+    from tests import block32 as B
+    blk, _ = B.hand_q8_0()
+    blk[0:2] = np.frombuffer(np.array([np.inf], np.float16).tobytes(), np.uint8)
+    with pytest.raises(O.OracleError):
+        O.dequantize(O.TYPE_Q8_0, blk, 32)
