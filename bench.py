@@ -81,9 +81,11 @@ def parse():
                         "peer memory, or with an NCCL all-reduce per layer")
     p.add_argument("--no-graph", action="store_true",
                    help="launch every layer from Python instead of replaying one CUDA graph")
-    p.add_argument("--workload", default="stack", choices=["stack", "config1", "config2"],
+    p.add_argument("--workload", default="stack",
+                   choices=["stack", "config1", "config2", "q8_0", "q5_0"],
                    help="stack: the config-5 MoE decode stack (the headline line); "
-                        "config1/config2: one dense dequant-GEMV of --batch tokens")
+                        "config1/config2: one dense dequant-GEMV of --batch tokens; "
+                        "q8_0/q5_0: a 32-value-block GEMV at Nemotron-H width 2688")
     return p.parse_args()
 
 
@@ -275,17 +277,33 @@ def time_cpu_stack(cfg, layers, batch, seed, steps, warmup):
 
 # ----------------------------------------------------------------- kernels alone
 
+def fill_block32(torch, buf, type_tag, nblocks, seed, LB):
+    """Random Q5_0 / Q8_0 blocks in device memory: random bytes, then each
+    block's fp16 d set to |N(0,1)| * 0.02 (no Inf/NaN)."""
+    bb = LB._native.BLOCK32_BYTES[type_tag]
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    blocks = buf[: nblocks * bb].view(nblocks, bb)
+    blocks.copy_(torch.randint(0, 256, (nblocks, bb), dtype=torch.uint8, device="cuda",
+                               generator=g))
+    d = (torch.randn(nblocks, device="cuda", generator=g).abs() * 0.02).half()
+    blocks[:, 0:2] = d.view(torch.uint8).view(nblocks, 2)
+
+
 def time_dense_gemv(torch, LB, cfg, tokens, reps=20):
-    """Dense GEMV (configs 1/2) timed alone; rotates weight copies past L2."""
+    """Dense GEMV (configs 1/2, Q5_0/Q8_0 shapes) timed alone; rotates weight
+    copies past L2."""
     from llambda_b200 import configs as CF
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
     wb = cfg.weight_bytes
     copies = max(1, math.ceil(3 * l2 / wb))
-    unit = 144 if cfg.type == LB.TYPE_Q4_K else 210
     bufs, sessions = [], []
     for c in range(copies):
         b = torch.empty(wb + 256, dtype=torch.uint8, device="cuda")
-        LB.synth_fill_device(cfg.type, c, CF.S_DENSE, 0, wb // unit, cfg.dscale, b)
+        if cfg.type in (LB.TYPE_Q5_0, LB.TYPE_Q8_0):
+            fill_block32(torch, b, cfg.type, wb // LB._native.BLOCK32_BYTES[cfg.type], c, LB)
+        else:
+            unit = 144 if cfg.type == LB.TYPE_Q4_K else 210
+            LB.synth_fill_device(cfg.type, c, CF.S_DENSE, 0, wb // unit, cfg.dscale, b)
         bufs.append(b)
         sessions.append(LB.ProjectionSession.from_device(cfg.type, cfg.cols, cfg.rows, b))
     x = torch.randn(tokens, cfg.cols, device="cuda")
@@ -354,7 +372,8 @@ def run_reference(args):
 def run_dense(args, torch, LB, CF):
     """--workload config1|config2: one dense dequant-GEMV (rank 0 only) with
     --batch tokens; value = algorithmic HBM GB/s (weights + inputs + outputs)."""
-    cfg = CF.CONFIG1 if args.workload == "config1" else CF.CONFIG2
+    cfg = {"config1": CF.CONFIG1, "config2": CF.CONFIG2, "q8_0": CF.DENSE_Q8_0,
+           "q5_0": CF.DENSE_Q5_0}[args.workload]
     r = time_dense_gemv(torch, LB, cfg, args.batch, reps=max(args.steps, 1))
     peak, peak_kind = hbm_peak()
     line = {"metric": "dequant-GEMV HBM GB/s", "value": round(r["achieved_gbs"], 1),
@@ -376,7 +395,7 @@ def run_ours(args):
     import torch
     import llambda_b200 as LB
     from llambda_b200 import configs as CF
-    if args.workload in ("config1", "config2"):
+    if args.workload in ("config1", "config2", "q8_0", "q5_0"):
         if LB.probe() != 1:
             raise SystemExit("CUDA backend unavailable: " + LB._native.last_error())
         return run_dense(args, torch, LB, CF)

@@ -47,6 +47,10 @@ class DenseConfig:
 
 CONFIG1 = DenseConfig("config1_q4k_gemv_14336x4096", TYPE_Q4_K, 14336, 4096, Q4K_DSCALE)
 CONFIG2 = DenseConfig("config2_q6k_lmhead_128256x4096", TYPE_Q6_K, 128256, 4096, Q6K_DSCALE)
+# 32-value-block GEMVs at a Nemotron-H width that is not a multiple of 256
+# (hidden 2688), rows enough to exceed L2; random blocks, d = |N(0,1)| * 0.02
+DENSE_Q8_0 = DenseConfig("q8_0_gemv_65536x2688", 8, 65536, 2688, 0.02)
+DENSE_Q5_0 = DenseConfig("q5_0_gemv_65536x2688", 6, 65536, 2688, 0.02)
 
 
 @dataclass(frozen=True)

@@ -695,12 +695,15 @@ __global__ void __launch_bounds__(128) gemv_f32_kernel(const float* __restrict__
 }
 
 // Q5_0 / Q8_0 rows (32-value blocks; dot-product-with-q5-0-tensor-data,
-// llambda.lisp L4037-4068, and -q8-0-, L4070-4094): one warp per row, lane l
-// takes blocks l, l + 32, ...; the tokens' inputs sit in shared memory, so a
-// block's bytes are read once for all of them.  Per block the integer values
-// times x are summed in fp32 and scaled by d once (the reference scales each
-// product; the values are exact, so only the rounding order differs).
-// Rows are 2-byte aligned (22- and 34-byte blocks): 16-bit loads.
+// llambda.lisp L4037-4068, and -q8-0-, L4070-4094): one warp per row, 8
+// blocks (256 values) per step, lane l taking values [8l, 8l + 8) of the step
+// (block l/4, part l%4), so the weight loads of a step are one contiguous
+// run and the activation reads are contiguous shared-memory reads; the
+// tokens' inputs sit in shared memory, so a block's bytes are read once for
+// all of them.  Per lane and block the exact integer values times x are
+// summed in fp32 and scaled by d (the reference scales each product; only
+// the rounding order differs).  Rows are 2-byte aligned (22- and 34-byte
+// blocks): 16-bit loads.
 template <int TYPE>
 __global__ void __launch_bounds__(256) gemv_q32_kernel(const uint8_t* __restrict__ W, size_t rb,
                                                        int rows, int K,
@@ -709,52 +712,75 @@ __global__ void __launch_bounds__(256) gemv_q32_kernel(const uint8_t* __restrict
                                                        long ldy) {
   constexpr int kMaxTok = 8;
   constexpr int BB = TYPE == LB_TYPE_Q5_0 ? LB_Q5_0 : LB_Q8_0;
-  extern __shared__ float xs[];  // [tokens][K]
+  extern __shared__ __align__(16) float xs[];  // [tokens][K]
   for (int i = threadIdx.x; i < tokens * K; i += blockDim.x) {
     const int t = i / K;
     xs[i] = x[(long)t * ldx + (i - t * K)];
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nblk = K >> 5;
+  const int nblk = K >> 5, part = lane & 3;
   for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
     const uint8_t* wr = W + (size_t)row * rb;
     float acc[kMaxTok];
 #pragma unroll
     for (int t = 0; t < kMaxTok; ++t) acc[t] = 0.f;
-    for (int b = lane; b < nblk; b += 32) {
-      const unsigned short* h = reinterpret_cast<const unsigned short*>(wr + (size_t)b * BB);
-      const float d = __half2float(__ushort_as_half(__ldg(h)));
-      float q[32];
-      if (TYPE == LB_TYPE_Q8_0) {
+    constexpr int U = 4;  // steps whose loads are issued before any is used
+    for (int b0 = 0; b0 < nblk; b0 += 8 * U) {
+      // per step: d, this lane's 8 value bytes as two words (Q8_0: qs bytes
+      // [8 part, +8); Q5_0: qs bytes [(8 part) % 16, +8)), Q5_0's qh
+      uint32_t rd[U], ra[U], rb2[U], rh[U];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t v = __ldg(h + 1 + i);
-          q[2 * i] = (float)(int8_t)(v & 0xFFu);
-          q[2 * i + 1] = (float)(int8_t)(v >> 8);
-        }
-      } else {
-        const uint32_t qh = (uint32_t)__ldg(h + 1) | ((uint32_t)__ldg(h + 2) << 16);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint32_t v = __ldg(h + 3 + i);  // qs bytes 2i, 2i + 1
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int j = 2 * i + k;
-            const uint32_t byte = (v >> (8 * k)) & 0xFFu;
-            q[j] = (float)((int)((byte & 15u) | (((qh >> j) & 1u) << 4)) - 16);
-            q[16 + j] = (float)((int)((byte >> 4) | (((qh >> (j + 16)) & 1u) << 4)) - 16);
-          }
-        }
+      for (int u = 0; u < U; ++u) {
+        const int b = min(b0 + 8 * u + (lane >> 2), nblk - 1);  // clamped: loads overlap
+        const unsigned short* h = reinterpret_cast<const unsigned short*>(wr + (size_t)b * BB);
+        rd[u] = __ldg(h);
+        const unsigned short* q = h + (TYPE == LB_TYPE_Q8_0 ? 1 + 4 * part : 3 + ((8 * part) & 15) / 2);
+        ra[u] = (uint32_t)__ldg(q) | ((uint32_t)__ldg(q + 1) << 16);
+        rb2[u] = (uint32_t)__ldg(q + 2) | ((uint32_t)__ldg(q + 3) << 16);
+        rh[u] = TYPE == LB_TYPE_Q5_0 ? ((uint32_t)__ldg(h + 1) | ((uint32_t)__ldg(h + 2) << 16)) : 0u;
       }
 #pragma unroll
-      for (int t = 0; t < kMaxTok; ++t) {
-        if (t < tokens) {
-          const float* xb = xs + t * K + b * 32;
-          float s = 0.f;
+      for (int u = 0; u < U; ++u) {
+        const int b = b0 + 8 * u + (lane >> 2);
+        if (b >= nblk) continue;
+        const float d = __half2float(__ushort_as_half((unsigned short)rd[u]));
+        // each value byte becomes the float 2^23 + byte (one PRMT under the
+        // exponent byte 0x4B); subtracting 2^23 + offset is exact
+        uint32_t w[2];
+        float off;
+        if (TYPE == LB_TYPE_Q8_0) {  // signed bytes: xor 0x80 gives q + 128
+          w[0] = ra[u] ^ 0x80808080u;
+          w[1] = rb2[u] ^ 0x80808080u;
+          off = 8388608.0f + 128.0f;
+        } else {  // nibble | qh bit j << 4 gives q + 16
+          const int sh = part >= 2 ? 4 : 0;
+          const uint32_t hb = (rh[u] >> (8 * part)) & 0xFFu;  // qh bits 8 part .. 8 part + 7
+          w[0] = ((ra[u] >> sh) & 0x0F0F0F0Fu) | ((((hb & 15u) * 0x00204081u) & 0x01010101u) << 4);
+          w[1] = ((rb2[u] >> sh) & 0x0F0F0F0Fu) | ((((hb >> 4) * 0x00204081u) & 0x01010101u) << 4);
+          off = 8388608.0f + 16.0f;
+        }
+        float q[8];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) s = fmaf(q[j], xb[j], s);
-          acc[t] = fmaf(d, s, acc[t]);
+        for (int i = 0; i < 4; ++i) {
+          q[i] = __uint_as_float(__byte_perm(w[0], 0x4B000000u, 0x7440u | i)) - off;
+          q[4 + i] = __uint_as_float(__byte_perm(w[1], 0x4B000000u, 0x7440u | i)) - off;
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxTok; ++t) {
+          if (t < tokens) {
+            const float4* xb = reinterpret_cast<const float4*>(xs + t * K + b * 32 + 8 * part);
+            const float4 xa = xb[0], xc = xb[1];
+            float sum = q[0] * xa.x;
+            sum = fmaf(q[1], xa.y, sum);
+            sum = fmaf(q[2], xa.z, sum);
+            sum = fmaf(q[3], xa.w, sum);
+            sum = fmaf(q[4], xc.x, sum);
+            sum = fmaf(q[5], xc.y, sum);
+            sum = fmaf(q[6], xc.z, sum);
+            sum = fmaf(q[7], xc.w, sum);
+            acc[t] = fmaf(d, sum, acc[t]);
+          }
         }
       }
     }
