@@ -545,12 +545,15 @@ def run_ours(args):
     # e2e through the C ABI with host buffers (one call per layer per step)
     e2e = None
     if not args.no_e2e:
-        x_host = x0.cpu().numpy().copy()
+        # page-locked host buffers (the library copies them by DMA, no staging)
+        pinned = [x0.cpu().pin_memory()] + [torch.empty(tuple(x0.shape), dtype=torch.float32,
+                                                        pin_memory=True) for _ in range(2)]
+        x_host = pinned[0].numpy()
         if world > 1:
             import torch.distributed as dist
             gloo = dist.new_group(backend="gloo")
 
-        host_bufs = [np.empty_like(x_host) for _ in range(2)]  # run-into destinations
+        host_bufs = [t.numpy() for t in pinned[1:]]  # run-into destinations
 
         def e2e_step():
             cur_h = x_host
@@ -574,8 +577,8 @@ def run_ours(args):
         e2e = {"value": B / dt, "unit": "tokens/s",
                "h2d_bytes_per_step": NL * B * cfg.hidden * 4,
                "d2h_bytes_per_step": NL * B * cfg.hidden * 4,
-               "path": "llambda_cuda_moe_session_run per layer into preallocated host float "
-                       "buffers (the reference's run-into convention)"}
+               "path": "llambda_cuda_moe_session_run per layer from and into preallocated "
+                       "page-locked host float buffers (the reference's run-into convention)"}
 
     kernels = None
     cpu = None

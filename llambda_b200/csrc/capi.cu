@@ -130,6 +130,20 @@ struct DeviceGuard {
 };
 
 // Pinned host bounce buffer, grown on demand.
+// [p, p + bytes) lies in page-locked host memory (cudaHostAlloc'd or
+// registered), so the GPU can copy it by DMA without staging.
+bool page_locked(const void* p, size_t bytes) {
+  auto locked = [](const void* q) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+      cudaGetLastError();  // clear the sticky-free error of an unknown pointer
+      return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+  };
+  return bytes && locked(p) && locked(static_cast<const char*>(p) + bytes - 1);
+}
+
 struct Pinned {
   void* p = nullptr;
   size_t n = 0;
@@ -483,12 +497,16 @@ static int session_run_rows(llambda_cuda_session* s, int expert, const float* in
       throw Failure("Expert index " + std::to_string(expert) + " is out of range for a tensor with " +
                     std::to_string(s->ne2) + " experts.");
     const size_t in_bytes = tokens * s->ne0 * 4, out_bytes = tokens * s->ne1 * 4;
-    float* hin = static_cast<float*>(s->hin.get(in_bytes));
-    float* hout = static_cast<float*>(s->hout.get(out_bytes));
+    // page-locked caller buffers are copied directly, pageable ones staged
+    const bool direct_in = page_locked(input, in_bytes), direct_out = page_locked(output, out_bytes);
+    float* hin = direct_in ? nullptr : static_cast<float*>(s->hin.get(in_bytes));
+    float* hout = direct_out ? output : static_cast<float*>(s->hout.get(out_bytes));
     float* din = static_cast<float*>(s->din.get(in_bytes));
     float* dout = static_cast<float*>(s->dout.get(out_bytes));
-    std::memcpy(hin, input, in_bytes);
-    cuda_check(cudaMemcpyAsync(din, hin, in_bytes, cudaMemcpyHostToDevice, s->stream), "input copy");
+    if (!direct_in) std::memcpy(hin, input, in_bytes);
+    cuda_check(cudaMemcpyAsync(din, direct_in ? input : hin, in_bytes, cudaMemcpyHostToDevice,
+                               s->stream),
+               "input copy");
     const uint8_t* W = static_cast<const uint8_t*>(s->weights) + (size_t)expert * s->ne1 * s->rb;
     session_launch(s, W, din, tokens, dout, s->stream);
     int status = 0;
@@ -501,7 +519,7 @@ static int session_run_rows(llambda_cuda_session* s, int expert, const float* in
       throw Failure("A GEMV shared-memory stage wait timed out (device status " +
                     std::to_string(status) + ").");
     }
-    std::memcpy(output, hout, out_bytes);
+    if (!direct_out) std::memcpy(output, hout, out_bytes);
     return 0;
   });
 }
@@ -783,20 +801,32 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
     float* dx = static_cast<float*>(s->dx.get(xb));
     float* dout = static_cast<float*>(s->dout.get(xb));
     int* hstatus = static_cast<int*>(s->hstatus.get(4));
-    std::memcpy(hx, x, xb);
+    // Page-locked caller buffers are copied to and from directly (DMA, no
+    // staging memcpy), outside the cached graph, which then holds the
+    // layer's kernels only; pageable ones go through the session's staging.
+    const bool direct = page_locked(x, xb) && page_locked(out, xb);
+    if (!direct) std::memcpy(hx, x, xb);
     auto enqueue = [&]() {
       cuda_check(cudaMemsetAsync(s->w.status, 0, 4, s->stream), "memset");
-      cuda_check(cudaMemcpyAsync(dx, hx, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
+      if (!direct)
+        cuda_check(cudaMemcpyAsync(dx, hx, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
       cuda_check(lb::launch_moe(s->m, s->w, dx, T, dout, &s->maps, s->stream,
                                 s->timing ? s->marks : nullptr),
                  "MoE launch");
-      cuda_check(cudaMemcpyAsync(hout, dout, xb, cudaMemcpyDeviceToHost, s->stream),
-                 "output copy");
+      if (!direct)
+        cuda_check(cudaMemcpyAsync(hout, dout, xb, cudaMemcpyDeviceToHost, s->stream),
+                   "output copy");
       cuda_check(cudaMemcpyAsync(hstatus, s->w.status, 4, cudaMemcpyDeviceToHost, s->stream),
                  "copy");
     };
-    const bool same = s->graph && s->graph_tokens == T && s->graph_key[0] == hx &&
-                      s->graph_key[1] == hout && s->graph_prefill_min == lb::prefill_min_tokens();
+    // graph key: the staging buffers, or a tag for the kernels-only graph
+    static const char kDirectTag = 0;
+    const void* key0 = direct ? static_cast<const void*>(&kDirectTag) : hx;
+    const void* key1 = direct ? static_cast<const void*>(&kDirectTag) : hout;
+    if (direct)
+      cuda_check(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, s->stream), "input copy");
+    const bool same = s->graph && s->graph_tokens == T && s->graph_key[0] == key0 &&
+                      s->graph_key[1] == key1 && s->graph_prefill_min == lb::prefill_min_tokens();
     if (s->timing || selected || weights || (!same && s->eager_tokens != T)) {
       enqueue();  // timed or checked calls, and a new token count's first call
       s->eager_tokens = T;
@@ -818,12 +848,15 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
         cudaGraphDestroy(g);
         cuda_check(ie, "graph instantiate");
         s->graph_tokens = T;
-        s->graph_key[0] = hx;
-        s->graph_key[1] = hout;
+        s->graph_key[0] = key0;
+        s->graph_key[1] = key1;
         s->graph_prefill_min = lb::prefill_min_tokens();
       }
       cuda_check(cudaGraphLaunch(s->graph, s->stream), "graph launch");
     }
+    if (direct)
+      cuda_check(cudaMemcpyAsync(out, dout, xb, cudaMemcpyDeviceToHost, s->stream),
+                 "output copy");
     int32_t* hsel = selected ? static_cast<int32_t*>(s->hsel.get(sb)) : nullptr;
     float* hw = weights ? static_cast<float*>(s->hw.get(sb)) : nullptr;
     if (hsel)
@@ -832,7 +865,7 @@ int llambda_cuda_moe_session_run(llambda_cuda_moe_session* s, const float* x, si
     cuda_check(cudaStreamSynchronize(s->stream), "MoE layer");
     if (*hstatus)
       throw Failure("MoE router produced non-positive top-k weight sum.");
-    std::memcpy(out, hout, xb);
+    if (!direct) std::memcpy(out, hout, xb);
     if (hsel) std::memcpy(selected, hsel, sb);
     if (hw) std::memcpy(weights, hw, sb);
     return 0;

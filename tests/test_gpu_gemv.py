@@ -180,3 +180,19 @@ def test_block32_rejects_fp16_specials():
     blk[0:2] = np.frombuffer(np.array([np.nan], np.float16).tobytes(), np.uint8)
     with pytest.raises(LB.LlambdaCudaError, match="Inf/NaN"):
         LB.ProjectionSession.from_tensor(LB.TYPE_Q8_0, 32, 1, blk)
+
+
+def test_page_locked_buffers_match_pageable():
+    """Page-locked input/output buffers are copied by DMA without staging;
+    results equal the pageable path's."""
+    import torch
+    t, K, rows = LB.TYPE_Q4_K, 2048, 96
+    w = host_tensor(t, K, rows, 1, 3, 11, CF.Q4K_DSCALE)
+    x = np.random.default_rng(3).standard_normal((3, K)).astype(np.float32)
+    s = LB.ProjectionSession.from_tensor(t, K, rows, w)
+    want = s.run_batch(x)
+    xp = torch.from_numpy(x.copy()).pin_memory()
+    out = torch.empty((3, rows), dtype=torch.float32, pin_memory=True)
+    LB._native._check(LB.lib().llambda_cuda_session_run_batch(
+        s._h, LB._native._fptr(xp.numpy()), 3, LB._native._fptr(out.numpy())))
+    assert np.array_equal(out.numpy(), want)

@@ -213,3 +213,22 @@ def test_config4_full_layer(tokens, decode_kernels_only):
     same = np.all(sel == sel_ref, axis=1)
     assert max_rel(out[same], ref[same]) < MAX_REL
     assert max_rel(out[same], ref[same]) < 1e-5
+
+
+def test_page_locked_host_buffers_are_copied_directly():
+    """Page-locked caller buffers skip the staging copies (DMA straight from
+    and into them); the bytes equal those of pageable buffers, on repeated
+    calls (the second one replays a captured graph) and alternating outputs."""
+    import torch
+    cfg = SMALL_QWEN
+    tensors = host_layer(cfg, seed=9)
+    x = O.synth_f32(9, CF.S_ACT, 0, 7 * cfg.hidden, 1.0).reshape(7, cfg.hidden)
+    s = _session(cfg, tensors, max_tokens=8)
+    want = s.run(x)
+    xp = torch.from_numpy(x.copy()).pin_memory()
+    outs = [torch.empty(x.shape, dtype=torch.float32, pin_memory=True) for _ in range(2)]
+    for i in range(4):
+        got = s.run_into(outs[i % 2].numpy(), xp.numpy())
+        assert np.array_equal(got, want)
+    assert s.status() == 0
+    s.close()
