@@ -232,3 +232,41 @@ def test_page_locked_host_buffers_are_copied_directly():
         assert np.array_equal(got, want)
     assert s.status() == 0
     s.close()
+
+
+@pytest.mark.parametrize("arch", [0, 1], ids=["qwen3next_dense", "nemotron_dense"])
+@pytest.mark.parametrize("tokens", [1, 5, 130])
+def test_dense_ffn_as_one_expert(arch, tokens):
+    """A dense FFN (qwen3next-dense-ffn-into, L5294-5319: down(silu(gate x) * up x);
+    nemotron: down(relu(up x)^2)) through the MoE session as one expert with top-1:
+    its routing weight normalises to exactly 1 (sigmoid(l) / sigmoid(l)), so the
+    layer output is the dense FFN.  fp32 path up to 129 tokens; 130 tokens take
+    the bf16 prefill path (tolerance 2e-2)."""
+    H, I = 1024, 512
+    rng_seed = 40 + arch
+    tensors = {
+        "ffn_gate_inp": (O.TYPE_F32, H, 1, 1, O.synth_f32(rng_seed, 1, 0, H, 0.02)),
+        "ffn_up_exps": (LB.TYPE_Q4_K, H, I, 1, O.synth_q4k(rng_seed, 2, 0, H * I // 256, CF.Q4K_DSCALE)),
+        "ffn_down_exps": (LB.TYPE_Q6_K, I, H, 1, O.synth_q6k(rng_seed, 3, 0, I * H // 256, CF.Q6K_DSCALE)),
+    }
+    if arch == 0:
+        tensors["ffn_gate_exps"] = (LB.TYPE_Q4_K, H, I, 1,
+                                    O.synth_q4k(rng_seed, 4, 0, H * I // 256, CF.Q4K_DSCALE))
+    x = O.synth_f32(rng_seed, CF.S_ACT, 0, tokens * H, 1.0).reshape(tokens, H)
+    ref = np.empty_like(x)
+    for t in range(tokens):
+        up = O.gemv(LB.TYPE_Q4_K, tensors["ffn_up_exps"][4], H, I, x[t])
+        if arch == 0:
+            gate = O.gemv(LB.TYPE_Q4_K, tensors["ffn_gate_exps"][4], H, I, x[t])
+            h = np.array([np.float32(O.silu(float(g))) * np.float32(u) for g, u in zip(gate, up)],
+                         np.float32)
+        else:
+            h = np.array([O.relu_squared(float(u)) for u in up], np.float32)
+        ref[t] = O.gemv(LB.TYPE_Q6_K, tensors["ffn_down_exps"][4], I, H, h)
+    s = LB.MoeSession.create(arch, H, 1, gpu_tensors(tensors), weights_norm=True,
+                             max_tokens=max(64, tokens))
+    out = s.run(x)
+    assert s.status() == 0
+    s.close()
+    tol = 2e-2 if tokens >= LB.prefill_min_tokens() else 1e-5
+    assert max_rel(out, ref) < tol
