@@ -226,6 +226,36 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_sess
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_kernel_ms(llambda_cuda_moe_session* session,
                                                         float* gate_up_ms, float* down_ms);
 
+/* GGUF files (replaces the ONNX export/cache of the reference's bridge,
+ * llambda.lisp L402-476 / L2976-3067, with the raw blocks themselves).
+ * llambda_cuda_gguf_open maps and parses a file as the reference loader does
+ * (read-gguf-header, L2049-2062; read-gguf-metadata-section, L2064-2084;
+ * read-gguf-tensor-infos, L2157-2238: 1..4 positive dimensions, the data
+ * start aligned to general.alignment, default 32, a power of two, every
+ * tensor inside the file); 0 on success, -1 with last_error otherwise, *out
+ * nulled on entry.  Tensor infos give the type tag, dimensions (ne[4],
+ * unused ones 1), byte size (0 for types the loader does not size) and a host
+ * pointer into the mapping, valid until llambda_cuda_gguf_close.
+ * llambda_cuda_gguf_upload copies the chosen tensors into one device arena
+ * (each 256-byte aligned) and returns its pointer and each tensor's device
+ * pointer, for projection sessions (llambda_cuda_session_create_device) and
+ * MoE descriptors (data_on_device = 1); free it with llambda_cuda_device_free
+ * after the sessions that use it. */
+typedef struct llambda_cuda_gguf llambda_cuda_gguf;
+LLAMBDA_CUDA_API int llambda_cuda_gguf_open(const char* path, llambda_cuda_gguf** out);
+LLAMBDA_CUDA_API void llambda_cuda_gguf_close(llambda_cuda_gguf* gguf);
+LLAMBDA_CUDA_API uint64_t llambda_cuda_gguf_tensor_count(const llambda_cuda_gguf* gguf);
+/* Index of the tensor named `name`, -1 if there is none. */
+LLAMBDA_CUDA_API int64_t llambda_cuda_gguf_find(const llambda_cuda_gguf* gguf, const char* name);
+LLAMBDA_CUDA_API int llambda_cuda_gguf_tensor_info(const llambda_cuda_gguf* gguf, uint64_t index,
+                                                   char* name_out, size_t name_capacity,
+                                                   int* type, uint32_t* n_dims, uint64_t* ne,
+                                                   uint64_t* byte_size, const void** host_data);
+LLAMBDA_CUDA_API int llambda_cuda_gguf_upload(const llambda_cuda_gguf* gguf,
+                                              const uint64_t* indices, size_t count,
+                                              void** device_arena, void** device_ptrs);
+LLAMBDA_CUDA_API int llambda_cuda_device_free(void* device_ptr);
+
 /* Prefill path (a tuning knob with no counterpart in the reference; the
  * reference runs every token through the same per-token code,
  * qwen3next-moe-into L5321-5426 / nemotron-h-moe-ffn-into L5827-5949).

@@ -8,12 +8,13 @@ mirror of llambda's accelerator-backend descriptor protocol.
 """
 from ._native import (ARCH_NEMOTRON_H_MOE, ARCH_QWEN3NEXT, TYPE_F32, TYPE_Q4_K,  # noqa: F401
                       TYPE_Q5_0, TYPE_Q6_K, TYPE_Q8_0, LlambdaCudaError, MoeSession,
-                      ProjectionSession, bridge_version,
+                      GgufFile, ProjectionSession, bridge_version, device_free,
                       lib, prefill_min_tokens, probe, row_bytes, runtime_version,
                       set_prefill_min_tokens, sha256, synth_fill_device)
 
 __all__ = ["ARCH_NEMOTRON_H_MOE", "ARCH_QWEN3NEXT", "TYPE_F32", "TYPE_Q4_K", "TYPE_Q5_0",
            "TYPE_Q6_K", "TYPE_Q8_0",
-           "LlambdaCudaError", "MoeSession", "ProjectionSession", "bridge_version", "lib",
+           "GgufFile", "LlambdaCudaError", "MoeSession", "ProjectionSession", "bridge_version",
+           "device_free", "lib",
            "prefill_min_tokens", "set_prefill_min_tokens",
            "probe", "row_bytes", "runtime_version", "sha256", "synth_fill_device"]

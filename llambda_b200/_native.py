@@ -90,6 +90,16 @@ SIGNATURES = {
     "llambda_cuda_moe_session_time_kernels": (C.c_int, [_vp, C.c_int]),
     "llambda_cuda_moe_session_kernel_ms": (C.c_int, [_vp, C.POINTER(C.c_float),
                                                       C.POINTER(C.c_float)]),
+    "llambda_cuda_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
+    "llambda_cuda_gguf_close": (None, [_vp]),
+    "llambda_cuda_gguf_tensor_count": (_u64, [_vp]),
+    "llambda_cuda_gguf_find": (C.c_int64, [_vp, C.c_char_p]),
+    "llambda_cuda_gguf_tensor_info": (C.c_int, [_vp, _u64, C.c_char_p, _sz, C.POINTER(C.c_int),
+                                               C.POINTER(C.c_uint32), C.POINTER(_u64),
+                                               C.POINTER(_u64), C.POINTER(_vp)]),
+    "llambda_cuda_gguf_upload": (C.c_int, [_vp, C.POINTER(_u64), _sz, C.POINTER(_vp),
+                                          C.POINTER(_vp)]),
+    "llambda_cuda_device_free": (C.c_int, [_vp]),
     "llambda_cuda_set_prefill_min_tokens": (C.c_int, [C.c_int]),
     "llambda_cuda_prefill_min_tokens": (C.c_int, []),
     "llambda_cuda_moe_peer_bytes": (_sz, [_vp, C.c_int]),
@@ -165,8 +175,9 @@ def sha256(data: bytes | np.ndarray) -> str:
 
 
 def _dev_ptr(t) -> int:
-    """Device pointer of a CUDA torch tensor (torch is only plumbing here)."""
-    return int(t.data_ptr())
+    """Device pointer of a CUDA torch tensor (torch is only plumbing here), or
+    a device address given as an int (e.g. from GgufFile.upload)."""
+    return int(t) if isinstance(t, int) else int(t.data_ptr())
 
 
 def _stream_ptr(stream) -> int | None:
@@ -401,3 +412,60 @@ def set_prefill_min_tokens(tokens: int) -> None:
 
 def prefill_min_tokens() -> int:
     return int(lib().llambda_cuda_prefill_min_tokens())
+
+
+class GgufFile:
+    """A mapped, parsed GGUF file (llambda_cuda_gguf_open): tensor infos by
+    name, host views of their raw bytes, and upload into a device arena."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        _check(lib().llambda_cuda_gguf_open(os.fsencode(path), C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().llambda_cuda_gguf_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        return int(lib().llambda_cuda_gguf_tensor_count(self._h))
+
+    def find(self, name: str) -> int:
+        return int(lib().llambda_cuda_gguf_find(self._h, name.encode()))
+
+    def info(self, index: int) -> dict:
+        name = C.create_string_buffer(4096)
+        t, nd = C.c_int(), C.c_uint32()
+        ne = (_u64 * 4)()
+        nb = _u64()
+        ptr = _vp()
+        _check(lib().llambda_cuda_gguf_tensor_info(self._h, index, name, 4096, C.byref(t),
+                                                   C.byref(nd), ne, C.byref(nb), C.byref(ptr)))
+        return {"name": name.value.decode(), "type": t.value, "dims": list(ne)[: nd.value],
+                "ne": list(ne), "byte_size": nb.value, "host_ptr": ptr.value}
+
+    def host_bytes(self, index: int) -> np.ndarray:
+        """The tensor's raw bytes (a copy out of the mapping)."""
+        i = self.info(index)
+        buf = (C.c_uint8 * i["byte_size"]).from_address(i["host_ptr"])
+        return np.frombuffer(buf, np.uint8).copy()
+
+    def upload(self, indices) -> tuple[int, list[int]]:
+        """(device arena, device pointer of each tensor); free the arena with
+        device_free once no session uses it."""
+        idx = (_u64 * len(indices))(*indices)
+        ptrs = (_vp * len(indices))()
+        arena = _vp()
+        _check(lib().llambda_cuda_gguf_upload(self._h, idx, len(indices), C.byref(arena), ptrs))
+        return arena.value, [p or 0 for p in ptrs]
+
+
+def device_free(ptr: int) -> None:
+    _check(lib().llambda_cuda_device_free(_vp(ptr)))

@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libllambda_cuda.so")
 
-CU_SOURCES = ["gemv.cu", "moe.cu", "prefill.cu", "capi.cu"]
+CU_SOURCES = ["gemv.cu", "moe.cu", "prefill.cu", "gguf.cu", "capi.cu"]
 C_SOURCES = ["sha256.c"]
 HEADERS = ["common.cuh", "engine.cuh", "kernels.h", "synth.h"]
 

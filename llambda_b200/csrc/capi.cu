@@ -1184,3 +1184,6 @@ int llambda_cuda_synth_fill_device(int type, uint64_t seed, uint64_t stream_id, 
 }
 
 }  // extern "C"
+
+// The GGUF loader (gguf.cu) reports through the same thread-local last error.
+void llambda_cuda_set_last_error(const std::string& message) { set_error(message); }
