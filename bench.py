@@ -71,6 +71,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--arch", default="qwen3next", choices=["qwen3next", "nemotron_h_moe"],
+                   help="layer of the stack: qwen3next (config 3 / 5, the headline) or "
+                        "nemotron_h_moe (config 4)")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -402,7 +405,7 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     if LB.probe() != 1:
         raise SystemExit("CUDA backend unavailable: " + LB._native.last_error())
-    cfg = CF.CONFIG3
+    cfg = CF.CONFIG3 if args.arch == "qwen3next" else CF.CONFIG4
     B, NL = args.batch, args.layers
     t_setup = time.time()
     peer = world > 1 and args.reduce == "peer"
@@ -518,15 +521,18 @@ def run_ours(args):
     layer_gbs = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
     prefill = B >= LB.prefill_min_tokens()
     if prefill:
-        gu_name = "pf_gemm_kernel<Q4_K, gate+up> (tcgen05 bf16 grouped GEMM, routed + shared)"
+        gu_name = ("pf_gemm_kernel<Q4_K, gate+up> (tcgen05 bf16 grouped GEMM, routed + shared)"
+                   if cfg.has_gate else
+                   "pf_gemm_kernel<Q4_K, up> (tcgen05 bf16 grouped GEMM, routed + shared)")
         dn_name = "pf_gemm_kernel<Q6_K, down> (tcgen05 bf16 grouped GEMM, routed + shared)"
-        gu_traffic = PF_GATE_UP_TRAFFIC_BYTES.get(B) if world == 1 else None
-        dn_traffic = PF_DOWN_TRAFFIC_BYTES.get(B) if world == 1 else None
+        gu_traffic = PF_GATE_UP_TRAFFIC_BYTES.get(B) if world == 1 and cfg is CF.CONFIG3 else None
+        dn_traffic = PF_DOWN_TRAFFIC_BYTES.get(B) if world == 1 and cfg is CF.CONFIG3 else None
     else:
-        gu_name = "moe_up_slab_kernel (gate/up pass, Q4_K)"
+        gu_name = ("moe_up_slab_kernel (gate/up pass, Q4_K)" if cfg.has_gate
+                   else "moe_up_slab_kernel (up pass, Q4_K)")
         dn_name = "moe_down_slab_kernel (routed, Q6_K)"
-        gu_traffic = GATE_UP_TRAFFIC_BYTES_N1 if world == 1 else None
-        dn_traffic = DOWN_TRAFFIC_BYTES_N1 if world == 1 else None
+        gu_traffic = GATE_UP_TRAFFIC_BYTES_N1 if world == 1 and cfg is CF.CONFIG3 else None
+        dn_traffic = DOWN_TRAFFIC_BYTES_N1 if world == 1 and cfg is CF.CONFIG3 else None
     roofline = {"bound": "hbm", "kernel": gu_name,
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
@@ -610,7 +616,9 @@ def run_ours(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16" if prefill else "f32", "data": "synthetic",
-            "config": {"workload": f"config5_qwen3next_moe_stack_{NL}L_{phase}_b{B}",
+            "config": {"workload": (f"config5_qwen3next_moe_stack_{NL}L_{phase}_b{B}"
+                                    if cfg is CF.CONFIG3 else
+                                    f"config4_nemotron_h_moe_stack_{NL}L_{phase}_b{B}"),
                        "batch": B, "layers": NL, "experts": cfg.experts, "top_k": cfg.top_k,
                        "hidden": cfg.hidden,
                        "parallelism": f"ep{world}" + ("-peer" if peer else "-nccl" if world > 1 else ""),
