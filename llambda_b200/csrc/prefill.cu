@@ -80,8 +80,10 @@ constexpr int kPfRouterSlices = 8;               // most K slices of the router 
 __host__ __device__ constexpr int pf_block_bytes(int wt) { return wt == LB_TYPE_Q4_K ? LB_Q4K : LB_Q6K; }
 // Bytes of one staged row (the inner box of the weights' tensor map): a Q4_K
 // super-block (144 bytes, always 16-byte aligned), or a Q6_K super-block with
-// the 0-14 bytes before it down to a 16-byte boundary (210 + 14 = 224).
-__host__ __device__ constexpr int pf_pitch(int wt) { return wt == LB_TYPE_Q4_K ? LB_Q4K : 224; }
+// the 0-14 bytes before it down to a 16-byte boundary (210 + 14 = 224),
+// rounded to 240: a 60-word row pitch puts a warp's rows on 8 distinct banks
+// (a 56-word pitch on 4: 8-way conflicts on every decode load).
+__host__ __device__ constexpr int pf_pitch(int wt) { return wt == LB_TYPE_Q4_K ? LB_Q4K : 240; }
 __host__ __device__ constexpr uint32_t pf_wstage(int wt, int nmat) {
   return (uint32_t)(nmat * kPfM * pf_pitch(wt));
 }
