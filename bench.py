@@ -57,8 +57,8 @@ GATE_UP_TRAFFIC_BYTES_N1 = 279_900_000
 DOWN_TRAFFIC_BYTES_N1 = 202_500_000
 # the same for the prefill path's tcgen05 GEMM launches at batch 2048 (ncu,
 # 2-layer capture of the same workload: DRAM read + write of one launch)
-PF_GATE_UP_TRAFFIC_BYTES = {2048: 719_800_000}
-PF_DOWN_TRAFFIC_BYTES = {2048: 616_200_000}
+PF_GATE_UP_TRAFFIC_BYTES = {2048: 719_400_000}
+PF_DOWN_TRAFFIC_BYTES = {2048: 614_700_000}
 # the same for one dense GEMV launch (workload, tokens)
 DENSE_TRAFFIC_BYTES = {("config1", 1): 33_100_000, ("config2", 1): 438_600_000,
                        ("config2", 8): 444_700_000}
