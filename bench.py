@@ -71,6 +71,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--prefill-min", type=int, default=0,
+                   help="batch size from which MoE calls take the tcgen05 prefill path "
+                        "(0: the library default)")
     p.add_argument("--arch", default="qwen3next", choices=["qwen3next", "nemotron_h_moe"],
                    help="layer of the stack: qwen3next (config 3 / 5, the headline) or "
                         "nemotron_h_moe (config 4)")
@@ -406,6 +409,8 @@ def run_ours(args):
     if LB.probe() != 1:
         raise SystemExit("CUDA backend unavailable: " + LB._native.last_error())
     cfg = CF.CONFIG3 if args.arch == "qwen3next" else CF.CONFIG4
+    if args.prefill_min:
+        LB.set_prefill_min_tokens(args.prefill_min)
     B, NL = args.batch, args.layers
     t_setup = time.time()
     peer = world > 1 and args.reduce == "peer"
