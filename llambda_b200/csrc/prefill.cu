@@ -242,14 +242,20 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// N little-endian words from a 2-byte-aligned shared-memory address: N + 1
-// aligned loads and a funnel shift each (the word after the run is read; the
-// callers' runs end at least 4 bytes before the end of the staged row).
+// N little-endian words from a 2-byte-aligned shared-memory address: N loads
+// when it is word-aligned, else N + 1 aligned loads and a funnel shift each
+// (the word after the run is read; the callers' runs end at least 4 bytes
+// before the end of the staged row).
 template <int N>
 __device__ __forceinline__ void lds_run(const uint8_t* p, uint32_t* out) {
   const uint32_t a = smem_addr(p);
-  const uint32_t s = (a & 3u) * 8u;
   const uint32_t* w = reinterpret_cast<const uint32_t*>(p - (a & 3u));
+  if ((a & 3u) == 0) {  // word-aligned run (warp-uniform for the prefill's staged rows)
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = w[i];
+    return;
+  }
+  const uint32_t s = (a & 3u) * 8u;
   uint32_t v[N + 1];
 #pragma unroll
   for (int i = 0; i <= N; ++i) v[i] = w[i];
