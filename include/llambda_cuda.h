@@ -225,6 +225,12 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_sess
                                                            int enable);
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_kernel_ms(llambda_cuda_moe_session* session,
                                                         float* gate_up_ms, float* down_ms);
+/* The stages of the last timed run, in milliseconds, into ms[0..n): router
+ * and top-k, gate/up pass, routed down pass, shared down pass, combine
+ * (with the expert-parallel exchange).  Returns the number written (at most
+ * 5), -1 on failure.  No counterpart in the reference (a measurement aid). */
+LLAMBDA_CUDA_API int llambda_cuda_moe_session_kernel_breakdown(llambda_cuda_moe_session* session,
+                                                               float* ms, int n);
 
 /* GGUF files (replaces the ONNX export/cache of the reference's bridge,
  * llambda.lisp L402-476 / L2976-3067, with the raw blocks themselves).
@@ -315,12 +321,16 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_sess
  * zero, but two calls that overlap on the GPU (different streams, threads or
  * devices sharing a context) race on it, so serialise them.
  *
- * The first call on each device looks up the array's device address with
- * that device current; make that first call before any stream capture.  The
- * call enqueues on `cuda_stream`, then waits for it, and returns -1 (message
- * in last_error) when a token's top-k weight sum is not positive, like
- * llambda_cuda_moe_session_run.  Inf/NaN fp16 scales are not checked here
- * (sessions check them at creation). */
+ * The first call on each device checks that the device is sm_100 and looks
+ * up the array's device address with that device current; make that first
+ * call before any stream capture.  Every call enqueues on `cuda_stream`, then
+ * waits for that stream before it returns, also when it fails part-way (so
+ * no kernel of a failed call still writes the array afterwards), and
+ * returns -1 (message in last_error) when a token's top-k weight sum is not
+ * positive, like llambda_cuda_moe_session_run.  Batches of at least
+ * llambda_cuda_prefill_min_tokens() tokens take the bf16 prefill path here
+ * too, as long as their working set fits the array.  Inf/NaN fp16 scales are
+ * not checked here (sessions check them at creation). */
 #define LLAMBDA_CUDA_STATIC_SCRATCH_BYTES (16u << 20)
 LLAMBDA_CUDA_API int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
                                                              const float* device_x,

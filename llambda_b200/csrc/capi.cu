@@ -267,7 +267,8 @@ struct llambda_cuda_moe_session {
   void* work = nullptr;
   Pinned hx, hout, hsel, hw;
   DevBuf dx, dout, dsel, dw;
-  cudaEvent_t marks[3] = {nullptr, nullptr, nullptr};  // kernel timing, when enabled
+  // kernel timing, when enabled (launch_moe's six marks)
+  cudaEvent_t marks[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   bool timing = false;
   // The host-buffer call (copies in, the layer's kernels, copies out, status)
   // as one CUDA graph, captured for one token count and replayed while the
@@ -940,6 +941,27 @@ int llambda_cuda_moe_session_kernel_ms(llambda_cuda_moe_session* s, float* gate_
   });
 }
 
+int llambda_cuda_moe_session_kernel_breakdown(llambda_cuda_moe_session* s, float* ms, int n) {
+  if (!s || !ms || n < 1) {
+    set_error("A session and an output array are required.");
+    return -1;
+  }
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    if (!s->timing) throw Failure("Kernel timing is not enabled on this session.");
+    cuda_check(cudaEventSynchronize(s->marks[5]), "timing events");
+    // marks: 3 layer start, 0 gate/up start, 1 gate/up end, 2 routed down end,
+    // 4 combine start, 5 layer end
+    const int order[6] = {3, 0, 1, 2, 4, 5};
+    const int parts = std::min(n, 5);
+    for (int i = 0; i < parts; ++i)
+      cuda_check(cudaEventElapsedTime(&ms[i], s->marks[order[i]], s->marks[order[i + 1]]),
+                 "stage time");
+    return parts;
+  });
+}
+
 int llambda_cuda_moe_session_status(llambda_cuda_moe_session* s) {
   if (!s) {
     set_error("A session is required.");
@@ -1019,6 +1041,9 @@ void* static_scratch_address(int dev) {
   if (dev < 0 || dev >= kMaxScratchDevices) throw Failure("device index out of range");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (!g_scratch_addr[dev]) {
+    // the first call on a device: refuse anything but sm_100 with the
+    // library's own message, before any launch
+    require_b200(dev);
     void* p = nullptr;
     cuda_check(cudaGetSymbolAddress(&p, g_moe_static_scratch), "cudaGetSymbolAddress");
     if (!p) throw Failure("cudaGetSymbolAddress returned a null scratch address");
@@ -1145,7 +1170,8 @@ int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
   }
   return guarded([&] {
     const lb::MoeDevice m = static_layer(desc);
-    if ((int64_t)tokens * m.top_k > 65536)
+    // bound checked in unsigned arithmetic before any narrowing (top_k >= 1)
+    if (tokens > 65536u / (size_t)m.top_k)
       throw Failure("tokens * top_k must be at most 65536.");
     const int T = (int)tokens;
     const size_t need = lb::moe_work_bytes(m, T);
@@ -1159,10 +1185,17 @@ int llambda_cuda_moe_forward_static_scratch(const llambda_cuda_moe_desc* desc,
     lb::moe_work_carve(m, T, base, &w);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     int status = 0;
-    cuda_check(cudaMemsetAsync(w.status, 0, 2 * sizeof(int), st), "clear status and ticket");
-    cuda_check(lb::launch_moe(m, w, device_x, T, device_out, nullptr, st), "MoE launch");
-    cuda_check(cudaMemcpyAsync(&status, w.status, sizeof(int), cudaMemcpyDeviceToHost, st),
-               "status copy");
+    // A launch that fails part-way leaves earlier kernels of this call
+    // writing the shared array: wait for them before reporting, so that the
+    // caller's next call (on any stream) does not race with them.
+    auto drained = [&](cudaError_t e, const char* what) {
+      if (e != cudaSuccess) cudaStreamSynchronize(st);
+      cuda_check(e, what);
+    };
+    drained(cudaMemsetAsync(w.status, 0, 2 * sizeof(int), st), "clear status and ticket");
+    drained(lb::launch_moe(m, w, device_x, T, device_out, nullptr, st), "MoE launch");
+    drained(cudaMemcpyAsync(&status, w.status, sizeof(int), cudaMemcpyDeviceToHost, st),
+            "status copy");
     cuda_check(cudaStreamSynchronize(st), "MoE layer");
     if (status) throw Failure("MoE router produced non-positive top-k weight sum.");
     return 0;
