@@ -24,6 +24,16 @@ Reported:
                 shared expert's) / its duration from CUDA events the sessions
                 record around it on the launch stream, against the measured
                 HBM peak; the routed down pass and the whole layer beside it
+  parity        layer 0's output of the measured run against a reference on
+                the same bytes: the CPU oracle at N=1 (inside the CPU leg),
+                a single-device session of the whole layer at N>1
+  ep_breakdown  per-layer stage times (router + top-k, gate/up, routed down,
+                shared down, combine with the cross-rank exchange), eager
+                launches with events between the stages, rank 0 and max over
+                ranks
+  extra         the other north-star workloads at the same N, each with
+                value, e2e, rooflines and parity: config-5 decode batch 1,
+                config-5 prefill batch 2048, config-4 decode batch 64
   kernels       dense dequant-GEMV roofline (configs 1 and 2) timed alone
   cpu_baseline  the CPU oracle (a C restatement of the reference path, AVX2,
                 all host threads) on a bounded sample, rank 0 only
@@ -82,6 +92,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-kernels", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the extra workloads (decode b1, prefill b2048, config-4 b64)")
     p.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
                    help="N > 1: sum the ranks' partial outputs in the combine kernel over "
                         "peer memory, or with an NCCL all-reduce per layer")
@@ -248,39 +260,6 @@ class _ShiftedPtr:
         return self.buf.data_ptr() + self.offset
 
 
-def distinct_experts(sel: np.ndarray, E: int) -> int:
-    return int(np.unique(sel[sel >= 0]).size)
-
-
-# ----------------------------------------------------------------- CPU side
-
-def cpu_layer_sample(cfg, seed, tokens):
-    """One host layer (oracle generator) and a timed CPU forward of `tokens`."""
-    from oracle import oracle as O
-    from tests.helpers import host_layer, oracle_layer
-    tensors = host_layer(cfg, seed)
-    L = oracle_layer(cfg, tensors, input_norm=np.ones(cfg.hidden, np.float32), eps=1e-6,
-                     residual=True)
-    x = O.synth_f32(seed, 1, 0, tokens * cfg.hidden, 1.0).reshape(tokens, cfg.hidden)
-    return O, L, x, tensors
-
-
-def time_cpu_stack(cfg, layers, batch, seed, steps, warmup):
-    """Seconds per layer for `batch` tokens through one layer on all host cores."""
-    O, L, x, keep = cpu_layer_sample(cfg, seed, batch)
-    O.set_workers(os.cpu_count() or 1)
-    for _ in range(warmup):
-        O.moe_forward(L, x, batch, cfg.top_k)
-    ts = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        O.moe_forward(L, x, batch, cfg.top_k)
-        ts.append(time.perf_counter() - t0)
-    per_layer = statistics.median(ts)
-    tok_s = batch / (per_layer * layers)
-    return tok_s, per_layer
-
-
 # ----------------------------------------------------------------- kernels alone
 
 def fill_block32(torch, buf, type_tag, nblocks, seed, LB):
@@ -335,37 +314,340 @@ def time_dense_gemv(torch, LB, cfg, tokens, reps=20):
             "weight_copies_rotated": copies}
 
 
+_S_ACT = 1  # generator stream of the activations (llambda_b200.configs.S_ACT)
+
+
+# ----------------------------------------------------------------- CPU side
+
+class HostLayer:
+    """Layer 0 of a stack on the host, for the CPU oracle: the oracle's copy
+    of the generator writes the same bytes the device generator wrote.  Used
+    only by the CPU leg (rank 0, N=1) and the reference arm."""
+
+    def __init__(self, cfg, layer_seed):
+        from oracle import oracle as O
+        from oracle.layers import host_layer, oracle_layer
+        self.O, self.cfg = O, cfg
+        self.tensors = host_layer(cfg, layer_seed)
+        self.L = oracle_layer(cfg, self.tensors, input_norm=np.ones(cfg.hidden, np.float32),
+                              eps=1e-6, residual=True)
+
+    def x(self, act_seed, tokens):
+        return self.O.synth_f32(act_seed, _S_ACT, 0, tokens * self.cfg.hidden, 1.0).reshape(
+            tokens, self.cfg.hidden)
+
+    def forward(self, x):
+        return self.O.moe_forward(self.L, x, x.shape[0], self.cfg.top_k)
+
+    def time(self, x, steps, warmup):
+        """Median seconds of one forward of x on all host cores."""
+        self.O.set_workers(os.cpu_count() or 1)
+        for _ in range(warmup):
+            self.forward(x)
+        ts = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            self.forward(x)
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+
+def parity_record(out, sel, ref, sel_ref, against, bar):
+    """max|out - ref| / max|ref| over the checked tokens, and the share of
+    tokens whose selected experts equal the reference's (rank order)."""
+    den = float(np.max(np.abs(ref)))
+    err = float(np.max(np.abs(out.astype(np.float64) - ref))) / (den if den > 0 else 1.0)
+    match = float(np.mean(np.all(sel == sel_ref, axis=1)))
+    return {"against": against, "max_rel": err, "bar": bar, "selection_match": match,
+            "checked_tokens": int(out.shape[0]), "ok": bool(err <= bar and match == 1.0)}
+
+
+# ----------------------------------------------------------------- stack measurement
+
+class Ctx:
+    def __init__(self, args, torch, LB, CF, rank, world, local):
+        self.args, self.torch, self.LB, self.CF = args, torch, LB, CF
+        self.rank, self.world, self.local = rank, world, local
+        self.peer = world > 1 and args.reduce == "peer"
+        self.collective = world > 1 and not self.peer
+
+
+def open_stack(ctx, cfg, max_tokens):
+    t0 = time.time()
+    sessions, keep = build_stack(cfg, ctx.args.layers, ctx.rank, ctx.world, ctx.args.seed,
+                                 max_tokens, ctx.torch, peer=ctx.peer)
+    if ctx.peer:  # each layer's combine sums every rank's partial over NVLink
+        from llambda_b200 import ep
+        keep.append(ep.attach_peer_reduction(sessions))
+    ref0 = None
+    if ctx.world > 1 and ctx.rank == 0:
+        # the whole layer 0 (every expert, shared expert, residual) as one
+        # single-device session: the parity reference of the N > 1 runs
+        r, rkeep = build_stack(cfg, 1, 0, 1, ctx.args.seed, max_tokens, ctx.torch)
+        ref0 = (r[0], rkeep)
+    return sessions, keep, ref0, time.time() - t0
+
+
+def close_stack(ctx, sessions, keep, ref0):
+    for s in sessions:
+        s.close()
+    if ref0 is not None:
+        ref0[0].close()
+    del keep
+    ctx.torch.cuda.synchronize()
+    ctx.torch.cuda.empty_cache()
+
+
+def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
+    """One workload (B tokens through the stack) on every rank: timed steps,
+    stage breakdown, rooflines, layer-0 output, e2e.  Returns rank 0's record
+    (other ranks return theirs too; only rank 0 prints)."""
+    torch, LB, CF, args = ctx.torch, ctx.LB, ctx.CF, ctx.args
+    world, rank, NL = ctx.world, ctx.rank, len(sessions)
+    H = cfg.hidden
+    x0 = torch.empty(B, H, device="cuda")
+    LB.synth_fill_device(LB.TYPE_F32, args.seed, CF.S_ACT, 0, B * H, 1.0, x0)
+    bufs = [torch.empty(B, H, device="cuda") for _ in range(2)]
+    stream = torch.cuda.current_stream()
+    if world > 1:
+        import torch.distributed as dist
+
+    def step(record=None):
+        st = torch.cuda.current_stream()  # the capture stream while a graph records
+        cur = x0
+        for li, s in enumerate(sessions):
+            out = bufs[li % 2]
+            if record is not None:
+                record[li][0].record(st)
+            s.run_device(cur, out, B, stream=st)
+            if ctx.collective:
+                dist.all_reduce(out)
+            if record is not None:
+                record[li][1].record(st)
+            cur = out
+        return cur
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # one CUDA graph replays the whole stack step (not with an NCCL all-reduce
+    # per layer, which stays outside graphs)
+    graph = None
+    if not ctx.collective and not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+    for s in sessions:
+        if s.status() != 0:
+            raise SystemExit("device status reported a failure (weight sum or a bounded wait)")
+    sampler = ClockSampler(ctx.local) if clocks else None
+    if sampler:
+        sampler.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = sampler.stop() if sampler else None
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    value = B / (ms * 1e-3)
+    del graph
+
+    # eager pass with events around every layer and between its stages
+    layer_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(NL)]
+    for s in sessions:
+        s.time_kernels(True)
+    step(layer_ev)
+    torch.cuda.synchronize()
+    layer_ms = [a.elapsed_time(b) for a, b in layer_ev]
+    kern_ms = [s.kernel_ms() for s in sessions]
+    stages = [s.kernel_breakdown() for s in sessions]
+    for s in sessions:
+        s.time_kernels(False)
+    names = ("route", "gate_up", "down", "shared_down", "combine")
+    mean_us = [statistics.mean(st[n] for st in stages) * 1e3 for n in names]
+    mine = torch.tensor(mean_us + [statistics.mean(layer_ms) * 1e3], dtype=torch.float64,
+                        device="cuda")
+    if world > 1:
+        dist.all_reduce(mine, op=dist.ReduceOp.MAX)
+    breakdown = {"rank0_us": {n: round(v, 2) for n, v in zip(names + ("layer",),
+                                                               mean_us + [statistics.mean(layer_ms) * 1e3])},
+                 "max_over_ranks_us": {n: round(v, 2) for n, v in zip(names + ("layer",),
+                                                                      mine.tolist())},
+                 "how": "eager launches, CUDA events between the stages of every layer, "
+                        "mean over layers"}
+
+    # routing of the timed steps (identical every step: same x0) -> algorithmic
+    # bytes; layer 0's output and selection for the parity check
+    sel = torch.empty(B, cfg.top_k, dtype=torch.int32, device="cuda")
+    eb, ee = rank * cfg.experts // world, (rank + 1) * cfg.experts // world
+    distinct, own_distinct = [], []
+    cur, layer0 = x0, None
+    for li, s in enumerate(sessions):
+        out = bufs[li % 2]
+        s.run_device(cur, out, B, sel_dev=sel, stream=stream)
+        if ctx.collective:
+            dist.all_reduce(out)
+        ss = sel.cpu().numpy()
+        distinct.append(int(np.unique(ss[ss >= 0]).size))
+        own_distinct.append(int(np.unique(ss[(ss >= eb) & (ss < ee)]).size))
+        if li == 0:
+            layer0 = (out.cpu().numpy().copy(), ss.copy())
+        cur = out
+    torch.cuda.synchronize()
+    prefill = B >= LB.prefill_min_tokens()
+    parity = None
+    if ref0 is not None:  # N > 1: rank 0 checks against the single-device layer
+        rout = torch.empty(B, H, device="cuda")
+        rsel = torch.empty(B, cfg.top_k, dtype=torch.int32, device="cuda")
+        ref0[0].run_device(x0, rout, B, sel_dev=rsel, stream=stream)
+        torch.cuda.synchronize()
+        parity = parity_record(layer0[0], layer0[1], rout.cpu().numpy().astype(np.float64),
+                               rsel.cpu().numpy(),
+                               f"single-device session of the whole layer 0 (rank 0, "
+                               f"{'bf16 prefill' if prefill else 'fp32 decode'} kernels)",
+                               2e-2 if prefill else 1e-3)
+
+    from llambda_b200 import ep as _ep
+    streams_shared = _ep.layer_roles(rank, world, cfg.experts, ctx.peer)["shared_here"]
+    layer_bytes = [cfg.router_bytes() + (cfg.shared_bytes() if streams_shared else 0)
+                   + u * cfg.expert_bytes() + 2 * 4 * B * H for u in own_distinct]
+    peak, peak_kind = hbm_peak()
+    gu_bytes = [u * cfg.gate_up_bytes() + (cfg.shared_gate_up_bytes() if streams_shared else 0)
+                for u in own_distinct]
+    gu_ms = statistics.mean(k[0] for k in kern_ms)
+    dn_bytes = [u * cfg.down_bytes() for u in own_distinct]
+    dn_ms = statistics.mean(k[1] for k in kern_ms)
+    achieved = (sum(gu_bytes) / NL) / (gu_ms * 1e-3) / 1e9
+    layer_gbs = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
+    n1_q = world == 1 and cfg is CF.CONFIG3
+    if prefill:
+        gu_name = ("pf_gemm_kernel<Q4_K, gate+up> (tcgen05 bf16 grouped GEMM, routed + shared)"
+                   if cfg.has_gate else
+                   "pf_gemm_kernel<Q4_K, up> (tcgen05 bf16 grouped GEMM, routed + shared)")
+        dn_name = "pf_gemm_kernel<Q6_K, down> (tcgen05 bf16 grouped GEMM, routed + shared)"
+        gu_traffic = PF_GATE_UP_TRAFFIC_BYTES.get(B) if n1_q else None
+        dn_traffic = PF_DOWN_TRAFFIC_BYTES.get(B) if n1_q else None
+    else:
+        gu_name = ("moe_up_slab_kernel (gate/up pass, Q4_K)" if cfg.has_gate
+                   else "moe_up_slab_kernel (up pass, Q4_K)")
+        dn_name = "moe_down_slab_kernel (routed, Q6_K)"
+        gu_traffic = GATE_UP_TRAFFIC_BYTES_N1 if n1_q and B == 32 else None
+        dn_traffic = DOWN_TRAFFIC_BYTES_N1 if n1_q and B == 32 else None
+    roofline = {"bound": "hbm", "kernel": gu_name,
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "algorithmic_bytes_per_launch": int(sum(gu_bytes) / NL),
+                "launch_us_mean": round(gu_ms * 1e3, 2),
+                # DRAM read+write bytes of one gate/up launch at N=1 (ncu capture)
+                "traffic": gu_traffic,
+                "down": {"kernel": dn_name,
+                         "achieved": round((sum(dn_bytes) / NL) / (dn_ms * 1e-3) / 1e9, 1),
+                         "frac": round((sum(dn_bytes) / NL) / (dn_ms * 1e-3) / 1e9 / peak, 4),
+                         "launch_us_mean": round(dn_ms * 1e3, 2),
+                         "traffic": dn_traffic},
+                "layer": {"achieved": round(layer_gbs, 1), "frac": round(layer_gbs / peak, 4),
+                          "algorithmic_bytes": int(sum(layer_bytes) / NL),
+                          "us_mean": round(statistics.mean(layer_ms) * 1e3, 2)}}
+
+    e2e = None
+    if e2e_on and not args.no_e2e:
+        # page-locked host buffers (the library copies them by DMA, no staging)
+        pinned = [x0.cpu().pin_memory()] + [torch.empty((B, H), dtype=torch.float32,
+                                                        pin_memory=True) for _ in range(2)]
+        x_host = pinned[0].numpy()
+        gloo = dist.new_group(backend="gloo") if ctx.collective else None
+        host_bufs = [t.numpy() for t in pinned[1:]]  # run-into destinations
+
+        def e2e_step():
+            cur_h = x_host
+            for li, s in enumerate(sessions):
+                out_h = s.run_into(host_bufs[li % 2], cur_h)
+                if ctx.collective:
+                    t = torch.from_numpy(out_h)
+                    dist.all_reduce(t, group=gloo)
+                    out_h = t.numpy()
+                cur_h = out_h
+            return cur_h
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        dt = max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+        e2e = {"value": B / dt, "unit": "tokens/s",
+               "h2d_bytes_per_step": NL * B * H * 4, "d2h_bytes_per_step": NL * B * H * 4,
+               "path": "llambda_cuda_moe_session_run per layer from and into preallocated "
+                       "page-locked host float buffers (the reference's run-into convention)"}
+    # decode: rms-norm + router, top-k with routing, gate/up, routed down, shared
+    # down (ranks that compute a share of the shared expert), combine.
+    # prefill: rms-norm, router K slices, their sum, top-k with routing, gather,
+    # tile plan, gate/up, down, combine.
+    per_layer = 9 if prefill else 5 + (1 if streams_shared else 0)
+    return {"value": value, "ms_per_step": ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
+            "parity": parity, "ep_breakdown": breakdown, "layer0": layer0,
+            "gpu_launches": per_layer * NL * args.steps, "prefill": prefill,
+            "distinct_experts_per_layer_mean": round(statistics.mean(distinct), 1)}
+
+
+def workload_name(cfg, CF, NL, B, prefill):
+    phase = "prefill" if prefill else "decode"
+    if cfg is CF.CONFIG3:
+        return f"config5_qwen3next_moe_stack_{NL}L_{phase}_b{B}"
+    return f"config4_nemotron_h_moe_stack_{NL}L_{phase}_b{B}"
+
+
 # ----------------------------------------------------------------- main arms
 
 def run_reference(args):
-    """--impl reference: the reference CPU path (oracle port) on host cores."""
+    """--impl reference: the reference CPU path (the oracle port) on all host
+    cores.  Each step is a bounded sample: the step's tokens through layer 0
+    of the stack (the 48 layers have the same shape); `value` scales the
+    measured layer time to the whole stack, and ms_per_step is the time each
+    measured step actually took."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     from llambda_b200 import configs as CF
-    cfg = CF.CONFIG3
-    sample_tokens = args.batch
+    cfg = CF.CONFIG3 if args.arch == "qwen3next" else CF.CONFIG4
+    B, NL = args.batch, args.layers
     cores = os.cpu_count() or 1
-    O, L, x, keep = cpu_layer_sample(cfg, args.seed, sample_tokens)
-    O.set_workers(cores)
+    host = HostLayer(cfg, CF.layer_seed(args.seed, 0))
+    x = host.x(args.seed, B)
+    host.O.set_workers(cores)
     for _ in range(max(1, args.warmup)):
-        O.moe_forward(L, x, sample_tokens, cfg.top_k)
+        host.forward(x)
     ts = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.moe_forward(L, x, sample_tokens, cfg.top_k)
+        host.forward(x)
         ts.append(time.perf_counter() - t0)
     per_layer = sum(ts) / len(ts)
-    value = sample_tokens / (per_layer * args.layers)
-    sample = (f"{sample_tokens} decode tokens through 1 of the {args.layers} qwen3next layers per "
-              f"step, time x {args.layers} layers (CPU oracle: C restatement of llambda.lisp "
-              f"L4338-4658/L5321-5426, AVX2+FMA, {cores} OpenMP threads)")
-    line = {"impl": "reference", "metric": "MoE FFN decode tokens/s", "value": value,
-            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": per_layer * args.layers * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"config5_qwen3next_moe_stack_{args.layers}L_decode_b{args.batch}",
-                       "batch": args.batch, "layers": args.layers},
+    value = B / (per_layer * NL)
+    phase = "prefill" if B >= 128 else "decode"
+    sample = (f"{B} {phase} tokens through layer 0 of the {NL}-layer stack per step (all "
+              f"{NL} layers share its shape), layer time x {NL} (CPU oracle: C restatement of "
+              f"llambda.lisp L4338-4658/L5321-5426, AVX2+FMA, {cores} OpenMP threads)")
+    line = {"impl": "reference", "metric": f"MoE FFN {phase} tokens/s", "value": value,
+            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_layer * 1e3, "layers_timed": 1,
+            "stack_ms_per_step": per_layer * NL * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": workload_name(cfg, CF, NL, B, B >= 128), "batch": B,
+                       "layers": NL, "experts": cfg.experts, "top_k": cfg.top_k,
+                       "hidden": cfg.hidden},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -397,6 +679,23 @@ def run_dense(args, torch, LB, CF):
     return 0
 
 
+def compact(rec, cfg, CF, NL, B, peak):
+    """The record of an extra workload inside the main line."""
+    r = rec["roofline"]
+    return {"metric": f"MoE FFN {'prefill' if rec['prefill'] else 'decode'} tokens/s",
+            "workload": workload_name(cfg, CF, NL, B, rec["prefill"]),
+            "value": round(rec["value"], 2), "unit": "tokens/s",
+            "ms_per_step": round(rec["ms_per_step"], 4),
+            "dtype": "bf16" if rec["prefill"] else "f32",
+            "e2e": rec["e2e"],
+            "roofline": {"kernel": r["kernel"], "achieved": r["achieved"], "peak": peak,
+                         "frac": r["frac"], "launch_us_mean": r["launch_us_mean"],
+                         "traffic": r["traffic"], "down": r["down"], "layer": r["layer"]},
+            "parity": rec["parity"], "ep_breakdown": rec["ep_breakdown"],
+            "gpu_launches": rec["gpu_launches"],
+            "distinct_experts_per_layer_mean": rec["distinct_experts_per_layer_mean"]}
+
+
 def run_ours(args):
     import torch
     import llambda_b200 as LB
@@ -408,188 +707,26 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     if LB.probe() != 1:
         raise SystemExit("CUDA backend unavailable: " + LB._native.last_error())
+    ctx = Ctx(args, torch, LB, CF, rank, world, local)
     cfg = CF.CONFIG3 if args.arch == "qwen3next" else CF.CONFIG4
     if args.prefill_min:
         LB.set_prefill_min_tokens(args.prefill_min)
     B, NL = args.batch, args.layers
-    t_setup = time.time()
-    peer = world > 1 and args.reduce == "peer"
-    sessions, keep = build_stack(cfg, NL, rank, world, args.seed, max(B, 1), torch, peer=peer)
-    if peer:  # each layer's combine sums every rank's partial over NVLink
-        from llambda_b200 import ep
-        keep.append(ep.attach_peer_reduction(sessions))
-    collective = world > 1 and not peer
-    setup_s = time.time() - t_setup
-    x0 = torch.empty(B, cfg.hidden, device="cuda")
-    LB.synth_fill_device(LB.TYPE_F32, args.seed, CF.S_ACT, 0, B * cfg.hidden, 1.0, x0)
-    bufs = [torch.empty(B, cfg.hidden, device="cuda") for _ in range(2)]
-    stream = torch.cuda.current_stream()
-    if world > 1:
-        import torch.distributed as dist
-
-    def step(record=None):
-        st = torch.cuda.current_stream()  # the capture stream while a graph records
-        cur = x0
-        for li, s in enumerate(sessions):
-            out = bufs[li % 2]
-            if record is not None:
-                record[li][0].record(st)
-            s.run_device(cur, out, B, stream=st)
-            if collective:
-                dist.all_reduce(out)
-            if record is not None:
-                record[li][1].record(st)
-            cur = out
-        return cur
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    # one CUDA graph replays the whole stack step (not with an NCCL all-reduce
-    # per layer, which stays outside graphs)
-    graph = None
-    if not collective and not args.no_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        graph.replay()
-        torch.cuda.synchronize()
-    for s in sessions:
-        if s.status() != 0:
-            raise SystemExit("device status reported a non-positive router weight sum")
-    layer_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(NL)]
-    sampler = ClockSampler(local)
-    sampler.start()
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for k in range(args.steps):
-        if graph is not None:
-            graph.replay()
-        else:
-            step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    ms = max_over_ranks(ms, world)
-    value = B / (ms * 1e-3)
-    # per-layer times and, from CUDA events the sessions record on the same
-    # stream, the gate/up and routed down kernels of every layer (launched eagerly)
-    for s in sessions:
-        s.time_kernels(True)
-    step(layer_ev)
-    torch.cuda.synchronize()
-    layer_ms = [a.elapsed_time(b) for a, b in layer_ev]
-    kern_ms = [s.kernel_ms() for s in sessions]
-    for s in sessions:
-        s.time_kernels(False)
-
-    # routing of the timed steps (identical every step: same x0) -> algorithmic bytes
-    sel = torch.empty(B, cfg.top_k, dtype=torch.int32, device="cuda")
-    cur = x0
-    distinct = []
-    for li, s in enumerate(sessions):
-        out = bufs[li % 2]
-        s.run_device(cur, out, B, sel_dev=sel, stream=stream)
-        if collective:
-            dist.all_reduce(out)
-        distinct.append(distinct_experts(sel.cpu().numpy(), cfg.experts))
-        cur = out
-    torch.cuda.synchronize()
-    eb, ee = rank * cfg.experts // world, (rank + 1) * cfg.experts // world
-    own_distinct = []
-    cur = x0
-    for li, s in enumerate(sessions):
-        out = bufs[li % 2]
-        s.run_device(cur, out, B, sel_dev=sel, stream=stream)
-        if collective:
-            dist.all_reduce(out)
-        ss = sel.cpu().numpy()
-        own_distinct.append(int(np.unique(ss[(ss >= eb) & (ss < ee)]).size))
-        cur = out
-    from llambda_b200 import ep as _ep
-    streams_shared = _ep.layer_roles(rank, world, cfg.experts, peer)["shared_here"]
-    layer_bytes = [cfg.router_bytes() + (cfg.shared_bytes() if streams_shared else 0)
-                   + u * cfg.expert_bytes() + 2 * 4 * B * cfg.hidden for u in own_distinct]
-    peak, peak_kind = hbm_peak()
-    # the dominant kernel: the gate/up pass (its rows of every distinct routed
-    # expert this rank owns, plus the shared expert's where it runs here)
-    gu_bytes = [u * cfg.gate_up_bytes() + (cfg.shared_gate_up_bytes() if streams_shared else 0)
-                for u in own_distinct]
-    gu_ms = statistics.mean(k[0] for k in kern_ms)
-    dn_bytes = [u * cfg.down_bytes() for u in own_distinct]
-    dn_ms = statistics.mean(k[1] for k in kern_ms)
-    achieved = (sum(gu_bytes) / NL) / (gu_ms * 1e-3) / 1e9
-    layer_gbs = (sum(layer_bytes) / NL) / (statistics.mean(layer_ms) * 1e-3) / 1e9
-    prefill = B >= LB.prefill_min_tokens()
-    if prefill:
-        gu_name = ("pf_gemm_kernel<Q4_K, gate+up> (tcgen05 bf16 grouped GEMM, routed + shared)"
-                   if cfg.has_gate else
-                   "pf_gemm_kernel<Q4_K, up> (tcgen05 bf16 grouped GEMM, routed + shared)")
-        dn_name = "pf_gemm_kernel<Q6_K, down> (tcgen05 bf16 grouped GEMM, routed + shared)"
-        gu_traffic = PF_GATE_UP_TRAFFIC_BYTES.get(B) if world == 1 and cfg is CF.CONFIG3 else None
-        dn_traffic = PF_DOWN_TRAFFIC_BYTES.get(B) if world == 1 and cfg is CF.CONFIG3 else None
-    else:
-        gu_name = ("moe_up_slab_kernel (gate/up pass, Q4_K)" if cfg.has_gate
-                   else "moe_up_slab_kernel (up pass, Q4_K)")
-        dn_name = "moe_down_slab_kernel (routed, Q6_K)"
-        gu_traffic = GATE_UP_TRAFFIC_BYTES_N1 if world == 1 and cfg is CF.CONFIG3 else None
-        dn_traffic = DOWN_TRAFFIC_BYTES_N1 if world == 1 and cfg is CF.CONFIG3 else None
-    roofline = {"bound": "hbm", "kernel": gu_name,
-                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                "algorithmic_bytes_per_launch": int(sum(gu_bytes) / NL),
-                "launch_us_mean": round(gu_ms * 1e3, 2),
-                # DRAM read+write bytes of one gate/up launch at N=1 (ncu capture)
-                "traffic": gu_traffic,
-                "down": {"kernel": dn_name,
-                         "achieved": round((sum(dn_bytes) / NL) / (dn_ms * 1e-3) / 1e9, 1),
-                         "launch_us_mean": round(dn_ms * 1e3, 2),
-                         "traffic": dn_traffic},
-                "layer": {"achieved": round(layer_gbs, 1), "frac": round(layer_gbs / peak, 4),
-                          "algorithmic_bytes": int(sum(layer_bytes) / NL),
-                          "us_mean": round(statistics.mean(layer_ms) * 1e3, 2)}}
-
-    # e2e through the C ABI with host buffers (one call per layer per step)
-    e2e = None
-    if not args.no_e2e:
-        # page-locked host buffers (the library copies them by DMA, no staging)
-        pinned = [x0.cpu().pin_memory()] + [torch.empty(tuple(x0.shape), dtype=torch.float32,
-                                                        pin_memory=True) for _ in range(2)]
-        x_host = pinned[0].numpy()
-        if world > 1:
-            import torch.distributed as dist
-            gloo = dist.new_group(backend="gloo")
-
-        host_bufs = [t.numpy() for t in pinned[1:]]  # run-into destinations
-
-        def e2e_step():
-            cur_h = x_host
-            for li, s in enumerate(sessions):
-                out_h = s.run_into(host_bufs[li % 2], cur_h)
-                if collective:
-                    t = torch.from_numpy(out_h)
-                    dist.all_reduce(t, group=gloo)
-                    out_h = t.numpy()
-                cur_h = out_h
-            return cur_h
-
-        for _ in range(max(1, args.warmup)):
-            e2e_step()
-        barrier(world)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            e2e_step()
-        dt = (time.perf_counter() - t0) / args.steps
-        dt = max_over_ranks(dt, world)
-        e2e = {"value": B / dt, "unit": "tokens/s",
-               "h2d_bytes_per_step": NL * B * cfg.hidden * 4,
-               "d2h_bytes_per_step": NL * B * cfg.hidden * 4,
-               "path": "llambda_cuda_moe_session_run per layer from and into preallocated "
-                       "page-locked host float buffers (the reference's run-into convention)"}
+    extras_on = (not args.no_extras and cfg is CF.CONFIG3 and B == 32)
+    extra_q = [("config5_decode_b1", 1), ("config5_prefill_b2048", 2048)] if extras_on else []
+    max_tokens = max([B] + [b for _, b in extra_q])
+    sessions, keep, ref0, setup_s = open_stack(ctx, cfg, max_tokens)
+    main = measure(ctx, cfg, sessions, ref0, B, clocks=True)
+    extra_recs = []
+    for name, b in extra_q:
+        extra_recs.append((name, cfg, b, measure(ctx, cfg, sessions, ref0, b)))
+    close_stack(ctx, sessions, keep, ref0)
+    if extras_on:  # config 4: the nemotron_h_moe stack at decode batch 64
+        c4 = CF.CONFIG4
+        s4, k4, r4, _ = open_stack(ctx, c4, 64)
+        extra_recs.append(("config4_decode_b64", c4, 64, measure(ctx, c4, s4, r4, 64)))
+        close_stack(ctx, s4, k4, r4)
+    peak, _ = hbm_peak()
 
     kernels = None
     cpu = None
@@ -602,42 +739,56 @@ def run_ours(args):
                 kernels["config2_b8"] = time_dense_gemv(torch, LB, CF.CONFIG2, 8)
                 for v in kernels.values():
                     v["frac"] = round(v["achieved_gbs"] / peak, 4)
-            except Exception as e:  # memory pressure at N=1 with the stack resident
+            except Exception as e:  # memory pressure
                 kernels["error"] = str(e)
         if not args.no_cpu_baseline:
+            # the CPU leg: the oracle times layer 0 of the stack on all host
+            # cores and, as the checker, recomputes layer 0 of every measured
+            # workload on the same bytes (the parity of the N=1 runs)
             cores = os.cpu_count() or 1
-            tok_s, per_layer = time_cpu_stack(cfg, NL, B, args.seed, steps=3, warmup=1)
-            cpu = {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-                   "sample": f"{B} tokens through 1 qwen3next layer per sample "
+            host = HostLayer(cfg, CF.layer_seed(args.seed, 0))
+            per_layer = host.time(host.x(args.seed, B), steps=3, warmup=1)
+            cpu = {"value": B / (per_layer * NL), "unit": "tokens/s", "cores": cores,
+                   "kind": "port",
+                   "sample": f"{B} tokens through layer 0 of the stack per sample "
                              f"({per_layer * 1e3:.1f} ms), scaled to {NL} layers"}
+            recs = [(cfg, B, main)] + [(c, b, r) for _, c, b, r in extra_recs]
+            hosts = {id(cfg): host}
+            for c, b, r in recs:
+                if id(c) not in hosts:
+                    hosts[id(c)] = HostLayer(c, CF.layer_seed(args.seed, 0))
+                h = hosts[id(c)]
+                ref, sel_ref, _ = h.forward(h.x(args.seed, b))
+                r["parity"] = parity_record(
+                    r["layer0"][0], r["layer0"][1], ref, sel_ref,
+                    "CPU oracle, layer 0 of the stack, same synthetic bytes",
+                    2e-2 if r["prefill"] else 1e-3)
 
-    # decode: rms-norm + router, top-k with routing, gate/up, routed down, shared
-    # down (ranks that compute a share of the shared expert), combine.
-    # prefill: rms-norm, router K slices, their sum, top-k with routing, gather,
-    # tile plan, gate/up, down, combine.
-    launches_per_layer = 9 if prefill else 5 + (1 if streams_shared else 0)
-    phase = "prefill" if prefill else "decode"
-    line = {"metric": f"MoE FFN {phase} tokens/s", "value": round(value, 2), "unit": "tokens/s",
+    line = {"metric": f"MoE FFN {'prefill' if main['prefill'] else 'decode'} tokens/s",
+            "value": round(main["value"], 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16" if prefill else "f32", "data": "synthetic",
-            "config": {"workload": (f"config5_qwen3next_moe_stack_{NL}L_{phase}_b{B}"
-                                    if cfg is CF.CONFIG3 else
-                                    f"config4_nemotron_h_moe_stack_{NL}L_{phase}_b{B}"),
+            "ms_per_step": round(main["ms_per_step"], 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if main["prefill"] else "f32", "data": "synthetic",
+            "config": {"workload": workload_name(cfg, CF, NL, B, main["prefill"]),
                        "batch": B, "layers": NL, "experts": cfg.experts, "top_k": cfg.top_k,
                        "hidden": cfg.hidden,
-                       "parallelism": f"ep{world}" + ("-peer" if peer else "-nccl" if world > 1 else ""),
+                       "parallelism": f"ep{world}" + ("-peer" if ctx.peer else
+                                                      "-nccl" if world > 1 else ""),
                        "l2": "weights streamed per step exceed L2 (no flush needed)",
                        "setup_s": round(setup_s, 1)},
-            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": launches_per_layer * NL * args.steps,
-            "distinct_experts_per_layer_mean": round(statistics.mean(distinct), 1)}
+            "roofline": main["roofline"], "e2e": main["e2e"], "cpu_baseline": cpu,
+            "clocks": main["clocks"], "parity": main["parity"],
+            "ep_breakdown": main["ep_breakdown"],
+            "gpu_launches": main["gpu_launches"] + sum(r["gpu_launches"]
+                                                       for _, _, _, r in extra_recs),
+            "distinct_experts_per_layer_mean": main["distinct_experts_per_layer_mean"]}
+    if extra_recs:
+        line["extra"] = {name: compact(r, c, CF, NL, b, peak) for name, c, b, r in extra_recs}
     if kernels is not None:
         line["kernels"] = kernels
     if rank == 0:
         print(json.dumps(line), flush=True)
-    for s in sessions:
-        s.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -88,6 +88,7 @@ SIGNATURES = {
     "llambda_cuda_moe_session_run_device": (C.c_int, [_vp, _vp, _sz, _vp, _vp, _vp, _vp]),
     "llambda_cuda_moe_session_status": (C.c_int, [_vp]),
     "llambda_cuda_moe_session_time_kernels": (C.c_int, [_vp, C.c_int]),
+    "llambda_cuda_moe_session_kernel_breakdown": (C.c_int, [_vp, C.POINTER(C.c_float), C.c_int]),
     "llambda_cuda_moe_session_kernel_ms": (C.c_int, [_vp, C.POINTER(C.c_float),
                                                       C.POINTER(C.c_float)]),
     "llambda_cuda_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
@@ -378,6 +379,16 @@ class MoeSession:
         a, b = C.c_float(), C.c_float()
         _check(lib().llambda_cuda_moe_session_kernel_ms(self._h, C.byref(a), C.byref(b)))
         return float(a.value), float(b.value)
+
+    def kernel_breakdown(self) -> dict:
+        """Stage durations (ms) of the last timed run: router and top-k,
+        gate/up pass, routed down pass, shared down pass, combine."""
+        a = (C.c_float * 5)()
+        n = lib().llambda_cuda_moe_session_kernel_breakdown(self._h, a, 5)
+        if n < 0:
+            raise LlambdaCudaError(last_error())
+        names = ("route", "gate_up", "down", "shared_down", "combine")
+        return {names[i]: float(a[i]) for i in range(n)}
 
     def status(self) -> int:
         rc = lib().llambda_cuda_moe_session_status(self._h)

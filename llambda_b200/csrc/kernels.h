@@ -177,8 +177,9 @@ void moe_work_carve(const MoeDevice& m, int max_tokens, void* base, MoeWork* w);
 
 // out[t][h] for t < tokens.  maps: from moe_maps_build for this layer, or
 // null to build them for this call.
-// marks (optional, three events): recorded before the gate/up pass, after it
-// and after the routed down pass, for timing those kernels.
+// marks (optional, six events): [0] before the gate/up pass, [1] after it,
+// [2] after the routed down pass, [3] at the start of the layer (before the
+// router), [4] before the combine, [5] after it, for timing those stages.
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int tokens,
                        float* out, const SlabMaps* maps, cudaStream_t stream,
                        const cudaEvent_t* marks = nullptr);

@@ -1956,6 +1956,8 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
       reinterpret_cast<uintptr_t>(m.router_extra_row) | reinterpret_cast<uintptr_t>(m.input_norm);
   const int all_rows = m.router_rows + (m.router_extra_row ? 1 : 0);  // column E: shared gate
   const bool prefill = prefill_applies(m, w, T);
+  auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
+  if ((e = mark(3)) != cudaSuccess) return e;
   if (prefill) {
     if ((e = launch_prefill_router(m, w, x, T, s)) != cudaSuccess) return e;
   } else if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
@@ -2006,18 +2008,20 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     e = launch_expert_passes<LB_TYPE_Q6_K, LB_TYPE_Q4_K>(m, w, T, maps, s, marks);
   else
     return cudaErrorInvalidValue;
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || (e = mark(4)) != cudaSuccess) return e;
   const bool vec = (m.hidden & 3) == 0 &&
                    ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
   if (m.ep_world > 1) {  // every rank's partial meets here (peer memory, NVLink)
     if (!vec || T > m.ep_max_tokens) return cudaErrorInvalidValue;
-    return launch_pdl(combine_ep_kernel, dim3(kEpGrid), dim3(256), 0, s, m, w, T, x, out);
+    e = launch_pdl(combine_ep_kernel, dim3(kEpGrid), dim3(256), 0, s, m, w, T, x, out);
+  } else {
+    const long n = (long)T * m.hidden / (vec ? 4 : 1);
+    const int grid = std::max(1, (int)std::min<long>((n + 127) / 128, (long)sm_count() * 16));
+    auto kern = vec && m.top_k <= 16 ? combine_kernel<true, 16>
+                : vec ? combine_kernel<true, 32> : combine_kernel<false, 32>;
+    e = launch_pdl(kern, dim3(grid), dim3(128), 0, s, m, w, T, x, out);
   }
-  const long n = (long)T * m.hidden / (vec ? 4 : 1);
-  const int grid = std::max(1, (int)std::min<long>((n + 127) / 128, (long)sm_count() * 16));
-  auto kern = vec && m.top_k <= 16 ? combine_kernel<true, 16>
-              : vec ? combine_kernel<true, 32> : combine_kernel<false, 32>;
-  return launch_pdl(kern, dim3(grid), dim3(128), 0, s, m, w, T, x, out);
+  return e != cudaSuccess ? e : mark(5);
 }
 
 }  // namespace lb

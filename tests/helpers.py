@@ -1,66 +1,15 @@
 """Shared test helpers: host-side seeded layers (through the oracle's copy of
-the generator) and the parity measure."""
+the generator, oracle/layers.py) and the parity measure."""
 from __future__ import annotations
 
 import numpy as np
 
-from llambda_b200 import configs as CF
-from llambda_b200._native import TYPE_F32, TYPE_Q4_K
-from oracle import oracle as O
+from llambda_b200 import configs as CF  # noqa: F401  (re-exported for the tests)
+from oracle import oracle as O  # noqa: F401
+from oracle.layers import host_layer, host_tensor, max_rel, oracle_layer  # noqa: F401
 
 # Tolerance of the fp32 paths: max|y - r| / max|r| (north-star parity bar).
 MAX_REL = 1e-3
-
-
-def max_rel(y: np.ndarray, r: np.ndarray) -> float:
-    y = np.asarray(y, np.float64)
-    r = np.asarray(r, np.float64)
-    den = np.max(np.abs(r))
-    return float(np.max(np.abs(y - r)) / den) if den > 0 else float(np.max(np.abs(y - r)))
-
-
-def host_tensor(type_tag: int, ne0: int, ne1: int, ne2: int, seed: int, stream: int,
-                scale: float) -> np.ndarray:
-    units = CF.tensor_units(type_tag, ne0, ne1, ne2)
-    if type_tag == TYPE_F32:
-        return O.synth_f32(seed, stream, 0, units, scale)
-    if type_tag == TYPE_Q4_K:
-        return O.synth_q4k(seed, stream, 0, units, scale)
-    return O.synth_q6k(seed, stream, 0, units, scale)
-
-
-def host_layer(cfg: CF.MoeConfig, seed: int) -> dict:
-    """name -> (type, ne0, ne1, ne2, numpy array) for every tensor of a layer."""
-    out = {}
-    for name, t, ne0, ne1, ne2, stream, scale in CF.moe_tensor_specs(cfg):
-        arr = host_tensor(t, ne0, ne1, ne2, seed, stream, scale)
-        out[name] = (t, ne0, ne1, ne2, arr)
-    return out
-
-
-def oracle_layer(cfg: CF.MoeConfig, tensors: dict, input_norm=None, eps=1e-6,
-                 residual=False) -> O.MoeLayer:
-    L = O.MoeLayer()
-    L.arch, L.hidden, L.top_k = cfg.arch, cfg.hidden, cfg.top_k
-    L.weight_scale, L.weights_norm = cfg.weight_scale, int(cfg.weights_norm)
-
-    def T(name):
-        if name not in tensors:
-            return O.make_tensor(0, None, 0, 0, 0)
-        t, ne0, ne1, ne2, arr = tensors[name]
-        return O.make_tensor(t, arr, ne0, ne1, ne2)
-
-    L.router = T("ffn_gate_inp")
-    L.router_bias = tensors["exp_probs_b.bias"][4].ctypes.data if "exp_probs_b.bias" in tensors else None
-    L.shared_gate_inp = (tensors["ffn_gate_inp_shexp"][4].ctypes.data
-                         if "ffn_gate_inp_shexp" in tensors else None)
-    L.gate_exps, L.up_exps, L.down_exps = T("ffn_gate_exps"), T("ffn_up_exps"), T("ffn_down_exps")
-    L.gate_shexp, L.up_shexp, L.down_shexp = T("ffn_gate_shexp"), T("ffn_up_shexp"), T("ffn_down_shexp")
-    L._keep = input_norm
-    L.input_norm = input_norm.ctypes.data if input_norm is not None else None
-    L.norm_epsilon = eps
-    L.add_residual = int(residual)
-    return L
 
 
 def gpu_tensors(tensors: dict) -> dict:

@@ -61,8 +61,11 @@ def test_small_prefill_matches_oracle(cfg, tokens, prefill_from):
     assert max_rel(out[same], ref[same]) < PREFILL_MAX_REL
 
 
-@pytest.mark.parametrize("cfg,tokens", [(CF.CONFIG3, 512), (CF.CONFIG4, 1024)],
-                         ids=["config3_T512", "config4_T1024"])
+# config 3 at T=2048 is the config-5 prefill batch: the largest workspace
+# (T*k = 20480 grouped rows), tile lists and router slices the bench reaches
+@pytest.mark.parametrize("cfg,tokens", [(CF.CONFIG3, 512), (CF.CONFIG4, 1024),
+                                        (CF.CONFIG3, 2048)],
+                         ids=["config3_T512", "config4_T1024", "config3_T2048"])
 def test_prefill_full_layer(cfg, tokens, prefill_from):
     prefill_from(128)
     tensors = host_layer(cfg, seed=0)
