@@ -255,6 +255,12 @@ class AcceleratorProjection:
     run_mutex: threading.Lock = dataclasses.field(default_factory=threading.Lock)
 
 
+@dataclasses.dataclass(frozen=True)
+class MoeBinding(AcceleratorProjection):
+    """A layer's MoE block bound to a backend with the optional MoE slots
+    (closed through close_moe_session_function)."""
+
+
 class GgufModel:
     """The parts of gguf-model (L2366-2394) the projection and MoE paths use."""
 
@@ -267,6 +273,11 @@ class GgufModel:
         self.accelerator_projections: dict = {}
         self.moe_bindings: dict = {}
         self.runtime_mutex = threading.Lock()
+        # inference contexts in use, and the bindings unregistered while any
+        # was: closed when the count drops to zero (L2517-2549, L2662-2670)
+        self.active_inference_count = 0
+        self.retired_bindings: list = []
+        self.closed = False
 
     def tensor_info(self, name: str, required: bool = False) -> Optional[TensorInfo]:
         info = self.tensors.get(name)
@@ -334,22 +345,258 @@ def register_model_accelerator_projection(model: GgufModel, backend, tensor_name
     return model
 
 
+def _close_retired(bindings) -> None:
+    """close-retired-accelerator-projections, L2517-2530: close every
+    session, then re-raise the first close error."""
+    first = None
+    for p in bindings:
+        try:
+            with p.run_mutex:
+                if isinstance(p, MoeBinding):
+                    p.backend.close_moe_session_function(p.session)
+                else:
+                    p.backend.close_session_function(p.session)
+        except Exception as e:  # noqa: BLE001
+            first = first or e
+    if first is not None:
+        raise first
+
+
+def _defer_or_collect(model: "GgufModel", bindings: list) -> list:
+    """defer-or-collect-accelerator-projections, L2662-2670: with inference
+    contexts active the removed bindings wait on the model (closed by the
+    last release); otherwise they are returned for closing now.  Called with
+    the model's runtime mutex held."""
+    if model.active_inference_count > 0:
+        model.retired_bindings = bindings + model.retired_bindings
+        return []
+    return bindings
+
+
+def model_accelerator_projection(model: GgufModel, backend, tensor_name: str):
+    """model-accelerator-projection, L2636-2645: the tensor's binding to the
+    backend, or None."""
+    name = resolve_accelerator_backend(backend).name
+    for p in model.accelerator_projections.get(tensor_name, ()):
+        if p.backend.name == name:
+            return p
+    return None
+
+
 def unregister_model_accelerator_projection(model: GgufModel, backend, tensor_name: str) -> bool:
+    """unregister-model-accelerator-projection, L2742-2789 (close deferred
+    while inference contexts are active)."""
     b = resolve_accelerator_backend(backend)
     with model.runtime_mutex:
         cur = model.accelerator_projections.get(tensor_name, ())
         keep = tuple(p for p in cur if p.backend.name != b.name)
         gone = [p for p in cur if p.backend.name == b.name]
-        table = dict(model.accelerator_projections)
-        if keep:
-            table[tensor_name] = keep
-        else:
-            table.pop(tensor_name, None)
-        model.accelerator_projections = table
-    for p in gone:
-        with p.run_mutex:
-            b.close_session_function(p.session)
+        if gone:
+            table = dict(model.accelerator_projections)
+            if keep:
+                table[tensor_name] = keep
+            else:
+                table.pop(tensor_name, None)
+            model.accelerator_projections = table
+        to_close = _defer_or_collect(model, gone)
+    _close_retired(to_close)
     return bool(gone)
+
+
+def clear_model_accelerator_projections(model: GgufModel, backend=None) -> GgufModel:
+    """clear-model-accelerator-projections, L2791-2827: every binding, or
+    those of one backend."""
+    b = resolve_accelerator_backend(backend) if backend is not None else None
+    with model.runtime_mutex:
+        table, removed = {}, []
+        for name, bindings in model.accelerator_projections.items():
+            keep = tuple(p for p in bindings if b is not None and p.backend.name != b.name)
+            removed += [p for p in bindings if p not in keep]
+            if keep:
+                table[name] = keep
+        model.accelerator_projections = table
+        to_close = _defer_or_collect(model, removed)
+    _close_retired(to_close)
+    return model
+
+
+class InferenceContext:
+    """The part of llambda's inference context (L2415-2600) the accelerator
+    protocol depends on: while a context is in use, the model's unregistered
+    bindings are not closed."""
+
+    def __init__(self, model: GgufModel):
+        self.model = model
+        self.in_use = False
+        self.closed = False
+        self._mutex = threading.Lock()
+
+    def close(self) -> None:
+        """close-inference-context, L2591-2600."""
+        with self._mutex:
+            if self.in_use:
+                raise RuntimeError("Cannot close an inference context while it is in use.")
+            self.closed = True
+
+
+def make_inference_context(model: GgufModel) -> InferenceContext:
+    return InferenceContext(model)
+
+
+def acquire_model_inference_use(model: GgufModel) -> GgufModel:
+    """acquire-model-inference-use, L2532-2536."""
+    with model.runtime_mutex:
+        if model.closed:
+            raise RuntimeError("The model is closed.")
+        model.active_inference_count += 1
+    return model
+
+
+def release_model_inference_use(model: GgufModel) -> GgufModel:
+    """release-model-inference-use, L2538-2549: the last release closes the
+    bindings retired meanwhile."""
+    retired = []
+    with model.runtime_mutex:
+        model.active_inference_count -= 1
+        if model.active_inference_count < 0:
+            raise RuntimeError("Model inference use count became negative.")
+        if model.active_inference_count == 0:
+            retired, model.retired_bindings = model.retired_bindings, []
+    _close_retired(retired)
+    return model
+
+
+def call_with_inference_context(context: InferenceContext, function: Callable):
+    """call-with-inference-context, L2551-2581."""
+    with context._mutex:
+        if context.closed:
+            raise RuntimeError("The inference context is closed.")
+        if context.in_use:
+            raise RuntimeError("Inference context is already in use.")
+        context.in_use = True
+    acquired = False
+    try:
+        acquire_model_inference_use(context.model)
+        acquired = True
+        return function(context)
+    finally:
+        try:
+            if acquired:
+                release_model_inference_use(context.model)
+        finally:
+            with context._mutex:
+                context.in_use = False
+
+
+def close_model(model: GgufModel) -> None:
+    """close-model, L2849-2880: refuses while inference contexts are active,
+    then closes every projection and MoE session the model holds."""
+    with model.runtime_mutex:
+        if model.closed:
+            return
+        if model.active_inference_count > 0:
+            raise RuntimeError(f"Cannot close a model while {model.active_inference_count} "
+                               f"inference context(s) are active.")
+        bindings = [p for ps in model.accelerator_projections.values() for p in ps]
+        bindings += [p for ps in model.moe_bindings.values() for p in ps]
+        bindings += model.retired_bindings
+        model.accelerator_projections, model.moe_bindings, model.retired_bindings = {}, {}, []
+        model.closed = True
+    _close_retired(bindings)
+
+
+def _cache_component(text) -> str:
+    """accelerator-cache-component, L2963-2971: alphanumerics, '-' and '.'
+    kept, anything else becomes '-'."""
+    return "".join(c if c.isalnum() or c in "-." else "-" for c in str(text))
+
+
+def model_accelerator_projection_cache_key(model: GgufModel, backend, info: TensorInfo) -> str:
+    """model-accelerator-projection-cache-key, L2976-2993: bridge version,
+    runtime version, weight format, type tag, dimensions and a SHA-256 of the
+    tensor bytes (there is no ONNX generator script for this backend)."""
+    b = resolve_accelerator_backend(backend)
+    data = np.ascontiguousarray(info.data).view(np.uint8).ravel()
+    return "bridge-{}-runtime-{}-weights-{}-ggml-{}-{}-{}-{}-{}".format(
+        _cache_component(b.bridge_version_function()),
+        _cache_component(b.runtime_version_function()),
+        _cache_component(b.weight_format).lower(), info.type, info.ne0, info.ne1, info.ne2,
+        b.byte_vector_sha256_function(data))
+
+
+def ensure_model_accelerator_projection(model: GgufModel, backend, tensor_name: str,
+                                        cache_directory: Optional[str] = None):
+    """ensure-model-accelerator-projection, L3039-3066: (model, path,
+    reused_p); exports the projection file into the cache unless it is
+    there, then registers it.  An existing binding returns (model, None,
+    True)."""
+    b = resolve_accelerator_backend(backend)
+    if model_accelerator_projection(model, b, tensor_name) is not None:
+        return model, None, True
+    info = model.tensor_info(tensor_name, required=True)
+    key = model_accelerator_projection_cache_key(model, b, info)
+    root = cache_directory or b.default_cache_directory_function()
+    path = os.path.join(root, key, "projection.llbcuda")
+    reused = os.path.exists(path)
+    if not reused:
+        os.makedirs(os.path.dirname(path), exist_ok=True)
+        b.export_projection_function(model, tensor_name, path)
+    register_model_accelerator_projection(model, b, tensor_name, path,
+                                          cache_directory=root, cache_key=key)
+    return model, path, reused
+
+
+def enable_model_accelerator_projections(model: GgufModel, backend, tensor_names,
+                                         cache_directory: Optional[str] = None) -> GgufModel:
+    """enable-model-accelerator-projections, L3068-3091: all or nothing (the
+    tensors added by this call are unregistered again on failure)."""
+    b = resolve_accelerator_backend(backend)
+    added, done = [], False
+    try:
+        for name in tensor_names:
+            if model_accelerator_projection(model, b, name) is None:
+                ensure_model_accelerator_projection(model, b, name, cache_directory)
+                added.append(name)
+        done = True
+        return model
+    finally:
+        if not done:
+            for name in added:
+                unregister_model_accelerator_projection(model, b, name)
+
+
+def call_with_accelerator_setup_fallback(backend, setup_function: Callable):
+    """call-with-accelerator-setup-fallback, L3144-3152: any error during
+    set-up warns and returns None (the model keeps running on what it has)."""
+    b = resolve_accelerator_backend(backend)
+    try:
+        return setup_function()
+    except Exception as condition:  # noqa: BLE001 - mirrors handler-case error
+        warnings.warn(f"{b.display_name} setup failed; continuing with the next available "
+                      f"backend: {condition}")
+        return None
+
+
+def try_enable_model_accelerator_projections(model: GgufModel, backend, tensor_names,
+                                             cache_directory: Optional[str] = None):
+    """try-enable-model-accelerator-projections, L3160-3208: True when every
+    named projection is bound, None (with a warning) when the backend cannot
+    load, is unavailable, no projection was named, or set-up fails."""
+    b = resolve_accelerator_backend(backend)
+
+    def setup():
+        names = list(dict.fromkeys(tensor_names or ()))
+        if not names:
+            b.signal_error_function("%s acceleration was requested without any projections.",
+                                    b.display_name)
+        if not b.load_function():
+            b.signal_error_function("%s backend library could not be loaded.", b.display_name)
+        if not b.available_p_function():
+            b.signal_error_function("%s acceleration is unavailable.", b.display_name)
+        enable_model_accelerator_projections(model, b, names, cache_directory)
+        return True
+
+    return call_with_accelerator_setup_fallback(b, setup)
 
 
 def call_with_accelerator_runtime_fallback(backend, accelerator_function, fallback_function,
@@ -405,7 +652,10 @@ def register_model_moe_binding(model: GgufModel, backend, layer_index: int, **kw
     with model.runtime_mutex:
         cur = model.moe_bindings.get(layer_index, ())
         table = dict(model.moe_bindings)
-        table[layer_index] = tuple(sorted(cur + (AcceleratorProjection(b, session),),
+        if any(p.backend.name == b.name for p in cur):
+            b.close_moe_session_function(session)
+            raise ValueError(f"Layer {layer_index} already has a {b.display_name} MoE binding.")
+        table[layer_index] = tuple(sorted(cur + (MoeBinding(b, session),),
                                           key=lambda p: p.backend.priority))
         model.moe_bindings = table
     return model
@@ -423,9 +673,8 @@ def unregister_model_moe_binding(model: GgufModel, backend, layer_index: int) ->
         else:
             table.pop(layer_index, None)
         model.moe_bindings = table
-    for p in gone:
-        with p.run_mutex:
-            b.close_moe_session_function(p.session)
+        to_close = _defer_or_collect(model, gone)
+    _close_retired(to_close)
 
 
 def gguf_model_moe_into(dest: np.ndarray, model: GgufModel, layer_index: int,
@@ -458,3 +707,8 @@ def gguf_model_moe_into(dest: np.ndarray, model: GgufModel, layer_index: int,
             f"blk.{layer_index}.ffn")
 
     return attempt(0)
+
+
+# Loading the backend file registers its descriptor, as accelerators/*.lisp do
+# with (register-accelerator-backend ... :replace t).
+register_accelerator_backend(CUDA_BACKEND, replace=True)
