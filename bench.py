@@ -473,7 +473,7 @@ def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
     stages = [s.kernel_breakdown() for s in sessions]
     for s in sessions:
         s.time_kernels(False)
-    names = ("route", "gate_up", "down", "shared_down", "combine")
+    names = tuple(stages[0].keys())  # the combine's phases too at N > 1
     mean_us = [statistics.mean(st[n] for st in stages) * 1e3 for n in names]
     mine = torch.tensor(mean_us + [statistics.mean(layer_ms) * 1e3], dtype=torch.float64,
                         device="cuda")

@@ -225,10 +225,13 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_sess
                                                            int enable);
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_kernel_ms(llambda_cuda_moe_session* session,
                                                         float* gate_up_ms, float* down_ms);
-/* The stages of the last timed run, in milliseconds, into ms[0..n): router
- * and top-k, gate/up pass, routed down pass, shared down pass, combine
- * (with the expert-parallel exchange).  Returns the number written (at most
- * 5), -1 on failure.  No counterpart in the reference (a measurement aid). */
+/* The stages of the last timed run, in milliseconds, into ms[0..n): router,
+ * top-k with the routing, gate/up pass, routed down pass, shared down pass,
+ * combine (with the expert-parallel exchange); with n >= 9 on a session
+ * attached to peers also the combine's phases as its first CTA saw them
+ * (pushing its partial, waiting for every rank's, summing).  Returns the
+ * number written (6 or 9), -1 on failure.  No counterpart in the reference
+ * (a measurement aid). */
 LLAMBDA_CUDA_API int llambda_cuda_moe_session_kernel_breakdown(llambda_cuda_moe_session* session,
                                                                float* ms, int n);
 

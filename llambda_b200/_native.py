@@ -381,13 +381,17 @@ class MoeSession:
         return float(a.value), float(b.value)
 
     def kernel_breakdown(self) -> dict:
-        """Stage durations (ms) of the last timed run: router and top-k,
-        gate/up pass, routed down pass, shared down pass, combine."""
-        a = (C.c_float * 5)()
-        n = lib().llambda_cuda_moe_session_kernel_breakdown(self._h, a, 5)
+        """Stage durations (ms) of the last timed run: router (with the
+        rms-norm and the prepared gate/up input), top-k with the routing,
+        gate/up pass, routed down pass, shared down pass, combine; with the
+        expert-parallel reduction also the combine's phases (its first CTA):
+        pushing the partial, waiting for every rank, summing."""
+        a = (C.c_float * 9)()
+        n = lib().llambda_cuda_moe_session_kernel_breakdown(self._h, a, 9)
         if n < 0:
             raise LlambdaCudaError(last_error())
-        names = ("route", "gate_up", "down", "shared_down", "combine")
+        names = ("router", "topk", "gate_up", "down", "shared_down", "combine",
+                 "combine_push", "combine_wait", "combine_sum")
         return {names[i]: float(a[i]) for i in range(n)}
 
     def status(self) -> int:

@@ -268,7 +268,8 @@ struct llambda_cuda_moe_session {
   Pinned hx, hout, hsel, hw;
   DevBuf dx, dout, dsel, dw;
   // kernel timing, when enabled (launch_moe's six marks)
-  cudaEvent_t marks[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  cudaEvent_t marks[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  unsigned long long* ep_stamps = nullptr;  // combine phase stamps (timing, expert parallel)
   bool timing = false;
   // The host-buffer call (copies in, the layer's kernels, copies out, status)
   // as one CUDA graph, captured for one token count and replayed while the
@@ -919,6 +920,14 @@ int llambda_cuda_moe_session_time_kernels(llambda_cuda_moe_session* s, int enabl
     if (enable)
       for (cudaEvent_t& e : s->marks)
         if (!e) cuda_check(cudaEventCreate(&e), "create timing event");
+    if (enable && s->m.ep_world > 1 && !s->ep_stamps) {
+      void* p = nullptr;
+      cuda_check(cudaMalloc(&p, 8 * sizeof(unsigned long long)), "cudaMalloc");
+      cuda_check(cudaMemset(p, 0, 8 * sizeof(unsigned long long)), "memset");
+      s->owned.push_back(p);
+      s->ep_stamps = static_cast<unsigned long long*>(p);
+    }
+    s->m.ep_stamps = enable ? s->ep_stamps : nullptr;
     s->timing = enable != 0;
     return 0;
   });
@@ -951,14 +960,20 @@ int llambda_cuda_moe_session_kernel_breakdown(llambda_cuda_moe_session* s, float
     DeviceGuard g(s->device);
     if (!s->timing) throw Failure("Kernel timing is not enabled on this session.");
     cuda_check(cudaEventSynchronize(s->marks[5]), "timing events");
-    // marks: 3 layer start, 0 gate/up start, 1 gate/up end, 2 routed down end,
-    // 4 combine start, 5 layer end
-    const int order[6] = {3, 0, 1, 2, 4, 5};
-    const int parts = std::min(n, 5);
+    // marks: 3 layer start, 6 router end, 0 gate/up start, 1 gate/up end,
+    // 2 routed down end, 4 combine start, 5 layer end
+    const int order[7] = {3, 6, 0, 1, 2, 4, 5};
+    const int parts = std::min(n, 6);
     for (int i = 0; i < parts; ++i)
       cuda_check(cudaEventElapsedTime(&ms[i], s->marks[order[i]], s->marks[order[i + 1]]),
                  "stage time");
-    return parts;
+    if (n < 9 || !s->m.ep_stamps) return parts;
+    // the expert-parallel combine's phases (its CTA 0): pushing its partial
+    // to every rank, waiting for every rank's, summing
+    unsigned long long st[4];
+    cuda_check(cudaMemcpy(st, s->m.ep_stamps, sizeof(st), cudaMemcpyDeviceToHost), "stamps");
+    for (int i = 0; i < 3; ++i) ms[6 + i] = (float)((double)(st[i + 1] - st[i]) * 1e-6);
+    return 9;
   });
 }
 

@@ -106,6 +106,10 @@ struct MoeDevice {
   // [T*sh_part/sh_parts, T*(sh_part+1)/sh_parts) only (sh_parts <= 1: all):
   // expert-parallel ranks split its tokens, and the rank sum reunites them.
   int sh_part, sh_parts;
+  // Kernel timing only (null otherwise): the expert-parallel combine's CTA 0
+  // writes %globaltimer stamps here: start, its pushes done, every peer
+  // seen, end.
+  unsigned long long* ep_stamps;
 };
 
 // The tokens [t0, t1) of a T-token call the shared expert is computed for.
@@ -177,9 +181,10 @@ void moe_work_carve(const MoeDevice& m, int max_tokens, void* base, MoeWork* w);
 
 // out[t][h] for t < tokens.  maps: from moe_maps_build for this layer, or
 // null to build them for this call.
-// marks (optional, six events): [0] before the gate/up pass, [1] after it,
+// marks (optional, seven events): [0] before the gate/up pass, [1] after it,
 // [2] after the routed down pass, [3] at the start of the layer (before the
-// router), [4] before the combine, [5] after it, for timing those stages.
+// router), [4] before the combine, [5] after it, [6] between the router and
+// the top-k launch, for timing those stages.
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int tokens,
                        float* out, const SlabMaps* maps, cudaStream_t stream,
                        const cudaEvent_t* marks = nullptr);

@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "engine.cuh"
@@ -1161,6 +1162,9 @@ struct DownSync {
 
 // SB: the pass's entries' prepared inputs are staged with the weights (at
 // stage_w, i6_bytes(K) each) instead of being read through L1.
+// shared_pass: 0 the routed experts' slabs, 1 the shared expert's, 2 both in
+// one launch (routed units first; the shared down rows must then have the
+// routed rows' width).
 template <int KSPLIT, int CW, bool SB>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_down_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, int stage_bytes,
@@ -1188,9 +1192,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   griddep_launch();
   const int k = m.top_k, H = m.hidden;
   const int per = (H + RU - 1) / RU;
-  const int K = shared_pass ? m.k_down_sh : m.k_down;
+  const int K = shared_pass == 1 ? m.k_down_sh : m.k_down;
   const int nsb = K >> 8;
-  const size_t rb = shared_pass ? m.down_sh_rb : m.down_rb;
+  const size_t rb = shared_pass == 1 ? m.down_sh_rb : m.down_rb;
   const long ld_dn = down_ld_floats(m);
   const uint32_t xib = (uint32_t)i6_bytes(K);
 
@@ -1200,7 +1204,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       shared_tokens(m, T, sh_t0, sh_t1);
       const int passes_s = (sh_t1 - sh_t0 + NT - 1) / NT;
       const int nact = w.active[m.experts];
-      const int n_routed = shared_pass ? 0 : w.pass_off_dn[nact] * per;
+      const int n_routed = shared_pass == 1 ? 0 : w.pass_off_dn[nact] * per;
       const int n_shared = (shared_pass && m.shared_here && m.inter_sh) ? per * passes_s : 0;
       const int units = n_routed + n_shared;
       const int u0 = (int)((long)blockIdx.x * units / gridDim.x);
@@ -1211,9 +1215,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       RingPos rp;
       for (int i = 0; i < n_my; ++i, ++q, rp.next(stages)) {
         const int u = u0 + i;
+        const bool sh_u = u >= n_routed;  // a shared-expert unit
         int row0, t_begin, t_end;
         const uint8_t* src;
-        if (!shared_pass) {
+        if (!sh_u) {
           if (a < 0) {  // search once, then step on
             a = 0;
             int hi = nact;
@@ -1232,7 +1237,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
           t_end = min(view.ntok, t_begin + NT);
           src = m.down_exps + ((size_t)view.e * H + row0) * rb;
         } else {
-          const int slab = u / passes_s, p = u - slab * passes_s;
+          const int us = u - n_routed, slab = us / passes_s, p = us - slab * passes_s;
           row0 = slab * RU;
           t_begin = sh_t0 + p * NT;
           t_end = min(sh_t1, t_begin + NT);
@@ -1248,10 +1253,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
         du.nt = nt;
         for (int n = 0; n < NT; ++n) {
           const int tt = t_begin + min(n, nt - 1);
-          const int id = shared_pass ? T * k + tt : view.list[tt];
-          const int tok = shared_pass ? tt : id / k;
+          const int id = sh_u ? T * k + tt : view.list[tt];
+          const int tok = sh_u ? tt : id / k;
           du.id[n] = id;
-          du.orow[n] = tok * (k + 1) + (shared_pass ? k : id - tok * k);
+          du.orow[n] = tok * (k + 1) + (sh_u ? k : id - tok * k);
         }
         mbar_expect_tx(&sync->full[s], (uint32_t)(nblk * kTileRows * rb) + (SB ? nt * xib : 0u));
         uint8_t* st = smem + (size_t)s * stage_bytes;
@@ -1273,7 +1278,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     int sh_t0, sh_t1;
     shared_tokens(m, T, sh_t0, sh_t1);
     const int passes_s = (sh_t1 - sh_t0 + NT - 1) / NT;
-    const int n_routed = shared_pass ? 0 : w.pass_off_dn[w.active[m.experts]] * per;
+    const int n_routed = shared_pass == 1 ? 0 : w.pass_off_dn[w.active[m.experts]] * per;
     const int n_shared = (shared_pass && m.shared_here && m.inter_sh) ? per * passes_s : 0;
     units_c = n_routed + n_shared;
   }
@@ -1509,14 +1514,24 @@ __global__ void __launch_bounds__(128) combine_kernel(MoeDevice m, MoeWork w, in
 }
 
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+// Flags between ranks: one system-scope fence orders a CTA's data stores
+// (made visible to thread 0 by the barrier before it) ahead of every flag
+// store that follows, so the flags themselves are relaxed stores; a
+// release store per flag would wait for the previous remote store to be
+// acknowledged each time, one NVLink round trip per peer.  The waiting side
+// polls with relaxed loads and fences once, after every flag it needs.
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 // Expert-parallel combine with the cross-rank reduction fused in, over peer
@@ -1548,6 +1563,9 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(MoeDevice m, MoeWork w,
   }
   __syncthreads();
   const uint32_t epoch = s_epoch;
+  // phase stamps of CTA 0 (kernel timing only): start, pushed, peers seen, end
+  unsigned long long* stamps = blockIdx.x == 0 && threadIdx.x == 0 ? m.ep_stamps : nullptr;
+  if (stamps) stamps[0] = global_ns();
   const size_t slot = (size_t)m.ep_max_tokens * H;  // floats per (parity, rank)
   const size_t par = (size_t)(epoch & 1u) * world * slot;
   const long n4 = (long)T * H4;
@@ -1585,24 +1603,27 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(MoeDevice m, MoeWork w,
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    __threadfence_system();  // the CTA's pushes before any of its flags
     for (int q = 0; q < world; ++q)
-      st_release_sys(reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(m.ep_peers[q]) + 4096) +
+      st_relaxed_sys(reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(m.ep_peers[q]) + 4096) +
                          rank * kEpGrid + blockIdx.x,
                      epoch);
     const uint32_t* flags = reinterpret_cast<const uint32_t*>(self + 4096);
     const uint64_t t_start = global_ns();
+    if (stamps) stamps[1] = t_start;
     bool late = false;
     for (int q = 0; q < world && !late; ++q) {
-      while ((int)(ld_acquire_sys(flags + q * kEpGrid + blockIdx.x) - epoch) < 0) {
+      while ((int)(ld_relaxed_sys(flags + q * kEpGrid + blockIdx.x) - epoch) < 0) {
         if (global_ns() - t_start > 2000000000ull) {  // bounded: two seconds
           late = true;
           break;
         }
-        __nanosleep(64);
+        __nanosleep(32);
       }
     }
+    fence_acq_rel_sys();  // every rank's slot stores before the reads below
     if (late) atomicOr(w.status, 4);  // a peer never arrived: the output is not valid
+    if (stamps) stamps[2] = global_ns();
   }
   __syncthreads();
   const float* slots = reinterpret_cast<const float*>(self + 8192) + par;
@@ -1624,6 +1645,10 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(MoeDevice m, MoeWork w,
                         __fadd_rn(xv.w, acc.w));
     }
     *reinterpret_cast<float4*>(out + o) = acc;
+  }
+  if (blockIdx.x == 0 && m.ep_stamps) {
+    __syncthreads();
+    if (threadIdx.x == 0) m.ep_stamps[3] = global_ns();
   }
 }
 
@@ -1761,8 +1786,8 @@ cudaError_t launch_down_slab_k(const MoeDevice& m, const MoeWork& w, int T, int 
 cudaError_t launch_down_slab(const MoeDevice& m, const MoeWork& w, int T, int shared_pass,
                              cudaStream_t s) {
   DownPlan p;
-  if (!down_plan(shared_pass ? m.down_sh_rb : m.down_rb, shared_pass ? m.k_down_sh : m.k_down,
-                 &p))
+  if (!down_plan(shared_pass == 1 ? m.down_sh_rb : m.down_rb,
+                 shared_pass == 1 ? m.k_down_sh : m.k_down, &p))
     return cudaErrorInvalidValue;
 #define LB_DOWN_SLAB(KS)                                                                \
   return p.staged ? launch_down_slab_k<KS, true>(m, w, T, shared_pass, p, s)              \
@@ -1791,11 +1816,14 @@ cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const
 
 // Tokens per pass (NT) of the tensor-core gate/up launch, from the expected
 // tokens per active expert; the route kernel counts passes with the same NT.
+// With T*k entries spread over E experts, about E * (1 - exp(-T*k / E))
+// experts are hit, each by T*k / that many tokens on average; an expert-
+// parallel rank sees the same ratio on its share of the experts and entries.
 int up_pass_tokens(const MoeDevice& m, int T) {
   if (m.up_type != LB_TYPE_Q4_K || T == 1) return 1;
-  const long entries = (long)T * m.top_k;
-  const long owned = std::max(1, m.expert_end - m.expert_begin);
-  const double per_expert = (double)entries / (double)std::min(entries, owned);
+  const double entries = (double)T * m.top_k, E = std::max(1, m.experts);
+  const double hit = E * -std::expm1(-entries / E);
+  const double per_expert = entries / std::max(1.0, hit);
   return per_expert < 2.5 ? 2 : 4;
 }
 
@@ -1878,9 +1906,16 @@ cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T,
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (DT == LB_TYPE_Q6_K && down_uses_i6(m)) {
-    e = launch_down_slab(m, w, T, 0, s);
+    // Expert-parallel ranks hold a few tokens of the shared expert each: its
+    // down slabs ride in the routed launch (one launch less on the layer's
+    // critical path).  On one device its own launch overlaps the routed
+    // tail better (measured), so it stays apart there.
+    const bool ride = m.ep_world > 1 && m.shared_here && m.inter_sh &&
+                      m.k_down_sh == m.k_down && m.down_sh_rb == m.down_rb;
+    e = launch_down_slab(m, w, T, ride ? 2 : 0, s);
     if (e == cudaSuccess) e = mark(2);
-    if (e == cudaSuccess && m.shared_here && m.inter_sh) e = launch_down_slab(m, w, T, 1, s);
+    if (e == cudaSuccess && !ride && m.shared_here && m.inter_sh)
+      e = launch_down_slab(m, w, T, 1, s);
     return e;
   }
   e = launch_down<DT>(m, w, T, 0, s);
@@ -1984,6 +2019,7 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     e = launch_gemv_f32(m.router, m.router_rows, m.hidden, xr, m.hidden, T, w.logits, E + 1, s);
     if (e != cudaSuccess) return e;
   }
+  if ((e = mark(6)) != cudaSuccess) return e;
   {  // top-k per token, the routing on the last CTA
     const int per = (E + 31) / 32, pnt = up_pass_tokens(m, T);
     auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
