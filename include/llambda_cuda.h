@@ -47,6 +47,9 @@ extern "C" {
 #define LLAMBDA_CUDA_TYPE_Q5_0 6
 #define LLAMBDA_CUDA_TYPE_Q8_0 8
 #define LLAMBDA_CUDA_TYPE_Q4_K 12
+/* Q5_K (176-byte super-blocks, dot-product-with-q5-k-tensor-data L4387-4441):
+ * projection sessions and the latent projections of a MoE layer. */
+#define LLAMBDA_CUDA_TYPE_Q5_K 13
 #define LLAMBDA_CUDA_TYPE_Q6_K 14
 
 typedef struct llambda_cuda_session llambda_cuda_session;
@@ -183,6 +186,17 @@ typedef struct {
                                           first (post_attention_norm, L5739-5744) */
   float norm_epsilon;                  /* its epsilon (rms-norm-into, L859-879) */
   int add_residual;                    /* 1: out = x + MoE(...) (vector-add-into, L5746) */
+  /* nemotron_h_moe latent projections (ffn_latent_down / ffn_latent_up,
+   * nemotron-h-moe-ffn-into L5845-5855, L5883-5887, L5933-5938), both or
+   * neither (data NULL): latent_down (ne0 >= hidden, ne1 = latent size L)
+   * maps the input to the experts' input, the expert tensors then have
+   * latent widths (up rows >= L wide, down ne1 = L), and latent_up (ne0 >= L,
+   * ne1 = hidden) maps the experts' weighted sum back before the shared
+   * expert, which sees the input itself, is added.  Any projection type:
+   * F32, Q4_K, Q5_K, Q6_K, Q5_0, Q8_0.  Sessions only (not the
+   * static-scratch call), on one device (no peer attachment). */
+  llambda_cuda_tensor latent_down;
+  llambda_cuda_tensor latent_up;
 } llambda_cuda_moe_desc;
 
 /* Gate/up rows may be wider than `hidden` and down rows wider than the

@@ -17,10 +17,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libllambda_cuda.so")
 
-TYPE_F32, TYPE_Q4_K, TYPE_Q6_K = 0, 12, 14
+TYPE_F32, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 0, 12, 13, 14
 TYPE_Q5_0, TYPE_Q8_0 = 6, 8  # 32-value blocks: projection sessions only
 ARCH_QWEN3NEXT, ARCH_NEMOTRON_H_MOE = 0, 1
-BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210}
+BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q5_K: 176, TYPE_Q6_K: 210}
 BLOCK32_BYTES = {TYPE_Q5_0: 22, TYPE_Q8_0: 34}
 
 
@@ -58,7 +58,8 @@ class MoeDesc(C.Structure):
                 ("expert_begin", C.c_int), ("expert_end", C.c_int),
                 ("shared_here", C.c_int), ("max_tokens", C.c_int),
                 ("input_norm", C.c_void_p), ("norm_epsilon", C.c_float),
-                ("add_residual", C.c_int)]
+                ("add_residual", C.c_int),
+                ("latent_down", Tensor), ("latent_up", Tensor)]
 
 
 # name -> (restype, argtypes); every symbol the public header declares.
@@ -290,8 +291,8 @@ class MoeSession:
                max_tokens=64, input_norm=None, norm_epsilon=1e-6, add_residual=False):
         """tensors: name -> (type, ne0, ne1, ne2, array); names follow GGUF:
         ffn_gate_inp, exp_probs_b.bias, ffn_gate_inp_shexp, ffn_{gate,up,down}_exps,
-        ffn_{gate,up,down}_shexp.  Arrays are numpy (host) or CUDA torch tensors
-        (on_device=True)."""
+        ffn_{gate,up,down}_shexp, ffn_latent_{down,up} (nemotron, optional).
+        Arrays are numpy (host) or CUDA torch tensors (on_device=True)."""
         keep = []
 
         def ptr(a):
@@ -329,6 +330,7 @@ class MoeSession:
         d.input_norm = ptr(input_norm) if input_norm is not None else None
         d.norm_epsilon = norm_epsilon
         d.add_residual = int(bool(add_residual))
+        d.latent_down, d.latent_up = T("ffn_latent_down"), T("ffn_latent_up")
         return cls(d, keep)
 
     def run_into(self, dest: np.ndarray, x: np.ndarray) -> np.ndarray:

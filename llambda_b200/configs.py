@@ -18,6 +18,7 @@ from ._native import ARCH_NEMOTRON_H_MOE, ARCH_QWEN3NEXT, TYPE_F32, TYPE_Q4_K, T
 # generator stream ids (synth.h)
 S_ACT, S_ROUTER, S_BIAS, S_SHGATE = 1, 2, 3, 4
 S_GATE, S_UP, S_DOWN, S_GATE_SH, S_UP_SH, S_DOWN_SH, S_DENSE = 5, 6, 7, 8, 9, 10, 11
+S_LAT_DOWN, S_LAT_UP = 12, 13
 
 Q4K_DSCALE = 0.02    # fp16 d, dmin = |N(0,1)| * 0.02
 Q6K_DSCALE = 0.001   # fp16 d = |N(0,1)| * 0.001
@@ -69,9 +70,22 @@ class MoeConfig:
     weight_scale: float = 1.0
     has_bias: bool = False
     tokens: tuple = field(default=(1,))
+    # nemotron latent projections (0: none): the routed experts work at this
+    # width, between ffn_latent_down and ffn_latent_up
+    latent: int = 0
+    latent_type: int = TYPE_Q4_K
+
+    @property
+    def expert_width(self) -> int:
+        """Input and output width of the routed experts."""
+        return self.latent or self.hidden
 
     @property
     def k_in(self) -> int:
+        return pad256(self.expert_width)
+
+    @property
+    def k_in_sh(self) -> int:
         return pad256(self.hidden)
 
     @property
@@ -89,7 +103,7 @@ class MoeConfig:
     def expert_bytes(self) -> int:
         up = row_bytes(self.up_type, self.k_in) * self.inter
         gate = up if self.has_gate else 0
-        down = row_bytes(self.down_type, self.k_down) * self.hidden
+        down = row_bytes(self.down_type, self.k_down) * self.expert_width
         return gate + up + down
 
     def gate_up_bytes(self) -> int:
@@ -97,14 +111,14 @@ class MoeConfig:
         return up * (2 if self.has_gate else 1)
 
     def down_bytes(self) -> int:
-        return row_bytes(self.down_type, self.k_down) * self.hidden
+        return row_bytes(self.down_type, self.k_down) * self.expert_width
 
     def shared_gate_up_bytes(self) -> int:
-        up = row_bytes(self.up_type, self.k_in) * self.inter_sh
+        up = row_bytes(self.up_type, self.k_in_sh) * self.inter_sh
         return up * (2 if self.has_gate else 1)
 
     def shared_bytes(self) -> int:
-        up = row_bytes(self.up_type, self.k_in) * self.inter_sh
+        up = row_bytes(self.up_type, self.k_in_sh) * self.inter_sh
         gate = up if self.has_gate else 0
         down = row_bytes(self.down_type, self.k_down_sh) * self.hidden
         return gate + up + down
@@ -151,13 +165,21 @@ def moe_tensor_specs(cfg: MoeConfig):
         specs.append(("ffn_gate_exps", cfg.gate_type, cfg.k_in, cfg.inter, cfg.experts, S_GATE,
                       Q4K_DSCALE))
     specs.append(("ffn_up_exps", cfg.up_type, cfg.k_in, cfg.inter, cfg.experts, S_UP, Q4K_DSCALE))
-    specs.append(("ffn_down_exps", cfg.down_type, cfg.k_down, cfg.hidden, cfg.experts, S_DOWN,
-                  Q6K_DSCALE))
+    specs.append(("ffn_down_exps", cfg.down_type, cfg.k_down, cfg.expert_width, cfg.experts,
+                  S_DOWN, Q6K_DSCALE))
+    if cfg.latent:
+        lt = cfg.latent_type
+        ds = Q6K_DSCALE if lt == TYPE_Q6_K else (ROUTER_SIGMA if lt == TYPE_F32 else Q4K_DSCALE)
+        specs.append(("ffn_latent_down", lt, cfg.k_in_sh if lt != TYPE_F32 else cfg.hidden,
+                      cfg.latent, 1, S_LAT_DOWN, ds))
+        specs.append(("ffn_latent_up", lt, pad256(cfg.latent) if lt != TYPE_F32 else cfg.latent,
+                      cfg.hidden, 1, S_LAT_UP, ds))
     if cfg.inter_sh:
         if cfg.arch == ARCH_QWEN3NEXT:
-            specs.append(("ffn_gate_shexp", cfg.gate_type, cfg.k_in, cfg.inter_sh, 1, S_GATE_SH,
+            specs.append(("ffn_gate_shexp", cfg.gate_type, cfg.k_in_sh, cfg.inter_sh, 1, S_GATE_SH,
                           Q4K_DSCALE))
-        specs.append(("ffn_up_shexp", cfg.up_type, cfg.k_in, cfg.inter_sh, 1, S_UP_SH, Q4K_DSCALE))
+        specs.append(("ffn_up_shexp", cfg.up_type, cfg.k_in_sh, cfg.inter_sh, 1, S_UP_SH,
+                      Q4K_DSCALE))
         specs.append(("ffn_down_shexp", cfg.down_type, cfg.k_down_sh, cfg.hidden, 1, S_DOWN_SH,
                       Q6K_DSCALE))
     return specs

@@ -41,6 +41,7 @@ size_t row_bytes(int type, uint64_t ne0) {
     case LLAMBDA_CUDA_TYPE_F32: return ne0 * 4;
     case LLAMBDA_CUDA_TYPE_Q4_K: return ne0 % 256 ? 0 : ne0 / 256 * 144;
     case LLAMBDA_CUDA_TYPE_Q6_K: return ne0 % 256 ? 0 : ne0 / 256 * 210;
+    case LLAMBDA_CUDA_TYPE_Q5_K: return ne0 % 256 ? 0 : ne0 / 256 * 176;
     case LLAMBDA_CUDA_TYPE_Q5_0: return ne0 % 32 ? 0 : ne0 / 32 * 22;
     case LLAMBDA_CUDA_TYPE_Q8_0: return ne0 % 32 ? 0 : ne0 / 32 * 34;
     default: return 0;
@@ -52,6 +53,7 @@ const char* type_name(int type) {
     case LLAMBDA_CUDA_TYPE_F32: return "F32";
     case LLAMBDA_CUDA_TYPE_Q4_K: return "Q4_K";
     case LLAMBDA_CUDA_TYPE_Q6_K: return "Q6_K";
+    case LLAMBDA_CUDA_TYPE_Q5_K: return "Q5_K";
     case LLAMBDA_CUDA_TYPE_Q5_0: return "Q5_0";
     case LLAMBDA_CUDA_TYPE_Q8_0: return "Q8_0";
     default: return "unsupported";
@@ -63,10 +65,12 @@ bool block32(int type) {
 }
 
 // Types of the MoE layer's tensors (the K-quants and the F32 router); a
-// projection session also takes Q5_0 and Q8_0 rows (projection = true).
+// projection session (and a latent projection of a MoE layer) also takes
+// Q5_K, Q5_0 and Q8_0 rows (projection = true).
 void require_rows(int type, uint64_t ne0, const char* what, bool projection = false) {
   if (type != LLAMBDA_CUDA_TYPE_F32 && type != LLAMBDA_CUDA_TYPE_Q4_K &&
-      type != LLAMBDA_CUDA_TYPE_Q6_K && !(projection && block32(type)))
+      type != LLAMBDA_CUDA_TYPE_Q6_K &&
+      !(projection && (block32(type) || type == LLAMBDA_CUDA_TYPE_Q5_K)))
     throw Failure(std::string(what) + ": unsupported GGML type tag " + std::to_string(type));
   if (!row_bytes(type, ne0))
     throw Failure(std::string(what) + ": " + type_name(type) + " rows need a multiple of " +
@@ -97,10 +101,13 @@ void* dev_alloc(size_t bytes) {
 }
 
 void validate_scales(int type, const void* dev, size_t bytes, cudaStream_t s, const char* what) {
-  if (type != LLAMBDA_CUDA_TYPE_Q4_K && type != LLAMBDA_CUDA_TYPE_Q6_K && !block32(type)) return;
+  if (type != LLAMBDA_CUDA_TYPE_Q4_K && type != LLAMBDA_CUDA_TYPE_Q6_K &&
+      type != LLAMBDA_CUDA_TYPE_Q5_K && !block32(type))
+    return;
   const size_t blocks =
       bytes / (type == LLAMBDA_CUDA_TYPE_Q4_K   ? 144
                : type == LLAMBDA_CUDA_TYPE_Q6_K ? 210
+               : type == LLAMBDA_CUDA_TYPE_Q5_K ? 176
                : type == LLAMBDA_CUDA_TYPE_Q5_0 ? 22
                                                 : 34);
   unsigned* bad = nullptr;
@@ -220,31 +227,12 @@ namespace {
 // The GEMV of `tokens` device vectors through the session's scratch.
 void session_launch(llambda_cuda_session* s, const uint8_t* W, const float* din, size_t tokens,
                     float* dout, cudaStream_t st) {
-  if (s->type == LLAMBDA_CUDA_TYPE_F32) {
-    cuda_check(lb::launch_gemv_f32(W, (int)s->ne1, (int)s->ne0, din, (long)s->ne0, (int)tokens,
-                                   dout, (long)s->ne1, st),
-               "GEMV launch");
-    return;
-  }
-  if (block32(s->type)) {
-    cuda_check(lb::launch_gemv_q32(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, din,
-                                   (long)s->ne0, (int)tokens, dout, (long)s->ne1, st),
-               "GEMV launch");
-    return;
-  }
-  cudaError_t fe = cudaSuccess;
-  if (lb::launch_gemv_fused(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, din, (long)s->ne0,
-                            (int)tokens, dout, (long)s->ne1, s->status, st, &fe)) {
-    cuda_check(fe, "GEMV launch");
-    return;
-  }
-  float* xp = static_cast<float*>(s->dxp.get(lb::xprep_floats((int)s->ne0, (int)tokens) * 4));
-  cuda_check(lb::launch_prep(s->type, (int)s->ne1, din, (long)s->ne0, (int)s->ne0, (int)s->ne0,
-                             (int)tokens,
-                             nullptr, xp, st),
-             "activation prep");
-  cuda_check(lb::launch_gemv_prepped(s->type, W, s->rb, (int)s->ne1, (int)s->ne0, xp,
-                                     (int)tokens, dout, (long)s->ne1, s->status, st),
+  const int K = (int)s->ne0;
+  float* xp = nullptr;
+  if (s->type == LLAMBDA_CUDA_TYPE_Q4_K || s->type == LLAMBDA_CUDA_TYPE_Q6_K)
+    xp = static_cast<float*>(s->dxp.get(lb::xprep_floats(K, (int)tokens) * 4));
+  cuda_check(lb::launch_projection(s->type, W, s->rb, (int)s->ne1, K, din, (long)K, K,
+                                   (int)tokens, dout, (long)s->ne1, xp, s->status, st),
              "GEMV launch");
 }
 
@@ -628,13 +616,30 @@ int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
       if (t.ne0 < min_ne0 || t.ne1 != ne1 || (ne2 && (t.ne2 ? t.ne2 : 1) != ne2))
         throw Failure(std::string("MoE tensor ") + what + " has unexpected dimensions.");
     };
-    dims(d->up_exps, H, I, E, "ffn_up_exps");
+    // latent projections: the experts' input and output width is L
+    const bool latent = d->latent_down.data || d->latent_up.data;
+    uint64_t XW = H;  // width of the routed experts' input and output
+    if (latent) {
+      if (qwen) throw Failure("Latent projections are only defined for nemotron_h_moe.");
+      if (!d->latent_down.data || !d->latent_up.data)
+        throw Failure("ffn_latent_down and ffn_latent_up must be given together.");
+      require_rows(d->latent_down.type, d->latent_down.ne0, "ffn_latent_down", true);
+      require_rows(d->latent_up.type, d->latent_up.ne0, "ffn_latent_up", true);
+      XW = d->latent_down.ne1;
+      if (!XW || XW > (1u << 20)) throw Failure("ffn_latent_down has no rows.");
+      dims(d->latent_down, H, XW, 1, "ffn_latent_down");
+      dims(d->latent_up, XW, H, 1, "ffn_latent_up");
+      if ((d->latent_down.type == LLAMBDA_CUDA_TYPE_F32 && d->latent_down.ne0 != H) ||
+          (d->latent_up.type == LLAMBDA_CUDA_TYPE_F32 && d->latent_up.ne0 != XW))
+        throw Failure("F32 latent projections must have exactly the input's width.");
+    }
+    dims(d->up_exps, XW, I, E, "ffn_up_exps");
     if (qwen) {
       dims(d->gate_exps, H, I, E, "ffn_gate_exps");
       if (d->gate_exps.ne0 != d->up_exps.ne0 || d->gate_exps.type != d->up_exps.type)
         throw Failure("ffn_gate_exps and ffn_up_exps must share type and width.");
     }
-    dims(d->down_exps, I, H, E, "ffn_down_exps");
+    dims(d->down_exps, I, XW, E, "ffn_down_exps");
     uint64_t Ish = 0;
     if (shared) {
       Ish = d->up_shexp.ne1;
@@ -750,6 +755,21 @@ int llambda_cuda_moe_session_create(const llambda_cuda_moe_desc* d,
       }
       m.expert_begin = eb;
       m.expert_end = ee;
+      if (latent) {
+        m.latent_dim = (int)XW;
+        m.lat_down_type = d->latent_down.type;
+        m.lat_up_type = d->latent_up.type;
+        m.k_lat_down = (int)d->latent_down.ne0;
+        m.k_lat_up = (int)d->latent_up.ne0;
+        m.lat_down = plain(d->latent_down, "ffn_latent_down");
+        m.lat_up = plain(d->latent_up, "ffn_latent_up");
+        m.lat_down_rb = row_bytes(d->latent_down.type, d->latent_down.ne0);
+        m.lat_up_rb = row_bytes(d->latent_up.type, d->latent_up.ne0);
+        if (m.shared_here &&
+            ((m.up_sh_type == LLAMBDA_CUDA_TYPE_F32 && m.k_in_sh != (int)H) ||
+             (m.down_sh_type == LLAMBDA_CUDA_TYPE_F32 && m.k_down_sh != m.inter_sh)))
+          throw Failure("F32 shared expert rows must have exactly the input's width.");
+      }
       if (d->input_norm) m.input_norm = static_cast<const float*>(upload(d->input_norm, H * 4));
       m.norm_epsilon = d->norm_epsilon;
       m.add_residual = d->add_residual ? 1 : 0;
@@ -1012,6 +1032,8 @@ int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_session* s, int rank,
       throw Failure("world must be 2.." + std::to_string(lb::kEpMaxWorld) +
                     " and 0 <= rank < world.");
     if (s->m.hidden % 4) throw Failure("The peer-memory reduction needs hidden % 4 == 0.");
+    if (s->m.latent_dim > 0)
+      throw Failure("A layer with latent projections runs on one device (no peer reduction).");
     if (bytes < lb::ep_buffer_bytes(world, s->max_tokens, s->m.hidden))
       throw Failure("The peer buffer is smaller than llambda_cuda_moe_peer_bytes.");
     for (int r = 0; r < world; ++r) require_aligned16(peer_buffers[r], "peer buffer");
@@ -1070,6 +1092,8 @@ void* static_scratch_address(int dev) {
 // The layer description of a device-resident desc, without uploads.
 lb::MoeDevice static_layer(const llambda_cuda_moe_desc* d) {
   if (!d->data_on_device) throw Failure("The static-scratch MoE call needs data_on_device = 1.");
+  if (d->latent_down.data || d->latent_up.data)
+    throw Failure("Latent projections need a MoE session (llambda_cuda_moe_session_create).");
   if (d->arch != LLAMBDA_CUDA_ARCH_QWEN3NEXT && d->arch != LLAMBDA_CUDA_ARCH_NEMOTRON_H_MOE)
     throw Failure("Unknown MoE architecture " + std::to_string(d->arch));
   const bool qwen = d->arch == LLAMBDA_CUDA_ARCH_QWEN3NEXT;

@@ -4,6 +4,7 @@
 // (llambda.lisp L2142-2144, L4338-4506):
 //   Q4_K (144 B): d:f16 @0, dmin:f16 @2, scales[12] @4, qs[128] @16
 //   Q6_K (210 B): ql[128] @0, qh[64] @128, scales:int8[16] @192, d:f16 @208
+//   Q5_K (176 B): d:f16 @0, dmin:f16 @2, scales[12] @4, qh[32] @16, qs[128] @48
 #pragma once
 
 #include <cuda_fp16.h>
@@ -13,12 +14,14 @@
 #define LB_QK 256
 #define LB_Q4K 144
 #define LB_Q6K 210
+#define LB_Q5K 176
 
 // GGML type tags (llambda.lisp L24-31).
 #define LB_TYPE_F32 0
 #define LB_TYPE_Q5_0 6
 #define LB_TYPE_Q8_0 8
 #define LB_TYPE_Q4_K 12
+#define LB_TYPE_Q5_K 13
 #define LB_TYPE_Q6_K 14
 
 // 32-value block formats (llambda.lisp L2139-2140):

@@ -708,14 +708,14 @@ template <int TYPE>
 __global__ void __launch_bounds__(256) gemv_q32_kernel(const uint8_t* __restrict__ W, size_t rb,
                                                        int rows, int K,
                                                        const float* __restrict__ x, long ldx,
-                                                       int tokens, float* __restrict__ y,
-                                                       long ldy) {
+                                                       int n_valid, int tokens,
+                                                       float* __restrict__ y, long ldy) {
   constexpr int kMaxTok = 8;
   constexpr int BB = TYPE == LB_TYPE_Q5_0 ? LB_Q5_0 : LB_Q8_0;
-  extern __shared__ __align__(16) float xs[];  // [tokens][K]
+  extern __shared__ __align__(16) float xs[];  // [tokens][K], zero past n_valid
   for (int i = threadIdx.x; i < tokens * K; i += blockDim.x) {
-    const int t = i / K;
-    xs[i] = x[(long)t * ldx + (i - t * K)];
+    const int t = i / K, c = i - t * K;
+    xs[i] = c < n_valid ? x[(long)t * ldx + c] : 0.f;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -794,13 +794,115 @@ __global__ void __launch_bounds__(256) gemv_q32_kernel(const uint8_t* __restrict
   }
 }
 
+// Q5_K rows (dot-product-with-q5-k-tensor-data, L4387-4441).  One warp per
+// row, up to 8 tokens whose inputs sit in shared memory (zero past n_valid).
+// Lane l takes values [8l, 8l + 8) of every block: sub-block s = l / 4
+// (pair g = s / 2, high nibbles for odd s) at positions 8 (l % 4) .. + 7, so
+// its 8 qs bytes and 8 qh bytes are two aligned 8-byte loads and the block
+// header (d, dmin, packed scales) one 16-byte load shared by the warp.  Each
+// value byte (nibble | qh bit s << 4, 0..31) becomes the float 2^23 + q by one
+// byte permute under the exponent byte 0x4B; per sub-block the lane sums q*x
+// and x in fp32 and applies the reference's delta = d*sc and offset =
+// dmin*m once, (delta * sum(q x)) - (offset * sum(x)): the same products in
+// another summation order.
+__global__ void __launch_bounds__(256) gemv_q5k_kernel(const uint8_t* __restrict__ W, size_t rb,
+                                                       int rows, int K,
+                                                       const float* __restrict__ x, long ldx,
+                                                       int n_valid, int tokens,
+                                                       float* __restrict__ y, long ldy) {
+  constexpr int kMaxTok = 8;
+  extern __shared__ __align__(16) float xs[];  // [tokens][K]
+  for (int i = threadIdx.x; i < tokens * K; i += blockDim.x) {
+    const int t = i / K, c = i - t * K;
+    xs[i] = c < n_valid ? x[(long)t * ldx + c] : 0.f;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nblk = K >> 8;
+  const int sb = lane >> 2, pair = sb >> 1, pos = (lane & 3) * 8;
+  const int nib_shift = (sb & 1) * 4;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    const uint8_t* wr = W + (size_t)row * rb;
+    float acc[kMaxTok];
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) acc[t] = 0.f;
+    constexpr int U = 4;  // blocks whose loads are issued before any is used
+    for (int b0 = 0; b0 < nblk; b0 += U) {
+      uint4 hdr[U];
+      uint2 qh[U], qs[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint8_t* blk = wr + (size_t)min(b0 + u, nblk - 1) * LB_Q5K;  // clamped
+        hdr[u] = __ldg(reinterpret_cast<const uint4*>(blk));
+        qh[u] = __ldg(reinterpret_cast<const uint2*>(blk + 16 + pos));
+        qs[u] = __ldg(reinterpret_cast<const uint2*>(blk + 48 + 32 * pair + pos));
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int b = b0 + u;
+        if (b >= nblk) continue;
+        const float d = __half2float(__ushort_as_half((unsigned short)(hdr[u].x & 0xFFFFu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[u].x >> 16)));
+        // get-scale-min-k4 (L4316-4336) of sub-block sb from scales[12] at
+        // byte 4: scales[0..3] in hdr.y, [4..7] in hdr.z, [8..11] in hdr.w
+        const int sh8 = 8 * (sb & 3);
+        const uint32_t by = (hdr[u].y >> sh8) & 0xFFu, bz = (hdr[u].z >> sh8) & 0xFFu;
+        uint32_t sc, mn;
+        if (sb < 4) {
+          sc = by & 63u;
+          mn = bz & 63u;
+        } else {
+          const uint32_t bw = (hdr[u].w >> sh8) & 0xFFu;
+          sc = (bw & 0x0Fu) | ((by >> 6) << 4);
+          mn = (bw >> 4) | ((bz >> 6) << 4);
+        }
+        const float delta = d * (float)sc, offset = dmin * (float)mn;
+        const uint32_t w0 = ((qs[u].x >> nib_shift) & 0x0F0F0F0Fu) |
+                            (((qh[u].x >> sb) & 0x01010101u) << 4);
+        const uint32_t w1 = ((qs[u].y >> nib_shift) & 0x0F0F0F0Fu) |
+                            (((qh[u].y >> sb) & 0x01010101u) << 4);
+        float q[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          q[i] = __uint_as_float(__byte_perm(w0, 0x4B000000u, 0x7440u | i)) - 8388608.0f;
+          q[4 + i] = __uint_as_float(__byte_perm(w1, 0x4B000000u, 0x7440u | i)) - 8388608.0f;
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxTok; ++t) {
+          if (t < tokens) {
+            const float4* xb = reinterpret_cast<const float4*>(xs + t * K + b * 256 + 8 * lane);
+            const float4 xa = xb[0], xc = xb[1];
+            float qx = q[0] * xa.x;
+            qx = fmaf(q[1], xa.y, qx);
+            qx = fmaf(q[2], xa.z, qx);
+            qx = fmaf(q[3], xa.w, qx);
+            qx = fmaf(q[4], xc.x, qx);
+            qx = fmaf(q[5], xc.y, qx);
+            qx = fmaf(q[6], xc.z, qx);
+            qx = fmaf(q[7], xc.w, qx);
+            const float sx = ((xa.x + xa.y) + (xa.z + xa.w)) + ((xc.x + xc.y) + (xc.z + xc.w));
+            acc[t] = fmaf(delta, qx, fmaf(-offset, sx, acc[t]));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) {
+      if (t < tokens) {
+        const float v = warp_sum(acc[t]);
+        if (lane == 0) y[(long)t * ldy + row] = v;
+      }
+    }
+  }
+}
+
 __global__ void check_scales_kernel(int type, const uint8_t* __restrict__ W, size_t blocks,
                                     unsigned* bad) {
   unsigned local = 0;
   for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < blocks;
        b += (size_t)gridDim.x * blockDim.x) {
-    if (type == LB_TYPE_Q4_K) {
-      const uint8_t* p = W + b * LB_Q4K;
+    if (type == LB_TYPE_Q4_K || type == LB_TYPE_Q5_K) {  // d, dmin at bytes 0, 2
+      const uint8_t* p = W + b * (type == LB_TYPE_Q4_K ? LB_Q4K : LB_Q5K);
       const uint32_t d = p[0] | (p[1] << 8), m = p[2] | (p[3] << 8);
       local += ((d & 0x7C00u) == 0x7C00u) || ((m & 0x7C00u) == 0x7C00u);
     } else if (type == LB_TYPE_Q5_0 || type == LB_TYPE_Q8_0) {
@@ -1074,14 +1176,16 @@ cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemv_q32(int type, const void* W, size_t rb, int rows, int K, const float* x,
-                            long ldx, int tokens, float* y, long ldy, cudaStream_t stream) {
-  if (rows <= 0 || tokens <= 0) return cudaSuccess;
-  if ((type != LB_TYPE_Q5_0 && type != LB_TYPE_Q8_0) || K % 32) return cudaErrorInvalidValue;
-  // tokens per launch: up to 8 whose inputs fit in 192 KB of shared memory
+namespace {
+
+// Launches a shared-memory-input GEMV kernel (Q5_0 / Q8_0 / Q5_K) over the
+// tokens in chunks of up to 8 whose inputs fit in 192 KB.
+template <typename Kern>
+cudaError_t launch_smem_gemv(Kern kern, const void* W, size_t rb, int rows, int K, const float* x,
+                             long ldx, int n_valid, int tokens, float* y, long ldy,
+                             cudaStream_t stream) {
+  if ((size_t)K * 4 > 192 * 1024 || n_valid > K || n_valid < 0) return cudaErrorInvalidValue;
   const int per = std::max(1, std::min(8, (int)((192 * 1024) / ((size_t)K * 4))));
-  if ((size_t)K * 4 > 192 * 1024) return cudaErrorInvalidValue;
-  auto kern = type == LB_TYPE_Q5_0 ? gemv_q32_kernel<LB_TYPE_Q5_0> : gemv_q32_kernel<LB_TYPE_Q8_0>;
   const int grid = std::max(1, std::min((rows + 7) / 8, sm_count() * 8));
   for (int t0 = 0; t0 < tokens; t0 += per) {
     const int nt = std::min(per, tokens - t0);
@@ -1090,16 +1194,66 @@ cudaError_t launch_gemv_q32(int type, const void* W, size_t rb, int rows, int K,
                                          (int)std::max<size_t>(smem, 1));
     if (e != cudaSuccess) return e;
     kern<<<grid, 256, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, K,
-                                      x + (long)t0 * ldx, ldx, nt, y + (long)t0 * ldy, ldy);
+                                      x + (long)t0 * ldx, ldx, n_valid, nt, y + (long)t0 * ldy,
+                                      ldy);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
 
+}  // namespace
+
+cudaError_t launch_gemv_q32(int type, const void* W, size_t rb, int rows, int K, const float* x,
+                            long ldx, int tokens, float* y, long ldy, cudaStream_t stream,
+                            int n_valid) {
+  if (rows <= 0 || tokens <= 0) return cudaSuccess;
+  if ((type != LB_TYPE_Q5_0 && type != LB_TYPE_Q8_0) || K % 32) return cudaErrorInvalidValue;
+  auto kern = type == LB_TYPE_Q5_0 ? gemv_q32_kernel<LB_TYPE_Q5_0> : gemv_q32_kernel<LB_TYPE_Q8_0>;
+  return launch_smem_gemv(kern, W, rb, rows, K, x, ldx, n_valid < 0 ? K : n_valid, tokens, y,
+                          ldy, stream);
+}
+
+cudaError_t launch_gemv_q5k(const void* W, size_t rb, int rows, int K, const float* x, long ldx,
+                            int n_valid, int tokens, float* y, long ldy, cudaStream_t stream) {
+  if (rows <= 0 || tokens <= 0) return cudaSuccess;
+  if (K % 256 || rb != (size_t)K / 256 * LB_Q5K || (reinterpret_cast<uintptr_t>(W) & 15))
+    return cudaErrorInvalidValue;
+  return launch_smem_gemv(gemv_q5k_kernel, W, rb, rows, K, x, ldx, n_valid < 0 ? K : n_valid,
+                          tokens, y, ldy, stream);
+}
+
+cudaError_t launch_projection(int type, const void* W, size_t rb, int rows, int K, const float* x,
+                              long ldx, int n_valid, int tokens, float* y, long ldy, float* xp,
+                              int* status, cudaStream_t stream) {
+  if (rows <= 0 || tokens <= 0) return cudaSuccess;
+  switch (type) {
+    case LB_TYPE_F32:
+      if (n_valid != K) return cudaErrorInvalidValue;
+      return launch_gemv_f32(W, rows, K, x, ldx, tokens, y, ldy, stream);
+    case LB_TYPE_Q5_0:
+    case LB_TYPE_Q8_0:
+      return launch_gemv_q32(type, W, rb, rows, K, x, ldx, tokens, y, ldy, stream, n_valid);
+    case LB_TYPE_Q5_K:
+      return launch_gemv_q5k(W, rb, rows, K, x, ldx, n_valid, tokens, y, ldy, stream);
+    case LB_TYPE_Q4_K:
+    case LB_TYPE_Q6_K: {
+      cudaError_t e = cudaSuccess;
+      if (n_valid == K && launch_gemv_fused(type, W, rb, rows, K, x, ldx, tokens, y, ldy, status,
+                                            stream, &e))
+        return e;
+      e = launch_prep(type, rows, x, ldx, n_valid, K, tokens, nullptr, xp, stream);
+      if (e != cudaSuccess) return e;
+      return launch_gemv_prepped(type, W, rb, rows, K, xp, tokens, y, ldy, status, stream);
+    }
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t check_fp16_scales(int type, const void* W, size_t blocks, unsigned* bad,
                               cudaStream_t stream) {
   if (type != LB_TYPE_Q4_K && type != LB_TYPE_Q6_K && type != LB_TYPE_Q5_0 &&
-      type != LB_TYPE_Q8_0)
+      type != LB_TYPE_Q8_0 && type != LB_TYPE_Q5_K)
     return cudaSuccess;
   const size_t grid = std::min<size_t>((blocks + 255) / 256, (size_t)sm_count() * 8);
   check_scales_kernel<<<(int)std::max<size_t>(grid, 1), 256, 0, stream>>>(

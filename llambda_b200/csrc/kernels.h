@@ -41,10 +41,22 @@ bool launch_gemv_fused(int type, const void* W, size_t row_bytes, int rows, int 
 cudaError_t launch_gemv_prepped(int type, const void* W, size_t row_bytes, int rows, int K,
                                 const float* xp, int tokens, float* y, long ldy, int* status,
                                 cudaStream_t stream);
-// Q5_0 / Q8_0 rows (32-value blocks): x natural layout, no preparation.
+// Q5_0 / Q8_0 rows (32-value blocks): x natural layout, no preparation;
+// n_valid values per token (zero past them), -1: K.
 cudaError_t launch_gemv_q32(int type, const void* W, size_t row_bytes, int rows, int K,
                             const float* x, long ldx, int tokens, float* y, long ldy,
+                            cudaStream_t stream, int n_valid = -1);
+// Q5_K rows (176-byte super-blocks): x natural layout, no preparation.
+cudaError_t launch_gemv_q5k(const void* W, size_t row_bytes, int rows, int K, const float* x,
+                            long ldx, int n_valid, int tokens, float* y, long ldy,
                             cudaStream_t stream);
+// Any projection type (F32, Q4_K, Q5_K, Q6_K, Q5_0, Q8_0): y[t][r] = W[r] .
+// x[t], x [tokens][ldx] with n_valid values per token, zero-extended to K
+// (F32 rows need n_valid == K).  xp: scratch of xprep_floats(K, tokens)
+// floats (Q4_K / Q6_K); status: the device status word of the staged kernels.
+cudaError_t launch_projection(int type, const void* W, size_t row_bytes, int rows, int K,
+                              const float* x, long ldx, int n_valid, int tokens, float* y,
+                              long ldy, float* xp, int* status, cudaStream_t stream);
 // F32 rows (router): x natural layout, no preparation.
 cudaError_t launch_gemv_f32(const void* W, int rows, int K, const float* x, long ldx, int tokens,
                             float* y, long ldy, cudaStream_t stream);
@@ -110,7 +122,25 @@ struct MoeDevice {
   // writes %globaltimer stamps here: start, its pushes done, every peer
   // seen, end.
   unsigned long long* ep_stamps;
+  // Nemotron latent projections (latent_dim > 0; ffn_latent_down and
+  // ffn_latent_up, llambda.lisp L5845-5855, L5883-5887, L5933-5938): the
+  // routed experts run on latent_down . x (latent_dim values; the expert
+  // tensors' widths are latent ones), their weighted sum goes through
+  // latent_up back to `hidden`, and then the shared expert (on x) is added.
+  int latent_dim;
+  int lat_down_type, lat_up_type;  // any projection type
+  int k_lat_down, k_lat_up;        // row widths (>= hidden, >= latent_dim)
+  const uint8_t* lat_down;         // [latent_dim][k_lat_down]
+  const uint8_t* lat_up;           // [hidden][k_lat_up]
+  size_t lat_down_rb, lat_up_rb;
+  // The router logits are already in the workspace (the routed sub-layer of
+  // a latent layer): no router stage.
+  int logits_ready;
 };
+
+// The routed experts of a latent layer as a layer of their own: hidden =
+// latent_dim, no norm, residual or shared expert, logits computed before.
+MoeDevice latent_routed_view(const MoeDevice& m);
 
 // The tokens [t0, t1) of a T-token call the shared expert is computed for.
 __host__ __device__ inline void shared_tokens(const MoeDevice& m, int T, int& t0, int& t1) {
@@ -164,6 +194,15 @@ struct MoeWork {
   int* pf_count;      // [2] tiles of the gate/up and the down pass
   float* pf_rlog;     // [slices][T][E+1] router logits per K slice
   long pf_max_up;
+  // Latent layers (m.latent_dim > 0), carved after the routed sub-layer's
+  // buffers (which are sized by latent_routed_view(m)):
+  float* lat_xr;      // [T][H] rms-normed input (with input_norm)
+  float* lat_x;       // [T][L] latent_down . x: the experts' input
+  float* lat_y;       // [T][L] the experts' weighted sum
+  float* lat_u;       // [T][H] latent_up . lat_y
+  float* lat_s1;      // [T][inter_sh] shared up, relu^2 in place
+  float* lat_s2;      // [T][H] shared down
+  float* lat_xp;      // prepared inputs of the K-quant projections
   size_t bytes;
 };
 

@@ -1851,7 +1851,9 @@ cudaError_t launch_up_mma(const MoeDevice& m, const MoeWork& w, int T, const Sla
 
 }  // namespace
 
-cudaError_t moe_maps_build(const MoeDevice& m, SlabMaps* out) {
+cudaError_t moe_maps_build(const MoeDevice& m_in, SlabMaps* out) {
+  // a latent layer's gate/up matrices are those of its routed sub-layer
+  const MoeDevice m = m_in.latent_dim > 0 ? latent_routed_view(m_in) : m_in;
   SlabMaps& mp = *out;
   mp.ready = 0;
   if (m.up_type != LB_TYPE_Q4_K) return cudaSuccess;
@@ -1932,7 +1934,50 @@ size_t moe_work_bytes(const MoeDevice& m, int T) {
   return w.bytes;
 }
 
+MoeDevice latent_routed_view(const MoeDevice& m) {
+  MoeDevice r = m;
+  r.hidden = m.latent_dim;
+  r.latent_dim = 0;
+  r.input_norm = nullptr;
+  r.add_residual = 0;
+  r.shared_here = 0;
+  r.inter_sh = 0;
+  r.router_rows = 0;
+  r.router_extra_row = nullptr;
+  r.logits_ready = 1;
+  r.ep_world = 0;
+  r.ep_peers = nullptr;
+  return r;
+}
+
 void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
+  if (m.latent_dim > 0) {
+    // the routed sub-layer's buffers first, then the latent path's own
+    const MoeDevice r = latent_routed_view(m);
+    moe_work_carve(r, T, base, w);
+    size_t off = w->bytes;
+    auto take = [&](size_t bytes) {
+      size_t o = off;
+      off += (bytes + 255) & ~size_t(255);
+      return base ? reinterpret_cast<float*>(static_cast<char*>(base) + o) : nullptr;
+    };
+    const size_t H = m.hidden, L = m.latent_dim, Ish = m.shared_here ? m.inter_sh : 0;
+    w->lat_xr = take(m.input_norm ? (size_t)T * H * 4 : 4);
+    w->lat_x = take((size_t)T * L * 4);
+    w->lat_y = take((size_t)T * L * 4);
+    w->lat_u = take((size_t)T * H * 4);
+    w->lat_s1 = take(std::max<size_t>((size_t)T * Ish * 4, 4));
+    w->lat_s2 = take(std::max<size_t>((size_t)T * (Ish ? H : 1) * 4, 4));
+    size_t xp = 1;
+    auto kq = [](int t) { return t == LB_TYPE_Q4_K || t == LB_TYPE_Q6_K; };
+    if (kq(m.lat_down_type)) xp = std::max(xp, xprep_floats(m.k_lat_down, T));
+    if (kq(m.lat_up_type)) xp = std::max(xp, xprep_floats(m.k_lat_up, T));
+    if (Ish && kq(m.up_sh_type)) xp = std::max(xp, xprep_floats(m.k_in_sh, T));
+    if (Ish && kq(m.down_sh_type)) xp = std::max(xp, xprep_floats(m.k_down_sh, T));
+    w->lat_xp = take(xp * 4);
+    w->bytes = off;
+    return;
+  }
   const int E = m.experts, k = m.top_k;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -1940,6 +1985,7 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
     off += (bytes + 255) & ~size_t(255);
     return base ? static_cast<char*>(base) + o : nullptr;
   };
+  w->lat_xr = w->lat_x = w->lat_y = w->lat_u = w->lat_s1 = w->lat_s2 = w->lat_xp = nullptr;
   w->max_tokens = T;
   w->logits = reinterpret_cast<float*>(take((size_t)T * (E + 1) * 4));
   w->sel = reinterpret_cast<int*>(take((size_t)T * k * 4));
@@ -1977,9 +2023,99 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
   w->bytes = off;
 }
 
+namespace {
+
+// rms-norm-into (llambda.lisp L859-879) of each token (one CTA per token):
+// scale = 1 / sqrt(mean(x^2) + eps), dest = (x * weight) * scale.
+__global__ void __launch_bounds__(256) latent_norm_kernel(MoeDevice m, const float* __restrict__ x,
+                                                          float* __restrict__ xn) {
+  __shared__ float s_part[8];
+  const int H = m.hidden;
+  const float* xt = x + (long)blockIdx.x * H;
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) acc = fmaf(xt[i], xt[i], acc);
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += s_part[i];
+  const float scale =
+      __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), m.norm_epsilon)));
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    xn[(long)blockIdx.x * H + i] = __fmul_rn(__fmul_rn(xt[i], m.input_norm[i]), scale);
+}
+
+// apply-relu-squared-into (L938-940, L945-979) in place.
+__global__ void relu_sq_kernel(float* __restrict__ v, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    v[i] = relu_sq_ref(v[i]);
+}
+
+// dest = latent_up . moe-output (L5933-5938), plus the shared expert's down
+// output (vector-add-bias-in-place, L5949), plus x when the layer carries
+// the residual (vector-add-into, L5746): out = x + (lu + sh).
+__global__ void latent_out_kernel(const float* __restrict__ x, const float* __restrict__ lu,
+                                  const float* __restrict__ sh, float* __restrict__ out, long n,
+                                  int residual) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    float v = lu[i];
+    if (sh) v = __fadd_rn(v, sh[i]);
+    out[i] = residual ? __fadd_rn(x[i], v) : v;
+  }
+}
+
+cudaError_t launch_moe_latent(const MoeDevice& m, const MoeWork& w, const float* x, int T,
+                              float* out, const SlabMaps* maps, cudaStream_t s,
+                              const cudaEvent_t* marks) {
+  const int H = m.hidden, L = m.latent_dim, E = m.experts;
+  cudaError_t e;
+  const float* xr = x;
+  if (m.input_norm) {
+    latent_norm_kernel<<<T, 256, 0, s>>>(m, x, w.lat_xr);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    xr = w.lat_xr;
+  }
+  // the router sees x itself (L5889-5892); its logits feed the routed sub-layer
+  e = launch_gemv_f32(m.router, E, H, xr, H, T, w.logits, E + 1, s);
+  if (e != cudaSuccess) return e;
+  e = launch_projection(m.lat_down_type, m.lat_down, m.lat_down_rb, L, m.k_lat_down, xr, H, H, T,
+                        w.lat_x, L, w.lat_xp, w.status, s);
+  if (e != cudaSuccess) return e;
+  const MoeDevice r = latent_routed_view(m);
+  if ((e = launch_moe(r, w, w.lat_x, T, w.lat_y, maps, s, marks)) != cudaSuccess) return e;
+  e = launch_projection(m.lat_up_type, m.lat_up, m.lat_up_rb, H, m.k_lat_up, w.lat_y, L, L, T,
+                        w.lat_u, H, w.lat_xp, w.status, s);
+  if (e != cudaSuccess) return e;
+  const bool shared = m.shared_here && m.inter_sh;
+  if (shared) {  // the shared expert on x (L5939-5949)
+    const int I = m.inter_sh;
+    e = launch_projection(m.up_sh_type, m.up_sh, m.up_sh_rb, I, m.k_in_sh, xr, H, H, T, w.lat_s1,
+                          I, w.lat_xp, w.status, s);
+    if (e != cudaSuccess) return e;
+    const long n = (long)T * I;
+    relu_sq_kernel<<<(int)std::min<long>((n + 255) / 256, sm_count() * 8L), 256, 0, s>>>(w.lat_s1, n);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    e = launch_projection(m.down_sh_type, m.down_sh, m.down_sh_rb, H, m.k_down_sh, w.lat_s1, I, I,
+                          T, w.lat_s2, H, w.lat_xp, w.status, s);
+    if (e != cudaSuccess) return e;
+  }
+  const long n = (long)T * H;
+  latent_out_kernel<<<(int)std::min<long>((n + 255) / 256, sm_count() * 8L), 256, 0, s>>>(
+      x, w.lat_u, shared ? w.lat_s2 : nullptr, out, n, m.add_residual);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int T, float* out,
                        const SlabMaps* maps, cudaStream_t s, const cudaEvent_t* marks) {
   if (T <= 0) return cudaSuccess;
+  if (m.latent_dim > 0) {
+    if (T > w.max_tokens || m.arch != 1 || m.ep_world > 1) return cudaErrorInvalidValue;
+    return launch_moe_latent(m, w, x, T, out, maps, s, marks);
+  }
   if (T > w.max_tokens || m.experts > kMaxExperts || m.top_k > 32 || T * m.top_k > kMaxEntries)
     return cudaErrorInvalidValue;
   if (m.inter_sh && m.k_in_sh != m.k_in) return cudaErrorInvalidValue;
@@ -1993,7 +2129,15 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   const bool prefill = prefill_applies(m, w, T);
   auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
   if ((e = mark(3)) != cudaSuccess) return e;
-  if (prefill) {
+  if (m.logits_ready) {  // the routed sub-layer of a latent layer: no router
+    if (!prefill) {
+      if (m.up_type == LB_TYPE_Q4_K)
+        moe_prep_kernel<LB_TYPE_Q4_K><<<T, 256, 0, s>>>(m, w, x);
+      else
+        moe_prep_kernel<LB_TYPE_Q6_K><<<T, 256, 0, s>>>(m, w, x);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+  } else if (prefill) {
     if ((e = launch_prefill_router(m, w, x, T, s)) != cudaSuccess) return e;
   } else if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
       router_smem <= 192 * 1024 &&

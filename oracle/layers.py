@@ -24,6 +24,16 @@ def max_rel(y: np.ndarray, r: np.ndarray) -> float:
     return float(np.max(np.abs(y - r)) / den) if den > 0 else float(np.max(np.abs(y - r)))
 
 
+def random_q5k(blocks: int, seed: int, stream: int, dscale: float) -> np.ndarray:
+    """Q5_K blocks (176 bytes) from numpy's seeded generator: d, dmin =
+    fp16(|N(0,1)| * dscale), the 12 packed scale bytes, qh and qs uniform.
+    The device generator has no Q5_K form; these blocks are uploaded."""
+    rng = np.random.default_rng([seed, stream, 13])
+    dm = (np.abs(rng.standard_normal((blocks, 2))) * dscale).astype(np.float16)
+    rest = rng.integers(0, 256, (blocks, 172), dtype=np.uint8)
+    return np.ascontiguousarray(np.concatenate([dm.view(np.uint8), rest], axis=1)).reshape(-1)
+
+
 def host_tensor(type_tag: int, ne0: int, ne1: int, ne2: int, seed: int, stream: int,
                 scale: float) -> np.ndarray:
     units = CF.tensor_units(type_tag, ne0, ne1, ne2)
@@ -31,6 +41,8 @@ def host_tensor(type_tag: int, ne0: int, ne1: int, ne2: int, seed: int, stream: 
         return O.synth_f32(seed, stream, 0, units, scale)
     if type_tag == TYPE_Q4_K:
         return O.synth_q4k(seed, stream, 0, units, scale)
+    if type_tag == O.TYPE_Q5_K:
+        return random_q5k(units, seed, stream, scale)
     return O.synth_q6k(seed, stream, 0, units, scale)
 
 
@@ -65,4 +77,5 @@ def oracle_layer(cfg: CF.MoeConfig, tensors: dict, input_norm=None, eps=1e-6,
     L.input_norm = input_norm.ctypes.data if input_norm is not None else None
     L.norm_epsilon = eps
     L.add_residual = int(residual)
+    L.latent_down, L.latent_up = T("ffn_latent_down"), T("ffn_latent_up")
     return L

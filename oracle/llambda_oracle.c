@@ -35,6 +35,7 @@
 #define OR_QK_K 256
 #define OR_Q4K_BLOCK 144 /* 4 + 12 + 128, L2142 */
 #define OR_Q6K_BLOCK 210 /* 2 + 16 + 192, L2144 */
+#define OR_Q5K_BLOCK 176 /* 4 + 12 + 32 + 128, L2143 */
 #define OR_Q5_0_BLOCK 22 /* 2 + 4 + 16, L2139 */
 #define OR_Q8_0_BLOCK 34 /* 2 + 32, L2140 */
 
@@ -196,6 +197,85 @@ int or_dot_q4_k(const uint8_t *row, const float *x, size_t count, float *out) {
     }
   }
   *out = or_hsum8(sum);
+  return 0;
+}
+
+/* One Q5_K value (dot-product-with-q5-k-tensor-data, L4418-4423;
+ * dequantize-q5-k, L6900-6911): in sub-block pair `group` (values
+ * 64*group .. +63), lane l's low nibble of qs[32*group + l] with qh bit
+ * 2*group is value l, its high nibble with qh bit 2*group + 1 is value 32 + l. */
+static int or_q5_k_value(const uint8_t *qh, const uint8_t *qs, int group, int lane, int high) {
+  const int packed = qs[32 * group + lane], bits = qh[lane];
+  const int u = 1 << (2 * group + high);
+  return (high ? (packed >> 4) : (packed & 0x0F)) + ((bits & u) ? 16 : 0);
+}
+
+/* dequantize-q5-k, L6861-6917: w = d*sc*q - dmin*m, each step rounded. */
+int or_dequantize_q5_k(const uint8_t *p, size_t count, float *out) {
+  if (count % OR_QK_K) {
+    or_fail("Q5_K dequantization requires ELEMENT-COUNT to be a multiple of 256.%s", 0);
+    return -1;
+  }
+  for (size_t b = 0; b < count / OR_QK_K; ++b) {
+    const uint8_t *blk = p + b * OR_Q5K_BLOCK;
+    int err = 0;
+    float d = or_read_fp16(blk, &err), dmin = or_read_fp16(blk + 2, &err);
+    if (err) return -1;
+    const uint8_t *scales = blk + 4, *qh = blk + 16, *qs = blk + 48;
+    float *r = out + b * OR_QK_K;
+    for (int group = 0; group < 4; ++group) {
+      int sc0, m0, sc1, m1;
+      or_get_scale_min_k4(scales, 2 * group, &sc0, &m0);
+      or_get_scale_min_k4(scales, 2 * group + 1, &sc1, &m1);
+      float delta0 = d * (float)sc0, offset0 = dmin * (float)m0;
+      float delta1 = d * (float)sc1, offset1 = dmin * (float)m1;
+      for (int lane = 0; lane < 32; ++lane) {
+        float lo = delta0 * (float)or_q5_k_value(qh, qs, group, lane, 0);
+        float hi = delta1 * (float)or_q5_k_value(qh, qs, group, lane, 1);
+        r[group * 64 + lane] = lo - offset0;
+        r[group * 64 + 32 + lane] = hi - offset1;
+      }
+    }
+  }
+  return 0;
+}
+
+/* dot-product-with-q5-k-tensor-data, L4387-4441: one single-float sum over
+ * the row, in order: for each sub-block pair, for each lane, the low value's
+ * product then the high value's, every multiply, subtract and add rounded on
+ * its own (no FMA: the reference's scalar loop, not an f32.8 one). */
+int or_dot_q5_k(const uint8_t *row, const float *x, size_t count, float *out) {
+  if (count % OR_QK_K) {
+    or_fail("Q5_K dot product requires ELEMENT-COUNT to be a multiple of 256.%s", 0);
+    return -1;
+  }
+  float sum = 0.0f;
+  for (size_t b = 0; b < count / OR_QK_K; ++b) {
+    const uint8_t *blk = row + b * OR_Q5K_BLOCK;
+    int err = 0;
+    float d = or_read_fp16(blk, &err), dmin = or_read_fp16(blk + 2, &err);
+    if (err) return -1;
+    const uint8_t *scales = blk + 4, *qh = blk + 16, *qs = blk + 48;
+    const float *xb = x + b * OR_QK_K;
+    for (int group = 0; group < 4; ++group) {
+      int sc0, m0, sc1, m1;
+      or_get_scale_min_k4(scales, 2 * group, &sc0, &m0);
+      or_get_scale_min_k4(scales, 2 * group + 1, &sc1, &m1);
+      float delta0 = d * (float)sc0, offset0 = dmin * (float)m0;
+      float delta1 = d * (float)sc1, offset1 = dmin * (float)m1;
+      for (int lane = 0; lane < 32; ++lane) {
+        float w0 = delta0 * (float)or_q5_k_value(qh, qs, group, lane, 0);
+        float w1 = delta1 * (float)or_q5_k_value(qh, qs, group, lane, 1);
+        w0 = w0 - offset0;
+        w1 = w1 - offset1;
+        float p0 = xb[64 * group + lane] * w0;
+        sum = sum + p0;
+        float p1 = xb[64 * group + 32 + lane] * w1;
+        sum = sum + p1;
+      }
+    }
+  }
+  *out = sum;
   return 0;
 }
 
@@ -361,6 +441,7 @@ size_t or_row_bytes(int type, size_t columns) {
     case OR_TYPE_F32: return columns * 4;
     case OR_TYPE_Q4_K: return columns % OR_QK_K ? 0 : columns / OR_QK_K * OR_Q4K_BLOCK;
     case OR_TYPE_Q6_K: return columns % OR_QK_K ? 0 : columns / OR_QK_K * OR_Q6K_BLOCK;
+    case OR_TYPE_Q5_K: return columns % OR_QK_K ? 0 : columns / OR_QK_K * OR_Q5K_BLOCK;
     case OR_TYPE_Q5_0: return columns % 32 ? 0 : columns / 32 * OR_Q5_0_BLOCK;
     case OR_TYPE_Q8_0: return columns % 32 ? 0 : columns / 32 * OR_Q8_0_BLOCK;
     default: return 0;
@@ -403,8 +484,10 @@ int or_gemv(const or_tensor *t, size_t start_row, size_t row_count,
   long n = (long)row_count;
 #pragma omp parallel for num_threads(parts) schedule(static) reduction(| : failed)
   for (long r = 0; r < n; ++r) {
-    int rc = t->type == OR_TYPE_Q4_K ? or_dot_q4_k(base + r * rb, x, cols, &y[r])
-                                     : or_dot_q6_k(base + r * rb, x, cols, &y[r]);
+    /* Q4_K, Q5_K and Q6_K rows split over the workers (L4600-4650) */
+    int rc = t->type == OR_TYPE_Q4_K   ? or_dot_q4_k(base + r * rb, x, cols, &y[r])
+             : t->type == OR_TYPE_Q5_K ? or_dot_q5_k(base + r * rb, x, cols, &y[r])
+                                       : or_dot_q6_k(base + r * rb, x, cols, &y[r]);
     failed |= rc != 0;
   }
   if (failed) { /* worker threads keep their own error text */
@@ -509,18 +592,25 @@ static void or_add_scaled(float *dest, const float *src, size_t n, float s) {
 static size_t or_max(size_t a, size_t b) { return a > b ? a : b; }
 
 /* qwen3next-moe-into, L5321-5426 (routed part L5354-5409, shared expert
- * L5410-5426), and nemotron-h-moe-ffn-into, L5827-5949 (without the optional
- * latent projections).  Tokens are independent calls, as in the reference.
- * selected/weights (optional) receive the top-k indices and final weights. */
+ * L5410-5426), and nemotron-h-moe-ffn-into, L5827-5949, with its optional
+ * latent projections: the experts run on latent_down . x (L5845-5855,
+ * L5883-5887), their weighted sum has the latent width, and latent_up maps
+ * it back to the hidden size before the shared expert is added (L5933-5938);
+ * the router and the shared expert see x itself.  Tokens are independent
+ * calls, as in the reference.  selected/weights (optional) receive the top-k
+ * indices and final weights. */
 int or_moe_forward(const or_moe_layer *L, const float *x, size_t tokens,
                    float *out, int32_t *selected, float *weights) {
   size_t H = L->hidden;
   size_t E = L->router.ne1;
   int k = L->top_k < (int)E ? L->top_k : (int)E;
   size_t inter = L->up_exps.ne1, inter_sh = L->up_shexp.data ? L->up_shexp.ne1 : 0;
+  const int latent = L->arch == 1 && L->latent_down.data && L->latent_up.data;
+  size_t LD = latent ? L->latent_down.ne1 : H; /* the experts' input and output width */
   size_t width = or_max(or_max(H, inter), inter_sh);
   width = or_max(width, or_max(L->up_exps.ne0, L->down_exps.ne0));
   if (L->up_shexp.data) width = or_max(width, or_max(L->up_shexp.ne0, L->down_shexp.ne0));
+  if (latent) width = or_max(width, or_max(L->latent_down.ne0, L->latent_up.ne0));
   float *logits = malloc(E * sizeof(float));
   float *pad = malloc(width * sizeof(float));
   float *gate = malloc(width * sizeof(float));
@@ -530,8 +620,10 @@ int or_moe_forward(const or_moe_layer *L, const float *x, size_t tokens,
   float *tl = malloc((size_t)k * sizeof(float));
   float *tw = malloc((size_t)k * sizeof(float));
   float *xn = malloc(H * sizeof(float));
+  float *xe = malloc(width * sizeof(float)); /* expert input (latent) */
+  float *mo = malloc(width * sizeof(float)); /* routed sum (latent) */
   int rc = -1;
-  if (!logits || !pad || !gate || !up || !down || !ti || !tl || !tw || !xn) {
+  if (!logits || !pad || !gate || !up || !down || !ti || !tl || !tw || !xn || !xe || !mo) {
     or_fail("Out of memory.%s", 0);
     goto done;
   }
@@ -543,6 +635,15 @@ int or_moe_forward(const or_moe_layer *L, const float *x, size_t tokens,
       xt = xn;
     }
     memset(dest, 0, H * sizeof(float));
+    /* the experts' input: latent_down . x (L5883-5887), else x */
+    const float *xin = xt;
+    float *acc = dest;
+    if (latent) {
+      if (or_project(&L->latent_down, -1, xt, H, pad, xe)) goto done;
+      xin = xe;
+      memset(mo, 0, LD * sizeof(float));
+      acc = mo;
+    }
     if (or_gemv(&L->router, 0, E, xt, logits)) goto done;
     if (L->arch == 1 && L->router_bias) /* vector-add-bias-in-place, L5892 */
       for (size_t i = 0; i < E; ++i) logits[i] = logits[i] + L->router_bias[i];
@@ -569,12 +670,14 @@ int or_moe_forward(const or_moe_layer *L, const float *x, size_t tokens,
         for (size_t j = 0; j < inter; ++j) gate[j] = or_silu(gate[j]);
         for (size_t j = 0; j < inter; ++j) gate[j] = gate[j] * up[j];
       } else {
-        if (or_project(&L->up_exps, e, xt, H, pad, gate)) goto done;
+        if (or_project(&L->up_exps, e, xin, LD, pad, gate)) goto done;
         for (size_t j = 0; j < inter; ++j) gate[j] = or_relu_squared(gate[j]);
       }
       if (or_project(&L->down_exps, e, gate, inter, pad, down)) goto done;
-      or_add_scaled(dest, down, H, tw[i]);
+      or_add_scaled(acc, down, LD, tw[i]);
     }
+    if (latent) /* dest = latent_up . moe-output (L5933-5938) */
+      if (or_project(&L->latent_up, -1, mo, LD, pad, dest)) goto done;
     if (L->arch == 0 && L->up_shexp.data) {
       float sw = or_sigmoid(or_dot_product(L->shared_gate_inp, xt, H));
       if (or_project(&L->gate_shexp, -1, xt, H, pad, gate)) goto done;
@@ -597,7 +700,7 @@ int or_moe_forward(const or_moe_layer *L, const float *x, size_t tokens,
   rc = 0;
 done:
   free(logits); free(pad); free(gate); free(up); free(down);
-  free(ti); free(tl); free(tw); free(xn);
+  free(ti); free(tl); free(tw); free(xn); free(xe); free(mo);
   return rc;
 }
 

@@ -22,6 +22,7 @@ enum {
   OR_TYPE_Q5_0 = 6,
   OR_TYPE_Q8_0 = 8,
   OR_TYPE_Q4_K = 12,
+  OR_TYPE_Q5_K = 13,
   OR_TYPE_Q6_K = 14
 };
 
@@ -48,6 +49,9 @@ typedef struct {
   const float *input_norm;  /* post_attention_norm weight, or NULL */
   float norm_epsilon;
   int add_residual;         /* out = x + moe(rms_norm(x)) */
+  /* nemotron ffn_latent_down [hidden -> latent] and ffn_latent_up
+   * [latent -> hidden], both or neither (data NULL: none) */
+  or_tensor latent_down, latent_up;
 } or_moe_layer;
 
 const char *or_last_error(void);
@@ -60,6 +64,8 @@ int or_dequantize_q4_k(const uint8_t *blocks, size_t count, float *out);
 int or_dequantize_q6_k(const uint8_t *blocks, size_t count, float *out);
 int or_dot_q4_k(const uint8_t *row, const float *x, size_t count, float *out);
 int or_dot_q6_k(const uint8_t *row, const float *x, size_t count, float *out);
+int or_dequantize_q5_k(const uint8_t *blocks, size_t count, float *out);
+int or_dot_q5_k(const uint8_t *row, const float *x, size_t count, float *out);
 int or_dequantize_q5_0(const uint8_t *blocks, size_t count, float *out);
 int or_dequantize_q8_0(const uint8_t *blocks, size_t count, float *out);
 int or_dot_q5_0(const uint8_t *row, const float *x, size_t count, float *out);

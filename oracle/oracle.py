@@ -17,9 +17,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
-TYPE_F32, TYPE_F16, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 12, 14
+TYPE_F32, TYPE_F16, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 0, 1, 12, 13, 14
 TYPE_Q5_0, TYPE_Q8_0 = 6, 8
-Q4K_BLOCK, Q6K_BLOCK, QK_K = 144, 210, 256
+Q4K_BLOCK, Q5K_BLOCK, Q6K_BLOCK, QK_K = 144, 176, 210, 256
 
 _lib = None
 
@@ -43,7 +43,8 @@ class MoeLayer(C.Structure):
                 ("gate_exps", Tensor), ("up_exps", Tensor), ("down_exps", Tensor),
                 ("gate_shexp", Tensor), ("up_shexp", Tensor), ("down_shexp", Tensor),
                 ("input_norm", C.c_void_p), ("norm_epsilon", C.c_float),
-                ("add_residual", C.c_int)]
+                ("add_residual", C.c_int),
+                ("latent_down", Tensor), ("latent_up", Tensor)]
 
 
 def lib():
@@ -58,10 +59,10 @@ def lib():
         L.or_fp16_to_f32.restype = C.c_float
         L.or_get_scale_min_k4.argtypes = [u8p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
         for name in ("or_dequantize_q4_k", "or_dequantize_q6_k", "or_dequantize_q5_0",
-                     "or_dequantize_q8_0"):
+                     "or_dequantize_q8_0", "or_dequantize_q5_k"):
             getattr(L, name).argtypes = [u8p, C.c_size_t, fp]
             getattr(L, name).restype = C.c_int
-        for name in ("or_dot_q4_k", "or_dot_q6_k", "or_dot_q5_0", "or_dot_q8_0"):
+        for name in ("or_dot_q4_k", "or_dot_q6_k", "or_dot_q5_0", "or_dot_q8_0", "or_dot_q5_k"):
             getattr(L, name).argtypes = [u8p, fp, C.c_size_t, fp]
             getattr(L, name).restype = C.c_int
         for name in ("or_dot_f32", "or_dot_product"):
@@ -119,7 +120,8 @@ def fp16_to_f32(bits: int) -> float:
 def dequantize(type_tag: int, blocks: np.ndarray, count: int) -> np.ndarray:
     out = np.empty(count, np.float32)
     fn = {TYPE_Q4_K: lib().or_dequantize_q4_k, TYPE_Q6_K: lib().or_dequantize_q6_k,
-          TYPE_Q5_0: lib().or_dequantize_q5_0, TYPE_Q8_0: lib().or_dequantize_q8_0}[type_tag]
+          TYPE_Q5_0: lib().or_dequantize_q5_0, TYPE_Q8_0: lib().or_dequantize_q8_0,
+          TYPE_Q5_K: lib().or_dequantize_q5_k}[type_tag]
     _check(fn(blocks.ctypes.data, count, _fptr(out)))
     return out
 
@@ -130,7 +132,8 @@ def dot_row(type_tag: int, row: np.ndarray, x: np.ndarray) -> float:
     if type_tag == TYPE_F32:
         return lib().or_dot_f32(_fptr(np.ascontiguousarray(row, np.float32)), _fptr(x), x.size)
     fn = {TYPE_Q4_K: lib().or_dot_q4_k, TYPE_Q6_K: lib().or_dot_q6_k,
-          TYPE_Q5_0: lib().or_dot_q5_0, TYPE_Q8_0: lib().or_dot_q8_0}[type_tag]
+          TYPE_Q5_0: lib().or_dot_q5_0, TYPE_Q8_0: lib().or_dot_q8_0,
+          TYPE_Q5_K: lib().or_dot_q5_k}[type_tag]
     _check(fn(row.ctypes.data, _fptr(x), x.size, _fptr(out)))
     return float(out[0])
 
