@@ -370,15 +370,23 @@ class Ctx:
         self.rank, self.world, self.local = rank, world, local
         self.peer = world > 1 and args.reduce == "peer"
         self.collective = world > 1 and not self.peer
+        self.dispatch = False  # token dispatch attached to the open stack
 
 
 def open_stack(ctx, cfg, max_tokens):
     t0 = time.time()
     sessions, keep = build_stack(cfg, ctx.args.layers, ctx.rank, ctx.world, ctx.args.seed,
                                  max_tokens, ctx.torch, peer=ctx.peer)
+    ctx.dispatch = False
     if ctx.peer:  # each layer's combine sums every rank's partial over NVLink
         from llambda_b200 import ep
         keep.append(ep.attach_peer_reduction(sessions))
+        if max_tokens >= ctx.LB.prefill_min_tokens() * ctx.world:
+            # prefill batches: each rank passes its own tokens, which travel to
+            # their experts' owners and back (the token dispatch)
+            keep.append(ep.attach_token_dispatch(sessions,
+                                                 (max_tokens + ctx.world - 1) // ctx.world))
+            ctx.dispatch = True
     ref0 = None
     if ctx.world > 1 and ctx.rank == 0:
         # the whole layer 0 (every expert, shared expert, residual) as one
@@ -407,7 +415,15 @@ def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
     H = cfg.hidden
     x0 = torch.empty(B, H, device="cuda")
     LB.synth_fill_device(LB.TYPE_F32, args.seed, CF.S_ACT, 0, B * H, 1.0, x0)
-    bufs = [torch.empty(B, H, device="cuda") for _ in range(2)]
+    # token dispatch (N > 1, prefill batches): each rank runs its own slice of
+    # the batch through the stack; otherwise every rank holds all B tokens
+    sharded = world > 1 and getattr(ctx, "dispatch", False) and B >= LB.prefill_min_tokens() * world
+    from llambda_b200 import ep as _ep
+    t_lo, t_hi = _ep.token_slice(rank, world, B) if sharded else (0, B)
+    x_full = x0
+    x0 = x0[t_lo:t_hi].contiguous()
+    Bl = t_hi - t_lo
+    bufs = [torch.empty(Bl, H, device="cuda") for _ in range(2)]
     stream = torch.cuda.current_stream()
     if world > 1:
         import torch.distributed as dist
@@ -419,7 +435,7 @@ def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
             out = bufs[li % 2]
             if record is not None:
                 record[li][0].record(st)
-            s.run_device(cur, out, B, stream=st)
+            s.run_device(cur, out, Bl, stream=st)
             if ctx.collective:
                 dist.all_reduce(out)
             if record is not None:
@@ -488,20 +504,28 @@ def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
 
     # routing of the timed steps (identical every step: same x0) -> algorithmic
     # bytes; layer 0's output and selection for the parity check
-    sel = torch.empty(B, cfg.top_k, dtype=torch.int32, device="cuda")
+    sel = torch.empty(Bl, cfg.top_k, dtype=torch.int32, device="cuda")
     eb, ee = rank * cfg.experts // world, (rank + 1) * cfg.experts // world
+
+    def gathered(t):  # every rank's rows, in token order (the token dispatch)
+        if not sharded:
+            return t
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous())
+        return torch.cat(parts)
+
     distinct, own_distinct = [], []
     cur, layer0 = x0, None
     for li, s in enumerate(sessions):
         out = bufs[li % 2]
-        s.run_device(cur, out, B, sel_dev=sel, stream=stream)
+        s.run_device(cur, out, Bl, sel_dev=sel, stream=stream)
         if ctx.collective:
             dist.all_reduce(out)
-        ss = sel.cpu().numpy()
+        ss = gathered(sel).cpu().numpy()
         distinct.append(int(np.unique(ss[ss >= 0]).size))
         own_distinct.append(int(np.unique(ss[(ss >= eb) & (ss < ee)]).size))
         if li == 0:
-            layer0 = (out.cpu().numpy().copy(), ss.copy())
+            layer0 = (gathered(out).cpu().numpy().copy(), ss.copy())
         cur = out
     torch.cuda.synchronize()
     prefill = B >= LB.prefill_min_tokens()
@@ -509,12 +533,13 @@ def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
     if ref0 is not None:  # N > 1: rank 0 checks against the single-device layer
         rout = torch.empty(B, H, device="cuda")
         rsel = torch.empty(B, cfg.top_k, dtype=torch.int32, device="cuda")
-        ref0[0].run_device(x0, rout, B, sel_dev=rsel, stream=stream)
+        ref0[0].run_device(x_full, rout, B, sel_dev=rsel, stream=stream)
         torch.cuda.synchronize()
         parity = parity_record(layer0[0], layer0[1], rout.cpu().numpy().astype(np.float64),
                                rsel.cpu().numpy(),
                                f"single-device session of the whole layer 0 (rank 0, "
-                               f"{'bf16 prefill' if prefill else 'fp32 decode'} kernels)",
+                               f"{'bf16 prefill' if prefill else 'fp32 decode'} kernels)"
+                               + (", all ranks' token slices gathered" if sharded else ""),
                                2e-2 if prefill else 1e-3)
 
     from llambda_b200 import ep as _ep
@@ -562,7 +587,7 @@ def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
     e2e = None
     if e2e_on and not args.no_e2e:
         # page-locked host buffers (the library copies them by DMA, no staging)
-        pinned = [x0.cpu().pin_memory()] + [torch.empty((B, H), dtype=torch.float32,
+        pinned = [x0.cpu().pin_memory()] + [torch.empty((Bl, H), dtype=torch.float32,
                                                         pin_memory=True) for _ in range(2)]
         x_host = pinned[0].numpy()
         gloo = dist.new_group(backend="gloo") if ctx.collective else None
@@ -587,14 +612,18 @@ def measure(ctx, cfg, sessions, ref0, B, clocks=False, e2e_on=True):
             e2e_step()
         dt = max_over_ranks((time.perf_counter() - t0) / args.steps, world)
         e2e = {"value": B / dt, "unit": "tokens/s",
-               "h2d_bytes_per_step": NL * B * H * 4, "d2h_bytes_per_step": NL * B * H * 4,
+               "h2d_bytes_per_step": NL * Bl * H * 4, "d2h_bytes_per_step": NL * Bl * H * 4,
                "path": "llambda_cuda_moe_session_run per layer from and into preallocated "
                        "page-locked host float buffers (the reference's run-into convention)"}
     # decode: rms-norm + router, top-k with routing, gate/up, routed down, shared
     # down (ranks that compute a share of the shared expert), combine.
     # prefill: rms-norm, router K slices, their sum, top-k with routing, gather,
     # tile plan, gate/up, down, combine.
-    per_layer = 9 if prefill else 5 + (1 if streams_shared else 0)
+    # token dispatch: rms-norm, router K slices, their sum, top-k, send,
+    # group, copy, tile plan, gate/up, down, done, wait, combine.
+    per_layer = (13 if sharded else 9) if prefill else 5 + (1 if streams_shared else 0)
+    if sharded:
+        breakdown["mode"] = f"token dispatch: {Bl} of the {B} tokens on each rank"
     return {"value": value, "ms_per_step": ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
             "parity": parity, "ep_breakdown": breakdown, "layer0": layer0,
             "gpu_launches": per_layer * NL * args.steps, "prefill": prefill,

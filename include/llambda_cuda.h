@@ -316,6 +316,36 @@ LLAMBDA_CUDA_API int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_sess
                                                            void* const* peer_buffers,
                                                            size_t bytes);
 
+/* Expert-parallel prefill by token dispatch.  These entry points have no
+ * counterpart in the reference (llambda runs every token through one device).
+ *
+ * Bytes of the symmetric device buffer that `world` ranks need when each
+ * passes at most `max_local_tokens` tokens per call (0 on a bad argument). */
+LLAMBDA_CUDA_API size_t llambda_cuda_moe_dispatch_bytes(const llambda_cuda_moe_session* session,
+                                                        int world, int max_local_tokens);
+
+/* After this call, runs of at least llambda_cuda_prefill_min_tokens()
+ * tokens take the token dispatch: every rank passes ITS OWN tokens (x and
+ * out hold that rank's rows only, at most max_local_tokens of them), each
+ * token's row travels over NVLink peer memory to the ranks owning its
+ * selected experts, those ranks multiply it on the tensor cores (the bf16
+ * prefill GEMMs) and store the result rows back into the source rank's
+ * buffer, and each rank combines its own tokens (weights, shared expert,
+ * residual) as one device would.  Rank r must own experts [r*E/world,
+ * (r+1)*E/world) with shared_here = 1, world * max_local_tokens must not
+ * exceed the session's max_tokens, and every rank must run the same sessions
+ * in the same order.  peer_buffers[r] is rank r's copy of one symmetric
+ * buffer of `bytes` bytes (>= llambda_cuda_moe_dispatch_bytes), mapped into
+ * this process, 256-byte aligned and zero-filled before the first run; the
+ * sessions of a stack may share it.  Smaller runs keep the decode path and
+ * need the peer reduction (llambda_cuda_moe_session_attach_peers).  A rank
+ * that waits more than two seconds for a peer sets bit 2 (value 4) of the
+ * session status. */
+LLAMBDA_CUDA_API int llambda_cuda_moe_session_attach_dispatch(llambda_cuda_moe_session* session,
+                                                              int rank, int world,
+                                                              void* const* peer_buffers,
+                                                              size_t bytes, int max_local_tokens);
+
 /* One MoE layer without any device allocation.  This entry point has no
  * counterpart in the reference.
  *

@@ -90,6 +90,9 @@ SIGNATURES = {
     "llambda_cuda_moe_session_status": (C.c_int, [_vp]),
     "llambda_cuda_moe_session_time_kernels": (C.c_int, [_vp, C.c_int]),
     "llambda_cuda_moe_session_kernel_breakdown": (C.c_int, [_vp, C.POINTER(C.c_float), C.c_int]),
+    "llambda_cuda_moe_dispatch_bytes": (_sz, [_vp, C.c_int, C.c_int]),
+    "llambda_cuda_moe_session_attach_dispatch": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(_vp),
+                                                           _sz, C.c_int]),
     "llambda_cuda_moe_session_kernel_ms": (C.c_int, [_vp, C.POINTER(C.c_float),
                                                       C.POINTER(C.c_float)]),
     "llambda_cuda_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
@@ -370,6 +373,17 @@ class MoeSession:
         peer_ptrs[r] is rank r's copy of one zero-filled symmetric buffer."""
         arr = (_vp * world)(*[int(p) for p in peer_ptrs])
         _check(lib().llambda_cuda_moe_session_attach_peers(self._h, rank, world, arr, nbytes))
+
+    def dispatch_bytes(self, world: int, max_local_tokens: int) -> int:
+        return int(lib().llambda_cuda_moe_dispatch_bytes(self._h, world, max_local_tokens))
+
+    def attach_dispatch(self, rank: int, world: int, peer_ptrs, nbytes: int,
+                        max_local_tokens: int) -> None:
+        """Prefill-sized runs route this rank's own tokens to the experts'
+        owners over peer memory (see llambda_cuda_moe_session_attach_dispatch)."""
+        arr = (_vp * world)(*[int(p) for p in peer_ptrs])
+        _check(lib().llambda_cuda_moe_session_attach_dispatch(self._h, rank, world, arr, nbytes,
+                                                              max_local_tokens))
 
     def time_kernels(self, enable: bool = True) -> None:
         """Record CUDA events around the gate/up and routed down passes of

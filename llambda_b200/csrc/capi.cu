@@ -1017,6 +1017,64 @@ size_t llambda_cuda_moe_peer_bytes(const llambda_cuda_moe_session* s, int world)
   return lb::ep_buffer_bytes(world, s->max_tokens, s->m.hidden);
 }
 
+size_t llambda_cuda_moe_dispatch_bytes(const llambda_cuda_moe_session* s, int world,
+                                       int max_local_tokens) {
+  if (!s || world < 2 || world > lb::kEpMaxWorld || max_local_tokens < 1) return 0;
+  return lb::dx_layout(world, max_local_tokens, s->m.top_k, s->m.k_in, s->m.hidden).bytes;
+}
+
+int llambda_cuda_moe_session_attach_dispatch(llambda_cuda_moe_session* s, int rank, int world,
+                                             void* const* peer_buffers, size_t bytes,
+                                             int max_local_tokens) {
+  if (!s || !peer_buffers) {
+    set_error("A session and the peer buffer pointers are required.");
+    return -1;
+  }
+  return guarded([&] {
+    std::lock_guard<std::mutex> lock(s->mu);
+    DeviceGuard g(s->device);
+    s->drop_graph();
+    s->eager_tokens = 0;
+    const lb::MoeDevice& m = s->m;
+    if (world < 2 || world > lb::kEpMaxWorld || rank < 0 || rank >= world)
+      throw Failure("world must be 2.." + std::to_string(lb::kEpMaxWorld) +
+                    " and 0 <= rank < world.");
+    if (m.latent_dim > 0)
+      throw Failure("A layer with latent projections runs on one device (no token dispatch).");
+    if (m.expert_begin != (int)((long)rank * m.experts / world) ||
+        m.expert_end != (int)((long)(rank + 1) * m.experts / world))
+      throw Failure("The token dispatch needs rank r to own experts [r*E/world, (r+1)*E/world).");
+    if (m.inter_sh && !m.shared_here)
+      throw Failure("Every rank computes the shared expert of its own tokens: shared_here = 1.");
+    if (max_local_tokens < 1 || (long)world * max_local_tokens > s->max_tokens ||
+        s->max_tokens < 64)
+      throw Failure("world * max_local_tokens must be at most the session's max_tokens "
+                    "(and max_tokens at least 64).");
+    const lb::DxLayout L = lb::dx_layout(world, max_local_tokens, m.top_k, m.k_in, m.hidden);
+    if (bytes < L.bytes) throw Failure("The peer buffer is smaller than llambda_cuda_moe_dispatch_bytes.");
+    for (int r = 0; r < world; ++r)
+      if (reinterpret_cast<uintptr_t>(peer_buffers[r]) & 255)
+        throw Failure("Token dispatch buffers must be 256-byte aligned.");
+    std::vector<void*> table(2 * world);
+    for (int r = 0; r < world; ++r) {
+      table[r] = peer_buffers[r];
+      table[world + r] = static_cast<char*>(peer_buffers[r]) + L.partial;
+    }
+    void* dev = nullptr;
+    cuda_check(cudaMalloc(&dev, sizeof(void*) * 2 * world), "cudaMalloc dispatch table");
+    s->owned.push_back(dev);
+    cuda_check(cudaMemcpy(dev, table.data(), sizeof(void*) * 2 * world, cudaMemcpyHostToDevice),
+               "dispatch table copy");
+    s->m.dx_peers = static_cast<void* const*>(dev);
+    s->m.dx_partials = reinterpret_cast<float* const*>(static_cast<void**>(dev) + world);
+    s->m.dx_partial_local = static_cast<float*>(table[world + rank]);
+    s->m.dx_rank = rank;
+    s->m.dx_world = world;
+    s->m.dx_cap = max_local_tokens;
+    return 0;
+  });
+}
+
 int llambda_cuda_moe_session_attach_peers(llambda_cuda_moe_session* s, int rank, int world,
                                           void* const* peer_buffers, size_t bytes) {
   if (!s || !peer_buffers) {

@@ -34,7 +34,10 @@ int kernel_occupancy(const void* kernel, int threads, size_t smem) {
   const auto key = std::make_pair(kernel, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+  // opt in to what this launch needs (at least 200 KB; at most the 227 KB a
+  // CTA may use)
+  const int optin = (int)std::min<size_t>(std::max<size_t>(smem, 200 * 1024), 227 * 1024);
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) !=
       cudaSuccess)
     return -1;
   int occ = 0;

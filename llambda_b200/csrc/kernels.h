@@ -136,7 +136,37 @@ struct MoeDevice {
   // The router logits are already in the workspace (the routed sub-layer of
   // a latent layer): no router stage.
   int logits_ready;
+  // Token dispatch across expert-parallel ranks (dx_world > 1, prefill
+  // batches): dx_peers is a device array of every rank's copy of one
+  // symmetric buffer (dx_layout()), dx_partials a device array of their
+  // partial regions, dx_partial_local this rank's (host-readable pointer);
+  // each rank passes its own tokens (at most dx_cap per call).
+  void* const* dx_peers;
+  float* const* dx_partials;
+  float* dx_partial_local;
+  int dx_rank, dx_world, dx_cap;
 };
+
+// Per-rank copy of the token-dispatch buffer:
+//   [0, 64)     local: u32 epoch, u32 arrival ticket, u32 entries sent to each rank [8]
+//   [64, 128)   u64 dispatch flag per source rank: epoch << 32 | entries it sent here
+//   [128, 192)  u64 done flag per rank: epoch << 32 once its rows for this rank landed
+//   meta        int2 [world][cap * k]: {expert, the source's partial row}
+//   rows        bf16 [world][cap * k][k_in]: the received input rows
+//   partial     fp32 [cap][k + 1][hidden]: expert outputs for this rank's tokens
+struct DxLayout {
+  size_t meta, rows, partial, bytes;
+};
+__host__ __device__ inline size_t dx_align(size_t v) { return (v + 255) & ~size_t(255); }
+__host__ __device__ inline DxLayout dx_layout(int world, int cap, int k, int k_in, int hidden) {
+  DxLayout L;
+  const size_t entries = (size_t)world * cap * k;
+  L.meta = 256;
+  L.rows = dx_align(L.meta + entries * 8);
+  L.partial = dx_align(L.rows + entries * k_in * 2);
+  L.bytes = dx_align(L.partial + (size_t)cap * (k + 1) * hidden * 4);
+  return L;
+}
 
 // The routed experts of a latent layer as a layer of their own: hidden =
 // latent_dim, no norm, residual or shared expert, logits computed before.
@@ -228,6 +258,18 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
                        float* out, const SlabMaps* maps, cudaStream_t stream,
                        const cudaEvent_t* marks = nullptr);
 
+// Top-k and weights of T tokens (w.sel, w.wts, w.shw); grouped_ids 1: also
+// group the entries by owned expert with their ids, 0: positions only (the
+// prefill gather), -1: no grouping (the token dispatch groups what it
+// receives).
+cudaError_t launch_topk(const MoeDevice& m, const MoeWork& w, int T, int grouped_ids,
+                        cudaStream_t stream);
+// out = (x +) the rank-ordered weighted sum of w.partial, plus the shared
+// expert's row, for T tokens (experts outside [expert_begin, expert_end) add
+// nothing).
+cudaError_t launch_combine(const MoeDevice& m, const MoeWork& w, int T, const float* x, float* out,
+                           cudaStream_t stream);
+
 // Prefill path (prefill.cu): the expert products of batches of at least
 // prefill_min_tokens() tokens as tcgen05 bf16 grouped GEMMs.
 void set_prefill_min_tokens(int n);
@@ -242,5 +284,12 @@ cudaError_t launch_prefill_router(const MoeDevice& m, const MoeWork& w, const fl
 // as in the decode path.  marks as in launch_moe.
 cudaError_t launch_prefill_passes(const MoeDevice& m, const MoeWork& w, const float* x, int T,
                                   cudaStream_t stream, const cudaEvent_t* marks);
+// A whole layer call through the token dispatch (m.dx_world > 1): this
+// rank's T tokens are routed here, their rows sent to the experts' owners,
+// the received rows multiplied by this rank's experts (tcgen05 prefill
+// GEMMs) with the results stored back into their source ranks' partial
+// buffers, and this rank's tokens combined.
+cudaError_t launch_moe_dispatch(const MoeDevice& m, const MoeWork& w, const float* x, int T,
+                                float* out, cudaStream_t stream, const cudaEvent_t* marks);
 
 }  // namespace lb

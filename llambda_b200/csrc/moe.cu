@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
     const int t = blockIdx.x * kTopkTokens + (threadIdx.x >> 5);
     if (t < T) topk_token<PER>(m, w, t, threadIdx.x & 31);
   }
+  if (grouped_ids < 0) return;  // the caller groups the entries (token dispatch)
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(w.tickets, 1) == (int)gridDim.x - 1;
@@ -2113,8 +2114,14 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
                        const SlabMaps* maps, cudaStream_t s, const cudaEvent_t* marks) {
   if (T <= 0) return cudaSuccess;
   if (m.latent_dim > 0) {
-    if (T > w.max_tokens || m.arch != 1 || m.ep_world > 1) return cudaErrorInvalidValue;
+    if (T > w.max_tokens || m.arch != 1 || m.ep_world > 1 || m.dx_world > 1)
+      return cudaErrorInvalidValue;
     return launch_moe_latent(m, w, x, T, out, maps, s, marks);
+  }
+  if (m.dx_world > 1) {  // token dispatch across ranks for prefill batches
+    if (T >= prefill_min_tokens()) return launch_moe_dispatch(m, w, x, T, out, s, marks);
+    // smaller calls hold the tokens of every rank and need the peer reduction
+    if (m.ep_world <= 1) return cudaErrorInvalidValue;
   }
   if (T > w.max_tokens || m.experts > kMaxExperts || m.top_k > 32 || T * m.top_k > kMaxEntries)
     return cudaErrorInvalidValue;
@@ -2164,16 +2171,8 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     if (e != cudaSuccess) return e;
   }
   if ((e = mark(6)) != cudaSuccess) return e;
-  {  // top-k per token, the routing on the last CTA
-    const int per = (E + 31) / 32, pnt = up_pass_tokens(m, T);
-    auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
-              : per <= 4 ? topk_route_kernel<4> : per <= 8 ? topk_route_kernel<8>
-              : per <= 16 ? topk_route_kernel<16> : topk_route_kernel<32>;
-    e = launch_pdl(kern, dim3((T + kTopkTokens - 1) / kTopkTokens), dim3(256), 0, s, m, w, T, pnt,
-                   prefill ? 0 : 1);
-    if (e != cudaSuccess) return e;
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
+  // top-k per token, the routing on the last CTA
+  if ((e = launch_topk(m, w, T, prefill ? 0 : 1, s)) != cudaSuccess) return e;
   const bool gate_ok = m.arch == 1 || m.gate_type == m.up_type;
   if (!gate_ok) return cudaErrorInvalidValue;
   if (prefill)
@@ -2195,13 +2194,31 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
     if (!vec || T > m.ep_max_tokens) return cudaErrorInvalidValue;
     e = launch_pdl(combine_ep_kernel, dim3(kEpGrid), dim3(256), 0, s, m, w, T, x, out);
   } else {
-    const long n = (long)T * m.hidden / (vec ? 4 : 1);
-    const int grid = std::max(1, (int)std::min<long>((n + 127) / 128, (long)sm_count() * 16));
-    auto kern = vec && m.top_k <= 16 ? combine_kernel<true, 16>
-                : vec ? combine_kernel<true, 32> : combine_kernel<false, 32>;
-    e = launch_pdl(kern, dim3(grid), dim3(128), 0, s, m, w, T, x, out);
+    e = launch_combine(m, w, T, x, out, s);
   }
   return e != cudaSuccess ? e : mark(5);
+}
+
+cudaError_t launch_topk(const MoeDevice& m, const MoeWork& w, int T, int grouped_ids,
+                        cudaStream_t s) {
+  const int per = (m.experts + 31) / 32, pnt = up_pass_tokens(m, T);
+  auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
+            : per <= 4 ? topk_route_kernel<4> : per <= 8 ? topk_route_kernel<8>
+            : per <= 16 ? topk_route_kernel<16> : topk_route_kernel<32>;
+  cudaError_t e = launch_pdl(kern, dim3((T + kTopkTokens - 1) / kTopkTokens), dim3(256), 0, s, m,
+                             w, T, pnt, grouped_ids);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_combine(const MoeDevice& m, const MoeWork& w, int T, const float* x, float* out,
+                           cudaStream_t s) {
+  const bool vec = (m.hidden & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const long n = (long)T * m.hidden / (vec ? 4 : 1);
+  const int grid = std::max(1, (int)std::min<long>((n + 127) / 128, (long)sm_count() * 16));
+  auto kern = vec && m.top_k <= 16 ? combine_kernel<true, 16>
+              : vec ? combine_kernel<true, 32> : combine_kernel<false, 32>;
+  return launch_pdl(kern, dim3(grid), dim3(128), 0, s, m, w, T, x, out);
 }
 
 }  // namespace lb

@@ -122,6 +122,9 @@ struct PfPass {
   long ld_h;
   float* partial;     // down output: [T][k+1][H]
   const int* prow;    // partial row of each grouped row
+  // Token dispatch across ranks (null otherwise): prow holds source rank << 24
+  // | row, and the row lands in that rank's partial buffer over peer memory.
+  float* const* partial_peers;
   int H;
   int* status;
 };
@@ -592,11 +595,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tmem_ld16(acc + n0, y0);
         if (PAIR) tmem_ld16(acc + kPfN + n0, y1);
         if (DOWN) {
-          if (row < p.H)
+          if (row < p.H) {
+            if (p.partial_peers) {  // the source rank's partial row, over NVLink
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (n0 + j < ntok)
-                p.partial[(long)__ldg(p.prow + tl.x + n0 + j) * p.H + row] = y0[j];
+              for (int j = 0; j < 16; ++j)
+                if (n0 + j < ntok) {
+                  const int pr = __ldg(p.prow + tl.x + n0 + j);
+                  p.partial_peers[pr >> 24][(long)(pr & 0xFFFFFF) * p.H + row] = y0[j];
+                }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (n0 + j < ntok)
+                  p.partial[(long)__ldg(p.prow + tl.x + n0 + j) * p.H + row] = y0[j];
+            }
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -620,6 +633,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sy->tempty[buf]);
     }
+    // dispatch: this thread's stores to other ranks are performed before it
+    // exits, so the flag raised after this launch orders behind them
+    if (DOWN && p.partial_peers) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();
@@ -686,7 +702,10 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(MoeDevice m, MoeWork w,
 // Tile lists of both passes, in expert order (then the shared expert): for
 // each active expert, its row blocks, each with its 64-token chunks in a row,
 // so CTAs running side by side read the same weight rows.
-__global__ void __launch_bounds__(1024) pf_plan_kernel(MoeDevice m, MoeWork w, int T) {
+// shared_base: the grouped row of the shared expert's first token (T*k when
+// this device routed its own T tokens; the dispatch path's fixed base).
+__global__ void __launch_bounds__(1024) pf_plan_kernel(MoeDevice m, MoeWork w, int T,
+                                                       int shared_base) {
   __shared__ int s_warp[32];
   const int E = m.experts, na = w.active[E];
   const int a = threadIdx.x, warp = a >> 5, lane = a & 31;
@@ -742,12 +761,12 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(MoeDevice m, MoeWork w, i
   for (int i = a; i < nsh * mbu_sh; i += blockDim.x) {
     const int mb = i / nsh, ch = i - mb * nsh;
     up[(long)routed * mbu + i] =
-        make_int4(T * m.top_k + t0 + ch * kPfN, min(kPfN, t1 - t0 - ch * kPfN), -1, mb);
+        make_int4(shared_base + t0 + ch * kPfN, min(kPfN, t1 - t0 - ch * kPfN), -1, mb);
   }
   for (int i = a; i < nsh * mbd; i += blockDim.x) {
     const int mb = i / nsh, ch = i - mb * nsh;
     dn[(long)routed * mbd + i] =
-        make_int4(T * m.top_k + t0 + ch * kPfN, min(kPfN, t1 - t0 - ch * kPfN), -1, mb);
+        make_int4(shared_base + t0 + ch * kPfN, min(kPfN, t1 - t0 - ch * kPfN), -1, mb);
   }
   if (a == 0) {
     w.pf_count[0] = routed * mbu + nsh * mbu_sh;
@@ -1070,16 +1089,20 @@ bool prefill_applies(const MoeDevice& m, const MoeWork& w, int T) {
   return (m.k_in % 256) == 0 && (m.k_down % 256) == 0;
 }
 
-cudaError_t launch_prefill_passes(const MoeDevice& m, const MoeWork& w, const float* x, int T,
-                                  cudaStream_t s, const cudaEvent_t* marks) {
+namespace {
+
+// Plan, gate/up and down passes over the grouped rows already in w.pf_xs
+// (the routed entries, then T shared-expert rows from shared_base on).
+// partial_peers: the token dispatch's partial regions of every rank (the
+// down pass stores each row into its source rank's), or null.
+cudaError_t pf_gemm_passes(const MoeDevice& m, const MoeWork& w, int T, int shared_base,
+                           float* const* partial_peers, cudaStream_t s,
+                           const cudaEvent_t* marks) {
   cudaError_t e;
   auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
-  if (m.experts > 1024) return cudaErrorInvalidValue;
-  pf_gather_kernel<<<T, 256, 0, s>>>(m, w, x, T);
+  pf_plan_kernel<<<1, 1024, 0, s>>>(m, w, T, shared_base);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  pf_plan_kernel<<<1, 1024, 0, s>>>(m, w, T);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  const long rows = (long)T * m.top_k + T;
+  const long rows = (long)shared_base + T;
   const int ld_h = pf_down_ld(m);
   const bool pair = m.arch == 0;
   const bool shared = m.shared_here && m.inter_sh;
@@ -1137,10 +1160,323 @@ cudaError_t launch_prefill_passes(const MoeDevice& m, const MoeWork& w, const fl
   dn.ntiles = w.pf_count + 1;
   dn.partial = w.partial;
   dn.prow = w.pf_prow;
+  dn.partial_peers = partial_peers;
   dn.H = m.hidden;
   dn.status = w.status;
   if ((e = launch_pf_pass<true>(m.down_type, false, dm, dn, s)) != cudaSuccess) return e;
   return mark(2);
+}
+
+}  // namespace
+
+cudaError_t launch_prefill_passes(const MoeDevice& m, const MoeWork& w, const float* x, int T,
+                                  cudaStream_t s, const cudaEvent_t* marks) {
+  cudaError_t e;
+  if (m.experts > 1024) return cudaErrorInvalidValue;
+  pf_gather_kernel<<<T, 256, 0, s>>>(m, w, x, T);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  return pf_gemm_passes(m, w, T, T * m.top_k, nullptr, s, marks);
+}
+
+// ------------------------------------------------------------ token dispatch
+//
+// Expert-parallel prefill: every rank holds a share of the tokens and a share
+// of the experts.  Per layer call, each rank normalises and routes its own
+// tokens, then (one CTA per token) stores the token's bf16 row into the
+// landing zone of each rank that owns one of its experts, over NVLink peer
+// memory, with the expert and the token's partial row beside it; the last CTA
+// raises one epoch-tagged flag per destination carrying the entry count,
+// after a single system-scope fence.  Each rank waits (bounded) for every
+// source's flag, groups what it received by expert, copies the rows into the
+// grouped layout the tcgen05 GEMMs read, and runs the gate/up and down passes;
+// the down pass's epilogue stores every output row straight into its source
+// rank's partial buffer.  A done flag per rank then lets each source combine
+// its own tokens (weights, shared expert, residual) exactly as on one device.
+// A rank sends rows of call n + 1 only after its combine of call n, which
+// waited for every rank's done flag of call n, so no landing zone or partial
+// buffer is overwritten while it is read.
+
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_sys_acq_rel() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Waits (bounded) until flag >> 32 == epoch; returns the low 32 bits, or -1
+// after the time limit (status bit 2, value 4).
+__device__ int dx_wait_flag(const uint64_t* flag, uint32_t epoch, int* status) {
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    const uint64_t v = ld_relaxed_sys_u64(flag);
+    if ((uint32_t)(v >> 32) == epoch) {
+      fence_sys_acq_rel();
+      return (int)(v & 0xFFFFFFFFu);
+    }
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicOr(status, 4);
+      return -1;
+    }
+    __nanosleep(32);
+  }
+}
+
+// The rank owning expert e: rank q holds [q*E/world, (q+1)*E/world).
+__device__ __forceinline__ int dx_owner(const MoeDevice& m, int e) {
+  int q = m.dx_world - 1;
+  while (q > 0 && (long)q * m.experts / m.dx_world > e) --q;
+  return q;
+}
+
+__global__ void __launch_bounds__(256) dx_send_kernel(MoeDevice m, MoeWork w,
+                                                      const float* __restrict__ x, int T) {
+  __shared__ int s_q[32], s_pos[32];
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_last;
+  const int t = blockIdx.x, k = m.top_k, H = m.hidden, K = m.k_in, me = m.dx_rank;
+  uint32_t* hdr = static_cast<uint32_t*>(m.dx_peers[me]);
+  const DxLayout L = dx_layout(m.dx_world, m.dx_cap, k, K, H);
+  const size_t src_base = (size_t)me * m.dx_cap * k;  // this rank's slots at a destination
+  if (threadIdx.x == 0) s_epoch = hdr[0] + 1u;  // the last CTA advances hdr[0]
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int q = -1, pos = 0;
+    if (lane < k) {
+      const int id = t * k + lane;
+      const int e = w.sel[id];
+      if (e >= 0 && e < m.experts) {  // an unselectable rank (status bit 0) sends nothing
+        q = dx_owner(m, e);
+        pos = (int)atomicAdd(&hdr[2 + q], 1u);
+        int2* meta = reinterpret_cast<int2*>(static_cast<uint8_t*>(m.dx_peers[q]) + L.meta);
+        meta[src_base + pos] = make_int2(e, t * (k + 1) + lane);
+      }
+    }
+    s_q[lane] = q;
+    s_pos[lane] = pos;
+  }
+  __syncthreads();
+  const float* xt = (m.input_norm ? w.xn : x) + (long)t * H;
+  for (int c0 = threadIdx.x * 8; c0 < K; c0 += blockDim.x * 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = c0 + j < H ? xt[c0 + j] : 0.f;
+    const uint4 pk = make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]),
+                                bf16x2(v[6], v[7]));
+    for (int j = 0; j < k; ++j) {
+      const int q = s_q[j];
+      if (q < 0) continue;
+      uint16_t* rows = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(m.dx_peers[q]) + L.rows);
+      *reinterpret_cast<uint4*>(rows + (src_base + s_pos[j]) * K + c0) = pk;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // this CTA's rows and entries before its arrival
+    s_last = atomicAdd(&hdr[1], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  __threadfence();
+  const uint32_t epoch = s_epoch;
+  for (int q = 0; q < m.dx_world; ++q) {
+    const uint32_t cnt = atomicExch(&hdr[2 + q], 0u);
+    uint64_t* dflag = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(m.dx_peers[q]) + 64) + me;
+    st_relaxed_sys_u64(dflag, ((uint64_t)epoch << 32) | cnt);
+  }
+  hdr[1] = 0;
+  hdr[0] = epoch;
+}
+
+// One CTA: waits for every source's rows, groups the received entries by
+// owned expert (counts, offsets, active list as the routing writes them for
+// the tile plan), and maps each grouped row to its landing slot (second half
+// of w.entries) and to its source's partial row (pf_prow: source << 24 | row).
+// The order of entries inside an expert's group does not matter: each row's
+// products depend on that row alone.
+__global__ void __launch_bounds__(1024) dx_group_kernel(MoeDevice m, MoeWork w, int T,
+                                                        int shared_base) {
+  __shared__ int s_cnt[kEpMaxWorld + 1], s_base[kEpMaxWorld + 1];
+  __shared__ int s_count[1024], s_warp[32], s_wact[32];
+  const int E = m.experts, k = m.top_k, W = m.dx_world, me = m.dx_rank;
+  const int eb = m.expert_begin, ne = m.expert_end - m.expert_begin;
+  const uint8_t* self = static_cast<const uint8_t*>(m.dx_peers[me]);
+  const uint32_t epoch = reinterpret_cast<const uint32_t*>(self)[0];
+  const DxLayout L = dx_layout(W, m.dx_cap, k, m.k_in, m.hidden);
+  const int2* meta = reinterpret_cast<const int2*>(self + L.meta);
+  const long nk = (long)w.max_tokens * k;
+  if (threadIdx.x < W) {
+    const int c = dx_wait_flag(reinterpret_cast<const uint64_t*>(self + 64) + threadIdx.x, epoch,
+                               w.status);
+    s_cnt[threadIdx.x] = c < 0 ? 0 : min(c, m.dx_cap * k);
+  }
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) s_count[e] = 0;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int q = 0; q < W; ++q) {
+      s_base[q] = run;
+      run += s_cnt[q];
+    }
+    s_base[W] = run;
+  }
+  __syncthreads();
+  const int M = s_base[W];
+  for (int i = threadIdx.x; i < M; i += blockDim.x) {  // slot of each entry in its expert
+    int q = 0;
+    while (i >= s_base[q + 1]) ++q;
+    const int e = meta[(size_t)q * m.dx_cap * k + (i - s_base[q])].x - eb;
+    w.entries[i] = (e >= 0 && e < ne) ? atomicAdd(&s_count[e], 1) : -1;
+  }
+  __syncthreads();
+  // exclusive scans over the owned experts: entry offsets and the active list
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = threadIdx.x;
+  const int cnt = e < ne ? s_count[e] : 0;
+  int incl = cnt, act = cnt > 0 ? 1 : 0;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    const int a = __shfl_up_sync(0xffffffffu, act, o);
+    if (lane >= o) {
+      incl += v;
+      act += a;
+    }
+  }
+  if (lane == 31) {
+    s_warp[warp] = incl;
+    s_wact[warp] = act;
+  }
+  __syncthreads();
+  int wbase = 0, abase = 0;
+  for (int q = 0; q < warp; ++q) {
+    wbase += s_warp[q];
+    abase += s_wact[q];
+  }
+  const int off = wbase + incl - cnt;
+  __syncthreads();
+  if (e < ne) {
+    w.counts[eb + e] = cnt;
+    w.offsets[eb + e] = off;
+    if (cnt > 0) w.active[abase + act - 1] = eb + e;
+    s_count[e] = off;  // from here: the expert's first grouped row
+  }
+  if (threadIdx.x == blockDim.x - 1) {
+    w.active[E] = abase + act;
+    w.offsets[E] = M;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < M; i += blockDim.x) {
+    int q = 0;
+    while (i >= s_base[q + 1]) ++q;
+    const int slot = i - s_base[q];
+    const int2 mt = meta[(size_t)q * m.dx_cap * k + slot];
+    const int pos = w.entries[i];
+    // a source's partial row lies inside its [cap][k+1] region
+    if (pos < 0 || mt.y < 0 || mt.y >= m.dx_cap * (k + 1)) continue;
+    const int g = s_count[mt.x - eb] + pos;
+    w.entries[nk + g] = (q << 24) | slot;
+    w.pf_prow[g] = (q << 24) | mt.y;
+  }
+  if (m.shared_here && m.inter_sh)
+    for (int t = threadIdx.x; t < T; t += blockDim.x)
+      w.pf_prow[shared_base + t] = (me << 24) | (t * (k + 1) + k);
+}
+
+// One warp per grouped row: the received bf16 rows into their grouped slots,
+// then this rank's tokens (rms-normed when the layer has input_norm) as the
+// shared expert's rows, zero-padded from H to k_in.
+__global__ void __launch_bounds__(256) dx_copy_kernel(MoeDevice m, MoeWork w,
+                                                      const float* __restrict__ x, int T,
+                                                      int shared_base) {
+  const int k = m.top_k, K = m.k_in, H = m.hidden;
+  const uint8_t* self = static_cast<const uint8_t*>(m.dx_peers[m.dx_rank]);
+  const DxLayout L = dx_layout(m.dx_world, m.dx_cap, k, K, H);
+  const uint16_t* rows = reinterpret_cast<const uint16_t*>(self + L.rows);
+  const long nk = (long)w.max_tokens * k;
+  const int M = w.offsets[m.experts];
+  const int nsh = (m.shared_here && m.inter_sh) ? T : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * 8 + warp; r < M + nsh; r += gridDim.x * 8) {
+    if (r < M) {
+      const int map = w.entries[nk + r];
+      const size_t slot = (size_t)(map >> 24) * m.dx_cap * k + (map & 0xFFFFFF);
+      const uint4* src = reinterpret_cast<const uint4*>(rows + slot * K);
+      uint4* dst = reinterpret_cast<uint4*>(w.pf_xs + (long)r * K);
+      for (int c = lane; c < K / 8; c += 32) dst[c] = src[c];
+    } else {
+      const int t = r - M;
+      const float* xt = (m.input_norm ? w.xn : x) + (long)t * H;
+      uint4* dst = reinterpret_cast<uint4*>(w.pf_xs + (long)(shared_base + t) * K);
+      for (int c = lane; c < K / 8; c += 32) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 8 * c + j < H ? xt[8 * c + j] : 0.f;
+        dst[c] = make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]),
+                            bf16x2(v[6], v[7]));
+      }
+    }
+  }
+}
+
+// After the down pass: every rank learns that this rank's rows for it landed.
+__global__ void dx_done_kernel(MoeDevice m) {
+  if (threadIdx.x != 0) return;
+  const uint32_t epoch = static_cast<const uint32_t*>(m.dx_peers[m.dx_rank])[0];
+  __threadfence_system();
+  for (int q = 0; q < m.dx_world; ++q)
+    st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(m.dx_peers[q]) + 128) +
+                           m.dx_rank,
+                       (uint64_t)epoch << 32);
+}
+
+// Before the combine: every rank's rows for this rank's tokens have landed.
+__global__ void dx_wait_kernel(MoeDevice m, MoeWork w) {
+  const uint8_t* self = static_cast<const uint8_t*>(m.dx_peers[m.dx_rank]);
+  const uint32_t epoch = reinterpret_cast<const uint32_t*>(self)[0];
+  if ((int)threadIdx.x < m.dx_world)
+    dx_wait_flag(reinterpret_cast<const uint64_t*>(self + 128) + threadIdx.x, epoch, w.status);
+}
+
+cudaError_t launch_moe_dispatch(const MoeDevice& m_in, const MoeWork& w, const float* x, int T,
+                                float* out, cudaStream_t s, const cudaEvent_t* marks) {
+  cudaError_t e;
+  auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
+  MoeDevice m = m_in;  // the decode reduction plays no part; the shared expert
+  m.ep_world = 0;      // runs on all of this rank's own tokens
+  m.ep_peers = nullptr;
+  m.sh_parts = 0;
+  if (T > m.dx_cap || T > w.max_tokens || !w.pf_xs || m.experts > 1024 ||
+      m.expert_end - m.expert_begin > 1024 || (long)m.dx_world * m.dx_cap > w.max_tokens ||
+      m.top_k > 32 || (m.k_in % 256) != 0)
+    return cudaErrorInvalidValue;
+  const int shared_base = w.max_tokens * m.top_k;
+  if ((e = mark(3)) != cudaSuccess) return e;
+  if ((e = launch_prefill_router(m, w, x, T, s)) != cudaSuccess) return e;
+  if ((e = mark(6)) != cudaSuccess) return e;
+  if ((e = launch_topk(m, w, T, -1, s)) != cudaSuccess) return e;
+  dx_send_kernel<<<T, 256, 0, s>>>(m, w, x, T);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  dx_group_kernel<<<1, 1024, 0, s>>>(m, w, T, shared_base);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  dx_copy_kernel<<<4 * sm_count(), 256, 0, s>>>(m, w, x, T, shared_base);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = pf_gemm_passes(m, w, T, shared_base, m.dx_partials, s, marks)) != cudaSuccess) return e;
+  dx_done_kernel<<<1, 32, 0, s>>>(m);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = mark(4)) != cudaSuccess) return e;
+  dx_wait_kernel<<<1, 32, 0, s>>>(m, w);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // every expert's row of this rank's tokens is in the local partial region
+  MoeDevice mc = m;
+  mc.expert_begin = 0;
+  mc.expert_end = m.experts;
+  MoeWork wc = w;
+  wc.partial = m.dx_partial_local;
+  if ((e = launch_combine(mc, wc, T, x, out, s)) != cudaSuccess) return e;
+  return mark(5);
 }
 
 }  // namespace lb

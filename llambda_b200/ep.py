@@ -14,6 +14,11 @@ per layer.  Two ways to sum them:
   * a collective (`allreduce_partial`): an all-reduce of the partial outputs
     (NCCL on GPUs, gloo on CPUs), with the residual on one rank only.
 
+Prefill batches can instead be split by token (`attach_token_dispatch`): each
+rank passes its own slice of the tokens, and every layer call sends each
+token's row to the ranks owning its selected experts and brings the expert
+outputs back over peer memory (llambda_cuda_moe_session_attach_dispatch).
+
 llambda itself runs on one device; this module has no counterpart there.
 """
 from __future__ import annotations
@@ -78,3 +83,37 @@ def allreduce_partial(out, group=None) -> None:
     import torch.distributed as dist
 
     dist.all_reduce(out, group=group)
+
+
+def token_slice(rank: int, world: int, tokens: int) -> tuple[int, int]:
+    """[begin, end) of the tokens rank `rank` of `world` holds under the token
+    dispatch (contiguous, as even as the count allows)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("need 0 <= rank < world")
+    return rank * tokens // world, (rank + 1) * tokens // world
+
+
+def attach_token_dispatch(sessions, max_local_tokens: int, group=None):
+    """One zero-filled symmetric buffer for the token dispatch of every
+    session (the sessions of a stack run one at a time and share it).
+    Returns the buffer and its handle; keep them alive while the sessions
+    run."""
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    group = group or dist.group.WORLD
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    nbytes = max(s.dispatch_bytes(world, max_local_tokens) for s in sessions)
+    if nbytes == 0:
+        raise ValueError("the sessions cannot dispatch over %d ranks" % world)
+    buf = symm_mem.empty(nbytes, dtype=torch.uint8, device="cuda")
+    buf.zero_()
+    handle = symm_mem.rendezvous(buf, group)
+    torch.cuda.synchronize()
+    dist.barrier(group)
+    ptrs = list(handle.buffer_ptrs)
+    for s in sessions:
+        s.attach_dispatch(rank, world, ptrs, nbytes, max_local_tokens)
+    return buf, handle
