@@ -1909,11 +1909,13 @@ cudaError_t launch_expert_passes(const MoeDevice& m, const MoeWork& w, int T,
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (DT == LB_TYPE_Q6_K && down_uses_i6(m)) {
-    // Expert-parallel ranks hold a few tokens of the shared expert each: its
-    // down slabs ride in the routed launch (one launch less on the layer's
-    // critical path).  On one device its own launch overlaps the routed
-    // tail better (measured), so it stays apart there.
-    const bool ride = m.ep_world > 1 && m.shared_here && m.inter_sh &&
+    // When this device computes the shared expert for a few tokens only
+    // (expert-parallel ranks, or small batches), its down slabs ride in the
+    // routed launch: one launch less on the layer's critical path (decode
+    // batch 1 on one B200: 469 -> 515 tokens/s).  For larger batches on one
+    // device its own launch overlaps the routed tail better (measured at 32
+    // tokens), so it stays apart there.
+    const bool ride = (m.ep_world > 1 || T <= 8) && m.shared_here && m.inter_sh &&
                       m.k_down_sh == m.k_down && m.down_sh_rb == m.down_rb;
     e = launch_down_slab(m, w, T, ride ? 2 : 0, s);
     if (e == cudaSuccess) e = mark(2);
