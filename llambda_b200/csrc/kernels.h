@@ -216,6 +216,8 @@ struct MoeWork {
   float* xp_down;     // [T*k + T] prepared down inputs: routed entry ids, then
                       // shared token rows (stride xp_stride(max(k_down, k_down_sh)))
   float* partial;     // [T][k+1][H] unscaled down outputs per (token, rank)
+  float* up_part;     // gate/up items split over K: each item's slices' row sums
+  int* up_tickets;    // and its arrival ticket
   // Prefill path (carved when max_tokens >= 64, null otherwise):
   uint16_t* pf_xs;    // [T*k + T][k_in] bf16 inputs grouped by expert, then shared rows
   uint16_t* pf_hs;    // [T*k + T][max(k_down, k_down_sh)] bf16 intermediates, same rows

@@ -44,6 +44,17 @@ constexpr int kRouteSplitChunks = 4;
 constexpr int kTopkTokens = 8;  // tokens per CTA of the top-k launch (one per warp)
 constexpr int kRouteSplitSlots = 8192;
 constexpr int kSlabMaxStages = 10;
+// Gate/up work items split over K: when a call has fewer (slab, pass) items
+// than CTAs (decode batches of a token or two), each item's super-block
+// columns are split over up to kUpMaxSplit CTAs and the last to finish sums
+// the slices in slice order.  Buffers cover kUpSplitItems items.
+constexpr int kUpMaxSplit = 4, kUpSplitItems = 160;
+constexpr int kUpPartFloats = 32 * kTileRows;  // consumer warps x tokens per pass <= 32
+
+__device__ __forceinline__ int up_split(int units, int grid, int nsb) {
+  if (units <= 0 || units > kUpSplitItems) return 1;
+  return max(1, min(min(kUpMaxSplit, nsb), grid / units));
+}
 // Rows of one 2-D tensor copy of the gate/up slabs (the slabs' rows per
 // matrix are multiples of it).
 constexpr int kUpBoxRows = 64;
@@ -239,6 +250,10 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
   __threadfence();  // every CTA's selections are visible from here
   route_block<true>(m, w, T, pass_nt, grouped_ids != 0);
   if (threadIdx.x == 0) *w.tickets = 0;
+  // the gate/up items' arrival tickets start at zero even after a launch
+  // that gave up part-way (each is reset by its last arriver otherwise)
+  if (w.up_tickets)
+    for (int i = threadIdx.x; i < kUpSplitItems; i += blockDim.x) w.up_tickets[i] = 0;
 }
 
 // Groups the (token, rank) entries by owned expert, stably.  One CTA of up to
@@ -864,9 +879,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   const int n_routed = w.pass_off[nact] * per_r;
   const int n_shared = (m.shared_here && m.inter_sh) ? per_s * passes_s : 0;
   const int units = n_routed + n_shared;
-  const int u0 = (int)((long)blockIdx.x * units / gridDim.x);
-  const int n_my = (int)((long)(blockIdx.x + 1) * units / gridDim.x) - u0;
   const int nsb = m.k_in >> 8;
+  // with few items (one-token passes: decode batch 1), each is cut into nks
+  // slices of its super-block columns; other pass sizes keep whole items
+  constexpr bool kSplit = NT == 1;
+  const int nks = kSplit && w.up_part ? up_split(units, gridDim.x, nsb) : 1;
+  const int u0 = (int)((long)blockIdx.x * units * nks / gridDim.x);
+  const int n_my = (int)((long)(blockIdx.x + 1) * units * nks / gridDim.x) - u0;
 
   struct Unit {
     int row0, rows_e, t_begin, t_end;
@@ -921,16 +940,18 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       RingPos rp;
       bool ok = true;
       for (int i = 0; i < n_my && ok; ++i) {
-        const Unit x = unit_at(u0 + i);
+        const int ub = (u0 + i) / nks, ks = (u0 + i) - ub * nks;
+        const Unit x = unit_at(ub);
+        const int sb_lo = ks * nsb / nks, sb_hi = (ks + 1) * nsb / nks;
         for (int t0 = x.t_begin; t0 < x.t_end && ok; t0 += NT) {
-          for (int sb = 0; sb < nsb; ++sb, ++q, rp.next(stages)) {
+          for (int sb = sb_lo; sb < sb_hi; ++sb, ++q, rp.next(stages)) {
             const int s = rp.s;
             if (q >= stages && !mbar_wait_or_abort(&sync->empty[s], rp.phase ^ 1u, w.status, abort)) {
               ok = false;
               break;
             }
             const int nt = min(NT, x.t_end - t0);
-            if (sb == 0) {  // the item's rows and entries travel with its first stage
+            if (sb == sb_lo) {  // the item's rows and entries travel with its first stage
               UpUnit& uu = sync->unit[s];
               uu.row0 = x.row0;
               uu.rows_e = x.rows_e;
@@ -978,9 +999,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   const int g = lane >> 2, t = lane & 3;
   const long ld_dn = down_ld_floats(m);
   RingPos rp;
-  int pass = 0;
+  int pass = 0;  // items whose epilogue this CTA ran (the exchange's parity)
   bool ok = true;
-  for (int i = 0; i < n_my && ok; ++i, ++pass) {
+  __shared__ int s_last;
+  for (int i = 0; i < n_my && ok; ++i) {
+    const int ub = (u0 + i) / nks, ks = (u0 + i) - ub * nks;
+    const int sb_lo = ks * nsb / nks, sb_hi = (ks + 1) * nsb / nks;
     UpUnit x;  // read with the item's first stage
     int nt = 0;
     float2 acc[NT][2];
@@ -988,13 +1012,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int r = 0; r < 2; ++r) acc[n][r] = make_float2(0.f, 0.f);
-    for (int sb = 0; sb < nsb; ++sb, rp.next(stages)) {
+    for (int sb = sb_lo; sb < sb_hi; ++sb, rp.next(stages)) {
       const int s = rp.s;
       if (!mbar_wait_or_abort(&sync->full[s], rp.phase, w.status, abort)) {
         ok = false;
         break;
       }
-      if (sb == 0) {  // the item, as the producer published it with this stage
+      if (sb == sb_lo) {  // the item, as the producer published it with this stage
         x = sync->unit[s];
         nt = x.nt;
       }
@@ -1022,7 +1046,38 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         v[r][n] = s;
       }
+    if (kSplit && nks > 1) {
+      // this slice's row sums to the item's slot; the last of the item's
+      // CTAs to arrive sums all slices in slice order and runs the epilogue
+      float* part = w.up_part + (size_t)ub * kUpMaxSplit * kUpPartFloats;
+      if (t == 0)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+            part[(size_t)ks * kUpPartFloats + (warp * kTileRows + g + 8 * r) * NT + n] = v[r][n];
+      __threadfence();
+      named_bar_sync(1, CW * 32);  // every consumer warp's slice is stored
+      if (threadIdx.x == 0) s_last = atomicAdd(&w.up_tickets[ub], 1) == nks - 1;
+      named_bar_sync(1, CW * 32);
+      if (!s_last) continue;  // another CTA finishes this item
+      __threadfence();
+      // every lane of a quad holds its rows' sums (the gate warps use all four)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            float sum = 0.f;
+            for (int q = 0; q < nks; ++q)
+              sum += q == ks ? v[r][n]
+                             : __ldcg(part + (size_t)q * kUpPartFloats +
+                                      (warp * kTileRows + g + 8 * r) * NT + n);
+            v[r][n] = sum;
+          }
+      if (threadIdx.x == 0) w.up_tickets[ub] = 0;  // zero for the next launch
+    }
     const int par = pass & 1, use = pass >> 1;
+    ++pass;
     float* xb = xch + (size_t)par * RU * NT;
     auto id_of = [&](int nn) {  // ids[nn] without indexing registers dynamically
       int id = x.ids[0];
@@ -2007,6 +2062,11 @@ void moe_work_carve(const MoeDevice& m, int T, void* base, MoeWork* w) {
   w->xp_down = reinterpret_cast<float*>(
       take((size_t)(T * k + T) * down_ld_floats(m) * 4));
   w->partial = reinterpret_cast<float*>(take((size_t)T * (k + 1) * m.hidden * 4));
+  // K-split gate/up items (decode): per item its slices' row sums, and an
+  // arrival ticket per item (zero between launches)
+  w->up_part = reinterpret_cast<float*>(
+      take((size_t)kUpSplitItems * kUpMaxSplit * kUpPartFloats * 4));
+  w->up_tickets = reinterpret_cast<int*>(take((size_t)kUpSplitItems * 4));
   size_t pf[6];
   if (prefill_work_bytes(m, T, pf)) {
     w->pf_xs = reinterpret_cast<uint16_t*>(take(pf[0]));
