@@ -127,7 +127,7 @@ __device__ __forceinline__ float topk_value(uint32_t key) {
 // selected (NaN, -inf, -FLT_MAX and below).  One warp per token t.
 template <int PER>
 __device__ __forceinline__ void topk_token(const MoeDevice& m, const MoeWork& w, int t,
-                                           int lane) {
+                                           int lane, int* s_sel = nullptr) {
   const int E = m.experts, k = m.top_k;
   const float* L = w.logits + (long)t * (E + 1);
   // Every load goes out before any is used: addresses are clamped into the
@@ -198,8 +198,13 @@ __device__ __forceinline__ void topk_token(const MoeDevice& m, const MoeWork& w,
       best();
     }
   }
-  // sigmoid per rank in parallel; the sum runs in rank order, as in L5367-5372
-  float wv = lane < k && my_i >= 0 ? sigmoid_ref(topk_value(my_k)) : 0.f;
+  // sigmoid per rank in parallel; the sum runs in rank order, as in L5367-5372.
+  // Lane k (when k < 32) evaluates the shared-expert gate's sigmoid in the
+  // same pass, so the token's chain holds one sigmoid instead of two.
+  const bool rank_lane = lane < k && my_i >= 0;
+  const float sig = sigmoid_ref(rank_lane ? topk_value(my_k) : gate_logit);
+  const float gate_sig = __shfl_sync(0xffffffffu, sig, k < 32 ? k : 0);
+  float wv = rank_lane ? sig : 0.f;
   float wsum = 0.f;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
@@ -215,17 +220,31 @@ __device__ __forceinline__ void topk_token(const MoeDevice& m, const MoeWork& w,
   if (lane < k) {
     w.sel[t * k + lane] = my_i;
     w.wts[t * k + lane] = wv;
+    if (s_sel) s_sel[t * k + lane] = my_i;
   }
   if (lane == 0) {
-    w.shw[t] = (m.arch == 0) ? sigmoid_ref(gate_logit) : 1.0f;
+    w.shw[t] = (m.arch == 0) ? (k < 32 ? gate_sig : sigmoid_ref(gate_logit)) : 1.0f;
     if (bad) atomicOr(w.status, 1);
   }
 }
 
+// Where route_block reads the selections: written by an earlier launch
+// (read-only path), by other CTAs of the same launch (L2), or copied into
+// shared memory by this CTA.
+enum SelSrc { kSelEarlier = 0, kSelSameLaunch = 1, kSelShared = 2 };
+
+template <int SRC>
+__device__ __forceinline__ int sel_at(const MoeWork& w, const int* s_sel, int id) {
+  if (SRC == kSelShared) return s_sel[id];
+  if (SRC == kSelSameLaunch) return __ldcg(w.sel + id);
+  return __ldg(w.sel + id);
+}
+
 // Declared here, defined with the routing below.
-template <bool CG>
+template <int SRC>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
-                                            int pass_nt, bool grouped_ids);
+                                            int pass_nt, bool grouped_ids,
+                                            const int* s_sel = nullptr);
 
 // Top-k (one warp per token, kTopkTokens tokens per CTA) with the routing on
 // the last CTA to finish (an arrival counter; its eight warps group the
@@ -248,10 +267,33 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
   __syncthreads();
   if (!s_last) return;
   __threadfence();  // every CTA's selections are visible from here
-  route_block<true>(m, w, T, pass_nt, grouped_ids != 0);
+  route_block<kSelSameLaunch>(m, w, T, pass_nt, grouped_ids != 0);
   if (threadIdx.x == 0) *w.tickets = 0;
   // the gate/up items' arrival tickets start at zero even after a launch
   // that gave up part-way (each is reset by its last arriver otherwise)
+  if (w.up_tickets)
+    for (int i = threadIdx.x; i < kUpSplitItems; i += blockDim.x) w.up_tickets[i] = 0;
+}
+
+// Small decode batches (T <= 8, E <= 512): the top-k of every token (one
+// warp each) and the routing in one CTA of 8 warps.  The selections meet in
+// shared memory behind one CTA barrier, so the launch needs neither the
+// arrival ticket of the multi-CTA form (a fence before it and after it) nor
+// L2 round trips for the selections (batch 1: 13.5 -> 12.3 us per layer).
+// Larger batches keep their tokens on several SMs: a token's top-k is a
+// long dependent chain, and 32 of them on one SM took 24 us against 18.
+constexpr int kTopkSmallTokens = 8;
+template <int PER>
+__global__ void __launch_bounds__(kTopkSmallTokens * 32) topk_route_small_kernel(
+    MoeDevice m, MoeWork w, int T, int pass_nt, int grouped_ids) {
+  __shared__ int s_sel[kTopkSmallTokens * 32];  // [token][rank], top_k <= 32
+  griddep_wait();
+  griddep_launch();
+  const int t = threadIdx.x >> 5;
+  if (t < T) topk_token<PER>(m, w, t, threadIdx.x & 31, s_sel);
+  if (grouped_ids < 0) return;  // the caller groups the entries (token dispatch)
+  __syncthreads();
+  route_block<kSelShared>(m, w, T, pass_nt, grouped_ids != 0, s_sel);
   if (w.up_tickets)
     for (int i = threadIdx.x; i < kUpSplitItems; i += blockDim.x) w.up_tickets[i] = 0;
 }
@@ -260,9 +302,9 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
 // 8 warps.  pass_nt: tokens per pass of the up kernel; pass_off counts
 // passes.  CG: the selections were written by other CTAs of the same launch
 // (read through L2).
-template <bool CG>
+template <int SRC>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
-                                            int pass_nt, bool grouped_ids) {
+                                            int pass_nt, bool grouped_ids, const int* s_sel) {
   __shared__ int s_count[kMaxExperts];
   __shared__ int s_offset[kMaxExperts + 1];
   const int E = m.experts, k = m.top_k;
@@ -294,8 +336,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int idj = c + 32 * j + lane;  // clamped, not guarded: the loads overlap
-          const int* p = w.sel + min(idj, n - 1);
-          const int v = CG ? __ldcg(p) : __ldg(p);
+          const int v = sel_at<SRC>(w, s_sel, min(idj, n - 1));
           ev[j] = idj < n && ci + j < c_hi ? v : -1;
         }
       const int id = c + lane;
@@ -339,7 +380,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
         for (int u = 0; u < 8; ++u) {
           const int id = min(id0 + 32 * u, id_end - 1);
           pos[u] = w.entries[id];
-          e[u] = CG ? __ldcg(w.sel + id) : w.sel[id];
+          e[u] = sel_at<SRC>(w, s_sel, id);
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -369,7 +410,8 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
       tot[2] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_nt - 1) / pass_nt));
       tot[3] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + 3) / 4));
     }
-    if (lane < 4) s_tot[warp][lane] = tot[lane];
+    if (lane < 4)  // (selects, not a register array indexed by the lane)
+      s_tot[warp][lane] = lane == 0 ? tot[0] : lane == 1 ? tot[1] : lane == 2 ? tot[2] : tot[3];
     __syncthreads();
     int run = 0, nact = 0, prun = 0, drun = 0;
     for (int q = 0; q < warp; ++q) {
@@ -432,7 +474,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
     for (int u = 0; u < 4; ++u) {
       const int id = min(id0 + u * (int)blockDim.x, n - 1);
       pos[u] = w.entries[id];
-      e[u] = CG ? __ldcg(w.sel + id) : w.sel[id];
+      e[u] = sel_at<SRC>(w, s_sel, id);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -2264,6 +2306,14 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
 cudaError_t launch_topk(const MoeDevice& m, const MoeWork& w, int T, int grouped_ids,
                         cudaStream_t s) {
   const int per = (m.experts + 31) / 32, pnt = up_pass_tokens(m, T);
+  if (T <= kTopkSmallTokens && per <= 16) {
+    auto small = per <= 1 ? topk_route_small_kernel<1> : per <= 2 ? topk_route_small_kernel<2>
+               : per <= 4 ? topk_route_small_kernel<4> : per <= 8 ? topk_route_small_kernel<8>
+               : topk_route_small_kernel<16>;
+    cudaError_t e = launch_pdl(small, dim3(1), dim3(32 * kTopkSmallTokens), 0, s, m, w, T, pnt,
+                               grouped_ids);
+    return e != cudaSuccess ? e : cudaGetLastError();
+  }
   auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
             : per <= 4 ? topk_route_kernel<4> : per <= 8 ? topk_route_kernel<8>
             : per <= 16 ? topk_route_kernel<16> : topk_route_kernel<32>;
