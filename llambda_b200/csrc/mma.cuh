@@ -407,6 +407,18 @@ __device__ __forceinline__ void m6_store_subblock(uint8_t* m6, int s_glob, float
   }
 }
 
+// Zeroes sub-block s_glob of an m6 buffer (padding past the matrix's rows).
+// 16 lanes; lane l < 8 writes the 8 bytes of (part l / 4, t l % 4), lane 0
+// the meta.
+__device__ __forceinline__ void m6_zero_subblock(uint8_t* m6, int s_glob, int l) {
+  uint8_t* base = m6 + (size_t)(s_glob >> 4) * 1152;
+  const int q = q6_step_of(s_glob & 15);
+  if (l < 8)
+    reinterpret_cast<uint2*>(base)[(((q >> 1) * 2 + (l >> 2)) * 4 + (l & 3)) * 2 + (q & 1)] =
+        make_uint2(0, 0);
+  if (l == 0) reinterpret_cast<float2*>(base + 1024)[q] = make_float2(0.f, 0.f);
+}
+
 // int8 byte b of w as a float, exactly (2^23 + 128 + v, minus 2^23 + 128).
 __device__ __forceinline__ float s8_to_float(uint32_t w_xor80, int b) {
   return __uint_as_float(__byte_perm(w_xor80, 0x4B000000u, 0x7440u | b)) - 8388736.0f;

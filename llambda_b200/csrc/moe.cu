@@ -874,7 +874,12 @@ struct SlabSync {
   uint4 zero[2];  // the B source of the threads whose column cannot be non-zero
 };
 
-template <int NT, bool PAIR, int DT, bool I6, int CW>
+// DL: the layout the gate/up epilogue writes the down input in: 0 the
+// warp-engine layout (xp_index), 1 i6 (Q6_K sub-block slots, for passes of
+// one or two entries), 2 m6 (four entries per mma, for passes of four).
+enum DownLayout { kDownPlain = 0, kDownI6 = 1, kDownM6 = 2 };
+
+template <int NT, bool PAIR, int DT, int DL, int CW>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_up_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, long map_row_base,
                        const __grid_constant__ CUtensorMap tm_gate,
@@ -1190,13 +1195,17 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
         }
     }
     if (writer) {
-      if (I6) {  // the block's 16 rows are one Q6_K sub-block of the down input
+      if (DL != kDownPlain) {  // the block's 16 rows are one Q6_K sub-block of the down input
         const int s_glob = (x.row0 + rb * kTileRows) >> 4;
 #pragma unroll
         for (int n = 0; n < NT; ++n)
-          if (n < nt)
-            i6_store_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(n) * ld_dn),
-                              s_glob, hv[0][n], hv[1][n], lane);
+          if (n < nt) {
+            uint8_t* dst = reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(n) * ld_dn);
+            if (DL == kDownM6)
+              m6_store_subblock(dst, s_glob, hv[0][n], hv[1][n], lane);
+            else
+              i6_store_subblock(dst, s_glob, hv[0][n], hv[1][n], lane);
+          }
       } else if (t == 0) {
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
@@ -1209,12 +1218,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       }
     }
     if (warp == 0 && x.row0 + RU >= x.rows_e) {  // last slab: zero the padding up to kd
-      if (I6) {  // sub-blocks past the slab (the slab's own are written above)
+      if (DL != kDownPlain) {  // sub-blocks past the slab (the slab's own are written above)
         const int s_from = (x.row0 + RU) >> 4, s_to = kd >> 4;
         for (int qq = lane >> 4; qq < nt * (s_to - s_from); qq += 2) {
           const int nn = qq / (s_to - s_from), sg = s_from + (qq - nn * (s_to - s_from));
-          i6_zero_subblock(reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(nn) * ld_dn), sg,
-                           lane & 15);
+          uint8_t* dst = reinterpret_cast<uint8_t*>(w.xp_down + (long)id_of(nn) * ld_dn);
+          if (DL == kDownM6)
+            m6_zero_subblock(dst, sg, lane & 15);
+          else
+            i6_zero_subblock(dst, sg, lane & 15);
         }
       } else {
         const int pad = kd - x.rows_e;
@@ -1260,10 +1272,12 @@ struct DownSync {
 
 // SB: the pass's entries' prepared inputs are staged with the weights (at
 // stage_w, i6_bytes(K) each) instead of being read through L1.
+// M6: the inputs are in the m6 layout (one mma per k-step serves all four
+// entries of a pass) instead of i6 (one mma per entry and k-step).
 // shared_pass: 0 the routed experts' slabs, 1 the shared expert's, 2 both in
 // one launch (routed units first; the shared down rows must then have the
 // routed rows' width).
-template <int KSPLIT, int CW, bool SB>
+template <int KSPLIT, int CW, bool SB, bool M6>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_down_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, int stage_bytes,
                          int stage_w, int shared_pass) {
@@ -1399,7 +1413,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       xin[n] = SB ? smem + (size_t)s * stage_bytes + stage_w + min(n, nt - 1) * xib
                   : reinterpret_cast<const uint8_t*>(w.xp_down + (long)du.id[n] * ld_dn);
     float2 y[1] = {make_float2(0.f, 0.f)};
-    if (row_blk < H) {
+    if (row_blk < H && M6) {
+      const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
+      for (int sb = sb0; sb < sb1; ++sb)
+        q6k_sb_mma<SB, 1>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, xin,
+                          nt, lane, y);
+    } else if (row_blk < H) {
       const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
       if (nt == 1) {
         q6i_block<SB, 1>(blk, rb, sb0, sb1, xin, bz, lane, 0, y[0]);
@@ -1820,10 +1839,10 @@ bool q4k_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t rb
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT, bool PAIR, int DT, bool I6, int CW>
+template <int NT, bool PAIR, int DT, int DL, int CW>
 cudaError_t launch_up_slab_cw(const MoeDevice& m, const MoeWork& w, int T, const SlabMaps& mp,
                               cudaStream_t s) {
-  auto kern = moe_up_slab_kernel<NT, PAIR, DT, I6, CW>;
+  auto kern = moe_up_slab_kernel<NT, PAIR, DT, DL, CW>;
   constexpr int RU = CW / (PAIR ? 2 : 1) * kTileRows;
   const size_t stage = up_stage_bytes(CW, NT);
   const size_t extra = sizeof(SlabSync) + (size_t)2 * RU * NT * 4;
@@ -1863,6 +1882,13 @@ bool down_plan(size_t rb, int K, DownPlan* p) {
 // The down input is written in the i6 layout and the down pass runs on the
 // Q6_K tensor-core slabs when the gate/up pass is the tensor-core one, the
 // down rows are Q6_K, the hidden size is a multiple of 16 and the slabs fit.
+int up_pass_tokens(const MoeDevice& m, int T);
+
+// With passes of four entries (expected tokens per active expert of 2.5 or
+// more) the down input is written in m6 and the down slabs take each k-step
+// of all four entries in one mma; with passes of one or two, in i6.
+bool down_uses_m6(const MoeDevice& m, int T) { return up_pass_tokens(m, T) >= 4; }
+
 bool down_uses_i6(const MoeDevice& m) {
   DownPlan p;
   if (m.up_type != LB_TYPE_Q4_K || m.down_type != LB_TYPE_Q6_K || m.hidden % kTileRows) return false;
@@ -1870,10 +1896,10 @@ bool down_uses_i6(const MoeDevice& m) {
   return !(m.shared_here && m.inter_sh) || down_plan(m.down_sh_rb, m.k_down_sh, &p);
 }
 
-template <int KSPLIT, bool SB>
+template <int KSPLIT, bool SB, bool M6>
 cudaError_t launch_down_slab_k(const MoeDevice& m, const MoeWork& w, int T, int shared_pass,
                                const DownPlan& p, cudaStream_t s) {
-  auto kern = moe_down_slab_kernel<KSPLIT, kDownWarps, SB>;
+  auto kern = moe_down_slab_kernel<KSPLIT, kDownWarps, SB, M6>;
   const size_t smem = (size_t)p.stages * p.stage_bytes + sizeof(DownSync) +
                       (KSPLIT > 1 ? (size_t)p.stages * kDownWarps * 32 * sizeof(float2) : 0);
   if (prepared_occupancy(kern, (kDownWarps + 1) * 32, smem) < 1) return cudaErrorUnknown;
@@ -1887,9 +1913,12 @@ cudaError_t launch_down_slab(const MoeDevice& m, const MoeWork& w, int T, int sh
   if (!down_plan(shared_pass == 1 ? m.down_sh_rb : m.down_rb,
                  shared_pass == 1 ? m.k_down_sh : m.k_down, &p))
     return cudaErrorInvalidValue;
+  const bool m6 = down_uses_m6(m, T);
 #define LB_DOWN_SLAB(KS)                                                                \
-  return p.staged ? launch_down_slab_k<KS, true>(m, w, T, shared_pass, p, s)              \
-                  : launch_down_slab_k<KS, false>(m, w, T, shared_pass, p, s);
+  return p.staged ? (m6 ? launch_down_slab_k<KS, true, true>(m, w, T, shared_pass, p, s)  \
+                        : launch_down_slab_k<KS, true, false>(m, w, T, shared_pass, p, s)) \
+                  : (m6 ? launch_down_slab_k<KS, false, true>(m, w, T, shared_pass, p, s) \
+                        : launch_down_slab_k<KS, false, false>(m, w, T, shared_pass, p, s));
   switch (kDownWarps / p.nb) {
     case 1: LB_DOWN_SLAB(1)
     case 2: LB_DOWN_SLAB(2)
@@ -1905,11 +1934,16 @@ cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const
   // 16 consumer warps where their registers fit (96 each), else 8
   constexpr int CW = NT <= 2 ? 16 : 8;
   const bool pair = m.arch == 0;
+  if constexpr (NT == 4) {  // passes of four: the down pass takes them in m6
+    if (DT == LB_TYPE_Q6_K && down_uses_i6(m) && down_uses_m6(m, T))
+      return pair ? launch_up_slab_cw<NT, true, DT, kDownM6, CW>(m, w, T, mp, s)
+                  : launch_up_slab_cw<NT, false, DT, kDownM6, CW>(m, w, T, mp, s);
+  }
   if (DT == LB_TYPE_Q6_K && down_uses_i6(m))
-    return pair ? launch_up_slab_cw<NT, true, DT, true, CW>(m, w, T, mp, s)
-                : launch_up_slab_cw<NT, false, DT, true, CW>(m, w, T, mp, s);
-  return pair ? launch_up_slab_cw<NT, true, DT, false, CW>(m, w, T, mp, s)
-              : launch_up_slab_cw<NT, false, DT, false, CW>(m, w, T, mp, s);
+    return pair ? launch_up_slab_cw<NT, true, DT, kDownI6, CW>(m, w, T, mp, s)
+                : launch_up_slab_cw<NT, false, DT, kDownI6, CW>(m, w, T, mp, s);
+  return pair ? launch_up_slab_cw<NT, true, DT, kDownPlain, CW>(m, w, T, mp, s)
+              : launch_up_slab_cw<NT, false, DT, kDownPlain, CW>(m, w, T, mp, s);
 }
 
 // Tokens per pass (NT) of the tensor-core gate/up launch, from the expected
