@@ -583,9 +583,13 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeDevice m, MoeWork w,
 // super-block of one token each), and every CTA forms its 16 x 8 logits (dot-product-with-f32-tensor-data, L4096-4107) with
 // packed fp32x2 FMAs and a 31-shuffle butterfly.  Row E of qwen3next (the
 // shared-expert gate) comes from router_extra_row when it is kept apart.
-constexpr int kRouterTok = 8, kRouterRows = 16, kRouterWarps = 8;
+// TOK: tokens per CTA, 8, or 4 where 8 tokens' and 16 rows' worth of the
+// hidden size would not fit in shared memory (config 4, hidden 2688).
+constexpr int kRouterRows = 16, kRouterWarps = 8;
+template <int TOK>
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     MoeDevice m, MoeWork w, const float* __restrict__ x, int T, int router_rows) {
+  constexpr int kRouterTok = TOK;
   extern __shared__ float4 rs4[];  // [8][H/4] tokens, then [16][H/4] router rows
   __shared__ __align__(8) uint64_t bar_x, bar_w;
   __shared__ float s_scale[kRouterTok];
@@ -683,20 +687,24 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
       }
     }
   }
-  // transpose-reduce of the warp's R * 8 sums over the 32 lanes: value
-  // r * 8 + n ends on lanes 2(r * 8 + n) and 2(r * 8 + n) + 1
+  // transpose-reduce of the warp's NV = R * TOK sums over the 32 lanes: each
+  // halving step keeps half of a lane's values (the upper lanes the upper
+  // half) and adds the partner's, so value r * TOK + n ends on the lanes
+  // whose bits above the low LS bits spell its index; the low bits are summed
+  // last
   constexpr int NV = R * kRouterTok;
-  static_assert(NV == 16, "two rows of eight tokens per warp");
+  static_assert(NV == 16 || NV == 8, "two rows of eight or four tokens per warp");
+  constexpr int LS = NV == 16 ? 1 : 2;
   float v[NV];
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
     for (int p = 0; p < kRouterTok / 2; ++p) {
-      v[r * 8 + 2 * p] = acc[r][p].x;
-      v[r * 8 + 2 * p + 1] = acc[r][p].y;
+      v[r * kRouterTok + 2 * p] = acc[r][p].x;
+      v[r * kRouterTok + 2 * p + 1] = acc[r][p].y;
     }
 #pragma unroll
-  for (int h = 16, cnt = NV / 2; h >= 2; h >>= 1, cnt >>= 1) {
+  for (int h = 16, cnt = NV / 2; cnt >= 1; h >>= 1, cnt >>= 1) {
     const bool upper = (lane & h) != 0;
 #pragma unroll
     for (int i = 0; i < cnt; ++i) {
@@ -705,9 +713,10 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
     }
   }
-  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-  const int idx = (lane >> 1) & (NV - 1), r = idx >> 3, n = idx & 7;
-  if ((lane & 1) == 0 && row0 + r < crows && n < nt)
+#pragma unroll
+  for (int h = 1 << (LS - 1); h >= 1; h >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], h);
+  const int idx = (lane >> LS) & (NV - 1), r = idx / kRouterTok, n = idx % kRouterTok;
+  if ((lane & ((1 << LS) - 1)) == 0 && row0 + r < crows && n < nt)
     w.logits[(long)(t0 + n) * (E + 1) + crow0 + row0 + r] = v[0];
 }
 
@@ -1882,12 +1891,15 @@ bool down_plan(size_t rb, int K, DownPlan* p) {
 // The down input is written in the i6 layout and the down pass runs on the
 // Q6_K tensor-core slabs when the gate/up pass is the tensor-core one, the
 // down rows are Q6_K, the hidden size is a multiple of 16 and the slabs fit.
-int up_pass_tokens(const MoeDevice& m, int T);
+double tokens_per_active_expert(const MoeDevice& m, int T);
 
-// With passes of four entries (expected tokens per active expert of 2.5 or
-// more) the down input is written in m6 and the down slabs take each k-step
-// of all four entries in one mma; with passes of one or two, in i6.
-bool down_uses_m6(const MoeDevice& m, int T) { return up_pass_tokens(m, T) >= 4; }
+// Where experts expect 2.5 or more tokens the down input is written in m6 and
+// the down slabs (passes of four entries) take each k-step of all four in
+// one mma; with fewer, most passes hold one or two entries and i6 gives each
+// its own mma.
+bool down_uses_m6(const MoeDevice& m, int T) {
+  return m.up_type == LB_TYPE_Q4_K && T > 1 && tokens_per_active_expert(m, T) >= 2.5;
+}
 
 bool down_uses_i6(const MoeDevice& m) {
   DownPlan p;
@@ -1934,7 +1946,7 @@ cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const
   // 16 consumer warps where their registers fit (96 each), else 8
   constexpr int CW = NT <= 2 ? 16 : 8;
   const bool pair = m.arch == 0;
-  if constexpr (NT == 4) {  // passes of four: the down pass takes them in m6
+  if constexpr (NT > 1) {  // the down pass takes passes of four in m6
     if (DT == LB_TYPE_Q6_K && down_uses_i6(m) && down_uses_m6(m, T))
       return pair ? launch_up_slab_cw<NT, true, DT, kDownM6, CW>(m, w, T, mp, s)
                   : launch_up_slab_cw<NT, false, DT, kDownM6, CW>(m, w, T, mp, s);
@@ -1951,12 +1963,19 @@ cudaError_t launch_up_slab_nt(const MoeDevice& m, const MoeWork& w, int T, const
 // With T*k entries spread over E experts, about E * (1 - exp(-T*k / E))
 // experts are hit, each by T*k / that many tokens on average; an expert-
 // parallel rank sees the same ratio on its share of the experts and entries.
-int up_pass_tokens(const MoeDevice& m, int T) {
-  if (m.up_type != LB_TYPE_Q4_K || T == 1) return 1;
+double tokens_per_active_expert(const MoeDevice& m, int T) {
   const double entries = (double)T * m.top_k, E = std::max(1, m.experts);
   const double hit = E * -std::expm1(-entries / E);
-  const double per_expert = entries / std::max(1.0, hit);
-  return per_expert < 2.5 ? 2 : 4;
+  return entries / std::max(1.0, hit);
+}
+
+// Two-token passes (16 consumer warps of 96 registers) up to 8 expected
+// tokens per expert: at 4.8 (config 4, batch 64) they beat four-token passes
+// (8 warps of 160 registers) by 15% although the weights are decoded twice
+// as often.
+int up_pass_tokens(const MoeDevice& m, int T) {
+  if (m.up_type != LB_TYPE_Q4_K || T == 1) return 1;
+  return tokens_per_active_expert(m, T) < 8.0 ? 2 : 4;
 }
 
 // Routed and shared gate/up in one tensor-core launch.
@@ -2266,7 +2285,11 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   if (m.inter_sh && m.k_in_sh != m.k_in) return cudaErrorInvalidValue;
   const int E = m.experts;
   cudaError_t e;
-  const size_t router_smem = (size_t)(kRouterTok + kRouterRows) * m.hidden * sizeof(float);
+  // the router's CTA tile: 8 tokens, or 4 where 8 do not fit beside the rows
+  const size_t router_smem8 = (size_t)(8 + kRouterRows) * m.hidden * sizeof(float);
+  const int router_tok = router_smem8 <= 192 * 1024 ? 8 : 4;
+  const size_t router_smem = (size_t)(router_tok + kRouterRows) * m.hidden * sizeof(float);
+  auto router_kern = router_tok == 8 ? moe_router_kernel<8> : moe_router_kernel<4>;
   const uintptr_t align =
       reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(m.router) |
       reinterpret_cast<uintptr_t>(m.router_extra_row) | reinterpret_cast<uintptr_t>(m.input_norm);
@@ -2285,11 +2308,10 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
   } else if (prefill) {
     if ((e = launch_prefill_router(m, w, x, T, s)) != cudaSuccess) return e;
   } else if (m.up_type == LB_TYPE_Q4_K && (m.hidden & 3) == 0 && (align & 15) == 0 &&
-      router_smem <= 192 * 1024 &&
-      prepared_occupancy(moe_router_kernel, kRouterWarps * 32, router_smem) >= 1) {
-    // top-k and routing ride on the router launch (its last CTAs)
-    dim3 grid((all_rows + kRouterRows - 1) / kRouterRows, (T + kRouterTok - 1) / kRouterTok);
-    e = launch_pdl(moe_router_kernel, grid, dim3(kRouterWarps * 32), router_smem, s, m, w, x, T,
+      router_smem <= 224 * 1024 &&
+      prepared_occupancy(router_kern, kRouterWarps * 32, router_smem) >= 1) {
+    dim3 grid((all_rows + kRouterRows - 1) / kRouterRows, (T + router_tok - 1) / router_tok);
+    e = launch_pdl(router_kern, grid, dim3(kRouterWarps * 32), router_smem, s, m, w, x, T,
                    all_rows);
     if (e != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
