@@ -243,7 +243,7 @@ __device__ __forceinline__ int sel_at(const MoeWork& w, const int* s_sel, int id
 // Declared here, defined with the routing below.
 template <int SRC>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
-                                            int pass_nt, bool grouped_ids,
+                                            int pass_nt, int pass_dn, bool grouped_ids,
                                             const int* s_sel = nullptr);
 
 // Top-k (one warp per token, kTopkTokens tokens per CTA) with the routing on
@@ -252,7 +252,8 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
 // between launches: the last CTA resets it.
 template <int PER>
 __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w, int T,
-                                                         int pass_nt, int grouped_ids) {
+                                                         int pass_nt, int pass_dn,
+                                                         int grouped_ids) {
   __shared__ int s_last;
   griddep_wait();
   griddep_launch();
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
   __syncthreads();
   if (!s_last) return;
   __threadfence();  // every CTA's selections are visible from here
-  route_block<kSelSameLaunch>(m, w, T, pass_nt, grouped_ids != 0);
+  route_block<kSelSameLaunch>(m, w, T, pass_nt, pass_dn, grouped_ids != 0);
   if (threadIdx.x == 0) *w.tickets = 0;
   // the gate/up items' arrival tickets start at zero even after a launch
   // that gave up part-way (each is reset by its last arriver otherwise)
@@ -285,7 +286,7 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
 constexpr int kTopkSmallTokens = 8;
 template <int PER>
 __global__ void __launch_bounds__(kTopkSmallTokens * 32) topk_route_small_kernel(
-    MoeDevice m, MoeWork w, int T, int pass_nt, int grouped_ids) {
+    MoeDevice m, MoeWork w, int T, int pass_nt, int pass_dn, int grouped_ids) {
   __shared__ int s_sel[kTopkSmallTokens * 32];  // [token][rank], top_k <= 32
   griddep_wait();
   griddep_launch();
@@ -293,18 +294,19 @@ __global__ void __launch_bounds__(kTopkSmallTokens * 32) topk_route_small_kernel
   if (t < T) topk_token<PER>(m, w, t, threadIdx.x & 31, s_sel);
   if (grouped_ids < 0) return;  // the caller groups the entries (token dispatch)
   __syncthreads();
-  route_block<kSelShared>(m, w, T, pass_nt, grouped_ids != 0, s_sel);
+  route_block<kSelShared>(m, w, T, pass_nt, pass_dn, grouped_ids != 0, s_sel);
   if (w.up_tickets)
     for (int i = threadIdx.x; i < kUpSplitItems; i += blockDim.x) w.up_tickets[i] = 0;
 }
 
 // Groups the (token, rank) entries by owned expert, stably.  One CTA of up to
-// 8 warps.  pass_nt: tokens per pass of the up kernel; pass_off counts
-// passes.  CG: the selections were written by other CTAs of the same launch
+// 8 warps.  pass_nt / pass_dn: tokens per pass of the up / down kernel;
+// pass_off / pass_off_dn count passes.  CG: the selections were written by other CTAs of the same launch
 // (read through L2).
 template <int SRC>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
-                                            int pass_nt, bool grouped_ids, const int* s_sel) {
+                                            int pass_nt, int pass_dn, bool grouped_ids,
+                                            const int* s_sel) {
   __shared__ int s_count[kMaxExperts];
   __shared__ int s_offset[kMaxExperts + 1];
   const int E = m.experts, k = m.top_k;
@@ -408,7 +410,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
       tot[0] += (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
       tot[1] += __popc(__ballot_sync(0xffffffffu, cnt > 0));
       tot[2] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_nt - 1) / pass_nt));
-      tot[3] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + 3) / 4));
+      tot[3] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_dn - 1) / pass_dn));
     }
     if (lane < 4)  // (selects, not a register array indexed by the lane)
       s_tot[warp][lane] = lane == 0 ? tot[0] : lane == 1 ? tot[1] : lane == 2 ? tot[2] : tot[3];
@@ -423,7 +425,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
     for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
       const int e = e0 + lane;
       const int cnt = e < e_hi ? s_count[e] : 0;
-      const int pc = (cnt + pass_nt - 1) / pass_nt, dc = (cnt + 3) / 4;
+      const int pc = (cnt + pass_nt - 1) / pass_nt, dc = (cnt + pass_dn - 1) / pass_dn;
       int incl = cnt, pincl = pc, dincl = dc;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -1265,8 +1267,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
 // `partial` (token * (k + 1) + slot).
 struct __align__(16) DownUnit {
   int row0, nt, pad[2];
-  int id[4];
-  int orow[4];
+  int id[8];
+  int orow[8];
 };
 
 struct DownSync {
@@ -1281,21 +1283,25 @@ struct DownSync {
 
 // SB: the pass's entries' prepared inputs are staged with the weights (at
 // stage_w, i6_bytes(K) each) instead of being read through L1.
-// M6: the inputs are in the m6 layout (one mma per k-step serves all four
+// M6: the inputs are in the m6 layout (one mma per k-step serves four
 // entries of a pass) instead of i6 (one mma per entry and k-step).
+// NTD: entries per pass, 4, or 8 in m6 (two groups of four per k-step, so an
+// expert with five to eight entries streams its rows once).
 // shared_pass: 0 the routed experts' slabs, 1 the shared expert's, 2 both in
 // one launch (routed units first; the shared down rows must then have the
 // routed rows' width).
-template <int KSPLIT, int CW, bool SB, bool M6>
+template <int KSPLIT, int CW, bool SB, bool M6, int NTD>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_down_slab_kernel(MoeDevice m, MoeWork w, int T, int stages, int stage_bytes,
                          int stage_w, int shared_pass) {
   constexpr int NB = CW / KSPLIT;  // 16-row blocks per slab
   constexpr int RU = NB * kTileRows;
-  constexpr int NT = 4;
+  constexpr int NT = NTD;
+  constexpr int NG = NTD / 4;  // groups of four entries
+  static_assert(NTD == 4 || (NTD == 8 && M6), "eight entries per pass in m6 only");
   extern __shared__ __align__(128) uint8_t smem[];
   DownSync* sync = reinterpret_cast<DownSync*>(smem + (size_t)stages * stage_bytes);
-  float2* red = reinterpret_cast<float2*>(sync + 1);  // [stages][CW][32]
+  float2* red = reinterpret_cast<float2*>(sync + 1);  // [stages][CW][32][NG]
   volatile int* abort = &sync->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -1421,12 +1427,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     for (int n = 0; n < NT; ++n)
       xin[n] = SB ? smem + (size_t)s * stage_bytes + stage_w + min(n, nt - 1) * xib
                   : reinterpret_cast<const uint8_t*>(w.xp_down + (long)du.id[n] * ld_dn);
-    float2 y[1] = {make_float2(0.f, 0.f)};
+    float2 y[NG];
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) y[grp] = make_float2(0.f, 0.f);
     if (row_blk < H && M6) {
       const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
       for (int sb = sb0; sb < sb1; ++sb)
-        q6k_sb_mma<SB, 1>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, xin,
-                          nt, lane, y);
+        q6k_sb_mma<SB, NG>(blk + g * rb + sb * LB_Q6K, blk + (g + 8) * rb + sb * LB_Q6K, sb, xin,
+                           nt, lane, y);
     } else if (row_blk < H) {
       const uint8_t* blk = smem + (size_t)s * stage_bytes + (size_t)b * kTileRows * rb;
       if (nt == 1) {
@@ -1442,31 +1450,38 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       }
     }
     if (KSPLIT > 1) {
-      float2* rs = red + ((size_t)s * CW) * 32;
+      float2* rs = red + ((size_t)s * CW) * 32 * NG;
       if (kp != 0) {
-        rs[warp * 32 + lane] = y[0];
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) rs[(warp * 32 + lane) * NG + grp] = y[grp];
         __syncwarp();
         if (lane == 0) mbar_arrive(&sync->red[s]);
       } else {
         if (!mbar_wait_or_abort(&sync->red[s], rp.phase, w.status, abort)) break;
 #pragma unroll
-        for (int p = 1; p < KSPLIT; ++p) {
-          const float2 o = rs[(warp + p) * 32 + lane];
-          y[0].x += o.x;
-          y[0].y += o.y;
-        }
+        for (int p = 1; p < KSPLIT; ++p)
+#pragma unroll
+          for (int grp = 0; grp < NG; ++grp) {
+            const float2 o = rs[((warp + p) * 32 + lane) * NG + grp];
+            y[grp].x += o.x;
+            y[grp].y += o.y;
+          }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sync->empty[s]);
-    if (kp == 0 && row_blk < H && t < nt) {
-      int orow = du.orow[0];
 #pragma unroll
-      for (int n2 = 1; n2 < NT; ++n2)
-        if (n2 == t) orow = du.orow[n2];
-      float* out = w.partial + (long)orow * H + row_blk;
-      out[g] = y[0].x;
-      out[g + 8] = y[0].y;
+    for (int grp = 0; grp < NG; ++grp) {
+      const int n = 4 * grp + t;  // this lane's entry of the group
+      if (kp == 0 && row_blk < H && n < nt) {
+        int orow = du.orow[0];
+#pragma unroll
+        for (int n2 = 1; n2 < NT; ++n2)
+          if (n2 == n) orow = du.orow[n2];
+        float* out = w.partial + (long)orow * H + row_blk;
+        out[g] = y[grp].x;
+        out[g + 8] = y[grp].y;
+      }
     }
   }
 }
@@ -1871,18 +1886,18 @@ struct DownPlan {
 };
 constexpr int kDownWarps = 8;
 
-bool down_plan(size_t rb, int K, DownPlan* p) {
+bool down_plan(size_t rb, int K, DownPlan* p, int ntd = 4) {
   const size_t block = (size_t)kTileRows * rb;
   int nb = 8;
   while (nb > 1 && nb * block > 56 * 1024) nb >>= 1;
   p->nb = nb;
   p->stage_w = (int)((nb * block + 127) & ~size_t(127));
   // the entries' inputs ride in the stage when three stages still fit
-  const size_t red = nb < kDownWarps ? (size_t)kDownWarps * 32 * sizeof(float2) : 0;
+  const size_t red = nb < kDownWarps ? (size_t)kDownWarps * 32 * sizeof(float2) * (ntd / 4) : 0;
   const size_t room = kTileSmemBudget - sizeof(DownSync);
   p->staged = 4 * i6_bytes(K) <= 24 * 1024 &&
-              room / (p->stage_w + 4 * i6_bytes(K) + red) >= 3;
-  p->stage_bytes = p->stage_w + (p->staged ? (int)(4 * i6_bytes(K)) : 0);
+              room / (p->stage_w + ntd * i6_bytes(K) + red) >= 3;
+  p->stage_bytes = p->stage_w + (p->staged ? (int)(ntd * i6_bytes(K)) : 0);
   const size_t per_stage = (size_t)p->stage_bytes + red;
   p->stages = (int)std::min<size_t>(kSlabMaxStages, room / per_stage);
   return p->stages >= 2;
@@ -1901,6 +1916,15 @@ bool down_uses_m6(const MoeDevice& m, int T) {
   return m.up_type == LB_TYPE_Q4_K && T > 1 && tokens_per_active_expert(m, T) >= 2.5;
 }
 
+// Entries per down pass: 8 (two m6 groups per k-step) in a launch of the
+// shared expert's slabs alone, which sees every token (config 4, batch 64:
+// 60 -> 50 us); 4 for the routed experts, whose passes of eight were slower
+// (223 -> 252 us: most experts hold four or fewer entries, and the second
+// group's registers and mma cost every pass).
+int down_pass_tokens(const MoeDevice& m, int T, int shared_pass) {
+  return shared_pass == 1 && down_uses_m6(m, T) ? 8 : 4;
+}
+
 bool down_uses_i6(const MoeDevice& m) {
   DownPlan p;
   if (m.up_type != LB_TYPE_Q4_K || m.down_type != LB_TYPE_Q6_K || m.hidden % kTileRows) return false;
@@ -1908,12 +1932,13 @@ bool down_uses_i6(const MoeDevice& m) {
   return !(m.shared_here && m.inter_sh) || down_plan(m.down_sh_rb, m.k_down_sh, &p);
 }
 
-template <int KSPLIT, bool SB, bool M6>
+template <int KSPLIT, bool SB, bool M6, int NTD = 4>
 cudaError_t launch_down_slab_k(const MoeDevice& m, const MoeWork& w, int T, int shared_pass,
                                const DownPlan& p, cudaStream_t s) {
-  auto kern = moe_down_slab_kernel<KSPLIT, kDownWarps, SB, M6>;
-  const size_t smem = (size_t)p.stages * p.stage_bytes + sizeof(DownSync) +
-                      (KSPLIT > 1 ? (size_t)p.stages * kDownWarps * 32 * sizeof(float2) : 0);
+  auto kern = moe_down_slab_kernel<KSPLIT, kDownWarps, SB, M6, NTD>;
+  const size_t smem =
+      (size_t)p.stages * p.stage_bytes + sizeof(DownSync) +
+      (KSPLIT > 1 ? (size_t)p.stages * kDownWarps * 32 * sizeof(float2) * (NTD / 4) : 0);
   if (prepared_occupancy(kern, (kDownWarps + 1) * 32, smem) < 1) return cudaErrorUnknown;
   return launch_pdl(kern, dim3(sm_count()), dim3((kDownWarps + 1) * 32), smem, s, m, w, T,
                     p.stages, p.stage_bytes, p.stage_w, shared_pass);
@@ -1922,14 +1947,18 @@ cudaError_t launch_down_slab_k(const MoeDevice& m, const MoeWork& w, int T, int 
 cudaError_t launch_down_slab(const MoeDevice& m, const MoeWork& w, int T, int shared_pass,
                              cudaStream_t s) {
   DownPlan p;
+  const int ntd = down_pass_tokens(m, T, shared_pass);
   if (!down_plan(shared_pass == 1 ? m.down_sh_rb : m.down_rb,
-                 shared_pass == 1 ? m.k_down_sh : m.k_down, &p))
+                 shared_pass == 1 ? m.k_down_sh : m.k_down, &p, ntd))
     return cudaErrorInvalidValue;
   const bool m6 = down_uses_m6(m, T);
-#define LB_DOWN_SLAB(KS)                                                                \
-  return p.staged ? (m6 ? launch_down_slab_k<KS, true, true>(m, w, T, shared_pass, p, s)  \
-                        : launch_down_slab_k<KS, true, false>(m, w, T, shared_pass, p, s)) \
-                  : (m6 ? launch_down_slab_k<KS, false, true>(m, w, T, shared_pass, p, s) \
+#define LB_DOWN_SLAB(KS)                                                                     \
+  if (ntd == 8)                                                                             \
+    return p.staged ? launch_down_slab_k<KS, true, true, 8>(m, w, T, shared_pass, p, s)        \
+                    : launch_down_slab_k<KS, false, true, 8>(m, w, T, shared_pass, p, s);      \
+  return p.staged ? (m6 ? launch_down_slab_k<KS, true, true>(m, w, T, shared_pass, p, s)       \
+                        : launch_down_slab_k<KS, true, false>(m, w, T, shared_pass, p, s))      \
+                  : (m6 ? launch_down_slab_k<KS, false, true>(m, w, T, shared_pass, p, s)      \
                         : launch_down_slab_k<KS, false, false>(m, w, T, shared_pass, p, s));
   switch (kDownWarps / p.nb) {
     case 1: LB_DOWN_SLAB(1)
@@ -2362,19 +2391,20 @@ cudaError_t launch_moe(const MoeDevice& m, const MoeWork& w, const float* x, int
 cudaError_t launch_topk(const MoeDevice& m, const MoeWork& w, int T, int grouped_ids,
                         cudaStream_t s) {
   const int per = (m.experts + 31) / 32, pnt = up_pass_tokens(m, T);
+  const int pdn = down_pass_tokens(m, T, 0);  // the routed down passes
   if (T <= kTopkSmallTokens && per <= 16) {
     auto small = per <= 1 ? topk_route_small_kernel<1> : per <= 2 ? topk_route_small_kernel<2>
                : per <= 4 ? topk_route_small_kernel<4> : per <= 8 ? topk_route_small_kernel<8>
                : topk_route_small_kernel<16>;
     cudaError_t e = launch_pdl(small, dim3(1), dim3(32 * kTopkSmallTokens), 0, s, m, w, T, pnt,
-                               grouped_ids);
+                               pdn, grouped_ids);
     return e != cudaSuccess ? e : cudaGetLastError();
   }
   auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
             : per <= 4 ? topk_route_kernel<4> : per <= 8 ? topk_route_kernel<8>
             : per <= 16 ? topk_route_kernel<16> : topk_route_kernel<32>;
   cudaError_t e = launch_pdl(kern, dim3((T + kTopkTokens - 1) / kTopkTokens), dim3(256), 0, s, m,
-                             w, T, pnt, grouped_ids);
+                             w, T, pnt, pdn, grouped_ids);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
