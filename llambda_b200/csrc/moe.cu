@@ -38,9 +38,12 @@ constexpr int kMaxExperts = 1024;
 // (token, rank) entries of one layer call (prefill batches included)
 constexpr int kMaxEntries = 64 * 1024;
 // The routing CTA splits the grouping of entries over its warps from
-// 8 * kRouteSplitChunks chunks of 32 entries on (prefill batches), with
-// per-warp expert counters in kRouteSplitSlots ints of shared memory.
-constexpr int kRouteSplitChunks = 4;
+// 8 * kRouteSplitChunks chunks of 32 entries on (decode batch 32 and up:
+// the grouping walk of its 320 entries took 4.0 us on one warp, 2.0 split;
+// at 80 entries the split's extra zeroing and fix-up cost more than they
+// save), with per-warp expert counters in kRouteSplitSlots ints of shared
+// memory.
+constexpr int kRouteSplitChunks = 1;
 constexpr int kTopkTokens = 8;  // tokens per CTA of the top-k launch (one per warp)
 constexpr int kRouteSplitSlots = 8192;
 constexpr int kSlabMaxStages = 10;
@@ -276,6 +279,70 @@ __global__ void __launch_bounds__(256) topk_route_kernel(MoeDevice m, MoeWork w,
     for (int i = threadIdx.x; i < kUpSplitItems; i += blockDim.x) w.up_tickets[i] = 0;
 }
 
+// The grouping of route_block for at most 32 entries (decode batches of a
+// token or three), by one warp with lane i on entry i: match_any gives each
+// entry its expert's group, its position (entries of the group on lower
+// lanes: the order stays stable) and the group's size; each group's leader
+// (its lowest lane) finds its place among the groups in increasing expert
+// id, and the entry, up-pass and down-pass offsets before it, by one pass
+// over the leaders.  Only the active experts' counts and offsets are
+// written: the decode passes read no others (every launch of the dense form
+// writes them all).  This replaces a scan over every expert (1.5 us of the
+// 3.1 us routing at one token and 512 experts).
+__device__ __forceinline__ void route_sparse_warp(const MoeDevice& m, const MoeWork& w, int T,
+                                                  int pass_nt, int pass_dn, bool grouped_ids,
+                                                  const int* s_sel, int lane) {
+  const int n = T * m.top_k;
+  const int e = lane < n ? s_sel[lane] : -1;
+  const bool own = e >= m.expert_begin && e < m.expert_end;
+  const unsigned owners = __ballot_sync(0xffffffffu, own);
+  const unsigned grp = __match_any_sync(0xffffffffu, own ? e : -1) & owners;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int pos = __popc(grp & lt_mask), cnt = __popc(grp);
+  const bool leader = own && pos == 0;
+  const unsigned leaders = __ballot_sync(0xffffffffu, leader);
+  // this leader's place among the groups and the offsets before it
+  int a = 0, off = 0, poff = 0, doff = 0;
+  for (unsigned rest = leaders; rest; rest &= rest - 1u) {
+    const int j = __ffs(rest) - 1;
+    const int ej = __shfl_sync(0xffffffffu, e, j), cj = __shfl_sync(0xffffffffu, cnt, j);
+    if (ej < e) {
+      ++a;
+      off += cj;
+      poff += (cj + pass_nt - 1) / pass_nt;
+      doff += (cj + pass_dn - 1) / pass_dn;
+    }
+  }
+  const int nact = __popc(leaders), n_own = __popc(owners);
+  if (leader) {
+    w.active[a] = e;
+    w.pass_off[a] = poff;
+    w.pass_off_dn[a] = doff;
+    w.counts[e] = cnt;
+    w.offsets[e] = off;
+  }
+  // the totals: the last group's offsets plus its own passes
+  int tp = leader ? poff + (cnt + pass_nt - 1) / pass_nt : 0;
+  int td = leader ? doff + (cnt + pass_dn - 1) / pass_dn : 0;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    tp = max(tp, __shfl_xor_sync(0xffffffffu, tp, o));
+    td = max(td, __shfl_xor_sync(0xffffffffu, td, o));
+  }
+  if (lane == 0) {
+    w.active[m.experts] = nact;
+    w.pass_off[nact] = tp;
+    w.pass_off_dn[nact] = td;
+    w.offsets[m.experts] = n_own;
+  }
+  if (lane < n) w.entries[lane] = own ? pos : -1;
+  if (grouped_ids && own) {
+    const int lead = __ffs(grp) - 1;  // the group's offset is its leader's
+    const int goff = __shfl_sync(grp, off, lead);
+    w.entries[n + goff + pos] = lane;
+  }
+}
+
 // Small decode batches (T <= 8, E <= 512): the top-k of every token (one
 // warp each) and the routing in one CTA of 8 warps.  The selections meet in
 // shared memory behind one CTA barrier, so the launch needs neither the
@@ -294,7 +361,12 @@ __global__ void __launch_bounds__(kTopkSmallTokens * 32) topk_route_small_kernel
   if (t < T) topk_token<PER>(m, w, t, threadIdx.x & 31, s_sel);
   if (grouped_ids < 0) return;  // the caller groups the entries (token dispatch)
   __syncthreads();
-  route_block<kSelShared>(m, w, T, pass_nt, pass_dn, grouped_ids != 0, s_sel);
+  if (T * m.top_k <= 32) {
+    if (threadIdx.x < 32)
+      route_sparse_warp(m, w, T, pass_nt, pass_dn, grouped_ids != 0, s_sel, threadIdx.x);
+  } else {
+    route_block<kSelShared>(m, w, T, pass_nt, pass_dn, grouped_ids != 0, s_sel);
+  }
   if (w.up_tickets)
     for (int i = threadIdx.x; i < kUpSplitItems; i += blockDim.x) w.up_tickets[i] = 0;
 }
