@@ -518,10 +518,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
   };
   // the tokens' prepared input, 128 values per warp item (mx_store4 wants the
   // 8 lanes of each 32-value sub-block together); a warp's next four items
-  // are loaded before any is converted, so their latencies overlap, and the
-  // first four before the tile copies are issued, so that these few loads do
-  // not wait behind the copies' traffic (config 1: the prepared input was
-  // ready 5.0 us after the CTAs started, now 3.7 us)
+  // are loaded before any is converted, so their latencies overlap.  The
+  // kernel is launched with programmatic stream serialization: its first
+  // tiles' copies (the weights depend on no kernel before it) are issued
+  // while the kernel before it still runs, and the input is read after
+  // griddepcontrol.wait (the input is that kernel's output; the output may
+  // still be its input).
   constexpr int kPrepBatch = 4;
   const int items = tokens * (K >> 7);
   float4 v[kPrepBatch];
@@ -533,12 +535,13 @@ __global__ void __launch_bounds__(NW * 32, 1)
       v[b] = __ldg(reinterpret_cast<const float4*>(x + (long)tok * ldx + e));
     }
   };
-  load_batch(warp);
   int issued = 0;  // meaningful in warp 0 (the producer)
   if (warp == 0)
     for (; issued < plan.stages && issued < n_my; ++issued) issue(issued);
+  griddep_wait();
+  griddep_launch();
   for (int it0 = warp; it0 < items; it0 += NW * kPrepBatch) {
-    if (it0 != warp) load_batch(it0);
+    load_batch(it0);
 #pragma unroll
     for (int b = 0; b < kPrepBatch; ++b) {
       const int it = it0 + b * NW;  // warp-uniform
@@ -1028,9 +1031,10 @@ cudaError_t launch_q4k_fused(const void* W, size_t rb, int rows, int K, const fl
   if (occ < CPS) return CPS > 1 ? cudaErrorNotReady : cudaErrorUnknown;
   const int tiles = (rows + kTileRows - 1) / kTileRows;
   const int grid = std::min(tiles, CPS * sm_count());
-  kern<<<grid, NW * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, K / 256, x, ldx,
-                                        tokens, y, ldy, plan, status);
-  return cudaGetLastError();
+  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(NW * 32), smem, stream,
+                                   static_cast<const uint8_t*>(W), rb, rows, K / 256, x, ldx,
+                                   tokens, y, ldy, plan, status);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int NG, bool SLOT>
