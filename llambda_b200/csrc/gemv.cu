@@ -99,6 +99,8 @@ __global__ void __launch_bounds__(64) m6_prep_kernel(const float* __restrict__ x
                                                      const int* __restrict__ gather,
                                                      uint8_t* __restrict__ m6) {
   const int sb = blockIdx.x, tok = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_wait();  // x is the kernel before's output; m6 may still be its input
+  griddep_launch();
   const long row = gather ? gather[tok] : tok;
   const float* s = x + row * ldx;
   uint8_t* dst = m6 + (size_t)tok * m6_bytes(K);
@@ -173,6 +175,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
     }
     return;
   }
+  // consumers: the prepared input is the kernel before's output (the
+  // producer's weight copies above need no wait)
+  griddep_wait();
+  griddep_launch();
   const int sb0 = warp * nsb / CW, sb1 = (warp + 1) * nsb / CW;
   const int g = lane >> 2, t = lane & 3;
   const size_t m6b = m6_bytes(nsb * 256);
@@ -1050,22 +1056,24 @@ cudaError_t launch_q6k_slab(const void* W, size_t rb, int rows, int K, const uin
   const size_t smem = (size_t)stages * per_stage + sizeof(DenseSync);
   const int units = rows / kTileRows;
   const int grid = std::max(1, std::min(units, sm_count()));
+  // programmatic launch: the weight copies start while the input's
+  // preparation (the kernel before) still runs
   if constexpr (NG == 1) {  // only one group is instantiated wide
     if (wide) {
       auto kern = gemv_q6k_slab_kernel<NG, 16, SLOT>;
       if (prepared_occupancy(kern, 17 * 32, smem) < 1) return cudaErrorUnknown;
-      kern<<<grid, 17 * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, nsb, m6,
-                                            tokens, y, ldy, stages, stage_bytes, status);
-      return cudaGetLastError();
+      const cudaError_t e =
+          launch_pdl(kern, dim3(grid), dim3(17 * 32), smem, stream, static_cast<const uint8_t*>(W),
+                     rb, rows, nsb, m6, tokens, y, ldy, stages, stage_bytes, status);
+      return e != cudaSuccess ? e : cudaGetLastError();
     }
   }
-  {
-    auto kern = gemv_q6k_slab_kernel<NG, 8, SLOT>;
-    if (prepared_occupancy(kern, 9 * 32, smem) < 1) return cudaErrorUnknown;
-    kern<<<grid, 9 * 32, smem, stream>>>(static_cast<const uint8_t*>(W), rb, rows, nsb, m6,
-                                         tokens, y, ldy, stages, stage_bytes, status);
-  }
-  return cudaGetLastError();
+  auto kern = gemv_q6k_slab_kernel<NG, 8, SLOT>;
+  if (prepared_occupancy(kern, 9 * 32, smem) < 1) return cudaErrorUnknown;
+  const cudaError_t e =
+      launch_pdl(kern, dim3(grid), dim3(9 * 32), smem, stream, static_cast<const uint8_t*>(W), rb,
+                 rows, nsb, m6, tokens, y, ldy, stages, stage_bytes, status);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // The sliced kernel for 3..8 tokens when K is 8 or 16 super-blocks; false
@@ -1116,11 +1124,11 @@ cudaError_t launch_prep(int type, int rows, const float* x, long ldx, int n_vali
   if (type == LB_TYPE_Q4_K)
     prep_kernel<LB_TYPE_Q4_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
   else if (type == LB_TYPE_Q6_K && q6k_dense_mma(rows) && q6k_dense_slots(tokens))
-    m6_prep_kernel<true><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather,
-                                                  reinterpret_cast<uint8_t*>(xp));
+    return launch_pdl(m6_prep_kernel<true>, grid, dim3(64), 0, stream, x, ldx, n_valid, K,
+                      gather, reinterpret_cast<uint8_t*>(xp));
   else if (type == LB_TYPE_Q6_K && q6k_dense_mma(rows))
-    m6_prep_kernel<false><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather,
-                                                   reinterpret_cast<uint8_t*>(xp));
+    return launch_pdl(m6_prep_kernel<false>, grid, dim3(64), 0, stream, x, ldx, n_valid, K,
+                      gather, reinterpret_cast<uint8_t*>(xp));
   else if (type == LB_TYPE_Q6_K)
     prep_kernel<LB_TYPE_Q6_K><<<grid, 64, 0, stream>>>(x, ldx, n_valid, K, gather, xp);
   else
