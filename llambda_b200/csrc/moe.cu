@@ -375,6 +375,88 @@ __global__ void __launch_bounds__(kTopkSmallTokens * 32) topk_route_small_kernel
 // 8 warps.  pass_nt / pass_dn: tokens per pass of the up / down kernel;
 // pass_off / pass_off_dn count passes.  CG: the selections were written by other CTAs of the same launch
 // (read through L2).
+// The per-expert part of the routing, from the entries' per-expert counts in
+// shared memory: exclusive scans over experts (entries, up passes, down
+// passes) and the active list in increasing expert id, written with the
+// counts and the offsets.  Whole CTA of up to 8 warps.
+__device__ __forceinline__ void route_scan(const MoeDevice& m, const MoeWork& w, int pass_nt,
+                                           int pass_dn, const int* s_count, int* s_offset) {
+  const int E = m.experts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Exclusive scans over experts (entries, up passes, down passes) and the
+  // active list in increasing expert id: warp wp takes experts
+  // [wp*per_w, (wp+1)*per_w); pass 1 sums each warp's range, pass 2 scans it
+  // from the sum of the ranges before it.
+  {
+    __shared__ int s_tot[8][4];
+    const int nw = blockDim.x >> 5;
+    const int per_w = ((E + nw - 1) / nw + 31) & ~31;
+    const int e_lo = warp * per_w, e_hi = min(E, e_lo + per_w);
+    const unsigned lt_mask = (1u << lane) - 1u;
+    int tot[4] = {0, 0, 0, 0};  // entries, active experts, up passes, down passes
+    for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
+      const int e = e0 + lane;
+      const int cnt = e < e_hi ? s_count[e] : 0;
+      tot[0] += (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
+      tot[1] += __popc(__ballot_sync(0xffffffffu, cnt > 0));
+      tot[2] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_nt - 1) / pass_nt));
+      tot[3] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_dn - 1) / pass_dn));
+    }
+    if (lane < 4)  // (selects, not a register array indexed by the lane)
+      s_tot[warp][lane] = lane == 0 ? tot[0] : lane == 1 ? tot[1] : lane == 2 ? tot[2] : tot[3];
+    __syncthreads();
+    int run = 0, nact = 0, prun = 0, drun = 0;
+    for (int q = 0; q < warp; ++q) {
+      run += s_tot[q][0];
+      nact += s_tot[q][1];
+      prun += s_tot[q][2];
+      drun += s_tot[q][3];
+    }
+    for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
+      const int e = e0 + lane;
+      const int cnt = e < e_hi ? s_count[e] : 0;
+      const int pc = (cnt + pass_nt - 1) / pass_nt, dc = (cnt + pass_dn - 1) / pass_dn;
+      int incl = cnt, pincl = pc, dincl = dc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        const int pv = __shfl_up_sync(0xffffffffu, pincl, o);
+        const int dv = __shfl_up_sync(0xffffffffu, dincl, o);
+        if (lane >= o) {
+          incl += v;
+          pincl += pv;
+          dincl += dv;
+        }
+      }
+      if (e < e_hi) s_offset[e] = run + incl - cnt;
+      const unsigned nz = __ballot_sync(0xffffffffu, cnt > 0);
+      if (cnt > 0) {
+        const int a = nact + __popc(nz & lt_mask);
+        w.active[a] = e;
+        w.pass_off[a] = prun + pincl - pc;
+        w.pass_off_dn[a] = drun + dincl - dc;
+      }
+      nact += __popc(nz);
+      run += __shfl_sync(0xffffffffu, incl, 31);
+      prun += __shfl_sync(0xffffffffu, pincl, 31);
+      drun += __shfl_sync(0xffffffffu, dincl, 31);
+    }
+    if (warp == nw - 1 && lane == 0) {
+      s_offset[E] = run;
+      w.active[E] = nact;
+      w.pass_off[nact] = prun;
+      w.pass_off_dn[nact] = drun;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    w.counts[e] = s_count[e];
+    w.offsets[e] = s_offset[e];
+  }
+  if (threadIdx.x == 0) w.offsets[E] = s_offset[E];
+  __syncthreads();
+}
+
 template <int SRC>
 __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w, int T,
                                             int pass_nt, int pass_dn, bool grouped_ids,
@@ -465,78 +547,7 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
     }
     __syncthreads();
   }
-  // Exclusive scans over experts (entries, up passes, down passes) and the
-  // active list in increasing expert id: warp wp takes experts
-  // [wp*per_w, (wp+1)*per_w); pass 1 sums each warp's range, pass 2 scans it
-  // from the sum of the ranges before it.
-  {
-    __shared__ int s_tot[8][4];
-    const int nw = blockDim.x >> 5;
-    const int per_w = ((E + nw - 1) / nw + 31) & ~31;
-    const int e_lo = warp * per_w, e_hi = min(E, e_lo + per_w);
-    const unsigned lt_mask = (1u << lane) - 1u;
-    int tot[4] = {0, 0, 0, 0};  // entries, active experts, up passes, down passes
-    for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
-      const int e = e0 + lane;
-      const int cnt = e < e_hi ? s_count[e] : 0;
-      tot[0] += (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
-      tot[1] += __popc(__ballot_sync(0xffffffffu, cnt > 0));
-      tot[2] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_nt - 1) / pass_nt));
-      tot[3] += (int)__reduce_add_sync(0xffffffffu, (unsigned)((cnt + pass_dn - 1) / pass_dn));
-    }
-    if (lane < 4)  // (selects, not a register array indexed by the lane)
-      s_tot[warp][lane] = lane == 0 ? tot[0] : lane == 1 ? tot[1] : lane == 2 ? tot[2] : tot[3];
-    __syncthreads();
-    int run = 0, nact = 0, prun = 0, drun = 0;
-    for (int q = 0; q < warp; ++q) {
-      run += s_tot[q][0];
-      nact += s_tot[q][1];
-      prun += s_tot[q][2];
-      drun += s_tot[q][3];
-    }
-    for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
-      const int e = e0 + lane;
-      const int cnt = e < e_hi ? s_count[e] : 0;
-      const int pc = (cnt + pass_nt - 1) / pass_nt, dc = (cnt + pass_dn - 1) / pass_dn;
-      int incl = cnt, pincl = pc, dincl = dc;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        const int pv = __shfl_up_sync(0xffffffffu, pincl, o);
-        const int dv = __shfl_up_sync(0xffffffffu, dincl, o);
-        if (lane >= o) {
-          incl += v;
-          pincl += pv;
-          dincl += dv;
-        }
-      }
-      if (e < e_hi) s_offset[e] = run + incl - cnt;
-      const unsigned nz = __ballot_sync(0xffffffffu, cnt > 0);
-      if (cnt > 0) {
-        const int a = nact + __popc(nz & lt_mask);
-        w.active[a] = e;
-        w.pass_off[a] = prun + pincl - pc;
-        w.pass_off_dn[a] = drun + dincl - dc;
-      }
-      nact += __popc(nz);
-      run += __shfl_sync(0xffffffffu, incl, 31);
-      prun += __shfl_sync(0xffffffffu, pincl, 31);
-      drun += __shfl_sync(0xffffffffu, dincl, 31);
-    }
-    if (warp == nw - 1 && lane == 0) {
-      s_offset[E] = run;
-      w.active[E] = nact;
-      w.pass_off[nact] = prun;
-      w.pass_off_dn[nact] = drun;
-    }
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    w.counts[e] = s_count[e];
-    w.offsets[e] = s_offset[e];
-  }
-  if (threadIdx.x == 0) w.offsets[E] = s_offset[E];
-  __syncthreads();
+  route_scan(m, w, pass_nt, pass_dn, s_count, s_offset);
   // Scatter entry ids into their expert-grouped slots (second half of entries;
   // the first half holds each entry's position within its expert).  The
   // prefill path reads positions only and skips it.  Four entries' loads
@@ -558,6 +569,46 @@ __device__ __forceinline__ void route_block(const MoeDevice& m, const MoeWork& w
   }
 }
 
+
+// Prefill batches: the top-k of every token (one warp each) and each owned
+// entry's position within its expert, taken by an atomic increment of the
+// expert's count (zeroed before the launch); the last CTA to finish (an
+// arrival ticket) scans the counts.  Positions within an expert follow
+// arrival, not entry order: the prefill passes compute every grouped row from
+// its own token alone, so the order changes no value.  The one-CTA stable
+// grouping it replaces walked all T * k entries (20480 at batch 2048) on the
+// routing CTA.
+template <int PER>
+__global__ void __launch_bounds__(256) topk_count_kernel(MoeDevice m, MoeWork w, int T,
+                                                         int pass_nt, int pass_dn) {
+  __shared__ int s_last;
+  __shared__ int s_count[kMaxExperts];
+  __shared__ int s_offset[kMaxExperts + 1];
+  griddep_wait();
+  griddep_launch();
+  const int lane = threadIdx.x & 31, k = m.top_k;
+  const int t = blockIdx.x * kTopkTokens + (threadIdx.x >> 5);
+  if (t < T) {
+    topk_token<PER>(m, w, t, lane);
+    if (lane < k) {
+      const int e = w.sel[t * k + lane];  // this thread's own store
+      const bool own = e >= m.expert_begin && e < m.expert_end;
+      w.entries[t * k + lane] = own ? atomicAdd(w.counts + e, 1) : -1;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(w.tickets, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // every CTA's counts are final from here
+  for (int e = threadIdx.x; e < m.experts; e += blockDim.x) s_count[e] = __ldcg(w.counts + e);
+  __syncthreads();
+  route_scan(m, w, pass_nt, pass_dn, s_count, s_offset);
+  if (threadIdx.x == 0) *w.tickets = 0;
+  if (w.up_tickets)
+    for (int i = threadIdx.x; i < kUpSplitItems; i += blockDim.x) w.up_tickets[i] = 0;
+}
 
 // ---------------------------------------------------------------- prep
 // Per token: optional rms-norm (rms-norm-into, llambda.lisp L859-879:
@@ -2470,6 +2521,16 @@ cudaError_t launch_topk(const MoeDevice& m, const MoeWork& w, int T, int grouped
                : topk_route_small_kernel<16>;
     cudaError_t e = launch_pdl(small, dim3(1), dim3(32 * kTopkSmallTokens), 0, s, m, w, T, pnt,
                                pdn, grouped_ids);
+    return e != cudaSuccess ? e : cudaGetLastError();
+  }
+  if (grouped_ids == 0) {  // prefill: positions by atomic counts, no stable walk
+    cudaError_t e = cudaMemsetAsync(w.counts, 0, (size_t)m.experts * sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    auto cnt = per <= 1 ? topk_count_kernel<1> : per <= 2 ? topk_count_kernel<2>
+             : per <= 4 ? topk_count_kernel<4> : per <= 8 ? topk_count_kernel<8>
+             : per <= 16 ? topk_count_kernel<16> : topk_count_kernel<32>;
+    e = launch_pdl(cnt, dim3((T + kTopkTokens - 1) / kTopkTokens), dim3(256), 0, s, m, w, T, pnt,
+                   pdn);
     return e != cudaSuccess ? e : cudaGetLastError();
   }
   auto kern = per <= 1 ? topk_route_kernel<1> : per <= 2 ? topk_route_kernel<2>
