@@ -814,22 +814,45 @@ __global__ void __launch_bounds__(256) pf_norm_kernel(MoeDevice m, MoeWork w,
 
 constexpr int kRtTok = 128, kRtRows = 64, kRtK = 32;
 
+// tf32 value of an fp32 (its top 10 mantissa bits) and the rest
+__device__ __forceinline__ uint32_t tf32_hi(float v) { return __float_as_uint(v) & 0xFFFFE000u; }
+__device__ __forceinline__ uint32_t tf32_lo(float v) {
+  return __float_as_uint(v - __uint_as_float(tf32_hi(v))) & 0xFFFFE000u;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Router logits of a prefill batch (dot-product-with-f32-tensor-data,
 // L4096-4107, for every router row; row E of the logits is the qwen3next
-// shared-expert gate, L3491-3500): an fp32 register-blocked GEMM, 128 tokens
-// x 64 rows per CTA over one K slice, K in chunks of 32 staged through shared
-// memory (the next chunk's float4 loads in flight during the current one's
-// FMAs), 8 tokens x 4 rows per thread on packed fp32x2 FMA.  fp32
-// throughout, so the expert selection is that of the decode path's router.
+// shared-expert gate, L3491-3500) on the tensor cores in three-pass tf32:
+// every fp32 operand is split into a tf32 high part and a tf32 part of the
+// rest, and each product is accumulated as lo*hi + hi*lo + hi*hi (the
+// dropped lo*lo and the truncations leave about 2^-21 of each product), fp32
+// accumulation.  A CTA takes 128 tokens x 64 rows over one K slice, K in
+// chunks of 32 staged through shared memory (the next chunk's float4 loads
+// in flight during the current one's mma); warp (wm, wn) of 4 x 2 takes 32
+// tokens x 32 rows, mma.m16n8k8: A = the tokens (rows of xs), B = the router
+// rows (rows of ws), rows 36 floats apart so the fragment loads of a warp
+// hit 32 distinct banks.  (The fp32 FMA form of the same tiling ran at 32
+// TFLOP/s: 134 us at batch 2048.)
 __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
                                                         const float* __restrict__ xr, int T,
                                                         int all_rows, int kc) {
-  __shared__ __align__(16) float xs[kRtK][kRtTok + 4];
-  __shared__ __align__(16) float ws[kRtK][kRtRows + 4];
+  constexpr int P = kRtK + 4;  // row pitch (floats)
+  __shared__ __align__(16) float xs[kRtTok][P];
+  __shared__ __align__(16) float ws[kRtRows][P];
   const int t0 = blockIdx.y * kRtTok, r0 = blockIdx.x * kRtRows;
   // K slice blockIdx.z of kc values (gridDim.z slices; one: the whole row)
   const int kb = blockIdx.z * kc, K = min(m.hidden - kb, kc);
-  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3, wm = warp & 3, wn = warp >> 2;
   // staging: token row tid/2 (16 values from (tid&1)*16), router row tid/4 (8 from (tid&3)*8)
   const int xr_row = tid >> 1, xk = (tid & 1) * 16, wr_row = tid >> 2, wk = (tid & 3) * 8;
   const float* xrow = xr + (long)min(t0 + xr_row, T - 1) * m.hidden + kb;
@@ -839,9 +862,13 @@ __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
   const bool vec = ((m.hidden | kb) & 3) == 0 &&
                    ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(m.router) |
                      reinterpret_cast<uintptr_t>(m.router_extra_row)) & 15) == 0;
-  float2 acc[8][2];
+  float acc[2][4][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
   float xv[16], wv[8];
   auto fetch = [&](int k0) {
     if (vec && k0 + kRtK <= K) {
@@ -866,37 +893,66 @@ __global__ void __launch_bounds__(256) pf_router_kernel(MoeDevice m, MoeWork w,
   for (int k0 = 0; k0 < K; k0 += kRtK) {
     __syncthreads();
 #pragma unroll
-    for (int j = 0; j < 16; ++j) xs[xk + j][xr_row] = xv[j];
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4*>(&xs[xr_row][xk + 4 * j]) =
+          make_float4(xv[4 * j], xv[4 * j + 1], xv[4 * j + 2], xv[4 * j + 3]);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ws[wk + j][wr_row] = wv[j];
+    for (int j = 0; j < 2; ++j)
+      *reinterpret_cast<float4*>(&ws[wr_row][wk + 4 * j]) =
+          make_float4(wv[4 * j], wv[4 * j + 1], wv[4 * j + 2], wv[4 * j + 3]);
     __syncthreads();
     if (k0 + kRtK < K) fetch(k0 + kRtK);
 #pragma unroll
-    for (int k = 0; k < kRtK; ++k) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&xs[k][ty * 8]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&xs[k][ty * 8 + 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    for (int ks = 0; ks < kRtK; ks += 8) {
+      uint32_t ah[2][4], al[2][4], bh[4][2], bl[4][2];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        acc[i][0] = __ffma2_rn(make_float2(av[i], av[i]), make_float2(b.x, b.y), acc[i][0]);
-        acc[i][1] = __ffma2_rn(make_float2(av[i], av[i]), make_float2(b.z, b.w), acc[i][1]);
+      for (int i = 0; i < 2; ++i) {
+        const int mr = wm * 32 + i * 16 + g;
+        const float a[4] = {xs[mr][ks + t], xs[mr + 8][ks + t], xs[mr][ks + t + 4],
+                            xs[mr + 8][ks + t + 4]};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          ah[i][c] = tf32_hi(a[c]);
+          al[i][c] = tf32_lo(a[c]);
+        }
       }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int nr = wn * 32 + j * 8 + g;
+        const float b[2] = {ws[nr][ks + t], ws[nr][ks + t + 4]};
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          bh[j][c] = tf32_hi(b[c]);
+          bl[j][c] = tf32_lo(b[c]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          mma_tf32(acc[i][j], al[i][0], al[i][1], al[i][2], al[i][3], bh[j][0], bh[j][1]);
+          mma_tf32(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bl[j][0], bl[j][1]);
+          mma_tf32(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bh[j][0], bh[j][1]);
+        }
     }
   }
   const int E1 = m.experts + 1;
   float* dst = gridDim.z == 1 ? w.logits : w.pf_rlog + (long)blockIdx.z * T * E1;
+  // D of tile (i, j): [0] token g, row 2t; [1] token g, row 2t+1; [2], [3] token g+8
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int t = t0 + ty * 8 + i;
-    if (t >= T) continue;
-    const float v[4] = {acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y};
+  for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = r0 + tx * 4 + j;
-      if (r < all_rows) dst[(long)t * E1 + r] = v[j];
+    for (int h = 0; h < 2; ++h) {
+      const int tok = t0 + wm * 32 + i * 16 + g + 8 * h;
+      if (tok >= T) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int r = r0 + wn * 32 + j * 8 + 2 * t + c;
+          if (r < all_rows) dst[(long)tok * E1 + r] = acc[i][j][2 * h + c];
+        }
     }
-  }
 }
 
 // logits = the K slices' partial logits summed in slice order.
